@@ -1,0 +1,112 @@
+"""Seeded random-init weights of a config, under the reference's tensor names (Text::new, runtime/model.rs:272-313).
+
+Distributions follow the graded configs: ternary codes uniform in {0,1,2}, fp16 scales U(0.01, 0.05) with bias -s
+(or the implicit -s of the reference pack), bf16 embedding / lm_head N(0, 0.02). The rest (not specified by the
+configs) keeps activations O(1): norm weights U(0.8, 1.2), GDN a/b rows N(0, 1/sqrt(hidden)) so the gate logits are
+~N(0, 1), A_log = dt_bias = 0 (decay exp(-softplus(a)) as config 2 states), conv taps N(0, 0.5).
+All values come from bcu_synth_fill, so the same seed gives the same bytes on every host.
+"""
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from .config import dims
+
+PFX = "language_model.model."
+
+
+def fill(kind, seed, stream, a, b, shape, dtype):
+    arr = np.empty(shape, dtype=dtype)
+    n = arr.size // 16 if kind == 3 else arr.size
+    if kind == 3:
+        n = arr.size
+    s = _lib.lib().bcu_synth_fill(kind, seed, stream, a, b, arr.ctypes.data_as(ctypes.c_void_p), n)
+    if s != _lib.OK:
+        raise RuntimeError("bcu_synth_fill failed")
+    return arr
+
+
+class TensorSet:
+    """Ordered (name, dtype code, array) triples; arrays are C-contiguous numpy views of the tensor bytes."""
+
+    def __init__(self):
+        self.items = []
+
+    def add(self, name, code, arr):
+        self.items.append((name, code, np.ascontiguousarray(arr)))
+
+    def __iter__(self):
+        return iter(self.items)
+
+    def get(self, name):
+        for n, c, a in self.items:
+            if n == name:
+                return a
+        raise KeyError(name)
+
+    def nbytes(self):
+        return sum(a.nbytes for _, _, a in self.items)
+
+
+def model_tensors(cfg, seed=1234):
+    d, ff = cfg.hidden, cfg.intermediate
+    dm = dims(cfg)
+    C, gw, aw, kvw = dm["C"], dm["gw"], dm["aw"], dm["kvw"]
+    g = cfg.group_size
+    ts = TensorSet()
+    stream = [0]
+
+    def nxt():
+        stream[0] += 1
+        return stream[0]
+
+    def packed(name, O, K):
+        ts.add(name + ".weight", _lib.U32, fill(3, seed, nxt(), 0, 0, (O, K // 16), np.uint32))
+        st = nxt()
+        ts.add(name + ".scales", _lib.F16, fill(4, seed, st, 0.01, 0.05, (O, K // g), np.uint16))
+        if cfg.has_bias:
+            ts.add(name + ".biases", _lib.F16, fill(6, seed, st, 0.01, 0.05, (O, K // g), np.uint16))
+        if cfg.has_signs:
+            ts.add(name + ".signs", _lib.F32, fill(5, seed, nxt(), 0, 0, (K,), np.float32))
+
+    def norm(name, n):
+        ts.add(name, _lib.F32, fill(0, seed, nxt(), 0.8, 1.2, (n,), np.float32))
+
+    for i in range(cfg.n_layers):
+        l = f"{PFX}layers.{i}."
+        norm(l + "input_layernorm.weight", d)
+        norm(l + "post_attention_layernorm.weight", d)
+        if cfg.layer_is_attn[i]:
+            a = l + "self_attn."
+            packed(a + "q_proj", 2 * aw, d)
+            packed(a + "k_proj", kvw, d)
+            packed(a + "v_proj", kvw, d)
+            packed(a + "o_proj", d, aw)
+            norm(a + "q_norm.weight", 256)
+            norm(a + "k_norm.weight", 256)
+        else:
+            a = l + "linear_attn."
+            packed(a + "in_proj_qkv", C, d)
+            packed(a + "in_proj_z", gw, d)
+            packed(a + "out_proj", d, gw)
+            nv = cfg.lin_v_heads
+            ts.add(a + "in_proj_a.weight", _lib.F32, fill(1, seed, nxt(), 0.0, d ** -0.5, (nv, d), np.float32))
+            ts.add(a + "in_proj_b.weight", _lib.F32, fill(1, seed, nxt(), 0.0, d ** -0.5, (nv, d), np.float32))
+            ts.add(a + "A_log", _lib.F32, np.zeros(nv, np.float32))
+            ts.add(a + "dt_bias", _lib.F32, np.zeros(nv, np.float32))
+            ts.add(a + "conv1d.weight", _lib.F32, fill(1, seed, nxt(), 0.0, 0.5, (C, 4), np.float32))
+            norm(a + "norm.weight", 128)
+        m = l + "mlp."
+        packed(m + "gate_proj", ff, d)
+        packed(m + "up_proj", ff, d)
+        packed(m + "down_proj", d, ff)
+    norm(PFX + "norm.weight", d)
+    ts.add(PFX + "embed_tokens.weight", _lib.BF16, fill(2, seed, nxt(), 0.0, 0.02, (cfg.vocab, d), np.uint16))
+    return ts
+
+
+def zipf_tokens(seed, n, vocab, s=1.1):
+    out = np.empty(n, np.uint32)
+    _lib.lib().bcu_synth_zipf(seed, s, vocab, out.ctypes.data_as(_lib.PU32), n)
+    return out

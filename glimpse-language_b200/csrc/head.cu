@@ -1,0 +1,207 @@
+// head.cu — tied bf16 lm_head over all T rows with the argmax and the accept length fused in (encode_head_to,
+// model.rs:941-985; argmax1/argmax2, kernels.metal:802-842; the accept length of decode_spec, runtime/mod.rs:866-868).
+//
+// The 248320 x 2048 bf16 table is 62% of a verify pass's bytes, so this kernel is a pure stream: the table is
+// stored in mma fragment order (one LDG.128 per lane per 16x16 tile), the normed rows are a bf16 hi/lo operand kept in
+// shared memory, and mma.m16n8k16 does the T-row products (fp32 accumulate). Logits never go to HBM: every warp keeps
+// a running (max, lowest index) per row; CTAs publish partials, and the last CTA to finish merges them in CTA order,
+// computes the accept length m on the device and advances the control block (KV offset, replay count, parity), so only
+// m and the bonus token need to reach the host.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace bcu {
+
+__global__ void repack_head_kernel(const uint16_t* __restrict__ table, int V, int d, uint32_t* __restrict__ out) {
+    size_t n = (size_t)V * d / 2;  // u32 outputs
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n) return;
+    int r = idx & 3;
+    int lane = (idx >> 2) & 31;
+    size_t tile = idx >> 7;  // mt * (d/16) + ks
+    int nks = d / 16;
+    int ks = tile % nks;
+    size_t mt = tile / nks;
+    int g = lane >> 2, t4 = lane & 3;
+    size_t row = mt * 16 + g + ((r & 1) ? 8 : 0);
+    int k = ks * 16 + 2 * t4 + ((r & 2) ? 8 : 0);
+    out[idx] = (uint32_t)table[row * d + k] | ((uint32_t)table[row * d + k + 1] << 16);
+}
+
+void repack_head_bf16(const uint16_t* table, int V, int d, uint32_t* out, cudaStream_t st) {
+    size_t n = (size_t)V * d / 2;
+    repack_head_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(table, V, d, out);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* bar = (uint64_t*)smem;
+    uint2* s_b = (uint2*)(smem + 128);
+    __shared__ float wbv[8][16];
+    __shared__ int wbi[8][16];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nks = a.d / 16;
+    const uint32_t b_bytes = (uint32_t)(nks * NT * 256);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();
+    if (tid == 0) {
+        mbar_expect_tx(bar, b_bytes);
+        bulk_g2s(s_b, a.bfrag, b_bytes, bar);
+    }
+    bool ok = mbar_wait_bounded(bar, 0);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) atomicOr(&a.ctl->err, ERR_MBAR_TIMEOUT);
+        mbar_wait_bounded(bar, 0, 1u << 20);
+        return;
+    }
+    const int keep = a.ctl->in.keep_logits;
+    const int T = a.T;
+    const int g = lane >> 2, t4 = lane & 3;
+    float bv[NT];
+    int bi[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        bv[n] = -INFINITY;
+        bi[n] = 0x7fffffff;
+    }
+    const int nmt = a.V / 16;
+    const int gw = blockIdx.x * 8 + warp, W = gridDim.x * 8;
+    // contiguous m-tile range per warp (rows visited in increasing order)
+    const int per = (nmt + W - 1) / W;
+    const int mt0 = gw * per, mt1 = min(nmt, mt0 + per);
+    for (int mt = mt0; mt < mt1; mt++) {
+        const uint4* wp = (const uint4*)a.w + (size_t)mt * nks * 32 + lane;
+        float acc[NT][4];
+#pragma unroll
+        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+        uint4 buf0[8], buf1[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) buf0[i] = __ldcs(wp + (size_t)i * 32);
+        for (int kb = 0; kb < nks; kb += 16) {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (kb + 8 + i < nks) buf1[i] = __ldcs(wp + (size_t)(kb + 8 + i) * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                int ks = kb + i;
+#pragma unroll
+                for (int n = 0; n < NT; n++) {
+                    uint2 b = s_b[((size_t)ks * NT + n) * 32 + lane];
+                    mma_bf16(acc[n], buf0[i].x, buf0[i].y, buf0[i].z, buf0[i].w, b.x, b.y);
+                }
+            }
+            if (kb + 8 >= nks) break;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (kb + 16 + i < nks) buf0[i] = __ldcs(wp + (size_t)(kb + 16 + i) * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                int ks = kb + 8 + i;
+                if (ks < nks) {
+#pragma unroll
+                    for (int n = 0; n < NT; n++) {
+                        uint2 b = s_b[((size_t)ks * NT + n) * 32 + lane];
+                        mma_bf16(acc[n], buf1[i].x, buf1[i].y, buf1[i].z, buf1[i].w, b.x, b.y);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            int token = n * 4 + t4;
+            float v0 = acc[n][0] + acc[n][1], v1 = acc[n][2] + acc[n][3];
+            int r0 = mt * 16 + g, r1 = r0 + 8;
+            if (keep && token < T) {
+                a.logits[(size_t)token * a.V + r0] = v0;
+                a.logits[(size_t)token * a.V + r1] = v1;
+            }
+            argmax_merge(bv[n], bi[n], v0, r0);
+            argmax_merge(bv[n], bi[n], v1, r1);
+        }
+    }
+    // lanes with the same t4 hold the same token: merge over g
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv[n], o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi[n], o);
+            argmax_merge(bv[n], bi[n], ov, oi);
+        }
+        if (g == 0) {
+            wbv[warp][n * 4 + t4] = bv[n];
+            wbi[warp][n * 4 + t4] = bi[n];
+        }
+    }
+    __syncthreads();
+    if (tid < T) {
+        float v = -INFINITY;
+        int i = 0x7fffffff;
+        for (int w = 0; w < 8; w++) argmax_merge(v, i, wbv[w][tid], wbi[w][tid]);
+        a.pv[(size_t)blockIdx.x * T + tid] = v;
+        a.pi[(size_t)blockIdx.x * T + tid] = i;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    __shared__ uint32_t pred[16];
+    if (tid < T) {
+        float v = -INFINITY;
+        int i = 0x7fffffff;
+        for (int c = 0; c < (int)gridDim.x; c++)
+            argmax_merge(v, i, __ldcg(a.pv + (size_t)c * T + tid), __ldcg(a.pi + (size_t)c * T + tid));
+        if (i == 0x7fffffff) i = 0;  // every logit NaN or -inf: index 0, like argmax2's initial value
+        pred[tid] = (uint32_t)i;
+        a.ctl->pred[tid] = (uint32_t)i;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        Ctl* c = a.ctl;
+        int m;
+        if (c->in.commit_all) {
+            m = T - 1;
+        } else {
+            m = 0;
+            while (m < T - 1 && c->used[m + 1] == pred[m]) m++;
+        }
+        c->accepted = m;
+        c->bonus = pred[m];
+        int nrows = c->in.commit_all ? T : m + 1;
+        c->replay_n = nrows;
+        c->off += nrows;
+        c->parity ^= 1;
+        *a.counter = 0;
+    }
+}
+
+template <int NT>
+static void launch_head_t(const HeadArgs& a, int grid, cudaStream_t st) {
+    size_t smem = 128 + (size_t)(a.d / 16) * NT * 256;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    HeadArgs aa = a;
+    void* args[] = {&aa};
+    launch_pdl((const void*)head_kernel<NT>, dim3(grid), dim3(256), smem, st, args);
+}
+
+void launch_head(const HeadArgs& a, int NT, int grid, cudaStream_t st) {
+    if (NT == 1) launch_head_t<1>(a, grid, st);
+    else if (NT == 2) launch_head_t<2>(a, grid, st);
+    else if (NT == 3) launch_head_t<3>(a, grid, st);
+    else launch_head_t<4>(a, grid, st);
+}
+
+}  // namespace bcu

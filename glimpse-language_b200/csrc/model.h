@@ -1,0 +1,124 @@
+// model.h — host-side model object behind the C ABI (include/bonsai_cuda.h).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/bonsai_cuda.h"
+#include "ctl.h"
+#include "kernels.h"
+
+namespace bcu {
+
+struct DevTensor {
+    int dtype = 0;
+    std::vector<int64_t> shape;
+    void* dev = nullptr;
+    size_t bytes = 0;
+};
+
+// One packed linear (possibly several reference matrices sharing an input, stacked by rows).
+struct Lin {
+    TernaryMat m;
+    const float* signs = nullptr;
+};
+
+struct Layer {
+    bool attn = false;
+    const float *in_norm = nullptr, *post_norm = nullptr;
+    Lin mix_in;   // GDN: [qkv; z]   attention: [q (with gate); k; v]
+    Lin mix_out;  // GDN: out_proj   attention: o_proj
+    Lin gu;       // [gate; up]
+    Lin down;
+    const float *wa = nullptr, *wb = nullptr, *a_log = nullptr, *dt_bias = nullptr, *convw = nullptr, *gnorm = nullptr;
+    const float *qn = nullptr, *kn = nullptr;
+    int gi = -1, ai = -1;
+};
+
+}  // namespace bcu
+
+struct bcu_state {
+    int len = 0;
+    float *gdn = nullptr, *conv = nullptr, *kc = nullptr, *vc = nullptr;
+    size_t gdn_bytes = 0, conv_bytes = 0, kv_bytes = 0;
+};
+
+struct bcu_model {
+    bcu_config c{};
+    int device = 0, num_sms = 148;
+    cudaStream_t st = nullptr;
+    std::string err;
+    bool finalized = false;
+    volatile int cancel = 0;
+    std::map<std::string, bcu::DevTensor> staged;
+
+    // derived sizes
+    int C = 0, gw = 0, aw = 0, kvw = 0, n_gdn = 0, n_attn = 0;
+
+    // weights
+    void* arena = nullptr;
+    size_t arena_bytes = 0, arena_used = 0;
+    std::vector<bcu::Layer> layers;
+    uint32_t* head_w = nullptr;     // fragment-ordered bf16 table
+    uint16_t* embed_rows = nullptr; // row-major bf16 table (gathers)
+    const float* final_norm = nullptr;
+    float* inv_freq = nullptr;
+
+    // state (fp32, the reference's layouts: gdn [NV][128][128], conv [3][C], K/V [ctx][KV][256] per layer)
+    float *gdn = nullptr, *conv = nullptr, *kc = nullptr, *vc = nullptr;
+    float *pend_qkv = nullptr, *pend_qkvc = nullptr, *pend_ab = nullptr;
+
+    // scratch
+    float *h = nullptr, *xn = nullptr, *mix = nullptr, *gubuf = nullptr, *y = nullptr, *q = nullptr, *apart = nullptr;
+    float* logits = nullptr;
+    uint32_t* bfrag = nullptr;
+    uint32_t* hfrag = nullptr;
+    float* xsum = nullptr;
+    int* xexp = nullptr;
+    float* partial = nullptr;
+    unsigned* counters = nullptr;
+    unsigned* head_counter = nullptr;
+    float* pv = nullptr;
+    int* pi = nullptr;
+    int head_grid = 0;
+    size_t partial_floats = 0;
+
+    bcu::Ctl* ctl = nullptr;       // device
+    bcu::CtlIn* h_in = nullptr;    // host copy of the next pass's ctl->in (edited freely; staged by stage_in)
+    static constexpr int IN_SLOTS = 64;
+    bcu::CtlIn* in_ring = nullptr;  // pinned staging slots: a slot is reused only after its copy has completed
+    cudaEvent_t in_ev[IN_SLOTS] = {};
+    bool in_used[IN_SLOTS] = {};
+    int in_next = 0;
+    bcu::Ctl* h_out = nullptr;     // pinned host copy of the control block
+    uint32_t* planted_dev = nullptr;
+    int planted_cap = 0;
+
+    cudaGraphExec_t graphs[bcu::VMAX + 1] = {};
+    int graph_nodes[bcu::VMAX + 1] = {};
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev_done = nullptr;
+    cudaEvent_t ev_ring[2] = {};  // plain decode: one event per token ring slot
+    uint32_t* h_ring = nullptr;   // pinned 2-slot token ring
+
+    // host mirror
+    int len = 0;          // committed tokens including the pending commit (= ctl->off)
+    int last_t = 0;       // rows of the last pass
+    int pending_n = 0;    // rows of the last pass still to be committed on the device
+
+    // drafting
+    std::vector<uint64_t> keys;   // token_key per vocab id
+    std::vector<std::string> vocab_bytes;
+    double cost[9] = {0};         // verify cost per draft count (policy), measured on first use
+    bool cost_ready = false;
+};
+
+namespace bcu {
+// Internal helpers shared by runtime.cu and decode.cpp.
+bcu_status run_pass(bcu_model* m, const uint32_t* ids, int T, int commit_all, int feed, bool sync);
+bcu_status wait_stream(bcu_model* m, double seconds);
+// Copies *m->h_in to ctl->in in stream order through a pinned slot that no later call can overwrite before the copy.
+bcu_status stage_in(bcu_model* m);
+bcu_status fail(bcu_model* m, bcu_status s, const std::string& msg);
+}  // namespace bcu

@@ -1,0 +1,125 @@
+// ops.cu — standalone hot ops of the C ABI on caller-owned device buffers: the rotate-then-ternary-linear of graded
+// config 1 and the GatedDeltaNet verify step with rollback of graded config 2.
+#include <cstring>
+#include <string>
+
+#include "../../include/bonsai_cuda.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace bcu;
+
+struct bcu_linear {
+    int device = 0;
+    TernaryMat m;
+    void* codes = nullptr;
+    uint32_t* scales = nullptr;
+    uint16_t* bias = nullptr;
+    // per-call scratch, sized for T <= 16
+    uint32_t* bfrag = nullptr;
+    float* xsum = nullptr;
+    int* xexp = nullptr;
+    float* partial = nullptr;
+    unsigned* counters = nullptr;
+    int* err = nullptr;
+};
+
+extern "C" {
+
+bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_host, const uint16_t* biases_host,
+                              int32_t O, int32_t K, int32_t group, int32_t device, bcu_linear** out) {
+    if (!w_host || !scales_host || !out || O <= 0 || K <= 0 || O % 128 || K % 512 || (group != 64 && group != 128))
+        return BCU_ERR_ARG;
+    if (cudaSetDevice(device) != cudaSuccess) return BCU_ERR_CUDA;
+    bcu_linear* l = new bcu_linear();
+    l->device = device;
+    size_t wb = (size_t)O * K / 4, sb = (size_t)O * (K / group) * 2;
+    uint32_t* dw = nullptr;
+    uint16_t *ds = nullptr, *db = nullptr;
+    bool ok = cudaMalloc(&dw, wb) == cudaSuccess && cudaMalloc(&ds, sb) == cudaSuccess &&
+              (!biases_host || cudaMalloc(&db, sb) == cudaSuccess) && cudaMalloc(&l->codes, wb) == cudaSuccess &&
+              cudaMalloc(&l->scales, sb) == cudaSuccess && cudaMalloc(&l->bias, sb) == cudaSuccess;
+    if (ok) {
+        ok = cudaMemcpy(dw, w_host, wb, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(ds, scales_host, sb, cudaMemcpyHostToDevice) == cudaSuccess &&
+             (!biases_host || cudaMemcpy(db, biases_host, sb, cudaMemcpyHostToDevice) == cudaSuccess);
+    }
+    if (ok) {
+        repack_ternary(dw, ds, db, O, K, group, l->codes, l->scales, l->bias, 0);
+        ok = cudaDeviceSynchronize() == cudaSuccess;
+    }
+    cudaFree(dw);
+    cudaFree(ds);
+    cudaFree(db);
+    l->m.codes = l->codes;
+    l->m.scales = l->scales;
+    l->m.bias = l->bias;
+    l->m.O = O;
+    l->m.K = K;
+    l->m.group = group;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    plan_ternary(l->m, sms);
+    ok = ok && cudaMalloc(&l->bfrag, (size_t)(K / 16) * 4 * 256) == cudaSuccess &&
+         cudaMalloc(&l->xsum, (size_t)VMAX * (K / 64) * 4) == cudaSuccess &&
+         cudaMalloc(&l->xexp, VMAX * 4) == cudaSuccess &&
+         cudaMalloc(&l->partial, (size_t)l->m.nsplit * VMAX * O * 4) == cudaSuccess &&
+         cudaMalloc(&l->counters, (size_t)(O / 128) * 4) == cudaSuccess && cudaMalloc(&l->err, 4) == cudaSuccess &&
+         cudaMemset(l->counters, 0, (size_t)(O / 128) * 4) == cudaSuccess && cudaMemset(l->err, 0, 4) == cudaSuccess;
+    if (!ok) {
+        bcu_linear_free(l);
+        return BCU_ERR_OOM;
+    }
+    *out = l;
+    return BCU_OK;
+}
+
+void bcu_linear_free(bcu_linear* l) {
+    if (!l) return;
+    cudaSetDevice(l->device);
+    void* p[] = {l->codes, l->scales, l->bias, l->bfrag, l->xsum, l->xexp, l->partial, l->counters, l->err};
+    for (void* q : p)
+        if (q) cudaFree(q);
+    delete l;
+}
+
+static bcu_status linear_run(bcu_linear* l, const uint16_t* xb, const float* xf, int T, int HB, const float* signs,
+                             float* y, void* stream) {
+    if (!l || (!xb && !xf) || !y || T < 1 || T > VMAX) return BCU_ERR_ARG;
+    if (HB && (HB != 512 && HB != 1024 && HB != 2048)) return BCU_ERR_ARG;
+    if (HB && l->m.K % HB) return BCU_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    TernaryAct act;
+    act.bfrag = l->bfrag;
+    act.xsum = l->xsum;
+    act.xexp = l->xexp;
+    act.K = l->m.K;
+    launch_rotate_prep(xb, xf, T, l->m.K, HB, signs, l->m.group, act, nullptr, st);
+    launch_ternary_gemv(l->m, act, T, y, 0, l->partial, l->counters, l->err, st);
+    if (cudaGetLastError() != cudaSuccess) return BCU_ERR_CUDA;
+    return BCU_OK;
+}
+
+bcu_status bcu_linear_rotate_forward(bcu_linear* l, const uint16_t* x_bf16_dev, int32_t T, int32_t hadamard,
+                                     const float* signs_dev, float* y_dev, void* stream) {
+    if (!l) return BCU_ERR_ARG;
+    cudaSetDevice(l->device);
+    return linear_run(l, x_bf16_dev, nullptr, T, hadamard, signs_dev, y_dev, stream);
+}
+
+bcu_status bcu_linear_forward(bcu_linear* l, const float* x_dev, int32_t T, float* y_dev, void* stream) {
+    if (!l) return BCU_ERR_ARG;
+    cudaSetDevice(l->device);
+    return linear_run(l, nullptr, x_dev, T, 0, nullptr, y_dev, stream);
+}
+
+bcu_status bcu_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
+                          const float* a_log, const float* dt_bias, float* state, float* y, int32_t T, int32_t NK,
+                          int32_t NV, int32_t n, void* stream) {
+    if (!q || !k || !v || !a_in || !b_in || !a_log || !dt_bias || !state || !y) return BCU_ERR_ARG;
+    if (T < 1 || NK < 1 || NV < 1 || NV % NK || n < 0 || n > T) return BCU_ERR_ARG;
+    launch_gdn_verify(q, k, v, a_in, b_in, a_log, dt_bias, state, y, T, NK, NV, n, (cudaStream_t)stream);
+    return cudaGetLastError() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
+}
+
+}  // extern "C"

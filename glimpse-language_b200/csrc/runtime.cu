@@ -1,0 +1,987 @@
+// runtime.cu — host runtime behind the C ABI: Model::load / Text::new (runtime/mod.rs:288-324, model.rs:270-368) on a
+// B200. Tensors arrive by reference name, are repacked on the device into the tensor-core layouts, and each pass of T
+// rows (T = 1 plain step, 2..16 verify, 16-row prefill chunks) is one CUDA graph captured once and replayed; its
+// parameters (input ids, KV offset, replay count, parity) live in a device control block, as the Vulkan backend's
+// recorded command buffers read per-step parameter slots (gpu_vk.rs:651-666, 778-838).
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+
+#include "model.h"
+
+using namespace bcu;
+
+namespace bcu {
+
+bcu_status fail(bcu_model* m, bcu_status s, const std::string& msg) {
+    if (m) m->err = msg;
+    return s;
+}
+
+#define CK(call)                                                                                              \
+    do {                                                                                                      \
+        cudaError_t e_ = (call);                                                                              \
+        if (e_ != cudaSuccess)                                                                                \
+            return fail(m, e_ == cudaErrorMemoryAllocation ? BCU_ERR_OOM : BCU_ERR_CUDA,                      \
+                        std::string(#call) + ": " + cudaGetErrorString(e_));                                  \
+    } while (0)
+
+// Polls the model stream with a deadline instead of blocking (every host wait is bounded).
+bcu_status wait_stream(bcu_model* m, double seconds) {
+    CK(cudaEventRecord(m->ev_done, m->st));
+    auto t0 = std::chrono::steady_clock::now();
+    int spins = 0;
+    for (;;) {
+        cudaError_t e = cudaEventQuery(m->ev_done);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return fail(m, BCU_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(e));
+        if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > seconds) return fail(m, BCU_ERR_TIMEOUT, "device work did not finish within the deadline");
+    }
+    return BCU_OK;
+}
+
+bcu_status stage_in(bcu_model* m) {
+    int i = m->in_next;
+    m->in_next = (i + 1) % bcu_model::IN_SLOTS;
+    if (m->in_used[i]) {  // bounded wait for the copy that last used this slot
+        auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+            cudaError_t e = cudaEventQuery(m->in_ev[i]);
+            if (e == cudaSuccess) break;
+            if (e != cudaErrorNotReady) return fail(m, BCU_ERR_CUDA, cudaGetErrorString(e));
+            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > 120.0)
+                return fail(m, BCU_ERR_TIMEOUT, "input staging slot did not free up");
+        }
+    }
+    m->in_ring[i] = *m->h_in;
+    CK(cudaMemcpyAsync(&m->ctl->in, &m->in_ring[i], sizeof(CtlIn), cudaMemcpyHostToDevice, m->st));
+    CK(cudaEventRecord(m->in_ev[i], m->st));
+    m->in_used[i] = true;
+    return BCU_OK;
+}
+
+}  // namespace bcu
+
+namespace {
+
+const char* PFX = "language_model.model.";
+const double WAIT_S = 120.0;
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+bcu_status check_config(const bcu_config* c, std::string* why) {
+    auto bad = [&](const std::string& s) {
+        *why = "unsupported config: " + s;
+        return BCU_ERR_ARG;
+    };
+    if (c->n_layers < 1 || c->n_layers > BCU_MAX_LAYERS) return bad("n_layers out of range");
+    if (c->head_dim != 256) return bad("head_dim must be 256");
+    if (c->lin_k_dim != 128 || c->lin_v_dim != 128) return bad("linear head dims must be 128");
+    if (c->conv_kernel != 4) return bad("linear_conv_kernel_dim must be 4");
+    if (c->kv_heads < 1 || c->heads % c->kv_heads != 0) return bad("heads not divisible by kv heads");
+    if (c->heads / c->kv_heads > 16) return bad("more than 16 q heads per kv head");
+    if (c->lin_k_heads < 1 || c->lin_v_heads % c->lin_k_heads != 0) return bad("v heads not divisible by k heads");
+    if (c->hidden % 512 || c->intermediate % 512) return bad("hidden/intermediate must be multiples of 512");
+    if (c->group_size != 64 && c->group_size != 128) return bad("group_size must be 64 or 128");
+    if (c->hadamard != 512 && c->hadamard != 1024 && c->hadamard != 2048) return bad("hadamard block must be 512/1024/2048");
+    int C = 2 * c->lin_k_heads * 128 + c->lin_v_heads * 128, gw = c->lin_v_heads * 128, aw = c->heads * 256;
+    int kvw = c->kv_heads * 256;
+    int dims[] = {c->hidden, c->intermediate, gw, aw};
+    for (int d : dims)
+        if (d % c->hadamard) return bad("activation widths must be multiples of the hadamard block");
+    if (C % 128 || (2 * aw + 2 * kvw) % 128) return bad("projection widths must be multiples of 128");
+    if (c->vocab < 16 || c->vocab % 16) return bad("vocab must be a multiple of 16");
+    if (c->head_kind != BCU_HEAD_BF16) return bad("only the bf16 tied head is implemented on the device");
+    int half = c->rotary_dims / 2;
+    if (c->rotary_dims % 2 || c->rotary_dims > 256 || c->mrope[0] + c->mrope[1] + c->mrope[2] != half)
+        return bad("rotary dims / mrope sections");
+    if (std::fabs(c->eps - 1e-6) > 1e-12) return bad("rms_norm_eps must be 1e-6");
+    if (c->vmax < 1 || c->vmax > VMAX) return bad("vmax must be 1..16");
+    if (c->ctx < 16 || c->ctx > 65536) return bad("ctx out of range");
+    return BCU_OK;
+}
+
+const DevTensor* find(bcu_model* m, const std::string& n) {
+    auto it = m->staged.find(n);
+    return it == m->staged.end() ? nullptr : &it->second;
+}
+
+// Suballocates the weight arena. On overflow it hands out the arena start (no out-of-bounds write) and the caller's
+// final size check reports the error.
+void* arena_take(bcu_model* m, size_t bytes) {
+    if (m->arena_used + align256(bytes) > m->arena_bytes) {
+        m->arena_used = m->arena_bytes + 1;
+        return m->arena;
+    }
+    void* p = (char*)m->arena + m->arena_used;
+    m->arena_used += align256(bytes);
+    return p;
+}
+
+// Copies a staged fp32 vector of `n` floats into the arena.
+bcu_status arena_f32(bcu_model* m, const std::string& name, size_t n, const float** out) {
+    const DevTensor* t = find(m, name);
+    if (!t) return fail(m, BCU_ERR_NOT_FOUND, "missing tensor " + name);
+    if (t->dtype != BCU_F32 || t->bytes != n * 4)
+        return fail(m, BCU_ERR_ARG, "tensor " + name + ": expected fp32 of " + std::to_string(n) + " values");
+    void* p = arena_take(m, n * 4);
+    CK(cudaMemcpyAsync(p, t->dev, n * 4, cudaMemcpyDeviceToDevice, m->st));
+    *out = (const float*)p;
+    return BCU_OK;
+}
+
+struct Part {
+    std::string name;
+    int O;
+};
+
+// Bytes of one stacked ternary linear in the arena.
+size_t lin_bytes(int O, int K, int group) {
+    return align256(ternary_codes_bytes(O, K)) + align256(ternary_scales_bytes(O, K, group)) +
+           align256((size_t)O * (K / group) * 2);
+}
+
+// Stacks the parts (rows in order) into one packed linear; `signs_of` names the part whose signs rotate the input.
+bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* out) {
+    int O = 0;
+    for (auto& p : parts) O += p.O;
+    int group = m->c.group_size;
+    TernaryMat tm;
+    tm.O = O;
+    tm.K = K;
+    tm.group = group;
+    uint8_t* codes = (uint8_t*)arena_take(m, ternary_codes_bytes(O, K));
+    uint8_t* scales = (uint8_t*)arena_take(m, ternary_scales_bytes(O, K, group));
+    uint16_t* bias = (uint16_t*)arena_take(m, (size_t)O * (K / group) * 2);
+    tm.codes = codes;
+    tm.scales = (const uint32_t*)scales;
+    tm.bias = bias;
+    int row = 0;
+    for (auto& p : parts) {
+        const DevTensor* w = find(m, p.name + ".weight");
+        const DevTensor* s = find(m, p.name + ".scales");
+        const DevTensor* b = m->c.has_bias ? find(m, p.name + ".biases") : nullptr;
+        if (!w || !s || (m->c.has_bias && !b)) return fail(m, BCU_ERR_NOT_FOUND, "missing packed linear " + p.name);
+        if (w->dtype != BCU_U32 || w->shape.size() != 2 || w->shape[0] != p.O || w->shape[1] * 16 != K)
+            return fail(m, BCU_ERR_ARG, p.name + ".weight: expected u32 [" + std::to_string(p.O) + ", " +
+                                            std::to_string(K / 16) + "]");
+        size_t ns = (size_t)p.O * (K / group) * 2;
+        if (s->dtype != BCU_F16 || s->bytes != ns) return fail(m, BCU_ERR_ARG, p.name + ".scales: wrong shape/dtype");
+        if (b && (b->dtype != BCU_F16 || b->bytes != ns)) return fail(m, BCU_ERR_ARG, p.name + ".biases: wrong shape/dtype");
+        // row offsets are multiples of 128, so each part lands on whole row blocks of the stacked layout
+        repack_ternary((const uint32_t*)w->dev, (const uint16_t*)s->dev, b ? (const uint16_t*)b->dev : nullptr, p.O, K,
+                       group, codes + ternary_codes_bytes(row, K), (uint32_t*)(scales + ternary_scales_bytes(row, K, group)),
+                       bias + (size_t)row * (K / group), m->st);
+        CK(cudaGetLastError());
+        row += p.O;
+    }
+    plan_ternary(tm, m->num_sms);
+    out->m = tm;
+    out->signs = nullptr;
+    if (m->c.has_signs) {
+        const DevTensor* sg = find(m, parts[0].name + ".signs");
+        if (!sg || sg->dtype != BCU_F32 || sg->bytes != (size_t)K * 4)
+            return fail(m, BCU_ERR_NOT_FOUND, "missing fp32 signs [" + std::to_string(K) + "] of " + parts[0].name);
+        void* p = arena_take(m, (size_t)K * 4);
+        CK(cudaMemcpyAsync(p, sg->dev, (size_t)K * 4, cudaMemcpyDeviceToDevice, m->st));
+        out->signs = (const float*)p;
+    }
+    return BCU_OK;
+}
+
+template <class T>
+bcu_status dmalloc(bcu_model* m, T** p, size_t bytes) {
+    cudaError_t e = cudaMalloc((void**)p, bytes < 16 ? 16 : bytes);
+    if (e != cudaSuccess) return fail(m, BCU_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    e = cudaMemset(*p, 0, bytes < 16 ? 16 : bytes);
+    if (e != cudaSuccess) return fail(m, BCU_ERR_CUDA, cudaGetErrorString(e));
+    return BCU_OK;
+}
+
+#define TRY(x)                          \
+    do {                                \
+        bcu_status s_ = (x);            \
+        if (s_ != BCU_OK) return s_;    \
+    } while (0)
+
+// The kernels of one pass of T rows, in order (Text::encode_embed + encode_layers + encode_head, model.rs:641-985).
+void enqueue_pass(bcu_model* m, int T) {
+    const bcu_config& c = m->c;
+    const int NT = (2 * T + 7) / 8, d = c.hidden, ff = c.intermediate;
+    cudaStream_t st = m->st;
+    TernaryAct act;
+    act.bfrag = m->bfrag;
+    act.xsum = m->xsum;
+    act.xexp = m->xexp;
+    for (size_t li = 0; li < m->layers.size(); li++) {
+        const Layer& L = m->layers[li];
+        PrepNormArgs pn{};
+        pn.ctl = m->ctl;
+        pn.embed_bf16 = li == 0 ? m->embed_rows : nullptr;
+        pn.h = m->h;
+        pn.w = L.in_norm;
+        pn.signs = L.mix_in.signs;
+        pn.xn = L.attn ? nullptr : m->xn;
+        pn.D = d;
+        pn.HB = c.hadamard;
+        pn.group = c.group_size;
+        pn.T = T;
+        pn.vocab = c.vocab;
+        pn.act = act;
+        launch_prep_norm(pn, NT, st);
+        launch_ternary_gemv(L.mix_in.m, act, T, m->mix, 0, m->partial, m->counters, &m->ctl->err, st);
+        if (!L.attn) {
+            GdnArgs g{};
+            g.ctl = m->ctl;
+            g.qkvz = m->mix;
+            g.xn = m->xn;
+            g.wa = L.wa;
+            g.wb = L.wb;
+            g.convw = L.convw;
+            g.a_log = L.a_log;
+            g.dt_bias = L.dt_bias;
+            g.conv_state = m->conv + (size_t)L.gi * 3 * m->C;
+            g.gdn_state = m->gdn + (size_t)L.gi * c.lin_v_heads * 128 * 128;
+            g.pend_qkv = m->pend_qkv + (size_t)L.gi * 2 * VMAX * m->C;
+            g.pend_qkvc = m->pend_qkvc + (size_t)L.gi * 2 * VMAX * m->C;
+            g.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * c.lin_v_heads;
+            g.y = m->y;
+            g.d = d;
+            g.C = m->C;
+            g.NK = c.lin_k_heads;
+            g.NV = c.lin_v_heads;
+            g.T = T;
+            launch_gdn_ab(g, st);
+            launch_gdn_conv(g, st);
+            launch_gdn_recurrent(g, st);
+            PrepGatedArgs pg{};
+            pg.y = m->y;
+            pg.qkvz = m->mix;
+            pg.w = L.gnorm;
+            pg.signs = L.mix_out.signs;
+            pg.gw = m->gw;
+            pg.C = m->C;
+            pg.HB = c.hadamard;
+            pg.group = c.group_size;
+            pg.T = T;
+            pg.act = act;
+            launch_prep_gated(pg, NT, st);
+        } else {
+            AttnArgs a{};
+            a.ctl = m->ctl;
+            a.qkv = m->mix;
+            a.qn = L.qn;
+            a.kn = L.kn;
+            a.inv_freq = m->inv_freq;
+            a.q = m->q;
+            a.kc = m->kc + (size_t)L.ai * c.ctx * m->kvw;
+            a.vc = m->vc + (size_t)L.ai * c.ctx * m->kvw;
+            a.part = m->apart;
+            a.H = c.heads;
+            a.KV = c.kv_heads;
+            a.rot = c.rotary_dims;
+            a.T = T;
+            a.ld = 2 * m->aw + 2 * m->kvw;
+            a.ctx = c.ctx;
+            launch_attn_prep(a, st);
+            launch_attn_split(a, st);
+            PrepAttnOutArgs po{};
+            po.part = m->apart;
+            po.qkv = m->mix;
+            po.signs = L.mix_out.signs;
+            po.H = c.heads;
+            po.HB = c.hadamard;
+            po.group = c.group_size;
+            po.T = T;
+            po.qkv_ld = a.ld;
+            po.act = act;
+            launch_prep_attn_out(po, NT, st);
+        }
+        launch_ternary_gemv(L.mix_out.m, act, T, m->h, 1, m->partial, m->counters, &m->ctl->err, st);
+        PrepNormArgs pp = pn;
+        pp.embed_bf16 = nullptr;
+        pp.w = L.post_norm;
+        pp.signs = L.gu.signs;
+        pp.xn = nullptr;
+        launch_prep_norm(pp, NT, st);
+        launch_ternary_gemv(L.gu.m, act, T, m->gubuf, 0, m->partial, m->counters, &m->ctl->err, st);
+        PrepSwigluArgs ps{};
+        ps.gu = m->gubuf;
+        ps.signs = L.down.signs;
+        ps.ff = ff;
+        ps.HB = c.hadamard;
+        ps.group = c.group_size;
+        ps.T = T;
+        ps.act = act;
+        launch_prep_swiglu(ps, NT, st);
+        launch_ternary_gemv(L.down.m, act, T, m->h, 1, m->partial, m->counters, &m->ctl->err, st);
+    }
+    PrepHeadArgs ph{};
+    ph.h = m->h;
+    ph.w = m->final_norm;
+    ph.bfrag = m->hfrag;
+    ph.D = d;
+    ph.T = T;
+    launch_prep_head(ph, NT, st);
+    HeadArgs ha{};
+    ha.ctl = m->ctl;
+    ha.w = m->head_w;
+    ha.bfrag = m->hfrag;
+    ha.logits = m->logits;
+    ha.pv = m->pv;
+    ha.pi = m->pi;
+    ha.counter = m->head_counter;
+    ha.V = c.vocab;
+    ha.d = d;
+    ha.T = T;
+    launch_head(ha, NT, m->head_grid, st);
+}
+
+bcu_status get_graph(bcu_model* m, int T, cudaGraphExec_t* out) {
+    if (m->graphs[T]) {
+        *out = m->graphs[T];
+        return BCU_OK;
+    }
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    enqueue_pass(m, T);
+    cudaError_t e = cudaStreamEndCapture(m->st, &g);
+    if (e != cudaSuccess) return fail(m, BCU_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    m->graph_nodes[T] = (int)n;
+    e = cudaGraphInstantiate(&m->graphs[T], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(m, BCU_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    *out = m->graphs[T];
+    return BCU_OK;
+}
+
+bcu_status read_ctl(bcu_model* m) {
+    CK(cudaMemcpyAsync(m->h_out, m->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost, m->st));
+    TRY(wait_stream(m, WAIT_S));
+    if (m->h_out->err) {
+        int e = m->h_out->err;
+        cudaMemsetAsync(&m->ctl->err, 0, 4, m->st);
+        if (e & ERR_MBAR_TIMEOUT) return fail(m, BCU_ERR_TIMEOUT, "a kernel gave up waiting for its bulk copies");
+        if (e & ERR_BAD_TOKEN) return fail(m, BCU_ERR_ARG, "token id out of vocabulary range");
+        if (e & ERR_CTX_FULL) return fail(m, BCU_ERR_STATE, "KV context full");
+        return fail(m, BCU_ERR_CUDA, "device error " + std::to_string(e));
+    }
+    return BCU_OK;
+}
+
+// Sets the KV offset and the replay count of the control block in stream order (snapshot restore).
+__global__ void ctl_set_kernel(Ctl* c, int off, int replay_n) {
+    c->off = off;
+    c->replay_n = replay_n;
+    c->err = 0;
+}
+
+__global__ void ctl_planted_kernel(Ctl* c, const uint32_t* p, int n) {
+    c->planted = p;
+    c->planted_n = n;
+}
+
+}  // namespace
+
+namespace bcu {
+
+// One pass of T rows: stage the inputs, replay the graph, optionally wait and read the control block back.
+bcu_status run_pass(bcu_model* m, const uint32_t* ids, int T, int commit_all, int feed, bool sync) {
+    if (!m->finalized) return fail(m, BCU_ERR_STATE, "bcu_finalize has not run");
+    if (T < 1 || T > m->c.vmax) return fail(m, BCU_ERR_ARG, "pass rows out of range");
+    if (m->len + T > m->c.ctx) return fail(m, BCU_ERR_STATE, "context full");
+    cudaGraphExec_t g;
+    TRY(get_graph(m, T, &g));
+    m->h_in->commit_all = commit_all;
+    m->h_in->feed = feed;
+    if (ids)
+        for (int t = 0; t < T; t++) m->h_in->ids[t] = ids[t];
+    TRY(stage_in(m));
+    CK(cudaGraphLaunch(g, m->st));
+    m->last_t = T;
+    if (!sync) return BCU_OK;
+    TRY(read_ctl(m));
+    m->len = m->h_out->off;
+    m->pending_n = m->h_out->replay_n;
+    return BCU_OK;
+}
+
+}  // namespace bcu
+
+// =============================================================================================== C ABI
+extern "C" {
+
+bcu_status bcu_config_check(const bcu_config* cfg, char* err, size_t err_len) {
+    std::string why;
+    bcu_status s = cfg ? check_config(cfg, &why) : BCU_ERR_ARG;
+    if (!cfg) why = "null config";
+    if (err && err_len) {
+        snprintf(err, err_len, "%s", why.c_str());
+    }
+    return s;
+}
+
+bcu_status bcu_create(const bcu_config* cfg, int device, bcu_model** out) {
+    if (!cfg || !out) return BCU_ERR_ARG;
+    std::string why;
+    if (check_config(cfg, &why) != BCU_OK) return BCU_ERR_ARG;
+    bcu_model* m = new bcu_model();
+    m->c = *cfg;
+    m->device = device;
+    *out = m;
+    CK(cudaSetDevice(device));
+    CK(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, device));
+    CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&m->ev_done, cudaEventDisableTiming));
+    CK(cudaEventCreate(&m->ev0));
+    CK(cudaEventCreate(&m->ev1));
+    CK(cudaEventCreateWithFlags(&m->ev_ring[0], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&m->ev_ring[1], cudaEventDisableTiming));
+    CK(cudaMallocHost(&m->h_ring, 16));
+    const bcu_config& c = m->c;
+    m->C = 2 * c.lin_k_heads * 128 + c.lin_v_heads * 128;
+    m->gw = c.lin_v_heads * 128;
+    m->aw = c.heads * 256;
+    m->kvw = c.kv_heads * 256;
+    for (int i = 0; i < c.n_layers; i++) (c.layer_is_attn[i] ? m->n_attn : m->n_gdn)++;
+    return BCU_OK;
+}
+
+bcu_status bcu_load_tensor(bcu_model* m, const char* name, int32_t dtype, const int64_t* shape, int32_t ndim,
+                           const void* host_data) {
+    if (!m || !name || !host_data || ndim < 0 || ndim > 4) return fail(m, BCU_ERR_ARG, "bad tensor arguments");
+    if (m->finalized) return fail(m, BCU_ERR_STATE, "tensors must be loaded before bcu_finalize");
+    CK(cudaSetDevice(m->device));
+    DevTensor t;
+    t.dtype = dtype;
+    size_t n = 1;
+    for (int i = 0; i < ndim; i++) {
+        if (shape[i] <= 0) return fail(m, BCU_ERR_ARG, std::string("bad shape of ") + name);
+        t.shape.push_back(shape[i]);
+        n *= (size_t)shape[i];
+    }
+    size_t es = (dtype == BCU_U32 || dtype == BCU_F32) ? 4 : 2;
+    t.bytes = n * es;
+    auto it = m->staged.find(name);
+    if (it != m->staged.end()) {
+        cudaFree(it->second.dev);
+        m->staged.erase(it);
+    }
+    CK(cudaMalloc(&t.dev, t.bytes));
+    CK(cudaMemcpy(t.dev, host_data, t.bytes, cudaMemcpyHostToDevice));
+    m->staged[name] = t;
+    return BCU_OK;
+}
+
+bcu_status bcu_finalize(bcu_model* m) {
+    if (!m) return BCU_ERR_ARG;
+    if (m->finalized) return fail(m, BCU_ERR_STATE, "already finalized");
+    CK(cudaSetDevice(m->device));
+    const bcu_config& c = m->c;
+    const int d = c.hidden, ff = c.intermediate, g = c.group_size;
+    std::string p = PFX;
+    // arena size
+    size_t bytes = 0;
+    for (int i = 0; i < c.n_layers; i++) {
+        if (c.layer_is_attn[i]) {
+            bytes += lin_bytes(2 * m->aw + 2 * m->kvw, d, g) + lin_bytes(d, m->aw, g) + 2 * 256 * 4;
+        } else {
+            bytes += lin_bytes(m->C + m->gw, d, g) + lin_bytes(d, m->gw, g);
+            bytes += align256((size_t)2 * c.lin_v_heads * d * 4) * 2 + align256((size_t)m->C * 16) + 4 * 1024;
+        }
+        bytes += lin_bytes(2 * ff, d, g) + lin_bytes(d, ff, g) + 4 * align256((size_t)std::max(d, ff) * 4) + 8192;
+    }
+    bytes += align256((size_t)c.vocab * d * 2) * 2 + align256((size_t)d * 4) + (4 << 20);
+    m->arena_bytes = bytes;
+    CK(cudaMalloc(&m->arena, bytes));
+    m->arena_used = 0;
+    m->layers.resize(c.n_layers);
+    int gi = 0, ai = 0;
+    for (int i = 0; i < c.n_layers; i++) {
+        Layer& L = m->layers[i];
+        std::string l = p + "layers." + std::to_string(i) + ".";
+        L.attn = c.layer_is_attn[i] != 0;
+        TRY(arena_f32(m, l + "input_layernorm.weight", d, &L.in_norm));
+        TRY(arena_f32(m, l + "post_attention_layernorm.weight", d, &L.post_norm));
+        if (L.attn) {
+            std::string a = l + "self_attn.";
+            TRY(build_lin(m, {{a + "q_proj", 2 * m->aw}, {a + "k_proj", m->kvw}, {a + "v_proj", m->kvw}}, d, &L.mix_in));
+            TRY(build_lin(m, {{a + "o_proj", d}}, m->aw, &L.mix_out));
+            TRY(arena_f32(m, a + "q_norm.weight", 256, &L.qn));
+            TRY(arena_f32(m, a + "k_norm.weight", 256, &L.kn));
+            L.ai = ai++;
+        } else {
+            std::string a = l + "linear_attn.";
+            TRY(build_lin(m, {{a + "in_proj_qkv", m->C}, {a + "in_proj_z", m->gw}}, d, &L.mix_in));
+            TRY(build_lin(m, {{a + "out_proj", d}}, m->gw, &L.mix_out));
+            TRY(arena_f32(m, a + "in_proj_a.weight", (size_t)c.lin_v_heads * d, &L.wa));
+            TRY(arena_f32(m, a + "in_proj_b.weight", (size_t)c.lin_v_heads * d, &L.wb));
+            TRY(arena_f32(m, a + "A_log", c.lin_v_heads, &L.a_log));
+            TRY(arena_f32(m, a + "dt_bias", c.lin_v_heads, &L.dt_bias));
+            TRY(arena_f32(m, a + "conv1d.weight", (size_t)m->C * 4, &L.convw));
+            TRY(arena_f32(m, a + "norm.weight", 128, &L.gnorm));
+            L.gi = gi++;
+        }
+        std::string mlp = l + "mlp.";
+        TRY(build_lin(m, {{mlp + "gate_proj", ff}, {mlp + "up_proj", ff}}, d, &L.gu));
+        TRY(build_lin(m, {{mlp + "down_proj", d}}, ff, &L.down));
+    }
+    TRY(arena_f32(m, p + "norm.weight", d, &m->final_norm));
+    const DevTensor* e = find(m, p + "embed_tokens.weight");
+    if (!e || e->dtype != BCU_BF16 || e->bytes != (size_t)c.vocab * d * 2)
+        return fail(m, BCU_ERR_NOT_FOUND, "missing bf16 embed_tokens.weight [vocab, hidden]");
+    m->embed_rows = (uint16_t*)arena_take(m, (size_t)c.vocab * d * 2);
+    CK(cudaMemcpyAsync(m->embed_rows, e->dev, (size_t)c.vocab * d * 2, cudaMemcpyDeviceToDevice, m->st));
+    m->head_w = (uint32_t*)arena_take(m, (size_t)c.vocab * d * 2);
+    repack_head_bf16((const uint16_t*)e->dev, c.vocab, d, m->head_w, m->st);
+    CK(cudaGetLastError());
+    {  // model.rs:316-321
+        int half = c.rotary_dims / 2;
+        std::vector<float> f(half);
+        for (int i = 0; i < half; i++) f[i] = 1.0f / std::pow((float)c.rope_theta, (float)(2 * i) / (float)c.rotary_dims);
+        m->inv_freq = (float*)arena_take(m, (size_t)half * 4 + 16);
+        CK(cudaMemcpyAsync(m->inv_freq, f.data(), (size_t)half * 4, cudaMemcpyHostToDevice, m->st));
+    }
+    if (m->arena_used > m->arena_bytes) return fail(m, BCU_ERR_STATE, "internal: arena overflow");
+    CK(cudaStreamSynchronize(m->st));
+    for (auto& kv : m->staged) cudaFree(kv.second.dev);
+    m->staged.clear();
+
+    // state and scratch
+    const int NV = c.lin_v_heads;
+    TRY(dmalloc(m, &m->gdn, (size_t)m->n_gdn * NV * 128 * 128 * 4));
+    TRY(dmalloc(m, &m->conv, (size_t)m->n_gdn * 3 * m->C * 4));
+    TRY(dmalloc(m, &m->kc, (size_t)m->n_attn * c.ctx * m->kvw * 4));
+    TRY(dmalloc(m, &m->vc, (size_t)m->n_attn * c.ctx * m->kvw * 4));
+    TRY(dmalloc(m, &m->pend_qkv, (size_t)m->n_gdn * 2 * VMAX * m->C * 4));
+    TRY(dmalloc(m, &m->pend_qkvc, (size_t)m->n_gdn * 2 * VMAX * m->C * 4));
+    TRY(dmalloc(m, &m->pend_ab, (size_t)m->n_gdn * 2 * VMAX * 2 * NV * 4));
+    int wide = std::max(std::max(d, ff), std::max(m->gw, m->aw));
+    int mixw = std::max(m->C + m->gw, 2 * m->aw + 2 * m->kvw);
+    TRY(dmalloc(m, &m->h, (size_t)VMAX * d * 4));
+    TRY(dmalloc(m, &m->xn, (size_t)VMAX * d * 4));
+    TRY(dmalloc(m, &m->mix, (size_t)VMAX * mixw * 4));
+    TRY(dmalloc(m, &m->gubuf, (size_t)VMAX * 2 * ff * 4));
+    TRY(dmalloc(m, &m->y, (size_t)VMAX * std::max(m->gw, m->aw) * 4));
+    TRY(dmalloc(m, &m->q, (size_t)VMAX * c.heads * 256 * 4));
+    TRY(dmalloc(m, &m->apart, (size_t)VMAX * c.heads * NSPLIT_ATTN * 258 * 4));
+    TRY(dmalloc(m, &m->logits, (size_t)VMAX * c.vocab * 4));
+    TRY(dmalloc(m, &m->bfrag, (size_t)(wide / 16) * 4 * 256));
+    TRY(dmalloc(m, &m->hfrag, (size_t)(d / 16) * 4 * 256));
+    TRY(dmalloc(m, &m->xsum, (size_t)VMAX * (wide / 64) * 4));
+    TRY(dmalloc(m, &m->xexp, (size_t)VMAX * 4));
+    size_t pf = 0;
+    int maxrb = 1;
+    for (auto& L : m->layers) {
+        for (const Lin* ln : {&L.mix_in, &L.mix_out, &L.gu, &L.down}) {
+            pf = std::max(pf, (size_t)ln->m.nsplit * VMAX * ln->m.O);
+            maxrb = std::max(maxrb, ln->m.O / 128);
+        }
+    }
+    m->partial_floats = pf;
+    TRY(dmalloc(m, &m->partial, pf * 4));
+    TRY(dmalloc(m, &m->counters, (size_t)maxrb * 4));
+    m->head_grid = 2 * m->num_sms;
+    TRY(dmalloc(m, &m->head_counter, 4));
+    TRY(dmalloc(m, &m->pv, (size_t)m->head_grid * VMAX * 4));
+    TRY(dmalloc(m, &m->pi, (size_t)m->head_grid * VMAX * 4));
+    TRY(dmalloc(m, &m->ctl, sizeof(Ctl)));
+    CK(cudaMallocHost(&m->h_in, sizeof(CtlIn)));
+    CK(cudaMallocHost(&m->in_ring, sizeof(CtlIn) * bcu_model::IN_SLOTS));
+    for (auto& e : m->in_ev) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CK(cudaMallocHost(&m->h_out, sizeof(Ctl)));
+    memset(m->h_in, 0, sizeof(CtlIn));
+    memset(m->h_out, 0, sizeof(Ctl));
+    m->finalized = true;
+    m->len = 0;
+    return BCU_OK;
+}
+
+bcu_status bcu_reset(bcu_model* m) {
+    if (!m || !m->finalized) return fail(m, BCU_ERR_STATE, "not finalized");
+    CK(cudaSetDevice(m->device));
+    const int NV = m->c.lin_v_heads;
+    CK(cudaMemsetAsync(m->gdn, 0, (size_t)m->n_gdn * NV * 128 * 128 * 4, m->st));
+    CK(cudaMemsetAsync(m->conv, 0, (size_t)m->n_gdn * 3 * m->C * 4, m->st));
+    Ctl z;
+    memset(&z, 0, sizeof(z));
+    memcpy(m->h_out, &z, sizeof(Ctl));
+    CK(cudaMemcpyAsync(m->ctl, m->h_out, sizeof(Ctl), cudaMemcpyHostToDevice, m->st));
+    TRY(wait_stream(m, WAIT_S));
+    m->len = 0;
+    m->pending_n = 0;
+    return BCU_OK;
+}
+
+const char* bcu_last_error(const bcu_model* m) { return m ? m->err.c_str() : "null model"; }
+
+void bcu_destroy(bcu_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->st) cudaStreamSynchronize(m->st);
+    for (auto& g : m->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto& kv : m->staged) cudaFree(kv.second.dev);
+    void* bufs[] = {m->arena, m->gdn, m->conv, m->kc, m->vc, m->pend_qkv, m->pend_qkvc, m->pend_ab, m->h, m->xn,
+                    m->mix, m->gubuf, m->y, m->q, m->apart, m->logits, m->bfrag, m->hfrag, m->xsum, m->xexp,
+                    m->partial, m->counters, m->head_counter, m->pv, m->pi, m->ctl, m->planted_dev};
+    for (void* b : bufs)
+        if (b) cudaFree(b);
+    if (m->h_in) cudaFreeHost(m->h_in);
+    if (m->in_ring) cudaFreeHost(m->in_ring);
+    for (auto e : m->in_ev)
+        if (e) cudaEventDestroy(e);
+    if (m->h_out) cudaFreeHost(m->h_out);
+    if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->ev1) cudaEventDestroy(m->ev1);
+    if (m->ev_done) cudaEventDestroy(m->ev_done);
+    for (auto e : m->ev_ring)
+        if (e) cudaEventDestroy(e);
+    if (m->h_ring) cudaFreeHost(m->h_ring);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+}
+
+bcu_status bcu_device_name(const bcu_model* m, char* out, size_t out_len) {
+    if (!m || !out) return BCU_ERR_ARG;
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, m->device) != cudaSuccess) return BCU_ERR_CUDA;
+    snprintf(out, out_len, "%s", p.name);
+    return BCU_OK;
+}
+
+bcu_status bcu_prefill(bcu_model* m, const uint32_t* ids, int32_t n, uint32_t* next) {
+    if (!m || !ids || n < 1) return fail(m, BCU_ERR_ARG, "prefill needs at least one id");
+    CK(cudaSetDevice(m->device));
+    if (m->len + n > m->c.ctx) return fail(m, BCU_ERR_STATE, "context full");
+    int chunk = m->c.vmax;
+    for (int i = 0; i < n; i += chunk) {
+        int t = std::min(chunk, n - i);
+        bool last = i + t == n;
+        TRY(run_pass(m, ids + i, t, 1, 0, last));
+        if (!last) m->len += t;  // mirror; the device advanced ctl->off by t
+    }
+    if (next) *next = m->h_out->bonus;
+    return BCU_OK;
+}
+
+bcu_status bcu_step(bcu_model* m, uint32_t id, uint32_t* next) {
+    if (!m) return BCU_ERR_ARG;
+    CK(cudaSetDevice(m->device));
+    TRY(run_pass(m, &id, 1, 1, 0, true));
+    if (next) *next = m->h_out->bonus;
+    return BCU_OK;
+}
+
+bcu_status bcu_verify(bcu_model* m, const uint32_t* ids, int32_t t, uint32_t* pred, int32_t* accepted) {
+    if (!m || !ids) return fail(m, BCU_ERR_ARG, "null ids");
+    CK(cudaSetDevice(m->device));
+    TRY(run_pass(m, ids, t, 0, 0, true));
+    if (pred)
+        for (int i = 0; i < t; i++) pred[i] = m->h_out->pred[i];
+    if (accepted) *accepted = m->h_out->accepted;
+    return BCU_OK;
+}
+
+bcu_status bcu_verify_accept(bcu_model* m, const uint32_t* ids, int32_t t, int32_t* accepted, uint32_t* bonus) {
+    if (!m || !ids) return fail(m, BCU_ERR_ARG, "null ids");
+    CK(cudaSetDevice(m->device));
+    TRY(run_pass(m, ids, t, 0, 0, false));
+    // only the accept count and the bonus token come back
+    CK(cudaMemcpyAsync(&m->h_out->accepted, &m->ctl->accepted, 8, cudaMemcpyDeviceToHost, m->st));
+    TRY(wait_stream(m, WAIT_S));
+    int32_t acc = m->h_out->accepted;
+    if (acc < 0 || acc >= t) return fail(m, BCU_ERR_CUDA, "device accept count out of range");
+    m->len += acc + 1;
+    m->pending_n = acc + 1;
+    if (accepted) *accepted = acc;
+    if (bonus) *bonus = m->h_out->bonus;
+    return BCU_OK;
+}
+
+bcu_status bcu_accept(bcu_model* m, int32_t t, int32_t n) {
+    if (!m) return BCU_ERR_ARG;
+    if (t != m->last_t || n < 1 || n > t || m->pending_n < 1) return fail(m, BCU_ERR_ARG, "accept does not match the last verify");
+    CK(cudaSetDevice(m->device));
+    TRY(read_ctl(m));
+    int base = m->h_out->off - m->h_out->replay_n;
+    int vals[2] = {base + n, n};  // off, replay_n (adjacent fields)
+    static_assert(offsetof(Ctl, replay_n) == offsetof(Ctl, off) + 4, "layout");
+    memcpy(&m->h_out->off, vals, 8);
+    CK(cudaMemcpyAsync(&m->ctl->off, &m->h_out->off, 8, cudaMemcpyHostToDevice, m->st));
+    TRY(wait_stream(m, WAIT_S));
+    m->len = base + n;
+    m->pending_n = n;
+    return BCU_OK;
+}
+
+bcu_status bcu_flush(bcu_model* m) {
+    if (!m || !m->finalized) return fail(m, BCU_ERR_STATE, "not finalized");
+    CK(cudaSetDevice(m->device));
+    TRY(read_ctl(m));
+    if (m->h_out->replay_n == 0) return BCU_OK;
+    // replay-only: the GDN conv and recurrent kernels with zero new rows commit the pending rows
+    for (auto& L : m->layers) {
+        if (L.attn) continue;
+        GdnArgs g{};
+        g.ctl = m->ctl;
+        g.qkvz = m->mix;
+        g.convw = L.convw;
+        g.a_log = L.a_log;
+        g.dt_bias = L.dt_bias;
+        g.conv_state = m->conv + (size_t)L.gi * 3 * m->C;
+        g.gdn_state = m->gdn + (size_t)L.gi * m->c.lin_v_heads * 128 * 128;
+        g.pend_qkv = m->pend_qkv + (size_t)L.gi * 2 * VMAX * m->C;
+        g.pend_qkvc = m->pend_qkvc + (size_t)L.gi * 2 * VMAX * m->C;
+        g.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * m->c.lin_v_heads;
+        g.y = m->y;
+        g.d = m->c.hidden;
+        g.C = m->C;
+        g.NK = m->c.lin_k_heads;
+        g.NV = m->c.lin_v_heads;
+        g.T = 0;
+        launch_gdn_conv(g, m->st);
+        launch_gdn_recurrent(g, m->st);
+    }
+    CK(cudaGetLastError());
+    CK(cudaMemsetAsync(&m->ctl->replay_n, 0, 4, m->st));
+    TRY(wait_stream(m, WAIT_S));
+    m->pending_n = 0;
+    return BCU_OK;
+}
+
+bcu_status bcu_length(const bcu_model* m, int32_t* len) {
+    if (!m || !len) return BCU_ERR_ARG;
+    *len = m->len;
+    return BCU_OK;
+}
+
+bcu_status bcu_set_keep_logits(bcu_model* m, int32_t keep) {
+    if (!m || !m->finalized) return fail(m, BCU_ERR_STATE, "not finalized");
+    m->h_in->keep_logits = keep ? 1 : 0;
+    return BCU_OK;
+}
+
+bcu_status bcu_read_logits(bcu_model* m, int32_t row, float* out) {
+    if (!m || !out || row < 0 || row >= m->last_t) return fail(m, BCU_ERR_ARG, "row out of range");
+    CK(cudaSetDevice(m->device));
+    CK(cudaMemcpyAsync(out, m->logits + (size_t)row * m->c.vocab, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, m->st));
+    return wait_stream(m, WAIT_S);
+}
+
+// ------------------------------------------------------------------------------------------------ snapshots
+static void state_sizes(const bcu_model* m, int len, size_t* g, size_t* c, size_t* kv) {
+    *g = (size_t)m->n_gdn * m->c.lin_v_heads * 128 * 128 * 4;
+    *c = (size_t)m->n_gdn * 3 * m->C * 4;
+    *kv = (size_t)m->n_attn * len * m->kvw * 4;
+}
+
+bcu_status bcu_state_new(bcu_model* m, int32_t len, bcu_state** out) {
+    if (!m || !out || len < 0 || len > m->c.ctx) return fail(m, BCU_ERR_ARG, "bad snapshot length");
+    CK(cudaSetDevice(m->device));
+    bcu_state* s = new bcu_state();
+    s->len = len;
+    state_sizes(m, len, &s->gdn_bytes, &s->conv_bytes, &s->kv_bytes);
+    bcu_status st;
+    if ((st = dmalloc(m, &s->gdn, s->gdn_bytes)) != BCU_OK || (st = dmalloc(m, &s->conv, s->conv_bytes)) != BCU_OK ||
+        (st = dmalloc(m, &s->kc, s->kv_bytes)) != BCU_OK || (st = dmalloc(m, &s->vc, s->kv_bytes)) != BCU_OK) {
+        bcu_state_free(s);
+        return st;
+    }
+    *out = s;
+    return BCU_OK;
+}
+
+void bcu_state_free(bcu_state* s) {
+    if (!s) return;
+    cudaFree(s->gdn);
+    cudaFree(s->conv);
+    cudaFree(s->kc);
+    cudaFree(s->vc);
+    delete s;
+}
+
+// Text::encode_copy_state (model.rs:1072-1086): GDN and conv state whole, K/V rows [0, len) of every layer.
+static bcu_status copy_kv(bcu_model* m, float* dst, int dst_cap, const float* src, int src_cap, int len) {
+    if (len == 0) return BCU_OK;
+    size_t row = (size_t)m->kvw * 4;
+    CK(cudaMemcpy2DAsync(dst, dst_cap * row, src, src_cap * row, len * row, m->n_attn, cudaMemcpyDeviceToDevice, m->st));
+    return BCU_OK;
+}
+
+bcu_status bcu_snapshot(bcu_model* m, bcu_state** out) {
+    if (!m || !out) return BCU_ERR_ARG;
+    TRY(bcu_flush(m));
+    bcu_state* s;
+    TRY(bcu_state_new(m, m->len, &s));
+    CK(cudaMemcpyAsync(s->gdn, m->gdn, s->gdn_bytes, cudaMemcpyDeviceToDevice, m->st));
+    CK(cudaMemcpyAsync(s->conv, m->conv, s->conv_bytes, cudaMemcpyDeviceToDevice, m->st));
+    TRY(copy_kv(m, s->kc, s->len, m->kc, m->c.ctx, s->len));
+    TRY(copy_kv(m, s->vc, s->len, m->vc, m->c.ctx, s->len));
+    TRY(wait_stream(m, WAIT_S));
+    *out = s;
+    return BCU_OK;
+}
+
+bcu_status bcu_restore(bcu_model* m, const bcu_state* s) {
+    if (!m || !s || !m->finalized) return fail(m, BCU_ERR_ARG, "bad restore");
+    CK(cudaSetDevice(m->device));
+    CK(cudaMemcpyAsync(m->gdn, s->gdn, s->gdn_bytes, cudaMemcpyDeviceToDevice, m->st));
+    CK(cudaMemcpyAsync(m->conv, s->conv, s->conv_bytes, cudaMemcpyDeviceToDevice, m->st));
+    TRY(copy_kv(m, m->kc, m->c.ctx, s->kc, s->len, s->len));
+    TRY(copy_kv(m, m->vc, m->c.ctx, s->vc, s->len, s->len));
+    ctl_set_kernel<<<1, 1, 0, m->st>>>(m->ctl, s->len, 0);
+    CK(cudaGetLastError());
+    m->len = s->len;
+    m->pending_n = 0;
+    return BCU_OK;
+}
+
+bcu_status bcu_state_parts(const bcu_model* m, const bcu_state* s, uint64_t sizes[4], int32_t* len) {
+    if (!m || !s || !sizes) return BCU_ERR_ARG;
+    sizes[0] = s->gdn_bytes;
+    sizes[1] = s->conv_bytes;
+    sizes[2] = s->kv_bytes;
+    sizes[3] = s->kv_bytes;
+    if (len) *len = s->len;
+    return BCU_OK;
+}
+
+static void* part_ptr(const bcu_state* s, int part, uint64_t* bytes) {
+    switch (part) {
+        case 0: *bytes = s->gdn_bytes; return s->gdn;
+        case 1: *bytes = s->conv_bytes; return s->conv;
+        case 2: *bytes = s->kv_bytes; return s->kc;
+        case 3: *bytes = s->kv_bytes; return s->vc;
+    }
+    return nullptr;
+}
+
+bcu_status bcu_state_read(const bcu_model* m, const bcu_state* s, int32_t part, void* host, uint64_t bytes) {
+    if (!m || !s || !host) return BCU_ERR_ARG;
+    uint64_t n;
+    void* p = part_ptr(s, part, &n);
+    if (!p || bytes != n) return BCU_ERR_ARG;
+    if (cudaMemcpy(host, p, n, cudaMemcpyDeviceToHost) != cudaSuccess) return BCU_ERR_CUDA;
+    return BCU_OK;
+}
+
+bcu_status bcu_state_write(bcu_model* m, bcu_state* s, int32_t part, const void* host, uint64_t bytes, int32_t len) {
+    if (!m || !s || !host || len != s->len) return fail(m, BCU_ERR_ARG, "state part does not match the snapshot");
+    uint64_t n;
+    void* p = part_ptr(s, part, &n);
+    if (!p || bytes != n) return fail(m, BCU_ERR_ARG, "state part size mismatch");
+    CK(cudaMemcpy(p, host, n, cudaMemcpyHostToDevice));
+    return BCU_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ introspection
+bcu_status bcu_pass_launches(const bcu_model* m, int32_t t, int32_t* launches) {
+    if (!m || !launches || t < 1 || t > VMAX) return BCU_ERR_ARG;
+    *launches = m->graph_nodes[t];
+    return BCU_OK;
+}
+
+bcu_status bcu_pass_bytes(const bcu_model* m, int32_t t, double* bytes) {
+    if (!m || !bytes || !m->finalized) return BCU_ERR_ARG;
+    const bcu_config& c = m->c;
+    double b = 0;
+    for (auto& L : m->layers)
+        for (const Lin* ln : {&L.mix_in, &L.mix_out, &L.gu, &L.down}) {
+            double O = ln->m.O, K = ln->m.K, g = ln->m.group;
+            b += O * K / 4 + O * (K / g) * 2 * (c.has_bias ? 2 : 1);
+        }
+    b += (double)c.vocab * c.hidden * 2;                                          // bf16 head
+    b += (double)m->n_gdn * 2 * c.lin_v_heads * c.hidden * 4;                     // dense a/b
+    b += (double)m->n_gdn * c.lin_v_heads * 128 * 128 * 4 * 2;                    // GDN state r+w
+    b += (double)m->n_gdn * 3 * m->C * 4 * 2;                                     // conv state r+w
+    b += (double)m->n_attn * (m->len + t / 2.0) * m->kvw * 4 * 2;                 // fp32 K+V read
+    *bytes = b;
+    return BCU_OK;
+}
+
+bcu_status bcu_set_planted(bcu_model* m, const uint32_t* ids, int32_t n, int32_t base) {
+    if (!m || !m->finalized || (!ids && n) || n < 0) return fail(m, BCU_ERR_ARG, "bad planted stream");
+    CK(cudaSetDevice(m->device));
+    TRY(wait_stream(m, WAIT_S));
+    if (n > m->planted_cap) {
+        if (m->planted_dev) cudaFree(m->planted_dev);
+        m->planted_dev = nullptr;
+        TRY(dmalloc(m, &m->planted_dev, (size_t)n * 4));
+        m->planted_cap = n;
+    }
+    if (n) CK(cudaMemcpy(m->planted_dev, ids, (size_t)n * 4, cudaMemcpyHostToDevice));
+    ctl_planted_kernel<<<1, 1, 0, m->st>>>(m->ctl, m->planted_dev, n);
+    CK(cudaGetLastError());
+    m->h_in->planted_base = base;
+    return wait_stream(m, WAIT_S);
+}
+
+bcu_status bcu_enqueue_passes(bcu_model* m, int32_t t, int32_t passes, int32_t feed) {
+    if (!m || !m->finalized || t < 1 || t > m->c.vmax || passes < 0 || feed < 0 || feed > 2)
+        return fail(m, BCU_ERR_ARG, "bad pass request");
+    CK(cudaSetDevice(m->device));
+    cudaGraphExec_t g;
+    TRY(get_graph(m, t, &g));
+    m->h_in->commit_all = 0;
+    m->h_in->feed = feed;
+    TRY(stage_in(m));
+    for (int i = 0; i < passes; i++) CK(cudaGraphLaunch(g, m->st));
+    m->last_t = t;
+    return BCU_OK;
+}
+
+bcu_status bcu_sync(bcu_model* m) {
+    if (!m || !m->finalized) return fail(m, BCU_ERR_STATE, "not finalized");
+    CK(cudaSetDevice(m->device));
+    TRY(read_ctl(m));
+    m->len = m->h_out->off;
+    m->pending_n = m->h_out->replay_n;
+    return BCU_OK;
+}
+
+bcu_status bcu_stream(bcu_model* m, void** stream) {
+    if (!m || !stream) return BCU_ERR_ARG;
+    *stream = (void*)m->st;
+    return BCU_OK;
+}
+
+bcu_status bcu_time_pass(bcu_model* m, int32_t t, int32_t iters, float* ms_per_pass) {
+    if (!m || !ms_per_pass || iters < 1 || t < 1 || t > m->c.vmax) return fail(m, BCU_ERR_ARG, "bad timing args");
+    CK(cudaSetDevice(m->device));
+    if (m->len + t > m->c.ctx) return fail(m, BCU_ERR_STATE, "context full");
+    bcu_state* snap;
+    TRY(bcu_snapshot(m, &snap));
+    cudaGraphExec_t g;
+    TRY(get_graph(m, t, &g));
+    uint32_t ids[VMAX];
+    for (int i = 0; i < t; i++) ids[i] = (uint32_t)(i * 7919 % m->c.vocab);
+    for (int i = 0; i < t; i++) m->h_in->ids[i] = ids[i];
+    m->h_in->commit_all = 0;
+    m->h_in->feed = 0;
+    TRY(stage_in(m));
+    // each replay verifies on top of the previous one; restore the state every pass so the length stays put
+    float total = 0;
+    for (int i = 0; i < iters + 1; i++) {
+        TRY(bcu_restore(m, snap));
+        CK(cudaEventRecord(m->ev0, m->st));
+        CK(cudaGraphLaunch(g, m->st));
+        CK(cudaEventRecord(m->ev1, m->st));
+        TRY(wait_stream(m, WAIT_S));
+        float ms;
+        CK(cudaEventElapsedTime(&ms, m->ev0, m->ev1));
+        if (i > 0) total += ms;
+    }
+    TRY(bcu_restore(m, snap));
+    bcu_state_free(snap);
+    *ms_per_pass = total / iters;
+    return BCU_OK;
+}
+
+}  // extern "C"
