@@ -142,6 +142,27 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args, local):
+    """A short run for kernel profiling: model load, a --profile-prefix token prefill (16-row passes), then
+    --profile verify passes of 9 rows with planted drafts. Prints the kernel launches of one 9-row pass."""
+    import torch
+
+    torch.cuda.set_device(local)
+    from bonsai_b200 import config, synth
+    from bonsai_b200.runtime import Model
+
+    cfg = config.bonsai_2b_graded(ctx=2048)
+    m = Model(cfg, device=local).load(synth.model_tensors(cfg, args.seed))
+    first = m.prefill(synth.zipf_tokens(args.seed + 1, args.profile_prefix, cfg.vocab))
+    rows = [first] + [int(x) for x in synth.zipf_tokens(args.seed + 3, 8, cfg.vocab)]
+    for _ in range(args.profile):
+        m.verify(rows)
+    m.sync()
+    print(json.dumps({"profile_passes": args.profile, "launches_per_pass": m.pass_launches(9),
+                      "prefix": args.profile_prefix}), flush=True)
+    m.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -150,11 +171,17 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="profiling run for ncu: prefill --profile-prefix tokens, then this many 9-row verify passes")
+    ap.add_argument("--profile-prefix", type=int, default=256)
     args = ap.parse_args()
     ws, rank, local = dist_env()
 
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        return
+    if args.profile:
+        run_profile(args, local)
         return
 
     import torch

@@ -31,15 +31,16 @@ def make_config(hidden, intermediate, vocab, n_layers, heads, kv_heads, lin_k_he
 
 def bonsai_2b_graded(ctx=2048):
     """Graded config 3: Bonsai-2B shape, 24 layers 3:1, hidden 2048, MLP 6144, 16 q / 2 kv heads (head_dim 256),
-    GDN 16 key / 32 value heads, vocab 248320; ternary pack g64 + fp16 bias; activations rotated by the normalised
-    2048-point Walsh-Hadamard transform (the config-1 convention); bf16 tied embedding / lm_head."""
-    return make_config(2048, 6144, 248320, 24, 16, 2, 16, 32, group_size=64, has_bias=True, hadamard=2048,
-                       has_signs=False, ctx=ctx)
+    GDN 16 key / 32 value heads, vocab 248320; ternary pack g64 + fp16 bias; activations rotated like the reference
+    model (512-point Walsh-Hadamard blocks with per-input signs, kernels.metal:117-144); bf16 tied embedding /
+    lm_head."""
+    return make_config(2048, 6144, 248320, 24, 16, 2, 16, 32, group_size=64, has_bias=True, hadamard=512,
+                       has_signs=True, ctx=ctx)
 
 
 def bonsai_4b_graded(ctx=4608):
-    """Graded config 4 shape: 32 layers 3:1, hidden 2560, MLP 9216, 16 q / 4 kv heads, GDN 16 / 32 heads. 2560 is not a
-    multiple of 2048, so this shape uses the reference's 512-point blocks."""
+    """Graded config 4 shape: 32 layers 3:1, hidden 2560, MLP 9216, 16 q / 4 kv heads, GDN 16 / 32 heads, 512-point
+    rotation blocks with signs."""
     return make_config(2560, 9216, 248320, 32, 16, 4, 16, 32, group_size=64, has_bias=True, hadamard=512,
                        has_signs=True, ctx=ctx)
 

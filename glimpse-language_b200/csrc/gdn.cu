@@ -1,130 +1,26 @@
-// gdn.cu — GatedDeltaNet layer kernels for the verify pass (gdn_ab, gdn_conv, conv_state, gdn_gates, gdn_recurrent:
-// kernels.metal:504-622) with rollback by deferred commit instead of the reference's candidate-state copies and
-// re-runs (encode_accept, model.rs:1025-1069).
+// gdn.cu — GatedDeltaNet layer of the verify pass in one kernel: causal conv (gdn_conv + conv_state,
+// kernels.metal:515-553), the gates (gdn_gates :556-561) and the gated delta rule (gdn_recurrent :566-622), with
+// rollback by deferred commit instead of the reference's candidate-state copies and re-runs (encode_accept,
+// model.rs:1025-1069).
 //
-// Deferred commit: a pass never writes its candidate recurrent state. It saves its own conv inputs (raw qkv rows), conv
-// outputs and gate inputs in the pending buffer of its parity; the accept step records how many rows n were accepted.
-// The next pass first replays those n rows on the committed state (conv shift + n gated-delta steps, in registers),
-// writes the committed state once, and only then runs its own rows. State traffic per pass is one read and one write of
-// the fp32 state, whatever the accept length, and rollback costs nothing.
+// Deferred commit: a pass never writes its candidate recurrent state. It saves its raw conv inputs, conv outputs and
+// gate inputs in the pending buffers of its parity; the accept step records how many rows n were accepted. The next
+// pass first replays those n rows on the committed state (conv shift + n gated-delta steps, in registers), writes the
+// committed state once and then runs its own rows. State traffic per pass is one read and one write of the fp32 state
+// whatever the accept length, and rollback costs nothing. The conv state is double-buffered by parity because several
+// CTAs read the q/k channels of a key head while one of them writes the new committed rows.
+//
+// CTA = (value head, 16 dv rows), 128 threads: warp w owns dv rows 4w..4w+3, lane = 4 dk entries. Thread c convolves
+// q and k channel c of the head's key head; threads < 16 also the CTA's 16 v channels. All rows are staged in shared
+// memory first, so the sequential steps run without global loads on the critical path.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace bcu {
 
 constexpr float EPS_G = 1e-6f;
+constexpr int RMAX = 2 * VMAX;  // replayed + new rows
 
-// gdn_ab (kernels.metal:504-510, gdn_ab_row :265-273): dense fp32 a/b gate rows. One CTA per row (4 warps split K,
-// partials summed in warp order), all T tokens at once.
-__global__ void __launch_bounds__(128) gdn_ab_kernel(GdnArgs a) {
-    __shared__ float part[4][VMAX];
-    const int row = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int d = a.d, NV = a.NV, T = a.T;
-    const float* wr = row < NV ? a.wa + (size_t)row * d : a.wb + (size_t)(row - NV) * d;
-    const int q = d / 4;
-    // weights before the dependency wait
-    float4 wv[4];
-    int nv = 0;
-    for (int i = w * q + lane * 4; i < (w + 1) * q && nv < 4; i += 128) wv[nv++] = *(const float4*)(wr + i);
-    pdl_trigger();
-    pdl_wait();
-    const int par = a.ctl->parity;
-    float acc[VMAX];
-#pragma unroll
-    for (int t = 0; t < VMAX; t++) acc[t] = 0.0f;
-    int j = 0;
-    for (int i = w * q + lane * 4; i < (w + 1) * q; i += 128, j++) {
-        float4 ww = j < 4 ? wv[j] : *(const float4*)(wr + i);
-#pragma unroll
-        for (int t = 0; t < VMAX; t++)
-            if (t < T) {
-                float4 x = *(const float4*)(a.xn + (size_t)t * d + i);
-                acc[t] += ww.x * x.x + ww.y * x.y + ww.z * x.z + ww.w * x.w;
-            }
-    }
-#pragma unroll
-    for (int t = 0; t < VMAX; t++)
-        if (t < T) {
-            float v = warp_sum(acc[t]);
-            if (lane == 0) part[w][t] = v;
-        }
-    __syncthreads();
-    if (threadIdx.x < T) {
-        int t = threadIdx.x;
-        float v = part[0][t] + part[1][t] + part[2][t] + part[3][t];
-        a.pend_ab[((size_t)par * VMAX + t) * 2 * NV + row] = v;
-    }
-}
-
-void launch_gdn_ab(const GdnArgs& a, cudaStream_t st) {
-    GdnArgs aa = a;
-    void* args[] = {&aa};
-    launch_pdl((const void*)gdn_ab_kernel, dim3(2 * a.NV), dim3(128), 0, st, args);
-}
-
-// gdn_conv (kernels.metal:515-541) + conv_state (:544-553). CTA = one 128-channel head group, thread = channel.
-// First commits the previous pass: the committed conv state becomes rows n..n+2 of [state(3); qkv_prev(n)]. Then the
-// causal width-4 conv of this pass's rows over [state; qkv], SiLU, and for q/k groups the per-head RMS norm scaled by
-// 1/128 (q) or 1/sqrt(128) (k). Raw rows and outputs go to the pending buffers of this pass's parity.
-__global__ void __launch_bounds__(128) gdn_conv_kernel(GdnArgs a) {
-    __shared__ float red[32];
-    const int grp = blockIdx.x, c = grp * 128 + threadIdx.x, C = a.C, T = a.T;
-    float cw[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) cw[i] = a.convw[(size_t)c * 4 + i];
-    pdl_trigger();
-    pdl_wait();
-    const int par = a.ctl->parity, prev = par ^ 1, rn = a.ctl->replay_n;
-    float st[3];
-#pragma unroll
-    for (int j = 0; j < 3; j++) st[j] = a.conv_state[(size_t)j * C + c];
-    if (rn > 0) {
-        const float* pq = a.pend_qkv + (size_t)prev * VMAX * C;
-        float ns[3];
-#pragma unroll
-        for (int j = 0; j < 3; j++) {
-            int k = rn + j;
-            ns[j] = k < 3 ? st[k] : pq[(size_t)(k - 3) * C + c];
-        }
-#pragma unroll
-        for (int j = 0; j < 3; j++) {
-            st[j] = ns[j];
-            a.conv_state[(size_t)j * C + c] = ns[j];
-        }
-    }
-    const int ld = C + a.NV * 128;  // qkvz row stride
-    float rows[3 + VMAX];
-    rows[0] = st[0];
-    rows[1] = st[1];
-    rows[2] = st[2];
-    for (int t = 0; t < T; t++) {
-        float v = a.qkvz[(size_t)t * ld + c];
-        rows[3 + t] = v;
-        a.pend_qkv[((size_t)par * VMAX + t) * C + c] = v;
-    }
-    const bool qk = grp < 2 * a.NK;
-    const float scale = grp < a.NK ? (1.0f / 128.0f) : 0.08838834764831845f;
-    for (int t = 0; t < T; t++) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc += cw[i] * rows[t + i];
-        float v = acc / (1.0f + expf(-acc));
-        if (qk) {
-            float ss = block_sum(v * v, red);
-            float r = rsqrtf(ss / 128.0f + EPS_G);
-            v = v * r * scale;
-        }
-        a.pend_qkvc[((size_t)par * VMAX + t) * C + c] = v;
-    }
-}
-
-void launch_gdn_conv(const GdnArgs& a, cudaStream_t st) {
-    GdnArgs aa = a;
-    void* args[] = {&aa};
-    launch_pdl((const void*)gdn_conv_kernel, dim3(a.C / 128), dim3(128), 0, st, args);
-}
-
-// gdn_gates (kernels.metal:556-561).
 __device__ __forceinline__ void gates(float a_in, float b_in, float ea, float dtb, float& g, float& beta) {
     float x = a_in + dtb;
     float sp = fmaxf(x, 0.0f) + logf(1.0f + expf(-fabsf(x)));
@@ -132,8 +28,8 @@ __device__ __forceinline__ void gates(float a_in, float b_in, float ea, float dt
     beta = 1.0f / (1.0f + expf(-b_in));
 }
 
-// One gated-delta step for the 4 dv rows a warp holds (lane: dk 4*lane..4*lane+3), kernels.metal:607-620:
-// S *= g; kv = S.k; delta = (v - kv) beta; S += k delta; y = S.q.
+// One gated-delta step for the 4 dv rows of a warp (kernels.metal:607-620): S *= g; kv = S.k; delta = (v - kv) beta;
+// S += k delta; y = S.q.
 __device__ __forceinline__ void gdn_step4(float4* st, float4 q, float4 k, const float* v, float g, float beta, float* o) {
     float kv[4];
 #pragma unroll
@@ -153,58 +49,177 @@ __device__ __forceinline__ void gdn_step4(float4* st, float4 q, float4 k, const 
     for (int r = 0; r < 4; r++) o[r] = warp_sum(o[r]);
 }
 
-// gdn_recurrent (kernels.metal:566-622) with the deferred replay. Grid (NV, 8): CTA = 16 dv rows of one value head,
-// warp = 4 rows, lane = 4 dk entries. V head h reads q/k head h / (NV / NK).
-__global__ void __launch_bounds__(128) gdn_recurrent_kernel(GdnArgs a) {
-    const int hd = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int NK = a.NK, NV = a.NV, C = a.C;
+struct GdnSmem {
+    float q[RMAX][128];
+    float k[RMAX][128];
+    float v[RMAX][16];
+    float g[RMAX], beta[RMAX];
+    float red[2][4][VMAX];
+};
+
+__global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
+    __shared__ GdnSmem sm;
+    const int hd = blockIdx.x, blk = blockIdx.y, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int NK = a.NK, NV = a.NV, C = a.C, T = a.T;
     const int hk = hd / (NV / NK);
-    const int dv0 = blockIdx.y * 16 + w * 4;
-    float4 st[4];
-    float* S = a.gdn_state + ((size_t)hd * 128 + dv0) * 128 + lane * 4;
+    const int dv0 = blk * 16;
+    // channels of this thread: q and k channel `tid` of key head hk, v channel dv0 + tid (tid < 16)
+    const int cq = hk * 128 + tid, ck = (NK + hk) * 128 + tid, cv = (2 * NK + hd) * 128 + dv0 + tid;
+    const bool has_v = tid < 16;
+    const bool qk_writer = (hd % (NV / NK)) == 0 && blk == 0;  // one CTA commits the shared q/k channels
+    float wq[4], wk[4], wv[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        wq[i] = a.convw[(size_t)cq * 4 + i];
+        wk[i] = a.convw[(size_t)ck * 4 + i];
+        if (has_v) wv[i] = a.convw[(size_t)cv * 4 + i];
+    }
     const float ea = expf(a.a_log[hd]), dtb = a.dt_bias[hd];
     pdl_trigger();
     pdl_wait();
+    const int par = a.ctl->parity, prev = par ^ 1, rn = a.ctl->replay_n;
+    // recurrent state rows of this warp (issued first, they overlap the conv work)
+    float* S = a.gdn_state + ((size_t)hd * 128 + dv0 + w * 4) * 128 + lane * 4;
+    float4 st[4];
 #pragma unroll
     for (int r = 0; r < 4; r++) st[r] = *(const float4*)(S + (size_t)r * 128);
-    const int par = a.ctl->parity, prev = par ^ 1, rn = a.ctl->replay_n;
-    float o[4], vv[4];
-    for (int t = 0; t < rn; t++) {
-        const float* row = a.pend_qkvc + ((size_t)prev * VMAX + t) * C;
-        const float* ab = a.pend_ab + ((size_t)prev * VMAX + t) * 2 * NV;
-        float g, beta;
-        gates(ab[hd], ab[NV + hd], ea, dtb, g, beta);
-        float4 q = *(const float4*)(row + hk * 128 + lane * 4);
-        float4 k = *(const float4*)(row + (NK + hk) * 128 + lane * 4);
-#pragma unroll
-        for (int r = 0; r < 4; r++) vv[r] = row[(2 * NK + hd) * 128 + dv0 + r];
-        gdn_step4(st, q, k, vv, g, beta, o);
+
+    // ---- stage the replayed rows (conv outputs + gates of the previous pass)
+    const float* pqc = a.pend_qkvc + (size_t)prev * VMAX * C;
+    const float* pab = a.pend_ab + (size_t)prev * VMAX * 2 * NV;
+    for (int r = 0; r < rn; r++) {
+        sm.q[r][tid] = pqc[(size_t)r * C + cq];
+        sm.k[r][tid] = pqc[(size_t)r * C + ck];
+        if (has_v) sm.v[r][tid] = pqc[(size_t)r * C + cv];
     }
-    if (rn > 0) {
-#pragma unroll
-        for (int r = 0; r < 4; r++) *(float4*)(S + (size_t)r * 128) = st[r];
-    }
-    for (int t = 0; t < a.T; t++) {
-        const float* row = a.pend_qkvc + ((size_t)par * VMAX + t) * C;
+    if (tid < rn) gates(pab[(size_t)tid * 2 * NV + hd], pab[(size_t)tid * 2 * NV + NV + hd], ea, dtb, sm.g[tid], sm.beta[tid]);
+    if (tid >= 32 && tid - 32 < T) {
+        int t = tid - 32;
         const float* ab = a.pend_ab + ((size_t)par * VMAX + t) * 2 * NV;
-        float g, beta;
-        gates(ab[hd], ab[NV + hd], ea, dtb, g, beta);
-        float4 q = *(const float4*)(row + hk * 128 + lane * 4);
-        float4 k = *(const float4*)(row + (NK + hk) * 128 + lane * 4);
+        gates(ab[hd], ab[NV + hd], ea, dtb, sm.g[rn + t], sm.beta[rn + t]);
+    }
+
+    // ---- conv: commit the previous pass's rows, then this pass's rows
+    const float* cs_in = a.conv_state + (size_t)prev * 3 * C;  // committed state lives at the previous parity
+    float* cs_out = a.conv_state + (size_t)par * 3 * C;
+    const float* pq = a.pend_qkv + (size_t)prev * VMAX * C;
+    float* pq_out = a.pend_qkv + (size_t)par * VMAX * C;
+    float* pqc_out = a.pend_qkvc + (size_t)par * VMAX * C;
+    const int ld = C + NV * 128;
+    float rq[3 + VMAX], rk[3 + VMAX], rv[3 + VMAX];
+    {
+        float oq[3], ok[3], ov[3];
 #pragma unroll
-        for (int r = 0; r < 4; r++) vv[r] = row[(2 * NK + hd) * 128 + dv0 + r];
-        gdn_step4(st, q, k, vv, g, beta, o);
-        if (lane < 4) {
+        for (int j = 0; j < 3; j++) {
+            oq[j] = cs_in[(size_t)j * C + cq];
+            ok[j] = cs_in[(size_t)j * C + ck];
+            ov[j] = has_v ? cs_in[(size_t)j * C + cv] : 0.0f;
+        }
+        // rows rn..rn+2 of [state(3); previous raw rows]
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            int kk = rn + j;
+            rq[j] = kk < 3 ? oq[kk] : pq[(size_t)(kk - 3) * C + cq];
+            rk[j] = kk < 3 ? ok[kk] : pq[(size_t)(kk - 3) * C + ck];
+            rv[j] = kk < 3 ? ov[kk] : (has_v ? pq[(size_t)(kk - 3) * C + cv] : 0.0f);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < VMAX; t++)
+        if (t < T) {
+            rq[3 + t] = a.qkvz[(size_t)t * ld + cq];
+            rk[3 + t] = a.qkvz[(size_t)t * ld + ck];
+            rv[3 + t] = has_v ? a.qkvz[(size_t)t * ld + cv] : 0.0f;
+        }
+    if (qk_writer) {
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            cs_out[(size_t)j * C + cq] = rq[j];
+            cs_out[(size_t)j * C + ck] = rk[j];
+        }
+#pragma unroll
+        for (int t = 0; t < VMAX; t++)
+            if (t < T) {
+                pq_out[(size_t)t * C + cq] = rq[3 + t];
+                pq_out[(size_t)t * C + ck] = rk[3 + t];
+            }
+    }
+    if (has_v) {
+#pragma unroll
+        for (int j = 0; j < 3; j++) cs_out[(size_t)j * C + cv] = rv[j];
+#pragma unroll
+        for (int t = 0; t < VMAX; t++)
+            if (t < T) pq_out[(size_t)t * C + cv] = rv[3 + t];
+    }
+    // conv + SiLU; q, k rows then get the per-head RMS norm scaled by 1/128 and 1/sqrt(128)
+    float cq_[VMAX], ck_[VMAX];
+#pragma unroll
+    for (int t = 0; t < VMAX; t++)
+        if (t < T) {
+            float aq = 0.0f, ak = 0.0f, av = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                aq += wq[i] * rq[t + i];
+                ak += wk[i] * rk[t + i];
+                av += wv[i] * rv[t + i];
+            }
+            cq_[t] = aq / (1.0f + expf(-aq));
+            ck_[t] = ak / (1.0f + expf(-ak));
+            if (has_v) {
+                float vv = av / (1.0f + expf(-av));
+                sm.v[rn + t][tid] = vv;
+                pqc_out[(size_t)t * C + cv] = vv;
+            }
+        }
+#pragma unroll
+    for (int t = 0; t < VMAX; t++)
+        if (t < T) {
+            float sq = warp_sum(cq_[t] * cq_[t]), sk = warp_sum(ck_[t] * ck_[t]);
+            if (lane == 0) {
+                sm.red[0][w][t] = sq;
+                sm.red[1][w][t] = sk;
+            }
+        }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < VMAX; t++)
+        if (t < T) {
+            float sq = ((sm.red[0][0][t] + sm.red[0][1][t]) + sm.red[0][2][t]) + sm.red[0][3][t];
+            float sk = ((sm.red[1][0][t] + sm.red[1][1][t]) + sm.red[1][2][t]) + sm.red[1][3][t];
+            float q = cq_[t] * rsqrtf(sq / 128.0f + EPS_G) * (1.0f / 128.0f);
+            float k = ck_[t] * rsqrtf(sk / 128.0f + EPS_G) * 0.08838834764831845f;
+            sm.q[rn + t][tid] = q;
+            sm.k[rn + t][tid] = k;
+            if (qk_writer) {
+                pqc_out[(size_t)t * C + cq] = q;
+                pqc_out[(size_t)t * C + ck] = k;
+            }
+        }
+    __syncthreads();
+
+    // ---- gated delta rule: replay (commit), then this pass's rows
+    float o[4], vv[4];
+    for (int r = 0; r < rn + T; r++) {
+        float4 q = *(const float4*)&sm.q[r][lane * 4];
+        float4 k = *(const float4*)&sm.k[r][lane * 4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) vv[i] = sm.v[r][w * 4 + i];
+        gdn_step4(st, q, k, vv, sm.g[r], sm.beta[r], o);
+        if (r == rn - 1) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) *(float4*)(S + (size_t)i * 128) = st[i];
+        }
+        if (r >= rn && lane < 4) {
             float ov = lane == 0 ? o[0] : (lane == 1 ? o[1] : (lane == 2 ? o[2] : o[3]));
-            a.y[(size_t)t * NV * 128 + hd * 128 + dv0 + lane] = ov;
+            a.y[(size_t)(r - rn) * NV * 128 + hd * 128 + dv0 + w * 4 + lane] = ov;
         }
     }
 }
 
-void launch_gdn_recurrent(const GdnArgs& a, cudaStream_t st) {
+void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
     GdnArgs aa = a;
     void* args[] = {&aa};
-    launch_pdl((const void*)gdn_recurrent_kernel, dim3(a.NV, 8), dim3(128), 0, st, args);
+    launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(128), 0, st, args);
 }
 
 // Graded config 2: T rows from explicit q/k/v/gate inputs, outputs for every row, and the state written back as it

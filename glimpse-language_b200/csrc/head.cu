@@ -33,36 +33,59 @@ void repack_head_bf16(const uint16_t* table, int V, int d, uint32_t* out, cudaSt
     repack_head_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(table, V, d, out);
 }
 
+// Final norm of row t (model.rs:945-961; the bf16 table takes the normed row as is, no rotation) written as the
+// bf16 hi/lo operand of the head GEMV (hi = bf16(x), lo = bf16(x - hi): 16 significant bits) in mma B-fragment order.
+template <int NT>
+__device__ void head_operand(const HeadArgs& a, int t, uint32_t* s_b) {
+    const int lane = threadIdx.x & 31, d = a.d;
+    float ss = 0.0f;
+    for (int i = lane; i < a.nss; i += 32) ss += a.ss[i * VMAX + t];
+    float r = rsqrtf(warp_sum(ss) / (float)d + 1e-6f);
+    const int nt = t >> 2, gb = (t & 3) * 2, t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
+    for (int k0 = 0; k0 < d; k0 += 32) {
+        int k = k0 + lane;
+        float x0 = (a.h[(size_t)t * d + k] * r) * a.norm[k];
+        float x1 = __shfl_down_sync(0xffffffffu, x0, 1);
+        if ((lane & 1) == 0) {
+            __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+            __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
+            __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
+            size_t base = ((size_t)(k >> 4) * NT + nt) * 32;
+            s_b[(base + gb * 4 + t4) * 2 + which] = pack_bf162(h0, h1);
+            s_b[(base + (gb + 1) * 4 + t4) * 2 + which] = pack_bf162(l0, l1);
+        }
+    }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bar = (uint64_t*)smem;
-    uint2* s_b = (uint2*)(smem + 128);
+    uint2* s_b = (uint2*)smem;
     __shared__ float wbv[8][16];
     __shared__ int wbi[8][16];
     __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nks = a.d / 16;
-    const uint32_t b_bytes = (uint32_t)(nks * NT * 256);
-    if (tid == 0) {
-        mbar_init(bar, 1);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const int T = a.T;
+    const int nmt = a.V / 16;
+    const int gw = blockIdx.x * 8 + warp, W = gridDim.x * 8;
+    // contiguous m-tile range per warp (rows visited in increasing order)
+    const int per = (nmt + W - 1) / W;
+    const int mt0 = gw * per, mt1 = min(nmt, mt0 + per);
+    // the table does not depend on the previous kernel: start streaming it before the dependency wait
+    uint4 buf0[8], buf1[8];
+    if (mt0 < mt1) {
+        const uint4* wp = (const uint4*)a.w + (size_t)mt0 * nks * 32 + lane;
+#pragma unroll
+        for (int i = 0; i < 8; i++) buf0[i] = __ldcs(wp + (size_t)i * 32);
     }
+    for (size_t i = tid; i < (size_t)nks * NT * 256 / 16; i += 256) ((uint4*)smem)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
     pdl_trigger();
     pdl_wait();
-    if (tid == 0) {
-        mbar_expect_tx(bar, b_bytes);
-        bulk_g2s(s_b, a.bfrag, b_bytes, bar);
-    }
-    bool ok = mbar_wait_bounded(bar, 0);
-    if (__syncthreads_or(!ok)) {
-        if (tid == 0) atomicOr(&a.ctl->err, ERR_MBAR_TIMEOUT);
-        mbar_wait_bounded(bar, 0, 1u << 20);
-        return;
-    }
+    for (int t = warp; t < T; t += 8) head_operand<NT>(a, t, (uint32_t*)smem);
+    __syncthreads();
     const int keep = a.ctl->in.keep_logits;
-    const int T = a.T;
     const int g = lane >> 2, t4 = lane & 3;
     float bv[NT];
     int bi[NT];
@@ -71,19 +94,15 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
         bv[n] = -INFINITY;
         bi[n] = 0x7fffffff;
     }
-    const int nmt = a.V / 16;
-    const int gw = blockIdx.x * 8 + warp, W = gridDim.x * 8;
-    // contiguous m-tile range per warp (rows visited in increasing order)
-    const int per = (nmt + W - 1) / W;
-    const int mt0 = gw * per, mt1 = min(nmt, mt0 + per);
     for (int mt = mt0; mt < mt1; mt++) {
         const uint4* wp = (const uint4*)a.w + (size_t)mt * nks * 32 + lane;
         float acc[NT][4];
 #pragma unroll
         for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-        uint4 buf0[8], buf1[8];
+        if (mt != mt0) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) buf0[i] = __ldcs(wp + (size_t)i * 32);
+            for (int i = 0; i < 8; i++) buf0[i] = __ldcs(wp + (size_t)i * 32);
+        }
         for (int kb = 0; kb < nks; kb += 16) {
 #pragma unroll
             for (int i = 0; i < 8; i++)
@@ -186,7 +205,7 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
 
 template <int NT>
 static void launch_head_t(const HeadArgs& a, int grid, cudaStream_t st) {
-    size_t smem = 128 + (size_t)(a.d / 16) * NT * 256;
+    size_t smem = (size_t)(a.d / 16) * NT * 256;
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -66,17 +66,16 @@ struct bcu_model {
     const float* final_norm = nullptr;
     float* inv_freq = nullptr;
 
-    // state (fp32, the reference's layouts: gdn [NV][128][128], conv [3][C], K/V [ctx][KV][256] per layer)
+    // state (fp32, the reference's layouts: gdn [NV][128][128], conv [3][C], K/V [ctx][KV][256] per layer); the conv
+    // state is double-buffered by pass parity: [n_gdn][2][3][C], committed rows at parity ^ 1
     float *gdn = nullptr, *conv = nullptr, *kc = nullptr, *vc = nullptr;
     float *pend_qkv = nullptr, *pend_qkvc = nullptr, *pend_ab = nullptr;
 
     // scratch
-    float *h = nullptr, *xn = nullptr, *mix = nullptr, *gubuf = nullptr, *y = nullptr, *q = nullptr, *apart = nullptr;
+    float *h = nullptr, *mix = nullptr, *gubuf = nullptr, *y = nullptr, *apart = nullptr;
+    float* ssbuf = nullptr;           // [hidden/128][VMAX] sums of squares of h by row block
+    unsigned* attn_counters = nullptr;
     float* logits = nullptr;
-    uint32_t* bfrag = nullptr;
-    uint32_t* hfrag = nullptr;
-    float* xsum = nullptr;
-    int* xexp = nullptr;
     float* partial = nullptr;
     unsigned* counters = nullptr;
     unsigned* head_counter = nullptr;

@@ -13,12 +13,8 @@ struct bcu_linear {
     int device = 0;
     TernaryMat m;
     void* codes = nullptr;
-    uint32_t* scales = nullptr;
-    uint16_t* bias = nullptr;
+    uint32_t* sb = nullptr;
     // per-call scratch, sized for T <= 16
-    uint32_t* bfrag = nullptr;
-    float* xsum = nullptr;
-    int* xexp = nullptr;
     float* partial = nullptr;
     unsigned* counters = nullptr;
     int* err = nullptr;
@@ -38,32 +34,28 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
     uint16_t *ds = nullptr, *db = nullptr;
     bool ok = cudaMalloc(&dw, wb) == cudaSuccess && cudaMalloc(&ds, sb) == cudaSuccess &&
               (!biases_host || cudaMalloc(&db, sb) == cudaSuccess) && cudaMalloc(&l->codes, wb) == cudaSuccess &&
-              cudaMalloc(&l->scales, sb) == cudaSuccess && cudaMalloc(&l->bias, sb) == cudaSuccess;
+              cudaMalloc(&l->sb, ternary_sb_bytes(O, K, group)) == cudaSuccess;
     if (ok) {
         ok = cudaMemcpy(dw, w_host, wb, cudaMemcpyHostToDevice) == cudaSuccess &&
              cudaMemcpy(ds, scales_host, sb, cudaMemcpyHostToDevice) == cudaSuccess &&
              (!biases_host || cudaMemcpy(db, biases_host, sb, cudaMemcpyHostToDevice) == cudaSuccess);
     }
     if (ok) {
-        repack_ternary(dw, ds, db, O, K, group, l->codes, l->scales, l->bias, 0);
+        repack_ternary(dw, ds, db, O, K, group, l->codes, l->sb, 0);
         ok = cudaDeviceSynchronize() == cudaSuccess;
     }
     cudaFree(dw);
     cudaFree(ds);
     cudaFree(db);
     l->m.codes = l->codes;
-    l->m.scales = l->scales;
-    l->m.bias = l->bias;
+    l->m.sb = l->sb;
     l->m.O = O;
     l->m.K = K;
     l->m.group = group;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     plan_ternary(l->m, sms);
-    ok = ok && cudaMalloc(&l->bfrag, (size_t)(K / 16) * 4 * 256) == cudaSuccess &&
-         cudaMalloc(&l->xsum, (size_t)VMAX * (K / 64) * 4) == cudaSuccess &&
-         cudaMalloc(&l->xexp, VMAX * 4) == cudaSuccess &&
-         cudaMalloc(&l->partial, (size_t)l->m.nsplit * VMAX * O * 4) == cudaSuccess &&
+    ok = ok && cudaMalloc(&l->partial, (size_t)l->m.nsplit * VMAX * O * 4) == cudaSuccess &&
          cudaMalloc(&l->counters, (size_t)(O / 128) * 4) == cudaSuccess && cudaMalloc(&l->err, 4) == cudaSuccess &&
          cudaMemset(l->counters, 0, (size_t)(O / 128) * 4) == cudaSuccess && cudaMemset(l->err, 0, 4) == cudaSuccess;
     if (!ok) {
@@ -77,7 +69,7 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
 void bcu_linear_free(bcu_linear* l) {
     if (!l) return;
     cudaSetDevice(l->device);
-    void* p[] = {l->codes, l->scales, l->bias, l->bfrag, l->xsum, l->xexp, l->partial, l->counters, l->err};
+    void* p[] = {l->codes, l->sb, l->partial, l->counters, l->err};
     for (void* q : p)
         if (q) cudaFree(q);
     delete l;
@@ -89,13 +81,18 @@ static bcu_status linear_run(bcu_linear* l, const uint16_t* xb, const float* xf,
     if (HB && (HB != 512 && HB != 1024 && HB != 2048)) return BCU_ERR_ARG;
     if (HB && l->m.K % HB) return BCU_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    TernaryAct act;
-    act.bfrag = l->bfrag;
-    act.xsum = l->xsum;
-    act.xexp = l->xexp;
-    act.K = l->m.K;
-    launch_rotate_prep(xb, xf, T, l->m.K, HB, signs, l->m.group, act, nullptr, st);
-    launch_ternary_gemv(l->m, act, T, y, 0, l->partial, l->counters, l->err, st);
+    ActSrc src;
+    src.mode = ACT_EXT;
+    src.x = xf;
+    src.xb = xb;
+    src.signs = signs;
+    src.HB = HB;
+    GemvOut o;
+    o.out = y;
+    o.partial = l->partial;
+    o.counters = l->counters;
+    o.err = l->err;
+    launch_ternary_gemv(l->m, src, T, o, nullptr, st);
     if (cudaGetLastError() != cudaSuccess) return BCU_ERR_CUDA;
     return BCU_OK;
 }

@@ -141,11 +141,10 @@ struct Part {
 
 // Bytes of one stacked ternary linear in the arena.
 size_t lin_bytes(int O, int K, int group) {
-    return align256(ternary_codes_bytes(O, K)) + align256(ternary_scales_bytes(O, K, group)) +
-           align256((size_t)O * (K / group) * 2);
+    return align256(ternary_codes_bytes(O, K)) + align256(ternary_sb_bytes(O, K, group));
 }
 
-// Stacks the parts (rows in order) into one packed linear; `signs_of` names the part whose signs rotate the input.
+// Stacks the parts (rows in order) into one packed linear; the first part's signs rotate the shared input.
 bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* out) {
     int O = 0;
     for (auto& p : parts) O += p.O;
@@ -155,11 +154,9 @@ bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* o
     tm.K = K;
     tm.group = group;
     uint8_t* codes = (uint8_t*)arena_take(m, ternary_codes_bytes(O, K));
-    uint8_t* scales = (uint8_t*)arena_take(m, ternary_scales_bytes(O, K, group));
-    uint16_t* bias = (uint16_t*)arena_take(m, (size_t)O * (K / group) * 2);
+    uint8_t* sb = (uint8_t*)arena_take(m, ternary_sb_bytes(O, K, group));
     tm.codes = codes;
-    tm.scales = (const uint32_t*)scales;
-    tm.bias = bias;
+    tm.sb = (const uint32_t*)sb;
     int row = 0;
     for (auto& p : parts) {
         const DevTensor* w = find(m, p.name + ".weight");
@@ -174,8 +171,8 @@ bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* o
         if (b && (b->dtype != BCU_F16 || b->bytes != ns)) return fail(m, BCU_ERR_ARG, p.name + ".biases: wrong shape/dtype");
         // row offsets are multiples of 128, so each part lands on whole row blocks of the stacked layout
         repack_ternary((const uint32_t*)w->dev, (const uint16_t*)s->dev, b ? (const uint16_t*)b->dev : nullptr, p.O, K,
-                       group, codes + ternary_codes_bytes(row, K), (uint32_t*)(scales + ternary_scales_bytes(row, K, group)),
-                       bias + (size_t)row * (K / group), m->st);
+                       group, codes + ternary_codes_bytes(row, K), (uint32_t*)(sb + ternary_sb_bytes(row, K, group)),
+                       m->st);
         CK(cudaGetLastError());
         row += p.O;
     }
@@ -208,129 +205,125 @@ bcu_status dmalloc(bcu_model* m, T** p, size_t bytes) {
         if (s_ != BCU_OK) return s_;    \
     } while (0)
 
-// The kernels of one pass of T rows, in order (Text::encode_embed + encode_layers + encode_head, model.rs:641-985).
+// GDN layer kernel arguments (also used with T = 0 by bcu_flush to commit the pending rows).
+GdnArgs gdn_args(bcu_model* m, const Layer& L, int T) {
+    const bcu_config& c = m->c;
+    GdnArgs g{};
+    g.ctl = m->ctl;
+    g.qkvz = m->mix;
+    g.convw = L.convw;
+    g.a_log = L.a_log;
+    g.dt_bias = L.dt_bias;
+    g.conv_state = m->conv + (size_t)L.gi * 2 * 3 * m->C;
+    g.gdn_state = m->gdn + (size_t)L.gi * c.lin_v_heads * 128 * 128;
+    g.pend_qkv = m->pend_qkv + (size_t)L.gi * 2 * VMAX * m->C;
+    g.pend_qkvc = m->pend_qkvc + (size_t)L.gi * 2 * VMAX * m->C;
+    g.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * c.lin_v_heads;
+    g.y = m->y;
+    g.C = m->C;
+    g.NK = c.lin_k_heads;
+    g.NV = c.lin_v_heads;
+    g.T = T;
+    return g;
+}
+
+// The kernels of one pass of T rows, in order (Text::encode_embed + encode_layers + encode_head, model.rs:641-985):
+// per layer the mixer's input GEMV (norm + rotation fused in; the GDN a/b gates ride along), the mixer core (GDN conv +
+// recurrence, or attention), the mixer's output GEMV (gated norm / gate + rotation fused in, residual add), the MLP
+// gate/up GEMV (norm + rotation fused in) and the down GEMV (SwiGLU + rotation fused in, residual add); then the head.
 void enqueue_pass(bcu_model* m, int T) {
     const bcu_config& c = m->c;
-    const int NT = (2 * T + 7) / 8, d = c.hidden, ff = c.intermediate;
+    const int NT = (2 * T + 7) / 8, d = c.hidden;
     cudaStream_t st = m->st;
-    TernaryAct act;
-    act.bfrag = m->bfrag;
-    act.xsum = m->xsum;
-    act.xexp = m->xexp;
+    GemvOut store, resid;
+    store.partial = resid.partial = m->partial;
+    store.counters = resid.counters = m->counters;
+    store.err = resid.err = &m->ctl->err;
+    store.out = nullptr;
+    resid.out = m->h;
+    resid.add = 1;
+    resid.ss_out = m->ssbuf;
     for (size_t li = 0; li < m->layers.size(); li++) {
         const Layer& L = m->layers[li];
-        PrepNormArgs pn{};
-        pn.ctl = m->ctl;
-        pn.embed_bf16 = li == 0 ? m->embed_rows : nullptr;
-        pn.h = m->h;
-        pn.w = L.in_norm;
-        pn.signs = L.mix_in.signs;
-        pn.xn = L.attn ? nullptr : m->xn;
-        pn.D = d;
-        pn.HB = c.hadamard;
-        pn.group = c.group_size;
-        pn.T = T;
-        pn.vocab = c.vocab;
-        pn.act = act;
-        launch_prep_norm(pn, NT, st);
-        launch_ternary_gemv(L.mix_in.m, act, T, m->mix, 0, m->partial, m->counters, &m->ctl->err, st);
+        ActSrc in;
+        in.mode = li == 0 ? ACT_EMBED : ACT_NORM;
+        in.x = m->h;
+        in.xb = m->embed_rows;
+        in.w = L.in_norm;
+        in.signs = L.mix_in.signs;
+        in.ss = m->ssbuf;
+        in.nss = d / 128;
+        in.ctl = m->ctl;
+        in.h_out = m->h;
+        in.HB = c.hadamard;
+        in.vocab = c.vocab;
+        GemvOut mixo = store;
+        mixo.out = m->mix;
+        ActSrc out;
+        out.HB = c.hadamard;
+        out.signs = L.mix_out.signs;
         if (!L.attn) {
-            GdnArgs g{};
-            g.ctl = m->ctl;
-            g.qkvz = m->mix;
-            g.xn = m->xn;
-            g.wa = L.wa;
-            g.wb = L.wb;
-            g.convw = L.convw;
-            g.a_log = L.a_log;
-            g.dt_bias = L.dt_bias;
-            g.conv_state = m->conv + (size_t)L.gi * 3 * m->C;
-            g.gdn_state = m->gdn + (size_t)L.gi * c.lin_v_heads * 128 * 128;
-            g.pend_qkv = m->pend_qkv + (size_t)L.gi * 2 * VMAX * m->C;
-            g.pend_qkvc = m->pend_qkvc + (size_t)L.gi * 2 * VMAX * m->C;
-            g.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * c.lin_v_heads;
-            g.y = m->y;
-            g.d = d;
-            g.C = m->C;
-            g.NK = c.lin_k_heads;
-            g.NV = c.lin_v_heads;
-            g.T = T;
-            launch_gdn_ab(g, st);
-            launch_gdn_conv(g, st);
-            launch_gdn_recurrent(g, st);
-            PrepGatedArgs pg{};
-            pg.y = m->y;
-            pg.qkvz = m->mix;
-            pg.w = L.gnorm;
-            pg.signs = L.mix_out.signs;
-            pg.gw = m->gw;
-            pg.C = m->C;
-            pg.HB = c.hadamard;
-            pg.group = c.group_size;
-            pg.T = T;
-            pg.act = act;
-            launch_prep_gated(pg, NT, st);
+            AbArgs ab;
+            ab.wa = L.wa;
+            ab.wb = L.wb;
+            ab.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * c.lin_v_heads;
+            ab.ctl = m->ctl;
+            ab.nv = c.lin_v_heads;
+            launch_ternary_gemv(L.mix_in.m, in, T, mixo, &ab, st);
+            launch_gdn_layer(gdn_args(m, L, T), st);
+            out.mode = ACT_GATED;
+            out.x = m->y;
+            out.x2 = m->mix;
+            out.ld2 = m->C + m->gw;
+            out.off2 = m->C;
+            out.w = L.gnorm;
         } else {
+            launch_ternary_gemv(L.mix_in.m, in, T, mixo, nullptr, st);
             AttnArgs a{};
             a.ctl = m->ctl;
             a.qkv = m->mix;
             a.qn = L.qn;
             a.kn = L.kn;
             a.inv_freq = m->inv_freq;
-            a.q = m->q;
             a.kc = m->kc + (size_t)L.ai * c.ctx * m->kvw;
             a.vc = m->vc + (size_t)L.ai * c.ctx * m->kvw;
             a.part = m->apart;
+            a.counters = m->attn_counters;
+            a.out = m->y;
             a.H = c.heads;
             a.KV = c.kv_heads;
             a.rot = c.rotary_dims;
             a.T = T;
             a.ld = 2 * m->aw + 2 * m->kvw;
             a.ctx = c.ctx;
-            launch_attn_prep(a, st);
-            launch_attn_split(a, st);
-            PrepAttnOutArgs po{};
-            po.part = m->apart;
-            po.qkv = m->mix;
-            po.signs = L.mix_out.signs;
-            po.H = c.heads;
-            po.HB = c.hadamard;
-            po.group = c.group_size;
-            po.T = T;
-            po.qkv_ld = a.ld;
-            po.act = act;
-            launch_prep_attn_out(po, NT, st);
+            launch_attn(a, st);
+            out.mode = ACT_GATE;
+            out.x = m->y;
+            out.x2 = m->mix;
+            out.ld2 = a.ld;
         }
-        launch_ternary_gemv(L.mix_out.m, act, T, m->h, 1, m->partial, m->counters, &m->ctl->err, st);
-        PrepNormArgs pp = pn;
-        pp.embed_bf16 = nullptr;
-        pp.w = L.post_norm;
-        pp.signs = L.gu.signs;
-        pp.xn = nullptr;
-        launch_prep_norm(pp, NT, st);
-        launch_ternary_gemv(L.gu.m, act, T, m->gubuf, 0, m->partial, m->counters, &m->ctl->err, st);
-        PrepSwigluArgs ps{};
-        ps.gu = m->gubuf;
-        ps.signs = L.down.signs;
-        ps.ff = ff;
-        ps.HB = c.hadamard;
-        ps.group = c.group_size;
-        ps.T = T;
-        ps.act = act;
-        launch_prep_swiglu(ps, NT, st);
-        launch_ternary_gemv(L.down.m, act, T, m->h, 1, m->partial, m->counters, &m->ctl->err, st);
+        launch_ternary_gemv(L.mix_out.m, out, T, resid, nullptr, st);
+        ActSrc post = in;
+        post.mode = ACT_NORM;
+        post.w = L.post_norm;
+        post.signs = L.gu.signs;
+        GemvOut guo = store;
+        guo.out = m->gubuf;
+        launch_ternary_gemv(L.gu.m, post, T, guo, nullptr, st);
+        ActSrc sw;
+        sw.mode = ACT_SWIGLU;
+        sw.x = m->gubuf;
+        sw.signs = L.down.signs;
+        sw.HB = c.hadamard;
+        launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st);
     }
-    PrepHeadArgs ph{};
-    ph.h = m->h;
-    ph.w = m->final_norm;
-    ph.bfrag = m->hfrag;
-    ph.D = d;
-    ph.T = T;
-    launch_prep_head(ph, NT, st);
     HeadArgs ha{};
     ha.ctl = m->ctl;
     ha.w = m->head_w;
-    ha.bfrag = m->hfrag;
+    ha.h = m->h;
+    ha.ss = m->ssbuf;
+    ha.nss = d / 128;
+    ha.norm = m->final_norm;
     ha.logits = m->logits;
     ha.pv = m->pv;
     ha.pi = m->pi;
@@ -380,6 +373,12 @@ __global__ void ctl_set_kernel(Ctl* c, int off, int replay_n) {
     c->off = off;
     c->replay_n = replay_n;
     c->err = 0;
+}
+
+// After a commit-only pass: nothing left to replay, next pass at the other parity.
+__global__ void ctl_flushed_kernel(Ctl* c) {
+    c->replay_n = 0;
+    c->parity ^= 1;
 }
 
 __global__ void ctl_planted_kernel(Ctl* c, const uint32_t* p, int n) {
@@ -556,7 +555,7 @@ bcu_status bcu_finalize(bcu_model* m) {
     // state and scratch
     const int NV = c.lin_v_heads;
     TRY(dmalloc(m, &m->gdn, (size_t)m->n_gdn * NV * 128 * 128 * 4));
-    TRY(dmalloc(m, &m->conv, (size_t)m->n_gdn * 3 * m->C * 4));
+    TRY(dmalloc(m, &m->conv, (size_t)m->n_gdn * 2 * 3 * m->C * 4));
     TRY(dmalloc(m, &m->kc, (size_t)m->n_attn * c.ctx * m->kvw * 4));
     TRY(dmalloc(m, &m->vc, (size_t)m->n_attn * c.ctx * m->kvw * 4));
     TRY(dmalloc(m, &m->pend_qkv, (size_t)m->n_gdn * 2 * VMAX * m->C * 4));
@@ -565,17 +564,14 @@ bcu_status bcu_finalize(bcu_model* m) {
     int wide = std::max(std::max(d, ff), std::max(m->gw, m->aw));
     int mixw = std::max(m->C + m->gw, 2 * m->aw + 2 * m->kvw);
     TRY(dmalloc(m, &m->h, (size_t)VMAX * d * 4));
-    TRY(dmalloc(m, &m->xn, (size_t)VMAX * d * 4));
     TRY(dmalloc(m, &m->mix, (size_t)VMAX * mixw * 4));
     TRY(dmalloc(m, &m->gubuf, (size_t)VMAX * 2 * ff * 4));
     TRY(dmalloc(m, &m->y, (size_t)VMAX * std::max(m->gw, m->aw) * 4));
-    TRY(dmalloc(m, &m->q, (size_t)VMAX * c.heads * 256 * 4));
     TRY(dmalloc(m, &m->apart, (size_t)VMAX * c.heads * NSPLIT_ATTN * 258 * 4));
+    TRY(dmalloc(m, &m->ssbuf, (size_t)(d / 128) * VMAX * 4));
+    TRY(dmalloc(m, &m->attn_counters, (size_t)VMAX * c.kv_heads * 4));
     TRY(dmalloc(m, &m->logits, (size_t)VMAX * c.vocab * 4));
-    TRY(dmalloc(m, &m->bfrag, (size_t)(wide / 16) * 4 * 256));
-    TRY(dmalloc(m, &m->hfrag, (size_t)(d / 16) * 4 * 256));
-    TRY(dmalloc(m, &m->xsum, (size_t)VMAX * (wide / 64) * 4));
-    TRY(dmalloc(m, &m->xexp, (size_t)VMAX * 4));
+    (void)wide;
     size_t pf = 0;
     int maxrb = 1;
     for (auto& L : m->layers) {
@@ -608,7 +604,8 @@ bcu_status bcu_reset(bcu_model* m) {
     CK(cudaSetDevice(m->device));
     const int NV = m->c.lin_v_heads;
     CK(cudaMemsetAsync(m->gdn, 0, (size_t)m->n_gdn * NV * 128 * 128 * 4, m->st));
-    CK(cudaMemsetAsync(m->conv, 0, (size_t)m->n_gdn * 3 * m->C * 4, m->st));
+    CK(cudaMemsetAsync(m->conv, 0, (size_t)m->n_gdn * 2 * 3 * m->C * 4, m->st));
+    CK(cudaMemsetAsync(m->attn_counters, 0, (size_t)VMAX * m->c.kv_heads * 4, m->st));
     Ctl z;
     memset(&z, 0, sizeof(z));
     memcpy(m->h_out, &z, sizeof(Ctl));
@@ -628,8 +625,8 @@ void bcu_destroy(bcu_model* m) {
     for (auto& g : m->graphs)
         if (g) cudaGraphExecDestroy(g);
     for (auto& kv : m->staged) cudaFree(kv.second.dev);
-    void* bufs[] = {m->arena, m->gdn, m->conv, m->kc, m->vc, m->pend_qkv, m->pend_qkvc, m->pend_ab, m->h, m->xn,
-                    m->mix, m->gubuf, m->y, m->q, m->apart, m->logits, m->bfrag, m->hfrag, m->xsum, m->xexp,
+    void* bufs[] = {m->arena, m->gdn, m->conv, m->kc, m->vc, m->pend_qkv, m->pend_qkvc, m->pend_ab, m->h,
+                    m->mix, m->gubuf, m->y, m->apart, m->ssbuf, m->attn_counters, m->logits,
                     m->partial, m->counters, m->head_counter, m->pv, m->pi, m->ctl, m->planted_dev};
     for (void* b : bufs)
         if (b) cudaFree(b);
@@ -726,31 +723,13 @@ bcu_status bcu_flush(bcu_model* m) {
     CK(cudaSetDevice(m->device));
     TRY(read_ctl(m));
     if (m->h_out->replay_n == 0) return BCU_OK;
-    // replay-only: the GDN conv and recurrent kernels with zero new rows commit the pending rows
-    for (auto& L : m->layers) {
-        if (L.attn) continue;
-        GdnArgs g{};
-        g.ctl = m->ctl;
-        g.qkvz = m->mix;
-        g.convw = L.convw;
-        g.a_log = L.a_log;
-        g.dt_bias = L.dt_bias;
-        g.conv_state = m->conv + (size_t)L.gi * 3 * m->C;
-        g.gdn_state = m->gdn + (size_t)L.gi * m->c.lin_v_heads * 128 * 128;
-        g.pend_qkv = m->pend_qkv + (size_t)L.gi * 2 * VMAX * m->C;
-        g.pend_qkvc = m->pend_qkvc + (size_t)L.gi * 2 * VMAX * m->C;
-        g.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * m->c.lin_v_heads;
-        g.y = m->y;
-        g.d = m->c.hidden;
-        g.C = m->C;
-        g.NK = m->c.lin_k_heads;
-        g.NV = m->c.lin_v_heads;
-        g.T = 0;
-        launch_gdn_conv(g, m->st);
-        launch_gdn_recurrent(g, m->st);
-    }
+    // replay-only: the GDN layer kernel with zero new rows commits the pending rows (it writes the conv state at this
+    // parity, so the parity flips as after a pass)
+    for (auto& L : m->layers)
+        if (!L.attn) launch_gdn_layer(gdn_args(m, L, 0), m->st);
     CK(cudaGetLastError());
-    CK(cudaMemsetAsync(&m->ctl->replay_n, 0, 4, m->st));
+    ctl_flushed_kernel<<<1, 1, 0, m->st>>>(m->ctl);
+    CK(cudaGetLastError());
     TRY(wait_stream(m, WAIT_S));
     m->pending_n = 0;
     return BCU_OK;
@@ -818,10 +797,16 @@ static bcu_status copy_kv(bcu_model* m, float* dst, int dst_cap, const float* sr
 bcu_status bcu_snapshot(bcu_model* m, bcu_state** out) {
     if (!m || !out) return BCU_ERR_ARG;
     TRY(bcu_flush(m));
+    TRY(read_ctl(m));
+    const int par = m->h_out->parity;
     bcu_state* s;
     TRY(bcu_state_new(m, m->len, &s));
     CK(cudaMemcpyAsync(s->gdn, m->gdn, s->gdn_bytes, cudaMemcpyDeviceToDevice, m->st));
-    CK(cudaMemcpyAsync(s->conv, m->conv, s->conv_bytes, cudaMemcpyDeviceToDevice, m->st));
+    // the committed conv rows of each layer live at parity ^ 1 of its double buffer
+    size_t cs = (size_t)3 * m->C * 4;
+    if (m->n_gdn)
+        CK(cudaMemcpy2DAsync(s->conv, cs, (const char*)m->conv + (par ^ 1) * cs, 2 * cs, cs, m->n_gdn,
+                             cudaMemcpyDeviceToDevice, m->st));
     TRY(copy_kv(m, s->kc, s->len, m->kc, m->c.ctx, s->len));
     TRY(copy_kv(m, s->vc, s->len, m->vc, m->c.ctx, s->len));
     TRY(wait_stream(m, WAIT_S));
@@ -833,7 +818,11 @@ bcu_status bcu_restore(bcu_model* m, const bcu_state* s) {
     if (!m || !s || !m->finalized) return fail(m, BCU_ERR_ARG, "bad restore");
     CK(cudaSetDevice(m->device));
     CK(cudaMemcpyAsync(m->gdn, s->gdn, s->gdn_bytes, cudaMemcpyDeviceToDevice, m->st));
-    CK(cudaMemcpyAsync(m->conv, s->conv, s->conv_bytes, cudaMemcpyDeviceToDevice, m->st));
+    // both halves of each layer's conv double buffer, so whichever parity comes next reads the restored rows
+    size_t cs = (size_t)3 * m->C * 4;
+    for (int half = 0; half < 2 && m->n_gdn; half++)
+        CK(cudaMemcpy2DAsync((char*)m->conv + half * cs, 2 * cs, s->conv, cs, cs, m->n_gdn, cudaMemcpyDeviceToDevice,
+                             m->st));
     TRY(copy_kv(m, m->kc, m->c.ctx, s->kc, s->len, s->len));
     TRY(copy_kv(m, m->vc, m->c.ctx, s->vc, s->len, s->len));
     ctl_set_kernel<<<1, 1, 0, m->st>>>(m->ctl, s->len, 0);
@@ -895,7 +884,7 @@ bcu_status bcu_pass_bytes(const bcu_model* m, int32_t t, double* bytes) {
     for (auto& L : m->layers)
         for (const Lin* ln : {&L.mix_in, &L.mix_out, &L.gu, &L.down}) {
             double O = ln->m.O, K = ln->m.K, g = ln->m.group;
-            b += O * K / 4 + O * (K / g) * 2 * (c.has_bias ? 2 : 1);
+            b += O * K / 4 + O * (K / g) * 4;  // codes + fp16 scale and bias per group
         }
     b += (double)c.vocab * c.hidden * 2;                                          // bf16 head
     b += (double)m->n_gdn * 2 * c.lin_v_heads * c.hidden * 4;                     // dense a/b

@@ -1,24 +1,27 @@
-// ternary.cu — tensor-core ternary verify GEMV for T <= 16 rows (the reference's qmvxm / qmvx / qmv_cm / qmvr / qmv4,
-// kernels.metal:275-404 and 664-709, kernels/qmvx.comp, kernels/qmv_cm.comp), plus the weight repack and the
-// standalone rotate-then-linear op of graded config 1.
+// ternary.cu — tensor-core ternary verify GEMV for T <= 16 rows with the activation producer fused in front (the
+// reference's qmvxm / qmvx / qmv_cm / qmvr / qmv4, kernels.metal:275-404 and 664-709, kernels/qmvx.comp,
+// kernels/qmv_cm.comp, and the rotation kernels of kernels.metal:118-226 that feed them).
 //
 // Why tensor cores at batch 1: a T = 9 verify does 9 multiply-adds per 2-bit weight. At the HBM rate of ~21 T
 // weights/s that is ~190 T FMA/s, five times what the CUDA cores can issue, so the products go to mma.m16n8k16 and
 // the CUDA cores only decode: per pair of weights one LOP3 ((w & mask) | 0x6400 gives fp16 1024 + c*4^j) and one
-// HFMA2 (x s, - 1024 s gives exactly c*s*4^j). The activation operand carries 4^-j and a per-row power-of-two scale
-// and is split into fp16 hi + lo columns, so products are exact and the sum is fp32-accurate; the bias term
-// sum_g b_g * sum_k x_k is added in fp32 from the producer's group sums. Every output's reduction order is fixed
-// and independent of T, so a row's result is bit-identical whether it is verified alone or among 9 rows.
+// HFMA2 (x s, - 1024 s gives exactly c*s*4^j). The activation operand carries 4^-j and a per-(CTA, row) power of
+// two and is split into fp16 hi + lo columns, so products are exact and sums fp32-accurate. The bias term
+// sum_g b_g * sum_k x_k is one more k16 MMA step per warp (A = 64 b, B = group sums / 64). Every output's reduction
+// order is fixed and independent of T: a row's result is bit-identical whether it is verified alone or among 16.
 //
-// CTA = 128 rows x kslice codes (8 warps = 2 row groups of 64 x 4 k-quarters). One thread streams the CTA's codes
-// and scales into shared memory with cp.async.bulk before waiting on the previous kernel (PDL), then the
-// activation tile. Split-K partials are summed in a fixed order by the last CTA of each row block.
+// CTA = 128 rows x kslice codes (8 warps = 2 row groups of 64 x 4 k-quarters). Before waiting on the previous kernel
+// (programmatic dependent launch) one thread streams the CTA's codes and scale/bias tiles into shared memory with
+// cp.async.bulk; after the wait every warp builds the operand of its tokens from the source rows (norm / SwiGLU /
+// gated norm / gate, signs, Walsh-Hadamard transform in registers). Split-K partials are summed in a fixed order by
+// the last CTA of each row block, which also applies the residual add and the sums of squares the next norm needs.
 #include <cstdio>
-#include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
 namespace bcu {
+
+constexpr float EPS_T = 1e-6f;
 
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
     cudaLaunchConfig_t cfg = {};
@@ -35,7 +38,7 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
 }
 
 size_t ternary_codes_bytes(int O, int K) { return (size_t)O * K / 4; }
-size_t ternary_scales_bytes(int O, int K, int group) { return (size_t)O * (K / group) * 2; }
+size_t ternary_sb_bytes(int O, int K, int group) { return (size_t)O * (K / group) * 4; }
 
 // ------------------------------------------------------------------------------------------------ repack
 // One thread per output code word.
@@ -67,114 +70,338 @@ __global__ void repack_codes_kernel(const uint32_t* __restrict__ w, int O, int K
     out[idx] = word;
 }
 
-__global__ void repack_scales_kernel(const uint16_t* __restrict__ s, const uint16_t* __restrict__ b, int O, int K,
-                                     int group, uint32_t* __restrict__ out, uint16_t* __restrict__ bias) {
+// One thread per sb entry: [rb][kc][mt][2][gpc][8].
+__global__ void repack_sb_kernel(const uint16_t* __restrict__ s, const uint16_t* __restrict__ b, int O, int K,
+                                 int group, uint32_t* __restrict__ out) {
     int gpc = 128 / group, ng = K / group;
-    size_t n = (size_t)(O / 16) * (K / 128) * gpc * 8;  // entries
+    size_t n = (size_t)(O / 16) * (K / 128) * 2 * gpc * 8;
     size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx < n) {
-        int g = idx & 7;
-        size_t r = idx >> 3;
-        int gi = r % gpc;
-        r /= gpc;
-        int mt = r & 7;
-        size_t rk = r >> 3;
-        int nkc = K / 128;
-        int kc = rk % nkc;
-        int rb = rk / nkc;
-        int row = rb * 128 + mt * 16 + g;
-        int grp = kc * gpc + gi;
-        out[idx] = (uint32_t)s[(size_t)row * ng + grp] | ((uint32_t)s[(size_t)(row + 8) * ng + grp] << 16);
+    if (idx >= n) return;
+    int g = idx & 7;
+    size_t r = idx >> 3;
+    int gi = r % gpc;
+    r /= gpc;
+    int which = r & 1;
+    r >>= 1;
+    int mt = r & 7;
+    size_t rk = r >> 3;
+    int nkc = K / 128;
+    int kc = rk % nkc;
+    int rb = rk / nkc;
+    int grp = kc * gpc + gi;
+    uint16_t v[2];
+    for (int half = 0; half < 2; half++) {
+        size_t row = (size_t)rb * 128 + mt * 16 + g + 8 * half;
+        uint16_t sv = s[row * ng + grp];
+        if (which == 0) {
+            v[half] = sv;
+        } else {
+            __half bb = b ? __ushort_as_half(b[row * ng + grp]) : __hneg(__ushort_as_half(sv));
+            v[half] = __half_as_ushort(__float2half_rn(__half2float(bb) * 64.0f));
+        }
     }
-    size_t nb = (size_t)O * ng;
-    for (size_t i = idx; i < nb; i += (size_t)gridDim.x * blockDim.x)
-        bias[i] = b ? b[i] : (uint16_t)(s[i] ^ 0x8000u);
+    out[idx] = (uint32_t)v[0] | ((uint32_t)v[1] << 16);
 }
 
 void repack_ternary(const uint32_t* w_mlx, const uint16_t* s, const uint16_t* b, int O, int K, int group,
-                    void* codes, uint32_t* scales, uint16_t* bias, cudaStream_t st) {
+                    void* codes, uint32_t* sb, cudaStream_t st) {
     size_t n = (size_t)O * K / 16;
     repack_codes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w_mlx, O, K, (uint32_t*)codes);
-    size_t ns = (size_t)(O / 16) * (K / 128) * (128 / group) * 8;
-    size_t nb = (size_t)O * (K / group);
-    size_t nmax = ns > nb ? ns : nb;
-    repack_scales_kernel<<<(unsigned)((nmax + 255) / 256), 256, 0, st>>>(s, b, O, K, group, scales, bias);
+    size_t ns = (size_t)(O / 16) * (K / 128) * 2 * (128 / group) * 8;
+    repack_sb_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(s, b, O, K, group, sb);
 }
 
-// Split-K plan: the fewest K-slices (multiples of 512 codes, at most 2048 so the CTA's tiles stay under 200 KB of
-// shared memory at NT = 4) that give at least one CTA per SM.
+// Split-K plan: the fewest K-slices (512, 1024 or 2048 codes) that give at least one CTA per SM.
 void plan_ternary(TernaryMat& m, int num_sms) {
     int rb = m.O / 128;
     int best = 0;
-    for (int ns = 1; ns <= m.K / 512; ns++) {
-        if (m.K % (ns * 512) != 0) continue;
-        if (m.K / ns > 2048) continue;
-        best = ns;
-        if (rb * ns >= num_sms) break;
+    for (int ks : {2048, 1024, 512}) {
+        if (m.K % ks) continue;
+        best = ks;
+        if (rb * (m.K / ks) >= num_sms) break;
     }
-    if (best == 0) best = m.K / 512;  // K/ns <= 2048 always holds for ns = K/512
-    m.nsplit = best;
-    m.kslice = m.K / best;
+    m.kslice = best;
+    m.nsplit = m.K / best;
 }
 
 // ------------------------------------------------------------------------------------------------ GEMV
 struct GemvParams {
-    const uint4* codes;
-    const uint32_t* scales;
-    const uint16_t* bias;
-    const uint32_t* bfrag;
-    const float* xsum;
-    const int* xexp;
-    float* out;
-    float* partial;
-    unsigned* counters;
-    int* err;
-    int O, K, group, kslice, nsplit, T, add;
+    const uint8_t* codes;
+    const uint32_t* sb;
+    ActSrc src;
+    GemvOut o;
+    AbArgs ab;
+    int O, K, group, kslice, nsplit, T, n_main, ab_rows;
 };
 
-template <int NT, int GPC>
+__device__ __forceinline__ float sigm(float z) { return 1.0f / (1.0f + expf(-z)); }
+
+__device__ __forceinline__ uint32_t resolve_id(const Ctl* ctl, int t) {
+    int feed = ctl->in.feed;
+    if (feed == 1 && t == 0) return ctl->bonus;
+    if (feed == 2 && ctl->planted) {
+        int i = ctl->off - ctl->in.planted_base + t;
+        if (i >= 0 && i < ctl->planted_n) return ctl->planted[i];
+    }
+    return ctl->in.ids[t];
+}
+
+// Per-row scalar of NORM / EMBED: r = rsqrt(mean(h^2) + eps). EMBED also records the id and, in CTA 0, writes the
+// row into the residual stream. Fixed-order reductions (lane strides, then the warp tree).
+__device__ float row_scale(const ActSrc& s, int t, int K, uint32_t* id_out, bool writer) {
+    const int lane = threadIdx.x & 31;
+    float acc = 0.0f;
+    if (s.mode == ACT_NORM) {
+        for (int i = lane; i < s.nss; i += 32) acc += s.ss[i * VMAX + t];
+    } else if (s.mode == ACT_EMBED) {
+        uint32_t id = resolve_id(s.ctl, t);
+        if (writer && lane == 0) {
+            ((Ctl*)s.ctl)->used[t] = id;
+            if (id >= (uint32_t)s.vocab) atomicOr(&((Ctl*)s.ctl)->err, ERR_BAD_TOKEN);
+        }
+        if (id >= (uint32_t)s.vocab) id = 0;
+        *id_out = id;
+        const uint16_t* row = s.xb + (size_t)id * K;
+        for (int k = lane; k < K; k += 32) {
+            float a = __bfloat162float(__ushort_as_bfloat16(row[k]));
+            acc += a * a;
+            if (writer) s.h_out[(size_t)t * K + k] = a;
+        }
+    } else {
+        return 1.0f;
+    }
+    acc = warp_sum(acc);
+    return rsqrtf(acc / (float)K + EPS_T);
+}
+
+// Pre-rotation value x_k of row t (modes other than GATED, which needs head norms).
+__device__ __forceinline__ float act_value(const ActSrc& s, int t, int k, int K, float r, uint32_t id) {
+    switch (s.mode) {
+        case ACT_NORM: return (s.x[(size_t)t * K + k] * r) * s.w[k];
+        case ACT_EMBED: return (__bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)id * K + k])) * r) * s.w[k];
+        case ACT_SWIGLU: {
+            float g = s.x[(size_t)t * 2 * K + k], u = s.x[(size_t)t * 2 * K + K + k];
+            return (g * u) * sigm(g);
+        }
+        case ACT_GATE: {
+            float gt = s.x2[(size_t)t * s.ld2 + (k >> 8) * 512 + 256 + (k & 255)];
+            return s.x[(size_t)t * K + k] * sigm(gt);
+        }
+        default:
+            return s.xb ? __bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)t * K + k])) : s.x[(size_t)t * K + k];
+    }
+}
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }  // |e| <= 126
+
+// Builds token t's operand for this CTA's K-slice into shared memory (one warp). SPAN = the values a lane holds x 32:
+// max(kslice, HB). Lane l holds element span0 + l + 32 e, the layout of fwht512 (kernels.metal:32-51), so the
+// transform's strides 1..16 run across lanes and 32.. inside the lane, in ascending order (bit-identical to an
+// in-memory radix-2 transform).
+template <int SPAN, int NT>
+__device__ void build_token(const GemvParams& p, int t, int ks, uint32_t* s_b, uint16_t* s_bb16, int* s_e) {
+    constexpr int VPL = SPAN / 32;
+    const int lane = threadIdx.x & 31;
+    const ActSrc& s = p.src;
+    const int K = p.K, kslice = p.kslice, HB = s.HB;
+    const int k0 = ks * kslice;
+    const int span0 = HB > kslice ? (k0 / HB) * HB : k0;
+    float v[VPL];
+    uint32_t id = 0;
+    float r = row_scale(s, t, K, &id, blockIdx.x == 0);
+    if (s.mode == ACT_GATED) {
+        float zz[VPL];
+#pragma unroll
+        for (int e = 0; e < VPL; e++) {
+            int k = span0 + lane + 32 * e;
+            v[e] = s.x[(size_t)t * K + k];
+            zz[e] = s.x2[(size_t)t * s.ld2 + s.off2 + k];
+        }
+#pragma unroll
+        for (int c = 0; c < VPL / 4; c++) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int e = 4 * c; e < 4 * c + 4; e++) ss += v[e] * v[e];
+            float rh = rsqrtf(warp_sum(ss) / 128.0f + EPS_T);
+#pragma unroll
+            for (int e = 4 * c; e < 4 * c + 4; e++) {
+                int d = (lane + 32 * e) & 127;
+                v[e] = (((zz[e] * v[e]) * rh) * s.w[d]) * sigm(zz[e]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < VPL; e++) v[e] = act_value(s, t, span0 + lane + 32 * e, K, r, id);
+    }
+    if (s.signs) {
+#pragma unroll
+        for (int e = 0; e < VPL; e++) v[e] *= s.signs[span0 + lane + 32 * e];
+    }
+    // Walsh-Hadamard transform of each HB block of the span (HB = 0: the input is already rotated)
+    if (HB > 0) {
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            bool up = (lane & m) != 0;
+#pragma unroll
+            for (int e = 0; e < VPL; e++) {
+                float o = __shfl_xor_sync(0xffffffffu, v[e], m);
+                v[e] = up ? o - v[e] : v[e] + o;
+            }
+        }
+#pragma unroll
+        for (int h = 1; h < VPL; h <<= 1) {
+            if (h * 32 >= HB) break;
+#pragma unroll
+            for (int e = 0; e < VPL; e++)
+                if ((e & h) == 0) {
+                    float a = v[e], b = v[e + h];
+                    v[e] = a + b;
+                    v[e + h] = a - b;
+                }
+        }
+        const float inv = HB == 512 ? 0.044194173824159216f : (HB == 2048 ? 0.02209708691207961f : 0.03125f);
+#pragma unroll
+        for (int e = 0; e < VPL; e++) v[e] *= inv;
+    }
+
+    // the slice [k0, k0 + kslice) within the span
+    const int e_lo = (k0 - span0) / 32, e_hi = e_lo + kslice / 32;
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < VPL; e++)
+        if (e >= e_lo && e < e_hi) amax = fmaxf(amax, fabsf(v[e]));
+    amax = warp_max(amax);
+    int E = 0;
+    if (amax > 0.0f && amax < INFINITY) {
+        int ex;
+        frexpf(amax, &ex);  // amax < 2^ex
+        E = min(max(14 - ex, -60), 100);
+    }
+    if (lane == 0) s_e[t] = E;
+    // 2^E split so that both factors stay normal: x * 2^E * 4^-j
+    const int j = lane >> 3;
+    const int nt = t >> 2, gb = (t & 3) * 2;
+    const int t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
+#pragma unroll
+    for (int e = 0; e < VPL; e++) {
+        if (e < e_lo || e >= e_hi) continue;
+        float x0 = v[e];
+        float x1 = __shfl_down_sync(0xffffffffu, x0, 1);
+        if ((lane & 1) == 0) {
+            int kl = (e - e_lo) * 32 + lane;
+            int E1 = E - 2 * j;
+            float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
+            float a0 = x0 * f, a1 = x1 * f;
+            __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
+            __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
+            size_t base = ((size_t)(kl >> 4) * NT + nt) * 32;
+            s_b[(base + gb * 4 + t4) * 2 + which] = pack_half2(h0, h1);
+            s_b[(base + (gb + 1) * 4 + t4) * 2 + which] = pack_half2(l0, l1);
+        }
+    }
+    // group sums of the slice for the bias step: element k of the bias operand = group k, scaled by 2^(E-6)
+    const int G = p.group, epg = G / 32;
+    const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
+    for (int gl = 0; gl < kslice / G; gl++) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int e = 0; e < VPL; e++)
+            if (e >= e_lo + gl * epg && e < e_lo + (gl + 1) * epg) sum += v[e];
+        sum = warp_sum(sum);
+        if (lane == 0) {
+            float a = sum * fb;
+            __half hv = __float2half_rn(a), lv = __float2half_rn(a - __half2float(hv));
+            int bs = gl >> 4, kk = gl & 15;
+            int tt = (kk & 7) >> 1, wh = kk >> 3, half = kk & 1;
+            size_t base = ((size_t)bs * NT + nt) * 32;
+            s_bb16[((base + gb * 4 + tt) * 2 + wh) * 2 + half] = __half_as_ushort(hv);
+            s_bb16[((base + (gb + 1) * 4 + tt) * 2 + wh) * 2 + half] = __half_as_ushort(lv);
+        }
+    }
+}
+
+// GDN a/b gate rows (dense fp32, gdn_ab_row kernels.metal:265-273) for rows [r0, r0 + nr) of [Wa; Wb]: warp = token,
+// x = the normed row (NORM / EMBED source, no rotation). Writes the pending gate inputs of this pass's parity.
+__device__ void ab_rows(const GemvParams& p, int r0, int nr, float* s_w) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int K = p.K, NV = p.ab.nv;
+    for (int i = threadIdx.x; i < nr * K; i += blockDim.x) {
+        int rr = i / K, k = i % K, row = r0 + rr;
+        s_w[i] = row < NV ? p.ab.wa[(size_t)row * K + k] : p.ab.wb[(size_t)(row - NV) * K + k];
+    }
+    pdl_wait();
+    __syncthreads();
+    const int par = p.ab.ctl->parity;
+    for (int t = warp; t < p.T; t += blockDim.x >> 5) {
+        uint32_t id = 0;
+        float r = row_scale(p.src, t, K, &id, false);
+        float acc[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) acc[q] = 0.0f;
+        for (int k = lane; k < K; k += 32) {
+            float x = act_value(p.src, t, k, K, r, id);
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                if (q < nr) acc[q] += s_w[q * K + k] * x;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+            if (q < nr) {
+                float a = warp_sum(acc[q]);
+                if (lane == 0) p.ab.pend_ab[((size_t)par * VMAX + t) * 2 * NV + r0 + q] = a;
+            }
+    }
+}
+
+template <int NT, int GPC, int SPAN>
 __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bar = (uint64_t*)smem;
-    const int kslice = p.kslice, nkc = kslice / 128;
-    uint4* s_codes = (uint4*)(smem + 128);
-    uint32_t* s_scales = (uint32_t*)(smem + 128 + (size_t)kslice * 32);
-    const size_t scales_bytes = (size_t)nkc * 8 * GPC * 32;
-    uint2* s_b = (uint2*)(smem + 128 + (size_t)kslice * 32 + scales_bytes);
-    const size_t b_bytes = (size_t)(kslice / 16) * NT * 256;
-
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows
+        pdl_trigger();
+        int r0 = ((int)blockIdx.x - p.n_main) * 8;
+        ab_rows(p, r0, min(8, p.ab_rows - r0), (float*)smem);
+        return;
+    }
+    uint64_t* bar = (uint64_t*)smem;
+    int* s_e = (int*)(smem + 16);
+    const int kslice = p.kslice, nkc = kslice / 128;
+    const size_t codes_bytes = (size_t)kslice * 32;
+    const size_t sb_bytes = (size_t)nkc * 8 * 2 * GPC * 32;
+    const int nbb = (kslice / p.group + 15) / 16;  // bias k16 steps
+    const size_t b_bytes = (size_t)(kslice / 16) * NT * 256, bb_bytes = (size_t)nbb * NT * 256;
+    uint8_t* s_codes = smem + 128;
+    uint32_t* s_sb = (uint32_t*)(smem + 128 + codes_bytes);
+    uint32_t* s_b = (uint32_t*)(smem + 128 + codes_bytes + sb_bytes);
+    uint32_t* s_bb = (uint32_t*)(smem + 128 + codes_bytes + sb_bytes + b_bytes);
+
     const int rb = blockIdx.x / p.nsplit, ks = blockIdx.x % p.nsplit;
     const int nkc_all = p.K / 128;
-
     if (tid == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
+    // zero the activation operand (padding columns and bias steps stay zero)
+    for (size_t i = tid; i < (b_bytes + bb_bytes) / 16; i += 256) ((uint4*)s_b)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
     pdl_trigger();
     if (tid == 0) {
-        mbar_expect_tx(bar, (uint32_t)((size_t)kslice * 32 + scales_bytes + b_bytes));
-        const uint8_t* gcodes = (const uint8_t*)p.codes + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 512;
-        bulk_g2s(s_codes, gcodes, (uint32_t)(kslice * 32), bar);
-        const uint8_t* gsc = (const uint8_t*)p.scales + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * GPC * 32;
-        bulk_g2s(s_scales, gsc, (uint32_t)scales_bytes, bar);
+        mbar_expect_tx(bar, (uint32_t)(codes_bytes + sb_bytes));
+        bulk_g2s(s_codes, p.codes + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 512, (uint32_t)codes_bytes, bar);
+        bulk_g2s(s_sb, (const uint8_t*)p.sb + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 2 * GPC * 32,
+                 (uint32_t)sb_bytes, bar);
     }
     pdl_wait();
-    if (tid == 0) {
-        const uint8_t* gb = (const uint8_t*)p.bfrag + (size_t)ks * (kslice / 16) * NT * 256;
-        bulk_g2s(s_b, gb, (uint32_t)b_bytes, bar);
-    }
+    for (int t = warp; t < p.T; t += 8) build_token<SPAN, NT>(p, t, ks, s_b, (uint16_t*)s_bb, s_e);
     bool ok = mbar_wait_bounded(bar, 0);
     if (__syncthreads_or(!ok)) {
-        if (tid == 0) atomicOr(p.err, ERR_MBAR_TIMEOUT);
-        // the copies may still land; wait (bounded) so none writes to shared memory after exit
+        if (tid == 0) atomicOr(p.o.err, ERR_MBAR_TIMEOUT);
         mbar_wait_bounded(bar, 0, 1u << 20);
         return;
     }
 
     const int rg = warp >> 2, kw = warp & 3;
-    const int g = lane >> 2;
+    const int g = lane >> 2, t4 = lane & 3;
     const int nkc_w = nkc / 4;
     float acc[4][NT][4];
 #pragma unroll
@@ -185,17 +412,18 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             for (int i = 0; i < 4; i++) acc[m][n][i] = 0.0f;
 
     const uint32_t MAGIC = 0x64006400u, NEG1024 = 0xE400E400u;
+    const uint2* s_b2 = (const uint2*)s_b;
     for (int c = 0; c < nkc_w; c++) {
         const int kcl = kw * nkc_w + c;
         uint4 cw[4];
 #pragma unroll
-        for (int m = 0; m < 4; m++) cw[m] = s_codes[(size_t)(kcl * 8 + rg * 4 + m) * 32 + lane];
+        for (int m = 0; m < 4; m++) cw[m] = ((const uint4*)s_codes)[(size_t)(kcl * 8 + rg * 4 + m) * 32 + lane];
 #pragma unroll
         for (int gi = 0; gi < GPC; gi++) {
             uint32_t s2lo[4], s2hi[4], n2lo[4], n2hi[4];
 #pragma unroll
             for (int m = 0; m < 4; m++) {
-                uint32_t u = s_scales[((size_t)(kcl * 8 + rg * 4 + m) * GPC + gi) * 8 + g];
+                uint32_t u = s_sb[(((size_t)(kcl * 8 + rg * 4 + m) * 2 + 0) * GPC + gi) * 8 + g];
                 s2lo[m] = __byte_perm(u, 0, 0x1010);
                 s2hi[m] = __byte_perm(u, 0, 0x3232);
                 asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(n2lo[m]) : "r"(s2lo[m]), "r"(NEG1024));
@@ -209,7 +437,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
                 const bool odd = f & 1;
                 uint2 bb[NT];
 #pragma unroll
-                for (int n = 0; n < NT; n++) bb[n] = s_b[((size_t)(kcl * 8 + f) * NT + n) * 32 + lane];
+                for (int n = 0; n < NT; n++) bb[n] = s_b2[((size_t)(kcl * 8 + f) * NT + n) * 32 + lane];
                 const uint32_t mask_a = odd ? 0x00300030u : 0x00030003u;
                 const uint32_t mask_b = odd ? 0x00C000C0u : 0x000C000Cu;
 #pragma unroll
@@ -226,8 +454,35 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             }
         }
     }
+    // bias step: A = 64 b for this warp's groups (columns [o0, o0 + ngw) of bias step bs), B = group sums / 64
+    {
+        const int ngw = kslice / 4 / p.group;
+        const int gw0 = kw * ngw, bs = gw0 >> 4, o0 = gw0 & 15;
+        uint2 bb[NT];
+#pragma unroll
+        for (int n = 0; n < NT; n++) bb[n] = ((const uint2*)s_bb)[((size_t)bs * NT + n) * 32 + lane];
+        const int cols[4] = {2 * t4, 2 * t4 + 1, 2 * t4 + 8, 2 * t4 + 9};
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            uint32_t u[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                int c = cols[i];
+                u[i] = 0;
+                if (c >= o0 && c < o0 + ngw) {
+                    int gl = bs * 16 + c;  // slice-local group
+                    int kc = gl * p.group / 128, gi = gl % GPC;
+                    u[i] = s_sb[(((size_t)(kc * 8 + rg * 4 + m) * 2 + 1) * GPC + gi) * 8 + g];
+                }
+            }
+            uint32_t a0 = __byte_perm(u[0], u[1], 0x5410), a1 = __byte_perm(u[0], u[1], 0x7632);
+            uint32_t a2 = __byte_perm(u[2], u[3], 0x5410), a3 = __byte_perm(u[2], u[3], 0x7632);
+#pragma unroll
+            for (int n = 0; n < NT; n++) mma_f16(acc[m][n], a0, a1, a2, a3, bb[n].x, bb[n].y);
+        }
+    }
 
-    // in-CTA reduction over the 4 k-quarters, fixed order
+    // in-CTA reduction over the 4 k-quarters, fixed order; partials in units of x (2^-E applied)
     __syncthreads();
     float* red = (float*)(smem + 128);  // [kw 4][rg 2][m 4][NT][2][32]
 #pragma unroll
@@ -239,11 +494,10 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             red[(base + 1) * 32 + lane] = acc[m][n][2] + acc[m][n][3];
         }
     __syncthreads();
-    const int ng_all = p.K / p.group;
-    const int ng_slice = kslice / p.group;
-    const int entries = 2 * 4 * NT * 2 * 32;
+    const int T = p.T, O = p.O;
     const size_t quarter = (size_t)2 * 4 * NT * 2 * 32;
-    for (int e = tid; e < entries; e += 256) {
+    float* fin = red + 4 * quarter;  // [T][128] final values when this CTA holds the whole K range
+    for (int e = tid; e < (int)quarter; e += 256) {
         int ln = e & 31;
         int r = e >> 5;
         int which = r & 1;
@@ -253,127 +507,121 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         int m = r & 3;
         int rgi = r >> 2;
         int token = n * 4 + (ln & 3);
-        if (token >= p.T) continue;
-        int row = rb * 128 + rgi * 64 + m * 16 + (ln >> 2) + 8 * which;
-        float v = red[e] + red[quarter + e] + red[2 * quarter + e] + red[3 * quarter + e];
-        v = ldexpf(v, -p.xexp[token]);
-        const uint16_t* br = p.bias + (size_t)row * ng_all + ks * ng_slice;
-        const float* xs = p.xsum + (size_t)token * ng_all + ks * ng_slice;
-        float bt = 0.0f;
-        for (int gi = 0; gi < ng_slice; gi++) bt += __half2float(__ushort_as_half(br[gi])) * xs[gi];
-        v += bt;
-        if (p.nsplit == 1) {
-            float* o = p.out + (size_t)token * p.O + row;
-            *o = p.add ? *o + v : v;
-        } else {
-            p.partial[((size_t)ks * p.T + token) * p.O + row] = v;
+        if (token >= T) continue;
+        int rloc = rgi * 64 + m * 16 + (ln >> 2) + 8 * which;
+        float v = ((red[e] + red[quarter + e]) + red[2 * quarter + e]) + red[3 * quarter + e];
+        v *= pow2f(-s_e[token]);
+        if (p.nsplit == 1) fin[token * 128 + rloc] = v;
+        else p.o.partial[((size_t)ks * T + token) * O + rb * 128 + rloc] = v;
+    }
+    __shared__ int s_last;
+    if (p.nsplit > 1) {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last = atomicAdd(&p.o.counters[rb], 1u) == (unsigned)(p.nsplit - 1);
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        for (int e = tid; e < 128 * T; e += 256) {
+            int token = e >> 7, rloc = e & 127;
+            const float* src = p.o.partial + (size_t)token * O + rb * 128 + rloc;
+            float pv[16];
+#pragma unroll
+            for (int s = 0; s < 16; s++) pv[s] = s < p.nsplit ? __ldcg(src + (size_t)s * T * O) : 0.0f;
+            float v = 0.0f;
+#pragma unroll
+            for (int s = 0; s < 16; s++)
+                if (s < p.nsplit) v += pv[s];
+            fin[token * 128 + rloc] = v;
+        }
+        if (tid == 0) p.o.counters[rb] = 0;
+    }
+    __syncthreads();
+    // output (store or residual add) and the sums of squares of the new rows
+    for (int e = tid; e < 128 * T; e += 256) {
+        int token = e >> 7, rloc = e & 127;
+        float* o = p.o.out + (size_t)token * O + rb * 128 + rloc;
+        float v = fin[e];
+        if (p.o.add) v = *o + v;
+        *o = v;
+        fin[e] = v;
+    }
+    if (p.o.ss_out) {
+        __syncthreads();
+        for (int token = warp; token < T; token += 8) {
+            float a = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float x = fin[token * 128 + i * 32 + lane];
+                a += x * x;
+            }
+            a = warp_sum(a);
+            if (lane == 0) p.o.ss_out[rb * VMAX + token] = a;
         }
     }
-    if (p.nsplit == 1) return;
-    __threadfence();
-    __syncthreads();
-    __shared__ int s_last;
-    if (tid == 0) s_last = atomicAdd(&p.counters[rb], 1u) == (unsigned)(p.nsplit - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int e = tid; e < 128 * p.T; e += 256) {
-        int token = e / 128, row = rb * 128 + (e % 128);
-        float v = 0.0f;
-        for (int s = 0; s < p.nsplit; s++) v += __ldcg(p.partial + ((size_t)s * p.T + token) * p.O + row);
-        float* o = p.out + (size_t)token * p.O + row;
-        *o = p.add ? *o + v : v;
-    }
-    if (tid == 0) p.counters[rb] = 0;
 }
 
-static size_t gemv_smem(int kslice, int nt, int group) {
+static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab) {
     int gpc = 128 / group;
-    size_t main = 128 + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * gpc * 32 + (size_t)(kslice / 16) * nt * 256;
-    size_t red = 128 + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4;
-    return main > red ? main : red;
+    int nbb = (kslice / group + 15) / 16;
+    size_t main = 128 + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
+                  (size_t)(kslice / 16) * nt * 256 + (size_t)nbb * nt * 256;
+    size_t red = 128 + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
+    size_t abs_ = ab ? (size_t)8 * K * 4 : 0;
+    size_t s = main > red ? main : red;
+    return s > abs_ ? s : abs_;
 }
 
-template <int NT, int GPC>
-static void launch_gemv_t(const GemvParams& p, cudaStream_t st) {
-    size_t smem = gemv_smem(p.kslice, NT, p.group);
-    auto fn = ternary_gemv_kernel<NT, GPC>;
+template <int NT, int GPC, int SPAN>
+static void launch_gemv_t(const GemvParams& p, size_t smem, cudaStream_t st) {
+    auto fn = ternary_gemv_kernel<NT, GPC, SPAN>;
     static bool attr_done = false;
     if (!attr_done) {
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         attr_done = true;
     }
     GemvParams pp = p;
     void* args[] = {&pp};
-    launch_pdl((const void*)fn, dim3((unsigned)((p.O / 128) * p.nsplit)), dim3(256), smem, st, args);
+    int grid = p.n_main + (p.ab_rows + 7) / 8;
+    launch_pdl((const void*)fn, dim3((unsigned)grid), dim3(256), smem, st, args);
 }
 
-void launch_ternary_gemv(const TernaryMat& m, const TernaryAct& a, int T, float* out, int add, float* partial,
-                         unsigned* counters, int* err, cudaStream_t st) {
+template <int NT, int GPC>
+static void launch_span(const GemvParams& p, int span, size_t smem, cudaStream_t st) {
+    if (span == 512) launch_gemv_t<NT, GPC, 512>(p, smem, st);
+    else if (span == 1024) launch_gemv_t<NT, GPC, 1024>(p, smem, st);
+    else launch_gemv_t<NT, GPC, 2048>(p, smem, st);
+}
+
+template <int NT>
+static void launch_gpc(const GemvParams& p, int span, size_t smem, cudaStream_t st) {
+    if (p.group == 64) launch_span<NT, 2>(p, span, smem, st);
+    else launch_span<NT, 1>(p, span, smem, st);
+}
+
+void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const GemvOut& o, const AbArgs* ab,
+                         cudaStream_t st) {
     GemvParams p;
-    p.codes = (const uint4*)m.codes;
-    p.scales = m.scales;
-    p.bias = m.bias;
-    p.bfrag = a.bfrag;
-    p.xsum = a.xsum;
-    p.xexp = a.xexp;
-    p.out = out;
-    p.partial = partial;
-    p.counters = counters;
-    p.err = err;
+    p.codes = (const uint8_t*)m.codes;
+    p.sb = m.sb;
+    p.src = src;
+    p.o = o;
+    p.ab = ab ? *ab : AbArgs();
     p.O = m.O;
     p.K = m.K;
     p.group = m.group;
     p.kslice = m.kslice;
     p.nsplit = m.nsplit;
     p.T = T;
-    p.add = add;
+    p.n_main = (m.O / 128) * m.nsplit;
+    p.ab_rows = ab ? 2 * ab->nv : 0;
+    int span = src.HB > m.kslice ? src.HB : m.kslice;
     int nt = (2 * T + 7) / 8;
-    if (m.group == 64) {
-        if (nt == 1) launch_gemv_t<1, 2>(p, st);
-        else if (nt == 2) launch_gemv_t<2, 2>(p, st);
-        else if (nt == 3) launch_gemv_t<3, 2>(p, st);
-        else launch_gemv_t<4, 2>(p, st);
-    } else {
-        if (nt == 1) launch_gemv_t<1, 1>(p, st);
-        else if (nt == 2) launch_gemv_t<2, 1>(p, st);
-        else if (nt == 3) launch_gemv_t<3, 1>(p, st);
-        else launch_gemv_t<4, 1>(p, st);
-    }
-}
-
-// ------------------------------------------------------------------------------------------------ config 1 producer
-// One CTA per padded token row: x (bf16 or fp32) -> rotate -> activation operand.
-__global__ void __launch_bounds__(512) rotate_prep_kernel(const uint16_t* x_bf16, const float* x_f32, int T, int K,
-                                                          int HB, const float* signs, int group, int NT,
-                                                          TernaryAct act, float* xrot) {
-    extern __shared__ float xs[];
-    __shared__ float red[32];
-    int t = blockIdx.x;
-    pdl_trigger();
-    pdl_wait();
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        float v = 0.0f;
-        if (t < T) v = x_f32 ? x_f32[(size_t)t * K + i] : __bfloat162float(__ushort_as_bfloat16(x_bf16[(size_t)t * K + i]));
-        xs[i] = v;
-    }
-    __syncthreads();
-    if (HB > 0) block_rotate(xs, K, HB, signs);
-    if (xrot && t < T)
-        for (int i = threadIdx.x; i < K; i += blockDim.x) xrot[(size_t)t * K + i] = xs[i];
-    write_ternary_act(xs, K, t, T, NT, group, act, red);
-}
-
-void launch_rotate_prep(const uint16_t* x_bf16, const float* x_f32, int T, int K, int HB, const float* signs,
-                        int group, TernaryAct act, float* xrot, cudaStream_t st) {
-    int nt = (2 * T + 7) / 8;
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaFuncSetAttribute(rotate_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-        attr_done = true;
-    }
-    void* args[] = {&x_bf16, &x_f32, &T, &K, &HB, &signs, &group, &nt, &act, &xrot};
-    launch_pdl((const void*)rotate_prep_kernel, dim3(4 * nt), dim3(512), (size_t)K * 4, st, args);
+    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0);
+    if (nt == 1) launch_gpc<1>(p, span, smem, st);
+    else if (nt == 2) launch_gpc<2>(p, span, smem, st);
+    else if (nt == 3) launch_gpc<3>(p, span, smem, st);
+    else launch_gpc<4>(p, span, smem, st);
 }
 
 }  // namespace bcu
