@@ -13,34 +13,18 @@ namespace bcu {
 
 constexpr float EPS_A = 1e-6f;
 
-// rmsnorm(x) * w then the interleaved mRoPE rotation of the first `rot` dims (text positions: the three position rows
-// are equal, so every section uses `pos`). Thread d holds x[d]; buf: 256 floats, red: 32 floats.
-__device__ float norm_rope(float x, float w, int pos, const float* inv_freq, int rot, float* buf, float* red) {
-    const int d = threadIdx.x;
-    float ss = block_sum(x * x, red);
-    x = (x * rsqrtf(ss / 256.0f + EPS_A)) * w;
-    __syncthreads();
-    buf[d] = x;
-    __syncthreads();
-    if (d < rot) {
-        int half = rot / 2, i = d % half;
-        float ang = (float)pos * inv_freq[i];
-        float sn, cs;
-        sincosf(ang, &sn, &cs);
-        x = d < half ? x * cs - buf[d + half] * sn : x * cs + buf[d - half] * sn;
-    }
-    return x;
-}
+// Score buffer length per query head: the largest key chunk, rounded up to 4 floats so the regions after it in shared
+// memory stay 16-byte aligned for the float4 key reads.
+__host__ __device__ inline int attn_chunk_max(int ctx) { return (((ctx + NSPLIT_ATTN - 1) / NSPLIT_ATTN) + 3) & ~3; }
 
 __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
-    extern __shared__ float sm[];
-    __shared__ float red[32];
+    extern __shared__ __align__(16) float sm[];
     __shared__ float buf[256];
     __shared__ int s_last;
     const int kh = blockIdx.x, s = blockIdx.y, t = blockIdx.z;
     const int H = a.H, KV = a.KV, qper = H / KV, aw = H * 256, kvw = KV * 256;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, d = threadIdx.x;
-    const int chunk_max = (a.ctx + NSPLIT_ATTN - 1) / NSPLIT_ATTN;
+    const int chunk_max = attn_chunk_max(a.ctx);
     float* qs = sm;                            // [qper][256]
     float* sc = qs + qper * 256;               // [qper][chunk_max]
     float* nk = sc + qper * chunk_max;         // [VMAX][256] this pass's keys
@@ -59,34 +43,98 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
         return;
     }
     if (j0 < j1) {
-        // queries of the qper heads (scaled by 1/16 = 1/sqrt(256))
-        const float* row = a.qkv + (size_t)t * a.ld;
-        for (int hq = 0; hq < qper; hq++) {
-            float x = row[(kh * qper + hq) * 512 + d];
-            qs[hq * 256 + d] = norm_rope(x, wq, off + t, a.inv_freq, a.rot, buf, red) * 0.0625f;
+        // rows to prepare: the qper query heads of row t, then this pass's keys in range (positions >= off);
+        // all loaded at once, one block reduction for every row's RMS norm
+        const int u0 = max(j0, off) - off, u1 = j1 - off, nkeys = max(u1 - u0, 0);
+        const int nrows = qper + nkeys;  // <= 16 + 16
+        float x[32], vvals[16];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            x[i] = 0.0f;
+            if (i < qper) x[i] = a.qkv[(size_t)t * a.ld + (kh * qper + i) * 512 + d];
+            else if (i < nrows) x[i] = a.qkv[(size_t)(u0 + i - qper) * a.ld + 2 * aw + kh * 256 + d];
         }
-        // this pass's keys in range
-        const int u0 = max(j0, off) - off, u1 = j1 - off;
-        for (int u = u0; u < u1; u++) {
-            const float* r = a.qkv + (size_t)u * a.ld;
-            float k = norm_rope(r[2 * aw + kh * 256 + d], wk, off + u, a.inv_freq, a.rot, buf, red);
-            float v = r[2 * aw + kvw + kh * 256 + d];
-            nk[u * 256 + d] = k;
-            nv[u * 256 + d] = v;
-            a.kc[((size_t)(off + u) * KV + kh) * 256 + d] = k;
-            a.vc[((size_t)(off + u) * KV + kh) * 256 + d] = v;
-        }
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (i < nkeys) vvals[i] = a.qkv[(size_t)(u0 + i) * a.ld + 2 * aw + kvw + kh * 256 + d];
+        float* rr = buf;  // [8 warps][32 rows]
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (i < nrows) {
+                float s2 = warp_sum(x[i] * x[i]);
+                if (lane == 0) rr[w * 32 + i] = s2;
+            }
         __syncthreads();
-        // scores: warp per key, lanes over dims (8 each)
-        for (int j = j0 + w; j < j1; j += 8) {
-            const float* k = j >= off ? nk + (j - off) * 256 + lane * 8 : a.kc + ((size_t)j * KV + kh) * 256 + lane * 8;
-            float4 ka = *(const float4*)k, kb = *(const float4*)(k + 4);
-            for (int hq = 0; hq < qper; hq++) {
-                const float* q = qs + hq * 256 + lane * 8;
-                float dd = q[0] * ka.x + q[1] * ka.y + q[2] * ka.z + q[3] * ka.w + q[4] * kb.x + q[5] * kb.y +
-                           q[6] * kb.z + q[7] * kb.w;
-                dd = warp_sum(dd);
-                if (lane == 0) sc[hq * chunk_max + (j - j0)] = dd;
+        float* xs = nk;  // staging of the normed rows [nrows][256] (nk/nv regions are free until below)
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (i < nrows) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 8; q++) ss += rr[q * 32 + i];
+                xs[i * 256 + d] = (x[i] * rsqrtf(ss / 256.0f + EPS_A)) * (i < qper ? wq : wk);
+            }
+        __syncthreads();
+        // interleaved mRoPE on the first `rot` dims; text positions: the three position rows are equal
+        float y[32];
+        const int half = a.rot / 2;
+        float invf = d < a.rot ? a.inv_freq[d % half] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (i < nrows) {
+                float xv = xs[i * 256 + d];
+                if (d < a.rot) {
+                    int pos = i < qper ? off + t : off + u0 + i - qper;
+                    float sn, cs;
+                    sincosf((float)pos * invf, &sn, &cs);
+                    xv = d < half ? xv * cs - xs[i * 256 + d + half] * sn : xv * cs + xs[i * 256 + d - half] * sn;
+                }
+                y[i] = xv;
+            }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            if (i < qper) qs[i * 256 + d] = y[i] * 0.0625f;  // queries scaled by 1/sqrt(256)
+            else if (i < nrows) {
+                int u = u0 + i - qper;
+                nk[u * 256 + d] = y[i];
+                a.kc[((size_t)(off + u) * KV + kh) * 256 + d] = y[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (i < nkeys) {
+                int u = u0 + i;
+                nv[u * 256 + d] = vvals[i];
+                a.vc[((size_t)(off + u) * KV + kh) * 256 + d] = vvals[i];
+            }
+        __syncthreads();
+        // scores: warp per key, lanes over dims (8 each); the next key's row is loaded while this one is used
+        {
+            int j = j0 + w;
+            float4 ka = make_float4(0, 0, 0, 0), kb = ka;
+            if (j < j1) {
+                const float* k = j >= off ? nk + (j - off) * 256 + lane * 8 : a.kc + ((size_t)j * KV + kh) * 256 + lane * 8;
+                ka = *(const float4*)k;
+                kb = *(const float4*)(k + 4);
+            }
+            for (; j < j1; j += 8) {
+                float4 na = make_float4(0, 0, 0, 0), nb = na;
+                int jn = j + 8;
+                if (jn < j1) {
+                    const float* k = jn >= off ? nk + (jn - off) * 256 + lane * 8 : a.kc + ((size_t)jn * KV + kh) * 256 + lane * 8;
+                    na = *(const float4*)k;
+                    nb = *(const float4*)(k + 4);
+                }
+                for (int hq = 0; hq < qper; hq++) {
+                    const float* q = qs + hq * 256 + lane * 8;
+                    float dd = q[0] * ka.x + q[1] * ka.y + q[2] * ka.z + q[3] * ka.w + q[4] * kb.x + q[5] * kb.y +
+                               q[6] * kb.z + q[7] * kb.w;
+                    dd = warp_sum(dd);
+                    if (lane == 0) sc[hq * chunk_max + (j - j0)] = dd;
+                }
+                ka = na;
+                kb = nb;
             }
         }
         __syncthreads();
@@ -112,12 +160,20 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
         float acc[16];
 #pragma unroll
         for (int hq = 0; hq < 16; hq++) acc[hq] = 0.0f;
-        for (int i = 0; i < cnt; i++) {
-            int j = j0 + i;
-            float v = j >= off ? nv[(j - off) * 256 + d] : a.vc[((size_t)j * KV + kh) * 256 + d];
+        for (int i0 = 0; i0 < cnt; i0 += 8) {  // 8 value loads in flight, accumulated in key order
+            float vv[8];
 #pragma unroll
-            for (int hq = 0; hq < 16; hq++)
-                if (hq < qper) acc[hq] += sc[hq * chunk_max + i] * v;
+            for (int q = 0; q < 8; q++) {
+                int j = j0 + i0 + q;
+                vv[q] = i0 + q >= cnt ? 0.0f : (j >= off ? nv[(j - off) * 256 + d] : a.vc[((size_t)j * KV + kh) * 256 + d]);
+            }
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                if (i0 + q < cnt) {
+#pragma unroll
+                    for (int hq = 0; hq < 16; hq++)
+                        if (hq < qper) acc[hq] += sc[hq * chunk_max + i0 + q] * vv[q];
+                }
         }
 #pragma unroll
         for (int hq = 0; hq < 16; hq++)
@@ -167,7 +223,7 @@ __global__ void __launch_bounds__(256) attn_kernel(AttnArgs a) {
 
 void launch_attn(const AttnArgs& a, cudaStream_t st) {
     int qper = a.H / a.KV;
-    int chunk_max = (a.ctx + NSPLIT_ATTN - 1) / NSPLIT_ATTN;
+    int chunk_max = attn_chunk_max(a.ctx);
     size_t smem = ((size_t)qper * 256 + (size_t)qper * chunk_max + 2 * VMAX * 256 + 2 * qper) * 4;
     static bool attr = false;
     if (!attr) {

@@ -214,7 +214,7 @@ bcu_status decode_plain(bcu_model* m, uint32_t feed, Run& r, Stop stop, bool* re
         // keep the next step queued while this one's token is examined
         inflight_next = r.n + 1 < r.max_tokens && !m->cancel && m->len + 2 <= m->c.ctx;
         if (inflight_next && (s = enqueue(k + 1, false)) != BCU_OK) return s;
-        uint32_t tok;
+        uint32_t tok = 0;
         if ((s = wait_tok(k, &tok)) != BCU_OK) return s;
         bool ok = r.push(tok);
         if (!ok || !inflight_next || m->cancel) {
@@ -225,7 +225,7 @@ bcu_status decode_plain(bcu_model* m, uint32_t feed, Run& r, Stop stop, bool* re
             return m->cancel ? BCU_ERR_CANCELLED : BCU_OK;
         }
         if (stop(tok)) {
-            uint32_t nt;
+            uint32_t nt = 0;
             if ((s = wait_tok(k + 1, &nt)) != BCU_OK) return s;
             if (!r.push(nt)) return BCU_OK;
             *resumed = true;

@@ -49,7 +49,7 @@ __device__ __forceinline__ void gdn_step4(float4* st, float4 q, float4 k, const 
     for (int r = 0; r < 4; r++) o[r] = warp_sum(o[r]);
 }
 
-struct GdnSmem {
+struct __align__(16) GdnSmem {
     float q[RMAX][128];
     float k[RMAX][128];
     float v[RMAX][16];
@@ -87,10 +87,22 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
     // ---- stage the replayed rows (conv outputs + gates of the previous pass)
     const float* pqc = a.pend_qkvc + (size_t)prev * VMAX * C;
     const float* pab = a.pend_ab + (size_t)prev * VMAX * 2 * NV;
-    for (int r = 0; r < rn; r++) {
-        sm.q[r][tid] = pqc[(size_t)r * C + cq];
-        sm.k[r][tid] = pqc[(size_t)r * C + ck];
-        if (has_v) sm.v[r][tid] = pqc[(size_t)r * C + cv];
+    {  // all replay loads in flight together
+        float lq[VMAX], lk[VMAX], lv[VMAX];
+#pragma unroll
+        for (int r = 0; r < VMAX; r++)
+            if (r < rn) {
+                lq[r] = pqc[(size_t)r * C + cq];
+                lk[r] = pqc[(size_t)r * C + ck];
+                lv[r] = has_v ? pqc[(size_t)r * C + cv] : 0.0f;
+            }
+#pragma unroll
+        for (int r = 0; r < VMAX; r++)
+            if (r < rn) {
+                sm.q[r][tid] = lq[r];
+                sm.k[r][tid] = lk[r];
+                if (has_v) sm.v[r][tid] = lv[r];
+            }
     }
     if (tid < rn) gates(pab[(size_t)tid * 2 * NV + hd], pab[(size_t)tid * 2 * NV + NV + hd], ea, dtb, sm.g[tid], sm.beta[tid]);
     if (tid >= 32 && tid - 32 < T) {

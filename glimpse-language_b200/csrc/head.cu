@@ -42,17 +42,25 @@ __device__ void head_operand(const HeadArgs& a, int t, uint32_t* s_b) {
     for (int i = lane; i < a.nss; i += 32) ss += a.ss[i * VMAX + t];
     float r = rsqrtf(warp_sum(ss) / (float)d + 1e-6f);
     const int nt = t >> 2, gb = (t & 3) * 2, t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
-    for (int k0 = 0; k0 < d; k0 += 32) {
-        int k = k0 + lane;
-        float x0 = (a.h[(size_t)t * d + k] * r) * a.norm[k];
-        float x1 = __shfl_down_sync(0xffffffffu, x0, 1);
-        if ((lane & 1) == 0) {
-            __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
-            __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
-            __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
-            size_t base = ((size_t)(k >> 4) * NT + nt) * 32;
-            s_b[(base + gb * 4 + t4) * 2 + which] = pack_bf162(h0, h1);
-            s_b[(base + (gb + 1) * 4 + t4) * 2 + which] = pack_bf162(l0, l1);
+    for (int kb = 0; kb < d; kb += 256) {  // 8 loads per lane in flight together
+        float hv[8], wv[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) hv[i] = a.h[(size_t)t * d + kb + i * 32 + lane];
+#pragma unroll
+        for (int i = 0; i < 8; i++) wv[i] = a.norm[kb + i * 32 + lane];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int k = kb + i * 32 + lane;
+            float x0 = (hv[i] * r) * wv[i];
+            float x1 = __shfl_down_sync(0xffffffffu, x0, 1);
+            if ((lane & 1) == 0) {
+                __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+                __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
+                __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
+                size_t base = ((size_t)(k >> 4) * NT + nt) * 32;
+                s_b[(base + gb * 4 + t4) * 2 + which] = pack_bf162(h0, h1);
+                s_b[(base + (gb + 1) * 4 + t4) * 2 + which] = pack_bf162(l0, l1);
+            }
         }
     }
 }

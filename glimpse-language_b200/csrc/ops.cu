@@ -57,7 +57,8 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
     plan_ternary(l->m, sms);
     ok = ok && cudaMalloc(&l->partial, (size_t)l->m.nsplit * VMAX * O * 4) == cudaSuccess &&
          cudaMalloc(&l->counters, (size_t)(O / 128) * 4) == cudaSuccess && cudaMalloc(&l->err, 4) == cudaSuccess &&
-         cudaMemset(l->counters, 0, (size_t)(O / 128) * 4) == cudaSuccess && cudaMemset(l->err, 0, 4) == cudaSuccess;
+         cudaMemset(l->counters, 0, (size_t)(O / 128) * 4) == cudaSuccess && cudaMemset(l->err, 0, 4) == cudaSuccess &&
+         cudaDeviceSynchronize() == cudaSuccess;  // callers may launch on a non-blocking stream
     if (!ok) {
         bcu_linear_free(l);
         return BCU_ERR_OOM;

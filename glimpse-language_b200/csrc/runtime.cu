@@ -190,11 +190,13 @@ bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* o
     return BCU_OK;
 }
 
+// Zeroed device allocation. The zeroing is ordered on the model's stream: the stream is non-blocking, so a memset on
+// the legacy default stream would not be ordered before the model's own copies into the new buffer.
 template <class T>
 bcu_status dmalloc(bcu_model* m, T** p, size_t bytes) {
     cudaError_t e = cudaMalloc((void**)p, bytes < 16 ? 16 : bytes);
     if (e != cudaSuccess) return fail(m, BCU_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
-    e = cudaMemset(*p, 0, bytes < 16 ? 16 : bytes);
+    e = cudaMemsetAsync(*p, 0, bytes < 16 ? 16 : bytes, m->st);
     if (e != cudaSuccess) return fail(m, BCU_ERR_CUDA, cudaGetErrorString(e));
     return BCU_OK;
 }
@@ -473,9 +475,11 @@ bcu_status bcu_load_tensor(bcu_model* m, const char* name, int32_t dtype, const 
         m->staged.erase(it);
     }
     CK(cudaMalloc(&t.dev, t.bytes));
-    CK(cudaMemcpy(t.dev, host_data, t.bytes, cudaMemcpyHostToDevice));
+    // on the model stream (the repack kernels that read it run there) and complete before the caller's buffer is
+    // released
+    CK(cudaMemcpyAsync(t.dev, host_data, t.bytes, cudaMemcpyHostToDevice, m->st));
     m->staged[name] = t;
-    return BCU_OK;
+    return wait_stream(m, WAIT_S);
 }
 
 bcu_status bcu_finalize(bcu_model* m) {
@@ -779,6 +783,8 @@ bcu_status bcu_state_new(bcu_model* m, int32_t len, bcu_state** out) {
 
 void bcu_state_free(bcu_state* s) {
     if (!s) return;
+    // a restore from this snapshot may still be copying on a model stream (bcu_restore is asynchronous)
+    cudaDeviceSynchronize();
     cudaFree(s->gdn);
     cudaFree(s->conv);
     cudaFree(s->kc);
@@ -857,8 +863,8 @@ bcu_status bcu_state_read(const bcu_model* m, const bcu_state* s, int32_t part, 
     uint64_t n;
     void* p = part_ptr(s, part, &n);
     if (!p || bytes != n) return BCU_ERR_ARG;
-    if (cudaMemcpy(host, p, n, cudaMemcpyDeviceToHost) != cudaSuccess) return BCU_ERR_CUDA;
-    return BCU_OK;
+    if (cudaMemcpyAsync(host, p, n, cudaMemcpyDeviceToHost, m->st) != cudaSuccess) return BCU_ERR_CUDA;
+    return cudaStreamSynchronize(m->st) == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
 }
 
 bcu_status bcu_state_write(bcu_model* m, bcu_state* s, int32_t part, const void* host, uint64_t bytes, int32_t len) {
@@ -866,8 +872,8 @@ bcu_status bcu_state_write(bcu_model* m, bcu_state* s, int32_t part, const void*
     uint64_t n;
     void* p = part_ptr(s, part, &n);
     if (!p || bytes != n) return fail(m, BCU_ERR_ARG, "state part size mismatch");
-    CK(cudaMemcpy(p, host, n, cudaMemcpyHostToDevice));
-    return BCU_OK;
+    CK(cudaMemcpyAsync(p, host, n, cudaMemcpyHostToDevice, m->st));
+    return wait_stream(m, WAIT_S);
 }
 
 // ------------------------------------------------------------------------------------------------ introspection
@@ -905,7 +911,7 @@ bcu_status bcu_set_planted(bcu_model* m, const uint32_t* ids, int32_t n, int32_t
         TRY(dmalloc(m, &m->planted_dev, (size_t)n * 4));
         m->planted_cap = n;
     }
-    if (n) CK(cudaMemcpy(m->planted_dev, ids, (size_t)n * 4, cudaMemcpyHostToDevice));
+    if (n) CK(cudaMemcpyAsync(m->planted_dev, ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
     ctl_planted_kernel<<<1, 1, 0, m->st>>>(m->ctl, m->planted_dev, n);
     CK(cudaGetLastError());
     m->h_in->planted_base = base;
@@ -968,6 +974,7 @@ bcu_status bcu_time_pass(bcu_model* m, int32_t t, int32_t iters, float* ms_per_p
         if (i > 0) total += ms;
     }
     TRY(bcu_restore(m, snap));
+    TRY(wait_stream(m, WAIT_S));
     bcu_state_free(snap);
     *ms_per_pass = total / iters;
     return BCU_OK;

@@ -15,13 +15,17 @@
 // cp.async.bulk; after the wait every warp builds the operand of its tokens from the source rows (norm / SwiGLU /
 // gated norm / gate, signs, Walsh-Hadamard transform in registers). Split-K partials are summed in a fixed order by
 // the last CTA of each row block, which also applies the residual add and the sums of squares the next norm needs.
+#include <cooperative_groups.h>
 #include <cstdio>
 #include "common.cuh"
 #include "kernels.h"
 
+namespace cg = cooperative_groups;
+
 namespace bcu {
 
 constexpr float EPS_T = 1e-6f;
+constexpr int GEMV_HDR = 384;  // shared-memory header: mbarrier at 0, exponents [16][4] at 128
 
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
     cudaLaunchConfig_t cfg = {};
@@ -132,6 +136,7 @@ struct GemvParams {
     GemvOut o;
     AbArgs ab;
     int O, K, group, kslice, nsplit, T, n_main, ab_rows;
+    int nrb;  // row blocks; CTA = ks * nrb + rb, so a cluster holds consecutive row blocks of one K-slice
 };
 
 __device__ __forceinline__ float sigm(float z) { return 1.0f / (1.0f + expf(-z)); }
@@ -147,7 +152,8 @@ __device__ __forceinline__ uint32_t resolve_id(const Ctl* ctl, int t) {
 }
 
 // Per-row scalar of NORM / EMBED: r = rsqrt(mean(h^2) + eps). EMBED also records the id and, in CTA 0, writes the
-// row into the residual stream. Fixed-order reductions (lane strides, then the warp tree).
+// row into the residual stream. Fixed-order reductions (lane strides, then the warp tree); loads are issued in
+// batches of 8 per lane so the row costs a few memory latencies, not one per element.
 __device__ float row_scale(const ActSrc& s, int t, int K, uint32_t* id_out, bool writer) {
     const int lane = threadIdx.x & 31;
     float acc = 0.0f;
@@ -162,10 +168,15 @@ __device__ float row_scale(const ActSrc& s, int t, int K, uint32_t* id_out, bool
         if (id >= (uint32_t)s.vocab) id = 0;
         *id_out = id;
         const uint16_t* row = s.xb + (size_t)id * K;
-        for (int k = lane; k < K; k += 32) {
-            float a = __bfloat162float(__ushort_as_bfloat16(row[k]));
-            acc += a * a;
-            if (writer) s.h_out[(size_t)t * K + k] = a;
+        for (int k0 = 0; k0 < K; k0 += 256) {
+            float a[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) a[i] = __bfloat162float(__ushort_as_bfloat16(row[k0 + i * 32 + lane]));
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                acc += a[i] * a[i];
+                if (writer) s.h_out[(size_t)t * K + k0 + i * 32 + lane] = a[i];
+            }
         }
     } else {
         return 1.0f;
@@ -174,49 +185,89 @@ __device__ float row_scale(const ActSrc& s, int t, int K, uint32_t* id_out, bool
     return rsqrtf(acc / (float)K + EPS_T);
 }
 
-// Pre-rotation value x_k of row t (modes other than GATED, which needs head norms).
-__device__ __forceinline__ float act_value(const ActSrc& s, int t, int k, int K, float r, uint32_t id) {
+// Pre-rotation values x_k, k = base + lane + 32 e (e < N), of row t for the modes other than GATED (which needs head
+// norms). The mode branch is outside the element loops and every load of the row is issued before the first use.
+template <int N>
+__device__ __forceinline__ void act_values(const ActSrc& s, int t, int base, int K, float r, uint32_t id, float* v) {
+    const int lane = threadIdx.x & 31;
+    float a[N], b[N];
     switch (s.mode) {
-        case ACT_NORM: return (s.x[(size_t)t * K + k] * r) * s.w[k];
-        case ACT_EMBED: return (__bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)id * K + k])) * r) * s.w[k];
-        case ACT_SWIGLU: {
-            float g = s.x[(size_t)t * 2 * K + k], u = s.x[(size_t)t * 2 * K + K + k];
-            return (g * u) * sigm(g);
-        }
-        case ACT_GATE: {
-            float gt = s.x2[(size_t)t * s.ld2 + (k >> 8) * 512 + 256 + (k & 255)];
-            return s.x[(size_t)t * K + k] * sigm(gt);
-        }
+        case ACT_NORM:
+#pragma unroll
+            for (int e = 0; e < N; e++) a[e] = s.x[(size_t)t * K + base + lane + 32 * e];
+#pragma unroll
+            for (int e = 0; e < N; e++) b[e] = s.w[base + lane + 32 * e];
+#pragma unroll
+            for (int e = 0; e < N; e++) v[e] = (a[e] * r) * b[e];
+            break;
+        case ACT_EMBED:
+#pragma unroll
+            for (int e = 0; e < N; e++) a[e] = __bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)id * K + base + lane + 32 * e]));
+#pragma unroll
+            for (int e = 0; e < N; e++) b[e] = s.w[base + lane + 32 * e];
+#pragma unroll
+            for (int e = 0; e < N; e++) v[e] = (a[e] * r) * b[e];
+            break;
+        case ACT_SWIGLU:
+#pragma unroll
+            for (int e = 0; e < N; e++) a[e] = s.x[(size_t)t * 2 * K + base + lane + 32 * e];
+#pragma unroll
+            for (int e = 0; e < N; e++) b[e] = s.x[(size_t)t * 2 * K + K + base + lane + 32 * e];
+#pragma unroll
+            for (int e = 0; e < N; e++) v[e] = (a[e] * b[e]) * sigm(a[e]);
+            break;
+        case ACT_GATE:
+#pragma unroll
+            for (int e = 0; e < N; e++) a[e] = s.x[(size_t)t * K + base + lane + 32 * e];
+#pragma unroll
+            for (int e = 0; e < N; e++) {
+                int k = base + lane + 32 * e;
+                b[e] = s.x2[(size_t)t * s.ld2 + (k >> 8) * 512 + 256 + (k & 255)];
+            }
+#pragma unroll
+            for (int e = 0; e < N; e++) v[e] = a[e] * sigm(b[e]);
+            break;
         default:
-            return s.xb ? __bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)t * K + k])) : s.x[(size_t)t * K + k];
+            if (s.xb) {
+#pragma unroll
+                for (int e = 0; e < N; e++)
+                    v[e] = __bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)t * K + base + lane + 32 * e]));
+            } else {
+#pragma unroll
+                for (int e = 0; e < N; e++) v[e] = s.x[(size_t)t * K + base + lane + 32 * e];
+            }
     }
 }
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }  // |e| <= 126
 
-// Builds token t's operand for this CTA's K-slice into shared memory (one warp). SPAN = the values a lane holds x 32:
-// max(kslice, HB). Lane l holds element span0 + l + 32 e, the layout of fwht512 (kernels.metal:32-51), so the
-// transform's strides 1..16 run across lanes and 32.. inside the lane, in ascending order (bit-identical to an
-// in-memory radix-2 transform).
-template <int SPAN, int NT>
-__device__ void build_token(const GemvParams& p, int t, int ks, uint32_t* s_b, uint16_t* s_bb16, int* s_e) {
-    constexpr int VPL = SPAN / 32;
+// Builds the operand of token t for Hadamard block b of this CTA's K-slice (one warp) and stores it into the shared
+// memory of every CTA of the cluster (they share the K-slice): the fragments, the group sums of the bias step and the
+// block's power-of-two exponent. Lane l holds element blk0 + l + 32 e (e < VPL = HB / 32), the layout of fwht512
+// (kernels.metal:32-51), so the transform's strides 1..16 run across lanes and 32.. inside the lane, in ascending order
+// (bit-identical to an in-memory radix-2 transform).
+template <int VPL, int NT>
+__device__ void build_task(const GemvParams& p, int t, int b, int ks, uint32_t* s_b, uint16_t* s_bb16, int* s_e,
+                           cg::cluster_group& cl, bool writer) {
     const int lane = threadIdx.x & 31;
     const ActSrc& s = p.src;
-    const int K = p.K, kslice = p.kslice, HB = s.HB;
+    const int K = p.K, kslice = p.kslice, HBe = VPL * 32;
     const int k0 = ks * kslice;
-    const int span0 = HB > kslice ? (k0 / HB) * HB : k0;
+    const int blk0 = HBe <= kslice ? k0 + b * HBe : (k0 / HBe) * HBe;
     float v[VPL];
     uint32_t id = 0;
-    float r = row_scale(s, t, K, &id, blockIdx.x == 0);
+    float r = row_scale(s, t, K, &id, writer);
     if (s.mode == ACT_GATED) {
         float zz[VPL];
 #pragma unroll
         for (int e = 0; e < VPL; e++) {
-            int k = span0 + lane + 32 * e;
+            int k = blk0 + lane + 32 * e;
             v[e] = s.x[(size_t)t * K + k];
             zz[e] = s.x2[(size_t)t * s.ld2 + s.off2 + k];
         }
+        float wv[4];  // norm weight at (lane + 32 e) & 127: period 4 in e
+#pragma unroll
+        for (int i = 0; i < 4; i++) wv[i] = s.w[(lane + 32 * i) & 127];
 #pragma unroll
         for (int c = 0; c < VPL / 4; c++) {
             float ss = 0.0f;
@@ -224,21 +275,19 @@ __device__ void build_token(const GemvParams& p, int t, int ks, uint32_t* s_b, u
             for (int e = 4 * c; e < 4 * c + 4; e++) ss += v[e] * v[e];
             float rh = rsqrtf(warp_sum(ss) / 128.0f + EPS_T);
 #pragma unroll
-            for (int e = 4 * c; e < 4 * c + 4; e++) {
-                int d = (lane + 32 * e) & 127;
-                v[e] = (((zz[e] * v[e]) * rh) * s.w[d]) * sigm(zz[e]);
-            }
+            for (int e = 4 * c; e < 4 * c + 4; e++) v[e] = (((zz[e] * v[e]) * rh) * wv[e & 3]) * sigm(zz[e]);
         }
     } else {
-#pragma unroll
-        for (int e = 0; e < VPL; e++) v[e] = act_value(s, t, span0 + lane + 32 * e, K, r, id);
+        act_values<VPL>(s, t, blk0, K, r, id, v);
     }
     if (s.signs) {
+        float sg[VPL];
 #pragma unroll
-        for (int e = 0; e < VPL; e++) v[e] *= s.signs[span0 + lane + 32 * e];
+        for (int e = 0; e < VPL; e++) sg[e] = s.signs[blk0 + lane + 32 * e];
+#pragma unroll
+        for (int e = 0; e < VPL; e++) v[e] *= sg[e];
     }
-    // Walsh-Hadamard transform of each HB block of the span (HB = 0: the input is already rotated)
-    if (HB > 0) {
+    if (s.HB > 0) {  // Walsh-Hadamard transform of the block (HB = 0: the input is already rotated)
 #pragma unroll
         for (int m = 1; m < 32; m <<= 1) {
             bool up = (lane & m) != 0;
@@ -249,23 +298,21 @@ __device__ void build_token(const GemvParams& p, int t, int ks, uint32_t* s_b, u
             }
         }
 #pragma unroll
-        for (int h = 1; h < VPL; h <<= 1) {
-            if (h * 32 >= HB) break;
+        for (int h = 1; h < VPL; h <<= 1)
 #pragma unroll
             for (int e = 0; e < VPL; e++)
                 if ((e & h) == 0) {
-                    float a = v[e], b = v[e + h];
-                    v[e] = a + b;
-                    v[e + h] = a - b;
+                    float a = v[e], c = v[e + h];
+                    v[e] = a + c;
+                    v[e + h] = a - c;
                 }
-        }
-        const float inv = HB == 512 ? 0.044194173824159216f : (HB == 2048 ? 0.02209708691207961f : 0.03125f);
+        const float inv = VPL == 16 ? 0.044194173824159216f : (VPL == 64 ? 0.02209708691207961f : 0.03125f);
 #pragma unroll
         for (int e = 0; e < VPL; e++) v[e] *= inv;
     }
-
-    // the slice [k0, k0 + kslice) within the span
-    const int e_lo = (k0 - span0) / 32, e_hi = e_lo + kslice / 32;
+    // the part of the block inside the slice: e in [e_lo, e_hi); slice-local k = blk0 - k0 + lane + 32 e
+    const int e_lo = HBe <= kslice ? 0 : (k0 - blk0) / 32;
+    const int e_hi = HBe <= kslice ? VPL : e_lo + kslice / 32;
     float amax = 0.0f;
 #pragma unroll
     for (int e = 0; e < VPL; e++)
@@ -277,45 +324,52 @@ __device__ void build_token(const GemvParams& p, int t, int ks, uint32_t* s_b, u
         frexpf(amax, &ex);  // amax < 2^ex
         E = min(max(14 - ex, -60), 100);
     }
-    if (lane == 0) s_e[t] = E;
-    // 2^E split so that both factors stay normal: x * 2^E * 4^-j
+    const int ncs = cl.num_blocks();
+    if (lane < ncs) cl.map_shared_rank(s_e, lane)[t * 4 + b] = E;
+    // x * 2^E * 4^-j in fp16 hi + lo, j = (k % 32) / 8 = lane / 8
     const int j = lane >> 3;
     const int nt = t >> 2, gb = (t & 3) * 2;
     const int t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
+    const int E1 = E - 2 * j;
+    const float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
 #pragma unroll
     for (int e = 0; e < VPL; e++) {
         if (e < e_lo || e >= e_hi) continue;
         float x0 = v[e];
         float x1 = __shfl_down_sync(0xffffffffu, x0, 1);
         if ((lane & 1) == 0) {
-            int kl = (e - e_lo) * 32 + lane;
-            int E1 = E - 2 * j;
-            float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
+            int kl = blk0 - k0 + lane + 32 * e;
             float a0 = x0 * f, a1 = x1 * f;
             __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
             __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
             size_t base = ((size_t)(kl >> 4) * NT + nt) * 32;
-            s_b[(base + gb * 4 + t4) * 2 + which] = pack_half2(h0, h1);
-            s_b[(base + (gb + 1) * 4 + t4) * 2 + which] = pack_half2(l0, l1);
+            uint32_t hv = pack_half2(h0, h1), lv = pack_half2(l0, l1);
+            for (int rk = 0; rk < ncs; rk++) {
+                uint32_t* dst = cl.map_shared_rank(s_b, rk);
+                dst[(base + gb * 4 + t4) * 2 + which] = hv;
+                dst[(base + (gb + 1) * 4 + t4) * 2 + which] = lv;
+            }
         }
     }
-    // group sums of the slice for the bias step: element k of the bias operand = group k, scaled by 2^(E-6)
+    // group sums of the block's slice part for the bias step: bias operand element = slice-local group, x 2^(E-6)
     const int G = p.group, epg = G / 32;
     const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
-    for (int gl = 0; gl < kslice / G; gl++) {
+    const int g0 = (blk0 - k0 + 32 * e_lo) / G, ng = (e_hi - e_lo) / epg;
+    for (int gi = 0; gi < ng; gi++) {
         float sum = 0.0f;
 #pragma unroll
         for (int e = 0; e < VPL; e++)
-            if (e >= e_lo + gl * epg && e < e_lo + (gl + 1) * epg) sum += v[e];
+            if (e >= e_lo + gi * epg && e < e_lo + (gi + 1) * epg) sum += v[e];
         sum = warp_sum(sum);
-        if (lane == 0) {
+        if (lane < 2 * ncs) {  // lane = 2 * rank + (0: hi, 1: lo)
             float a = sum * fb;
-            __half hv = __float2half_rn(a), lv = __float2half_rn(a - __half2float(hv));
-            int bs = gl >> 4, kk = gl & 15;
+            __half hv = __float2half_rn(a);
+            __half w = (lane & 1) ? __float2half_rn(a - __half2float(hv)) : hv;
+            int gl = g0 + gi, bs = gl >> 4, kk = gl & 15;
             int tt = (kk & 7) >> 1, wh = kk >> 3, half = kk & 1;
             size_t base = ((size_t)bs * NT + nt) * 32;
-            s_bb16[((base + gb * 4 + tt) * 2 + wh) * 2 + half] = __half_as_ushort(hv);
-            s_bb16[((base + (gb + 1) * 4 + tt) * 2 + wh) * 2 + half] = __half_as_ushort(lv);
+            cl.map_shared_rank(s_bb16, lane >> 1)[((base + (gb + (lane & 1)) * 4 + tt) * 2 + wh) * 2 + half] =
+                __half_as_ushort(w);
         }
     }
 }
@@ -338,11 +392,16 @@ __device__ void ab_rows(const GemvParams& p, int r0, int nr, float* s_w) {
         float acc[8];
 #pragma unroll
         for (int q = 0; q < 8; q++) acc[q] = 0.0f;
-        for (int k = lane; k < K; k += 32) {
-            float x = act_value(p.src, t, k, K, r, id);
+        for (int k0 = 0; k0 < K; k0 += 256) {
+            float x[8];
+            act_values<8>(p.src, t, k0, K, r, id, x);
 #pragma unroll
-            for (int q = 0; q < 8; q++)
-                if (q < nr) acc[q] += s_w[q * K + k] * x;
+            for (int i = 0; i < 8; i++) {
+                int k = k0 + i * 32 + lane;
+#pragma unroll
+                for (int q = 0; q < 8; q++)
+                    if (q < nr) acc[q] += s_w[q * K + k] * x[i];
+            }
         }
 #pragma unroll
         for (int q = 0; q < 8; q++)
@@ -353,29 +412,30 @@ __device__ void ab_rows(const GemvParams& p, int r0, int nr, float* s_w) {
     }
 }
 
-template <int NT, int GPC, int SPAN>
+template <int NT, int GPC, int VPL>
 __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows
+    if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows (whole clusters of their own: n_main % cluster == 0)
         pdl_trigger();
         int r0 = ((int)blockIdx.x - p.n_main) * 8;
-        ab_rows(p, r0, min(8, p.ab_rows - r0), (float*)smem);
+        if (r0 < p.ab_rows) ab_rows(p, r0, min(8, p.ab_rows - r0), (float*)smem);
         return;
     }
+    cg::cluster_group cl = cg::this_cluster();
     uint64_t* bar = (uint64_t*)smem;
-    int* s_e = (int*)(smem + 16);
+    int* s_e = (int*)(smem + 128);  // [T][4] exponent per (token, Hadamard block of the slice)
     const int kslice = p.kslice, nkc = kslice / 128;
     const size_t codes_bytes = (size_t)kslice * 32;
     const size_t sb_bytes = (size_t)nkc * 8 * 2 * GPC * 32;
     const int nbb = (kslice / p.group + 15) / 16;  // bias k16 steps
     const size_t b_bytes = (size_t)(kslice / 16) * NT * 256, bb_bytes = (size_t)nbb * NT * 256;
-    uint8_t* s_codes = smem + 128;
-    uint32_t* s_sb = (uint32_t*)(smem + 128 + codes_bytes);
-    uint32_t* s_b = (uint32_t*)(smem + 128 + codes_bytes + sb_bytes);
-    uint32_t* s_bb = (uint32_t*)(smem + 128 + codes_bytes + sb_bytes + b_bytes);
+    uint8_t* s_codes = smem + GEMV_HDR;
+    uint32_t* s_sb = (uint32_t*)(smem + GEMV_HDR + codes_bytes);
+    uint32_t* s_b = (uint32_t*)(smem + GEMV_HDR + codes_bytes + sb_bytes);
+    uint32_t* s_bb = (uint32_t*)(smem + GEMV_HDR + codes_bytes + sb_bytes + b_bytes);
 
-    const int rb = blockIdx.x / p.nsplit, ks = blockIdx.x % p.nsplit;
+    const int rb = blockIdx.x % p.nrb, ks = blockIdx.x / p.nrb;
     const int nkc_all = p.K / 128;
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -391,8 +451,19 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         bulk_g2s(s_sb, (const uint8_t*)p.sb + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 2 * GPC * 32,
                  (uint32_t)sb_bytes, bar);
     }
+    cl.sync();  // every CTA of the cluster has zeroed its operand before any of them writes into it
     pdl_wait();
-    for (int t = warp; t < p.T; t += 8) build_token<SPAN, NT>(p, t, ks, s_b, (uint16_t*)s_bb, s_e);
+    {
+        // the cluster's (token, block) tasks over all its warps; each writes its operand into every CTA
+        const int HBe = VPL * 32, nb = HBe < kslice ? kslice / HBe : 1;
+        const int ncs = (int)cl.num_blocks(), gw = (int)cl.block_rank() * 8 + warp;
+        const bool first_cluster = (int)blockIdx.x < ncs;  // ks == 0 and the first row blocks
+        for (int i = gw; i < p.T * nb; i += ncs * 8) {
+            int t = i / nb, b = i % nb;
+            build_task<VPL, NT>(p, t, b, ks, s_b, (uint16_t*)s_bb, s_e, cl, first_cluster && b == 0);
+        }
+    }
+    cl.sync();
     bool ok = mbar_wait_bounded(bar, 0);
     if (__syncthreads_or(!ok)) {
         if (tid == 0) atomicOr(p.o.err, ERR_MBAR_TIMEOUT);
@@ -484,7 +555,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
 
     // in-CTA reduction over the 4 k-quarters, fixed order; partials in units of x (2^-E applied)
     __syncthreads();
-    float* red = (float*)(smem + 128);  // [kw 4][rg 2][m 4][NT][2][32]
+    float* red = (float*)(smem + GEMV_HDR);  // [kw 4][rg 2][m 4][NT][2][32]
 #pragma unroll
     for (int m = 0; m < 4; m++)
 #pragma unroll
@@ -497,6 +568,9 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     const int T = p.T, O = p.O;
     const size_t quarter = (size_t)2 * 4 * NT * 2 * 32;
     float* fin = red + 4 * quarter;  // [T][128] final values when this CTA holds the whole K range
+    int blk_of_q[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) blk_of_q[q] = VPL * 32 < kslice ? q * (kslice / 4) / (VPL * 32) : 0;
     for (int e = tid; e < (int)quarter; e += 256) {
         int ln = e & 31;
         int r = e >> 5;
@@ -509,8 +583,12 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         int token = n * 4 + (ln & 3);
         if (token >= T) continue;
         int rloc = rgi * 64 + m * 16 + (ln >> 2) + 8 * which;
-        float v = ((red[e] + red[quarter + e]) + red[2 * quarter + e]) + red[3 * quarter + e];
-        v *= pow2f(-s_e[token]);
+        // quarter q of the slice lies in Hadamard block q * kslice / (4 * HB) (its operand's exponent)
+        const int* et = s_e + token * 4;
+        float v = red[e] * pow2f(-et[blk_of_q[0]]);
+        v += red[quarter + e] * pow2f(-et[blk_of_q[1]]);
+        v += red[2 * quarter + e] * pow2f(-et[blk_of_q[2]]);
+        v += red[3 * quarter + e] * pow2f(-et[blk_of_q[3]]);
         if (p.nsplit == 1) fin[token * 128 + rloc] = v;
         else p.o.partial[((size_t)ks * T + token) * O + rb * 128 + rloc] = v;
     }
@@ -525,13 +603,15 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         for (int e = tid; e < 128 * T; e += 256) {
             int token = e >> 7, rloc = e & 127;
             const float* src = p.o.partial + (size_t)token * O + rb * 128 + rloc;
-            float pv[16];
-#pragma unroll
-            for (int s = 0; s < 16; s++) pv[s] = s < p.nsplit ? __ldcg(src + (size_t)s * T * O) : 0.0f;
             float v = 0.0f;
+            for (int s0 = 0; s0 < p.nsplit; s0 += 16) {  // loads of a chunk in flight together, sums in split order
+                float pv[16];
 #pragma unroll
-            for (int s = 0; s < 16; s++)
-                if (s < p.nsplit) v += pv[s];
+                for (int s = 0; s < 16; s++) pv[s] = s0 + s < p.nsplit ? __ldcg(src + (size_t)(s0 + s) * T * O) : 0.0f;
+#pragma unroll
+                for (int s = 0; s < 16; s++)
+                    if (s0 + s < p.nsplit) v += pv[s];
+            }
             fin[token * 128 + rloc] = v;
         }
         if (tid == 0) p.o.counters[rb] = 0;
@@ -564,17 +644,24 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
 static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab) {
     int gpc = 128 / group;
     int nbb = (kslice / group + 15) / 16;
-    size_t main = 128 + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
+    size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
                   (size_t)(kslice / 16) * nt * 256 + (size_t)nbb * nt * 256;
-    size_t red = 128 + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
+    size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
     size_t abs_ = ab ? (size_t)8 * K * 4 : 0;
     size_t s = main > red ? main : red;
     return s > abs_ ? s : abs_;
 }
 
-template <int NT, int GPC, int SPAN>
+// Cluster size: the largest of 8, 4, 2, 1 that divides the row-block count (clusters never straddle K-slices).
+static int gemv_cluster(int nrb) {
+    for (int c = 8; c > 1; c >>= 1)
+        if (nrb % c == 0) return c;
+    return 1;
+}
+
+template <int NT, int GPC, int VPL>
 static void launch_gemv_t(const GemvParams& p, size_t smem, cudaStream_t st) {
-    auto fn = ternary_gemv_kernel<NT, GPC, SPAN>;
+    auto fn = ternary_gemv_kernel<NT, GPC, VPL>;
     static bool attr_done = false;
     if (!attr_done) {
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
@@ -582,21 +669,37 @@ static void launch_gemv_t(const GemvParams& p, size_t smem, cudaStream_t st) {
     }
     GemvParams pp = p;
     void* args[] = {&pp};
-    int grid = p.n_main + (p.ab_rows + 7) / 8;
-    launch_pdl((const void*)fn, dim3((unsigned)grid), dim3(256), smem, st, args);
+    const int cs = gemv_cluster(p.nrb);
+    int n_ab = (p.ab_rows + 7) / 8;
+    n_ab = (n_ab + cs - 1) / cs * cs;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.n_main + n_ab));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cs;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelExC(&cfg, (const void*)fn, args);
 }
 
 template <int NT, int GPC>
-static void launch_span(const GemvParams& p, int span, size_t smem, cudaStream_t st) {
-    if (span == 512) launch_gemv_t<NT, GPC, 512>(p, smem, st);
-    else if (span == 1024) launch_gemv_t<NT, GPC, 1024>(p, smem, st);
-    else launch_gemv_t<NT, GPC, 2048>(p, smem, st);
+static void launch_vpl(const GemvParams& p, int hb, size_t smem, cudaStream_t st) {
+    if (hb == 512) launch_gemv_t<NT, GPC, 16>(p, smem, st);
+    else if (hb == 1024) launch_gemv_t<NT, GPC, 32>(p, smem, st);
+    else launch_gemv_t<NT, GPC, 64>(p, smem, st);
 }
 
 template <int NT>
-static void launch_gpc(const GemvParams& p, int span, size_t smem, cudaStream_t st) {
-    if (p.group == 64) launch_span<NT, 2>(p, span, smem, st);
-    else launch_span<NT, 1>(p, span, smem, st);
+static void launch_gpc(const GemvParams& p, int hb, size_t smem, cudaStream_t st) {
+    if (p.group == 64) launch_vpl<NT, 2>(p, hb, smem, st);
+    else launch_vpl<NT, 1>(p, hb, smem, st);
 }
 
 void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const GemvOut& o, const AbArgs* ab,
@@ -615,13 +718,14 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     p.T = T;
     p.n_main = (m.O / 128) * m.nsplit;
     p.ab_rows = ab ? 2 * ab->nv : 0;
-    int span = src.HB > m.kslice ? src.HB : m.kslice;
+    p.nrb = m.O / 128;
+    int hb = src.HB > 0 ? src.HB : 512;  // unrotated sources use 512-element blocks for their exponents
     int nt = (2 * T + 7) / 8;
     size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0);
-    if (nt == 1) launch_gpc<1>(p, span, smem, st);
-    else if (nt == 2) launch_gpc<2>(p, span, smem, st);
-    else if (nt == 3) launch_gpc<3>(p, span, smem, st);
-    else launch_gpc<4>(p, span, smem, st);
+    if (nt == 1) launch_gpc<1>(p, hb, smem, st);
+    else if (nt == 2) launch_gpc<2>(p, hb, smem, st);
+    else if (nt == 3) launch_gpc<3>(p, hb, smem, st);
+    else launch_gpc<4>(p, hb, smem, st);
 }
 
 }  // namespace bcu

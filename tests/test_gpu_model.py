@@ -64,6 +64,77 @@ def test_prefill_and_verify_logits(pair):
     m.keep_logits(False)
 
 
+@pytest.mark.parametrize("T", [1, 2, 4, 5, 8, 12, 16])
+def test_verify_logits_every_width(pair, T):
+    """Every verify width (the n-tile variants of the kernels) against the oracle."""
+    name, cfg, m, o = pair
+    m.reset()
+    o.reset()
+    ids = prompt(cfg, 19, seed=T)
+    assert m.prefill(ids) == o.prefill(ids)
+    rows = prompt(cfg, T, seed=100 + T).astype(np.uint32)
+    m.keep_logits(True)
+    pred, _ = m.verify(rows)
+    opred, ol = o.forward(rows, logits=True)
+    for t in range(T):
+        check_logits(m.logits(t), ol[t], f"{name} T={T} row {t}")
+    m.keep_logits(False)
+
+
+def test_batch_invariance_bitwise(pair):
+    """Row t of a verify pass has the same logits bit for bit whatever the pass width T (the property that makes
+    speculative decoding token-identical to plain decoding)."""
+    name, cfg, m, o = pair
+    ids = prompt(cfg, 17, seed=31)
+    m.reset()
+    m.prefill(ids)
+    snap = m.snapshot()
+    rows = prompt(cfg, 16, seed=32).astype(np.uint32)
+    m.keep_logits(True)
+    ref = {}
+    for T in (16, 9, 5, 4, 2, 1):
+        m.restore(snap)
+        m.verify(rows[:T])
+        for t in range(T):
+            lg = m.logits(t)
+            if t in ref:
+                assert np.array_equal(lg.view(np.uint32), ref[t].view(np.uint32)), f"{name}: row {t} differs at T={T}"
+            else:
+                ref[t] = lg
+    m.keep_logits(False)
+    snap.free()
+
+
+def test_lookup_decode_repeatable(pair):
+    name, cfg, m, o = pair
+    ids = prompt(cfg, 30, seed=6)
+    m.reset()
+    first = m.prefill(ids)
+    snap = m.snapshot()
+    greedy, _ = m.decode(first, speculate=False, max_tokens=40)
+    for rep in range(4):
+        m.restore(snap)
+        look, st = m.decode(first, user=ids, mode=_lib.DRAFT_LOOKUP, max_tokens=40)
+        assert list(look) == list(greedy), f"{name} rep {rep}: verify calls {st.verify_calls} drafted {st.drafted}"
+    snap.free()
+
+
+def test_time_pass_keeps_state(pair):
+    """The cost calibration (bcu_time_pass) restores the state it found."""
+    name, cfg, m, o = pair
+    ids = prompt(cfg, 23, seed=21)
+    m.reset()
+    first = m.prefill(ids)
+    snap = m.snapshot()
+    g1, _ = m.decode(first, speculate=False, max_tokens=10)
+    m.restore(snap)
+    for t in (1, 3, 9):
+        m.time_pass(t, 2)
+    g2, _ = m.decode(first, speculate=False, max_tokens=10)
+    assert list(g1) == list(g2)
+    snap.free()
+
+
 def test_greedy_matches_oracle(pair):
     name, cfg, m, o = pair
     m.reset()
