@@ -116,13 +116,16 @@ void repack_ternary(const uint32_t* w_mlx, const uint16_t* s, const uint16_t* b,
 }
 
 // Split-K plan: the fewest K-slices (512, 1024 or 2048 codes) that give at least one CTA per SM.
+// K-slice plan: the longest slice (fewest splits) that still puts CTAs on at least ~45% of the SMs. Fewer splits save
+// the split-K reduction (a dependent global round trip) and the duplicated operand build; one CTA per SM gets the
+// SM's whole issue rate for the decode, so ~70 CTAs of 2048-code slices finish as fast as ~140 of 1024.
 void plan_ternary(TernaryMat& m, int num_sms) {
     int rb = m.O / 128;
     int best = 0;
     for (int ks : {2048, 1024, 512}) {
         if (m.K % ks) continue;
         best = ks;
-        if (rb * (m.K / ks) >= num_sms) break;
+        if (rb * (m.K / ks) * 20 >= num_sms * 9) break;
     }
     m.kslice = best;
     m.nsplit = m.K / best;
@@ -241,17 +244,33 @@ __device__ __forceinline__ void act_values(const ActSrc& s, int t, int base, int
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }  // |e| <= 126
 
-// Builds the operand of token t for Hadamard block b of this CTA's K-slice (one warp) and stores it into the shared
-// memory of every CTA of the cluster (they share the K-slice): the fragments, the group sums of the bias step and the
-// block's power-of-two exponent. Lane l holds element blk0 + l + 32 e (e < VPL = HB / 32), the layout of fwht512
-// (kernels.metal:32-51), so the transform's strides 1..16 run across lanes and 32.. inside the lane, in ascending order
-// (bit-identical to an in-memory radix-2 transform).
-template <int VPL, int NT>
-__device__ void build_task(const GemvParams& p, int t, int b, int ks, uint32_t* s_b, uint16_t* s_bb16, int* s_e,
-                           cg::cluster_group& cl, bool writer) {
+// Activation operand layout in shared memory: one region per (column tile nt of 4 tokens, block b of the K-slice),
+// region index nt * nb + b. A block is the part of a Walsh-Hadamard block inside the slice (sb = min(HB, kslice)
+// elements). Region = sb/16 main k16 steps of B fragments (256 B each: 4 tokens x fp16 hi, lo columns), then the
+// block's bias k16 steps (group sums, group-in-block = k), then the power-of-two exponents of its 4 tokens (16 B).
+__host__ __device__ inline int op_bias_steps(int sb, int group) { return (sb / group + 15) / 16; }
+__host__ __device__ inline int op_region_bytes(int sb, int group) { return (sb / 16 + op_bias_steps(sb, group)) * 256 + 16; }
+
+// Builds token t's columns of region (t / 4, b) of K-slice ks in this CTA's shared memory (one warp). Lane l holds
+// element blk0 + l + 32 e (e < VPL = HB / 32) of the Hadamard block, the layout of fwht512 (kernels.metal:32-51), so
+// the transform's strides 1..16 run across lanes and 32.. inside the lane, in ascending order (bit-identical to an
+// in-memory radix-2 transform). Tokens t >= T write zero columns.
+template <int VPL, int GPC>
+__device__ void build_token(const GemvParams& p, int t, int b, int ks, int sbsz, uint8_t* reg, bool writer) {
+    constexpr int G = 128 / GPC, EPG = G / 32, HBe = VPL * 32, NGH = HBe / G;
     const int lane = threadIdx.x & 31;
+    const int nsteps = sbsz / 16, nbs = op_bias_steps(sbsz, G);
+    uint32_t* rw = (uint32_t*)reg;
+    int* r_e = (int*)(reg + (nsteps + nbs) * 256);
+    const int col = (t & 3) * 2;  // hi column of the token in its tile; lo = col + 1
+    if (t >= p.T) {
+        // per k16 step the columns col, col + 1 are the 16 words [8 col, 8 col + 16)
+        for (int i = lane; i < (nsteps + nbs) * 16; i += 32) rw[(i >> 4) * 64 + col * 8 + (i & 15)] = 0u;
+        if (lane == 0) r_e[t & 3] = 0;
+        return;
+    }
     const ActSrc& s = p.src;
-    const int K = p.K, kslice = p.kslice, HBe = VPL * 32;
+    const int K = p.K, kslice = p.kslice;
     const int k0 = ks * kslice;
     const int blk0 = HBe <= kslice ? k0 + b * HBe : (k0 / HBe) * HBe;
     float v[VPL];
@@ -310,9 +329,10 @@ __device__ void build_task(const GemvParams& p, int t, int b, int ks, uint32_t* 
 #pragma unroll
         for (int e = 0; e < VPL; e++) v[e] *= inv;
     }
-    // the part of the block inside the slice: e in [e_lo, e_hi); slice-local k = blk0 - k0 + lane + 32 e
+    // the part of the Hadamard block inside the slice: e in [e_lo, e_hi); region-relative k = kr0 + lane + 32 e
     const int e_lo = HBe <= kslice ? 0 : (k0 - blk0) / 32;
     const int e_hi = HBe <= kslice ? VPL : e_lo + kslice / 32;
+    const int kr0 = HBe <= kslice ? 0 : blk0 - k0;
     float amax = 0.0f;
 #pragma unroll
     for (int e = 0; e < VPL; e++)
@@ -324,52 +344,63 @@ __device__ void build_task(const GemvParams& p, int t, int b, int ks, uint32_t* 
         frexpf(amax, &ex);  // amax < 2^ex
         E = min(max(14 - ex, -60), 100);
     }
-    const int ncs = cl.num_blocks();
-    if (lane < ncs) cl.map_shared_rank(s_e, lane)[t * 4 + b] = E;
-    // x * 2^E * 4^-j in fp16 hi + lo, j = (k % 32) / 8 = lane / 8
-    const int j = lane >> 3;
-    const int nt = t >> 2, gb = (t & 3) * 2;
-    const int t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
-    const int E1 = E - 2 * j;
-    const float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
+    if (lane == 0) r_e[t & 3] = E;
+    // x * 2^E * 4^-j in fp16 hi + lo, j = (k % 32) / 8 = lane / 8; each lane stores its element's two halves
+    {
+        const int j = lane >> 3;
+        const int t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
+        const int E1 = E - 2 * j;
+        const float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
+        uint16_t* r16 = (uint16_t*)reg;
+        const int h_hi = ((col * 4 + t4) * 2 + which) * 2 + (lane & 1), h_lo = h_hi + 16;
+        const int step0 = (kr0 >> 4) + (lane >> 4);
 #pragma unroll
-    for (int e = 0; e < VPL; e++) {
-        if (e < e_lo || e >= e_hi) continue;
-        float x0 = v[e];
-        float x1 = __shfl_down_sync(0xffffffffu, x0, 1);
-        if ((lane & 1) == 0) {
-            int kl = blk0 - k0 + lane + 32 * e;
-            float a0 = x0 * f, a1 = x1 * f;
-            __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
-            __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
-            size_t base = ((size_t)(kl >> 4) * NT + nt) * 32;
-            uint32_t hv = pack_half2(h0, h1), lv = pack_half2(l0, l1);
-            for (int rk = 0; rk < ncs; rk++) {
-                uint32_t* dst = cl.map_shared_rank(s_b, rk);
-                dst[(base + gb * 4 + t4) * 2 + which] = hv;
-                dst[(base + (gb + 1) * 4 + t4) * 2 + which] = lv;
+        for (int e = 0; e < VPL; e++) {
+            if (e >= e_lo && e < e_hi) {
+                const float a = v[e] * f;
+                const __half h = __float2half_rn(a);
+                const __half l = __float2half_rn(a - __half2float(h));
+                r16[(step0 + 2 * e) * 128 + h_hi] = __half_as_ushort(h);
+                r16[(step0 + 2 * e) * 128 + h_lo] = __half_as_ushort(l);
             }
         }
     }
-    // group sums of the block's slice part for the bias step: bias operand element = slice-local group, x 2^(E-6)
-    const int G = p.group, epg = G / 32;
-    const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
-    const int g0 = (blk0 - k0 + 32 * e_lo) / G, ng = (e_hi - e_lo) / epg;
-    for (int gi = 0; gi < ng; gi++) {
-        float sum = 0.0f;
+    // group sums of the block's part for the bias steps (x 2^(E-6)); all lanes hold every sum after the reduction
+    float gs[NGH];
 #pragma unroll
-        for (int e = 0; e < VPL; e++)
-            if (e >= e_lo + gi * epg && e < e_lo + (gi + 1) * epg) sum += v[e];
-        sum = warp_sum(sum);
-        if (lane < 2 * ncs) {  // lane = 2 * rank + (0: hi, 1: lo)
-            float a = sum * fb;
-            __half hv = __float2half_rn(a);
-            __half w = (lane & 1) ? __float2half_rn(a - __half2float(hv)) : hv;
-            int gl = g0 + gi, bs = gl >> 4, kk = gl & 15;
-            int tt = (kk & 7) >> 1, wh = kk >> 3, half = kk & 1;
-            size_t base = ((size_t)bs * NT + nt) * 32;
-            cl.map_shared_rank(s_bb16, lane >> 1)[((base + (gb + (lane & 1)) * 4 + tt) * 2 + wh) * 2 + half] =
-                __half_as_ushort(w);
+    for (int g = 0; g < NGH; g++) {
+        float a = 0.0f;
+#pragma unroll
+        for (int e = g * EPG; e < (g + 1) * EPG; e++) a += v[e];
+        gs[g] = a;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int g = 0; g < NGH; g++) gs[g] += __shfl_xor_sync(0xffffffffu, gs[g], o);
+    if (lane < 16) {
+        // lane -> column col + lane / 8, word (t4, which) of the bias step: k rows kk0, kk0 + 1
+        const int hl = lane >> 3, t4 = (lane >> 1) & 3, wh = lane & 1;
+        const int kk0 = wh * 8 + t4 * 2;
+        const int g_lo = e_lo / EPG, ngs = (e_hi - e_lo) / EPG;
+        const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
+        for (int bs = 0; bs < nbs; bs++) {
+            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+            for (int g = 0; g < NGH; g++) {
+                const int gr = g - g_lo;  // block-relative group
+                if (gr >= 0 && gr < ngs) {
+                    if (gr == bs * 16 + kk0) s0 = gs[g];
+                    if (gr == bs * 16 + kk0 + 1) s1 = gs[g];
+                }
+            }
+            float a0 = s0 * fb, a1 = s1 * fb;
+            __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
+            if (hl) {
+                h0 = __float2half_rn(a0 - __half2float(h0));
+                h1 = __float2half_rn(a1 - __half2float(h1));
+            }
+            rw[(nsteps + bs) * 64 + ((col + hl) * 4 + t4) * 2 + wh] = pack_half2(h0, h1);
         }
     }
 }
@@ -422,58 +453,87 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         if (r0 < p.ab_rows) ab_rows(p, r0, min(8, p.ab_rows - r0), (float*)smem);
         return;
     }
-    cg::cluster_group cl = cg::this_cluster();
-    uint64_t* bar = (uint64_t*)smem;
-    int* s_e = (int*)(smem + 128);  // [T][4] exponent per (token, Hadamard block of the slice)
+    constexpr int G = 128 / GPC;
+    uint64_t* bar = (uint64_t*)smem;           // codes + scales of this CTA
+    uint64_t* bar_op = (uint64_t*)(smem + 8);  // operand regions sent by the other CTAs of the cluster
+    int* s_e = (int*)(smem + 128);             // [token][block] exponents, kept for the reduction
     const int kslice = p.kslice, nkc = kslice / 128;
+    const int sbsz = min(VPL * 32, kslice), nb = kslice / sbsz;
+    const int nsteps = sbsz / 16, nbs = op_bias_steps(sbsz, G), rsz = op_region_bytes(sbsz, G);
     const size_t codes_bytes = (size_t)kslice * 32;
     const size_t sb_bytes = (size_t)nkc * 8 * 2 * GPC * 32;
-    const int nbb = (kslice / p.group + 15) / 16;  // bias k16 steps
-    const size_t b_bytes = (size_t)(kslice / 16) * NT * 256, bb_bytes = (size_t)nbb * NT * 256;
     uint8_t* s_codes = smem + GEMV_HDR;
     uint32_t* s_sb = (uint32_t*)(smem + GEMV_HDR + codes_bytes);
-    uint32_t* s_b = (uint32_t*)(smem + GEMV_HDR + codes_bytes + sb_bytes);
-    uint32_t* s_bb = (uint32_t*)(smem + GEMV_HDR + codes_bytes + sb_bytes + b_bytes);
+    uint8_t* s_op = smem + GEMV_HDR + codes_bytes + sb_bytes;
 
     const int rb = blockIdx.x % p.nrb, ks = blockIdx.x / p.nrb;
     const int nkc_all = p.K / 128;
+    // operand tasks (nt, b) = region index i: built by CTA (i % 2 ncs) / 2 of the cluster, warps 4 (i % 2) .. + 3
+    const int ncs = (int)cg::this_cluster().num_blocks(), rank = (int)cg::this_cluster().block_rank();
+    const int ntask = NT * nb, nslot = 2 * ncs;
+    int mine = 0;
+    for (int i = 0; i < ntask; i++) mine += (i % nslot) / 2 == rank;
     if (tid == 0) {
         mbar_init(bar, 1);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_init(bar_op, 1);
+        fence_mbar_init_cluster();
+        fence_proxy_async_smem();
     }
-    // zero the activation operand (padding columns and bias steps stay zero)
-    for (size_t i = tid; i < (b_bytes + bb_bytes) / 16; i += 256) ((uint4*)s_b)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
+    cluster_arrive();
     pdl_trigger();
     if (tid == 0) {
         mbar_expect_tx(bar, (uint32_t)(codes_bytes + sb_bytes));
         bulk_g2s(s_codes, p.codes + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 512, (uint32_t)codes_bytes, bar);
         bulk_g2s(s_sb, (const uint8_t*)p.sb + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 2 * GPC * 32,
                  (uint32_t)sb_bytes, bar);
+        mbar_expect_tx(bar_op, (uint32_t)((ntask - mine) * rsz));
     }
-    cl.sync();  // every CTA of the cluster has zeroed its operand before any of them writes into it
+    cluster_wait();  // every mbarrier of the cluster is initialised before any region is sent
     pdl_wait();
-    {
-        // the cluster's (token, block) tasks over all its warps; each writes its operand into every CTA
-        const int HBe = VPL * 32, nb = HBe < kslice ? kslice / HBe : 1;
-        const int ncs = (int)cl.num_blocks(), gw = (int)cl.block_rank() * 8 + warp;
-        const bool first_cluster = (int)blockIdx.x < ncs;  // ks == 0 and the first row blocks
-        for (int i = gw; i < p.T * nb; i += ncs * 8) {
-            int t = i / nb, b = i % nb;
-            build_task<VPL, NT>(p, t, b, ks, s_b, (uint16_t*)s_bb, s_e, cl, first_cluster && b == 0);
+    float res[8];  // residual rows of this row block (element e = tid + 256 i of [T][128]), read early
+    if (p.o.add) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int e = tid + 256 * i;
+            res[i] = e < 128 * p.T ? p.o.out[(size_t)(e >> 7) * p.O + rb * 128 + (e & 127)] : 0.0f;
         }
     }
-    cl.sync();
-    bool ok = mbar_wait_bounded(bar, 0);
+    {
+        const int half = warp >> 2, tw = warp & 3;
+        const bool first_cluster = (int)blockIdx.x < ncs;  // ks == 0 and the first row blocks
+        for (int i = 2 * rank + half; i < ntask; i += nslot) {
+            const int nt = i / nb, b = i % nb;
+            uint8_t* reg = s_op + (size_t)i * rsz;
+            build_token<VPL, GPC>(p, nt * 4 + tw, b, ks, sbsz, reg, first_cluster && b == 0);
+            fence_proxy_async_smem();  // each writer orders its region writes before the bulk copies that read them
+            named_sync(1 + half, 128);
+            if (tw == 0 && lane == 0 && ncs > 1) {
+                const uint32_t src = smem_u32(reg), mb = smem_u32(bar_op);
+                for (int rk = 0; rk < ncs; rk++)
+                    if (rk != rank) bulk_s2peer(peer_addr(src, rk), reg, (uint32_t)rsz, peer_addr(mb, rk));
+                bulk_commit();
+            }
+        }
+    }
+    __syncthreads();
+    bool ok = mbar_wait_bounded(bar, 0) && mbar_wait_cluster_bounded(bar_op, 0);
     if (__syncthreads_or(!ok)) {
         if (tid == 0) atomicOr(p.o.err, ERR_MBAR_TIMEOUT);
+        if ((warp & 3) == 0 && lane == 0) bulk_wait_read();
         mbar_wait_bounded(bar, 0, 1u << 20);
+        mbar_wait_cluster_bounded(bar_op, 0, 1u << 20);
         return;
+    }
+    if (tid < p.T * nb) {  // exponents to the header (the regions are overwritten by the reduction)
+        const int t = tid / nb, b = tid % nb;
+        s_e[t * 4 + b] = ((const int*)(s_op + (size_t)((t >> 2) * nb + b) * rsz + (nsteps + nbs) * 256))[t & 3];
     }
 
     const int rg = warp >> 2, kw = warp & 3;
     const int g = lane >> 2, t4 = lane & 3;
     const int nkc_w = nkc / 4;
+    const int bw = (kw * (kslice / 4)) / sbsz;  // this warp's block (its k-quarter lies inside one)
     float acc[4][NT][4];
 #pragma unroll
     for (int m = 0; m < 4; m++)
@@ -483,7 +543,9 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             for (int i = 0; i < 4; i++) acc[m][n][i] = 0.0f;
 
     const uint32_t MAGIC = 0x64006400u, NEG1024 = 0xE400E400u;
-    const uint2* s_b2 = (const uint2*)s_b;
+    // B fragments of k16 step (slice-local) st for tile n: regions (n, bw), step st - bw * nsteps
+    const uint2* s_b2 = (const uint2*)(s_op + (size_t)bw * rsz) - (size_t)bw * nsteps * 32;
+    const size_t tile_stride = (size_t)nb * rsz / 8;  // uint2 between tiles
     for (int c = 0; c < nkc_w; c++) {
         const int kcl = kw * nkc_w + c;
         uint4 cw[4];
@@ -508,7 +570,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
                 const bool odd = f & 1;
                 uint2 bb[NT];
 #pragma unroll
-                for (int n = 0; n < NT; n++) bb[n] = s_b2[((size_t)(kcl * 8 + f) * NT + n) * 32 + lane];
+                for (int n = 0; n < NT; n++) bb[n] = s_b2[n * tile_stride + (size_t)(kcl * 8 + f) * 32 + lane];
                 const uint32_t mask_a = odd ? 0x00300030u : 0x00030003u;
                 const uint32_t mask_b = odd ? 0x00C000C0u : 0x000C000Cu;
 #pragma unroll
@@ -525,13 +587,17 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             }
         }
     }
-    // bias step: A = 64 b for this warp's groups (columns [o0, o0 + ngw) of bias step bs), B = group sums / 64
+    // bias step: A = 64 b for this warp's groups (columns [o0, o0 + ngw) of its block's bias step bs), B = group
+    // sums / 64
     {
-        const int ngw = kslice / 4 / p.group;
-        const int gw0 = kw * ngw, bs = gw0 >> 4, o0 = gw0 & 15;
+        const int ngw = kslice / 4 / G;
+        const int gq0 = (kw * (kslice / 4) - bw * sbsz) / G;  // first group of the warp, block-relative
+        const int bs = gq0 >> 4, o0 = gq0 & 15;
+        const int gbase = bw * sbsz / G + bs * 16;  // slice-local group of column 0
         uint2 bb[NT];
 #pragma unroll
-        for (int n = 0; n < NT; n++) bb[n] = ((const uint2*)s_bb)[((size_t)bs * NT + n) * 32 + lane];
+        for (int n = 0; n < NT; n++)
+            bb[n] = ((const uint2*)(s_op + (size_t)(n * nb + bw) * rsz + (size_t)(nsteps + bs) * 256))[lane];
         const int cols[4] = {2 * t4, 2 * t4 + 1, 2 * t4 + 8, 2 * t4 + 9};
 #pragma unroll
         for (int m = 0; m < 4; m++) {
@@ -541,8 +607,8 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
                 int c = cols[i];
                 u[i] = 0;
                 if (c >= o0 && c < o0 + ngw) {
-                    int gl = bs * 16 + c;  // slice-local group
-                    int kc = gl * p.group / 128, gi = gl % GPC;
+                    int gl = gbase + c;  // slice-local group
+                    int kc = gl / GPC, gi = gl % GPC;
                     u[i] = s_sb[(((size_t)(kc * 8 + rg * 4 + m) * 2 + 1) * GPC + gi) * 8 + g];
                 }
             }
@@ -552,6 +618,8 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             for (int n = 0; n < NT; n++) mma_f16(acc[m][n], a0, a1, a2, a3, bb[n].x, bb[n].y);
         }
     }
+    // the regions' last readers: this CTA's warps (above) and the bulk copies it sent
+    if ((warp & 3) == 0 && lane == 0) bulk_wait_read();
 
     // in-CTA reduction over the 4 k-quarters, fixed order; partials in units of x (2^-E applied)
     __syncthreads();
@@ -570,7 +638,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     float* fin = red + 4 * quarter;  // [T][128] final values when this CTA holds the whole K range
     int blk_of_q[4];
 #pragma unroll
-    for (int q = 0; q < 4; q++) blk_of_q[q] = VPL * 32 < kslice ? q * (kslice / 4) / (VPL * 32) : 0;
+    for (int q = 0; q < 4; q++) blk_of_q[q] = q * (kslice / 4) / sbsz;
     for (int e = tid; e < (int)quarter; e += 256) {
         int ln = e & 31;
         int r = e >> 5;
@@ -594,12 +662,15 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
     __shared__ int s_last;
     if (p.nsplit > 1) {
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) s_last = atomicAdd(&p.o.counters[rb], 1u) == (unsigned)(p.nsplit - 1);
+        __syncthreads();  // every partial of this CTA is stored
+        if (tid == 0) {
+            // release: this CTA's partials before its count; acquire: the other CTAs' partials after theirs
+            unsigned old;
+            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.o.counters + rb) : "memory");
+            s_last = old == (unsigned)(p.nsplit - 1);
+        }
         __syncthreads();
         if (!s_last) return;
-        __threadfence();
         for (int e = tid; e < 128 * T; e += 256) {
             int token = e >> 7, rloc = e & 127;
             const float* src = p.o.partial + (size_t)token * O + rb * 128 + rloc;
@@ -618,13 +689,15 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
     __syncthreads();
     // output (store or residual add) and the sums of squares of the new rows
-    for (int e = tid; e < 128 * T; e += 256) {
-        int token = e >> 7, rloc = e & 127;
-        float* o = p.o.out + (size_t)token * O + rb * 128 + rloc;
-        float v = fin[e];
-        if (p.o.add) v = *o + v;
-        *o = v;
-        fin[e] = v;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int e = tid + 256 * i;
+        if (e < 128 * T) {
+            float v = fin[e];
+            if (p.o.add) v = res[i] + v;
+            p.o.out[(size_t)(e >> 7) * O + rb * 128 + (e & 127)] = v;
+            fin[e] = v;
+        }
     }
     if (p.o.ss_out) {
         __syncthreads();
@@ -641,11 +714,11 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
 }
 
-static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab) {
+static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb) {
     int gpc = 128 / group;
-    int nbb = (kslice / group + 15) / 16;
+    int sbsz = hb < kslice ? hb : kslice;
     size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
-                  (size_t)(kslice / 16) * nt * 256 + (size_t)nbb * nt * 256;
+                  (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
     size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
     size_t abs_ = ab ? (size_t)8 * K * 4 : 0;
     size_t s = main > red ? main : red;
@@ -721,7 +794,7 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     p.nrb = m.O / 128;
     int hb = src.HB > 0 ? src.HB : 512;  // unrotated sources use 512-element blocks for their exponents
     int nt = (2 * T + 7) / 8;
-    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0);
+    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb);
     if (nt == 1) launch_gpc<1>(p, hb, smem, st);
     else if (nt == 2) launch_gpc<2>(p, hb, smem, st);
     else if (nt == 3) launch_gpc<3>(p, hb, smem, st);
