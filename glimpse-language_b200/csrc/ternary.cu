@@ -405,41 +405,105 @@ __device__ void build_token(const GemvParams& p, int t, int b, int ks, int sbsz,
     }
 }
 
-// GDN a/b gate rows (dense fp32, gdn_ab_row kernels.metal:265-273) for rows [r0, r0 + nr) of [Wa; Wb]: warp = token,
-// x = the normed row (NORM / EMBED source, no rotation). Writes the pending gate inputs of this pass's parity.
-__device__ void ab_rows(const GemvParams& p, int r0, int nr, float* s_w) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int K = p.K, NV = p.ab.nv;
-    for (int i = threadIdx.x; i < nr * K; i += blockDim.x) {
-        int rr = i / K, k = i % K, row = r0 + rr;
-        s_w[i] = row < NV ? p.ab.wa[(size_t)row * K + k] : p.ab.wb[(size_t)(row - NV) * K + k];
+// GDN a/b gate rows (dense fp32, gdn_ab_row kernels.metal:265-273): rows [r0, r0 + nr) of [Wa; Wb], nr <= AB_ROWS,
+// applied to the normed source rows (NORM / EMBED, no rotation). The weight rows, pre-multiplied by the norm weight,
+// are staged before the dependency wait; the raw source rows of all tokens are then copied to shared memory with every
+// copy in flight at once. Warp w takes the K range w / 8; each lane's AB_ROWS x 16 (row, token) partial sums are
+// reduced across the warp by a halving butterfly (each stage keeps half of the slots), then across the warps in a
+// fixed order; the per-token norm scale is applied last (the sum is linear in it). Every token's result is computed
+// the same way whatever T is. Writes the pending gate inputs of this pass's parity.
+constexpr int AB_ROWS = 4;
+
+__device__ void ab_rows(const GemvParams& p, int r0, int nr, uint8_t* smem) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K, NV = p.ab.nv, T = p.T;
+    const ActSrc& s = p.src;
+    float* s_w = (float*)smem;          // [AB_ROWS][K] weight row x norm weight
+    float* xs = s_w + AB_ROWS * K;      // [T][K] source rows
+    float* red = xs + (size_t)T * K;    // [8 warps][64 slots]
+    float* s_r = red + 8 * 64;          // [16] norm scale per token
+    uint32_t* s_id = (uint32_t*)(s_r + 16);
+#pragma unroll 4
+    for (int i = tid * 4; i < AB_ROWS * K; i += 1024) {
+        const int q = i / K, k = i % K, row = r0 + q;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (q < nr) {
+            const float4 w = *(const float4*)(row < NV ? p.ab.wa + (size_t)row * K + k : p.ab.wb + (size_t)(row - NV) * K + k);
+            const float4 g = *(const float4*)(s.w + k);
+            v = make_float4(w.x * g.x, w.y * g.y, w.z * g.z, w.w * g.w);
+        }
+        *(float4*)(s_w + i) = v;
     }
     pdl_wait();
-    __syncthreads();
-    const int par = p.ab.ctl->parity;
-    for (int t = warp; t < p.T; t += blockDim.x >> 5) {
+    if (s.mode == ACT_NORM) {
+        for (int i = tid; i < T * K / 4; i += 256) cp_async16(xs + 4 * i, s.x + 4 * i);
+    }
+    for (int t = warp; t < T; t += 8) {
         uint32_t id = 0;
-        float r = row_scale(p.src, t, K, &id, false);
-        float acc[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) acc[q] = 0.0f;
-        for (int k0 = 0; k0 < K; k0 += 256) {
-            float x[8];
-            act_values<8>(p.src, t, k0, K, r, id, x);
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                int k = k0 + i * 32 + lane;
-#pragma unroll
-                for (int q = 0; q < 8; q++)
-                    if (q < nr) acc[q] += s_w[q * K + k] * x[i];
-            }
+        const float r = row_scale(s, t, K, &id, false);
+        if (lane == 0) {
+            s_r[t] = r;
+            s_id[t] = id;
         }
+    }
+    if (s.mode == ACT_NORM) {
+        cp_async_wait_all();
+        __syncthreads();
+    } else {  // EMBED: bf16 embedding rows of the resolved ids
+        __syncthreads();
+        for (int i0 = tid; i0 < T * K; i0 += 256 * 8) {
+            float a[8];
 #pragma unroll
-        for (int q = 0; q < 8; q++)
-            if (q < nr) {
-                float a = warp_sum(acc[q]);
-                if (lane == 0) p.ab.pend_ab[((size_t)par * VMAX + t) * 2 * NV + r0 + q] = a;
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + 256 * u;
+                a[u] = i < T * K ? __bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)s_id[i / K] * K + i % K])) : 0.0f;
             }
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (i0 + 256 * u < T * K) xs[i0 + 256 * u] = a[u];
+        }
+        __syncthreads();
+    }
+    // partial sums: slot = row * 16 + token
+    float v[64];
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = 0.0f;
+    const int kq = K / 8;
+    for (int k = warp * kq + lane; k < (warp + 1) * kq; k += 32) {
+        float w[AB_ROWS];
+#pragma unroll
+        for (int q = 0; q < AB_ROWS; q++) w[q] = s_w[q * K + k];
+#pragma unroll
+        for (int t = 0; t < 16; t++)
+            if (t < T) {
+                const float x = xs[t * K + k];
+#pragma unroll
+                for (int q = 0; q < AB_ROWS; q++) v[q * 16 + t] += w[q] * x;
+            }
+    }
+    // halving butterfly: after offsets 16, 8, 4, 2, 1 lane l holds the warp sums of slots 2 l, 2 l + 1
+#pragma unroll
+    for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < n; j++) {
+            const float send = up ? v[j] : v[j + n];
+            const float keep = up ? v[j + n] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    red[warp * 64 + 2 * lane] = v[0];
+    red[warp * 64 + 2 * lane + 1] = v[1];
+    __syncthreads();
+    if (tid < 64) {
+        const int q = tid >> 4, t = tid & 15;
+        if (q < nr && t < T) {
+            float a = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; w++) a += red[w * 64 + tid];
+            const int par = p.ab.ctl->parity;
+            p.ab.pend_ab[((size_t)par * VMAX + t) * 2 * NV + r0 + q] = a * s_r[t];
+        }
     }
 }
 
@@ -449,8 +513,8 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows (whole clusters of their own: n_main % cluster == 0)
         pdl_trigger();
-        int r0 = ((int)blockIdx.x - p.n_main) * 8;
-        if (r0 < p.ab_rows) ab_rows(p, r0, min(8, p.ab_rows - r0), (float*)smem);
+        int r0 = ((int)blockIdx.x - p.n_main) * AB_ROWS;
+        if (r0 < p.ab_rows) ab_rows(p, r0, min(AB_ROWS, p.ab_rows - r0), smem);
         return;
     }
     constexpr int G = 128 / GPC;
@@ -720,7 +784,7 @@ static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int
     size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
                   (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
     size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
-    size_t abs_ = ab ? (size_t)8 * K * 4 : 0;
+    size_t abs_ = ab ? ((size_t)(AB_ROWS + T) * K + 8 * 64 + 32) * 4 : 0;
     size_t s = main > red ? main : red;
     return s > abs_ ? s : abs_;
 }
@@ -743,7 +807,7 @@ static void launch_gemv_t(const GemvParams& p, size_t smem, cudaStream_t st) {
     GemvParams pp = p;
     void* args[] = {&pp};
     const int cs = gemv_cluster(p.nrb);
-    int n_ab = (p.ab_rows + 7) / 8;
+    int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
     n_ab = (n_ab + cs - 1) / cs * cs;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.n_main + n_ab));
