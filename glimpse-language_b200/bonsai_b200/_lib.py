@@ -13,8 +13,8 @@ MAX_LAYERS = 64
 VMAX = 16
 
 # bcu_status
-OK, ERR_CUDA, ERR_ARG, ERR_OOM, ERR_TIMEOUT, ERR_CANCELLED, ERR_STATE, ERR_NOT_FOUND = range(8)
-STATUS_NAMES = ["OK", "CUDA", "ARG", "OOM", "TIMEOUT", "CANCELLED", "STATE", "NOT_FOUND"]
+OK, ERR_CUDA, ERR_ARG, ERR_OOM, ERR_TIMEOUT, ERR_CANCELLED, ERR_STATE, ERR_NOT_FOUND, ERR_TOO_LARGE = range(9)
+STATUS_NAMES = ["OK", "CUDA", "ARG", "OOM", "TIMEOUT", "CANCELLED", "STATE", "NOT_FOUND", "TOO_LARGE"]
 # bcu_dtype
 U32, F16, BF16, F32 = range(4)
 # draft modes
@@ -114,6 +114,7 @@ SIGNATURES = {
     "bcu_linear_free": (None, [P]),
     "bcu_linear_rotate_forward": (I32, [P, P, I32, I32, P, P, P]),
     "bcu_linear_forward": (I32, [P, P, I32, P, P]),
+    "bcu_linear_rotate_forward_static": (I32, [P, P, I32, I32, P, P, P]),
     "bcu_gdn_verify": (I32, [P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
     "bcu_synth_fill": (I32, [I32, U64, U64, ctypes.c_double, ctypes.c_double, P, U64]),
     "bcu_synth_zipf": (I32, [U64, ctypes.c_double, I32, PU32, I32]),

@@ -1,6 +1,7 @@
 // ops.cu — standalone hot ops of the C ABI on caller-owned device buffers: the rotate-then-ternary-linear of graded
 // config 1 and the GatedDeltaNet verify step with rollback of graded config 2.
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/bonsai_cuda.h"
@@ -109,6 +110,66 @@ bcu_status bcu_linear_forward(bcu_linear* l, const float* x_dev, int32_t T, floa
     if (!l) return BCU_ERR_ARG;
     cudaSetDevice(l->device);
     return linear_run(l, nullptr, x_dev, T, 0, nullptr, y_dev, stream);
+}
+
+// ------------------------------------------------------------------------------------------ no-allocation variant
+// bcu_linear_rotate_forward with its scratch in a static device array instead of the handle's cudaMalloc'd buffers,
+// for callers that may not allocate device memory when they run the layer (a host whose device memory belongs to
+// its own pool, or a decode loop that must not stall on the synchronisation a cudaMalloc/cudaFree can cause).
+// Layout of the array: split-K partial sums (262144 floats, 1 MiB), then per-row-block counters (1024 words, so
+// O <= 131072 rows), then the error word. All calls share it: the counters and the error word are cleared on the
+// call's stream before its launch (the kernel's last CTA also leaves its counters at zero); the partial sums are
+// written before they are read. Calls that overlap on the GPU race on the array.
+constexpr size_t STATIC_PARTIAL_FLOATS = 262144;
+constexpr int STATIC_COUNTERS = 1024;
+constexpr size_t STATIC_SCRATCH_BYTES = STATIC_PARTIAL_FLOATS * 4 + STATIC_COUNTERS * 4 + 256;
+static __device__ __align__(256) unsigned char g_static_scratch[STATIC_SCRATCH_BYTES];
+
+// Device address of g_static_scratch, looked up once per device with that device current.
+static std::mutex g_static_mu;
+static void* g_static_ptr[64];
+
+static bcu_status static_scratch(int device, unsigned char** out) {
+    if (device < 0 || device >= 64) return BCU_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ptr[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return BCU_ERR_CUDA;
+        g_static_ptr[device] = p;
+    }
+    *out = (unsigned char*)g_static_ptr[device];
+    return BCU_OK;
+}
+
+bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf16_dev, int32_t T, int32_t hadamard,
+                                            const float* signs_dev, float* y_dev, void* stream) {
+    if (!l || !x_bf16_dev || !y_dev || T < 1 || T > VMAX) return BCU_ERR_ARG;
+    if (hadamard && (hadamard != 512 && hadamard != 1024 && hadamard != 2048)) return BCU_ERR_ARG;
+    if (hadamard && l->m.K % hadamard) return BCU_ERR_ARG;
+    const int nrb = l->m.O / 128;
+    if (nrb > STATIC_COUNTERS) return BCU_ERR_TOO_LARGE;
+    if (l->m.nsplit > 1 && (size_t)l->m.nsplit * T * l->m.O > STATIC_PARTIAL_FLOATS) return BCU_ERR_TOO_LARGE;
+    if (cudaSetDevice(l->device) != cudaSuccess) return BCU_ERR_CUDA;
+    unsigned char* scratch = nullptr;
+    bcu_status s = static_scratch(l->device, &scratch);
+    if (s != BCU_OK) return s;
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned* counters = (unsigned*)(scratch + STATIC_PARTIAL_FLOATS * 4);
+    int* err = (int*)(scratch + STATIC_PARTIAL_FLOATS * 4 + STATIC_COUNTERS * 4);
+    if (cudaMemsetAsync(counters, 0, (size_t)nrb * 4, st) != cudaSuccess) return BCU_ERR_CUDA;
+    if (cudaMemsetAsync(err, 0, 4, st) != cudaSuccess) return BCU_ERR_CUDA;
+    ActSrc src;
+    src.mode = ACT_EXT;
+    src.xb = x_bf16_dev;
+    src.signs = signs_dev;
+    src.HB = hadamard;
+    GemvOut o;
+    o.out = y_dev;
+    o.partial = (float*)scratch;
+    o.counters = counters;
+    o.err = err;
+    launch_ternary_gemv(l->m, src, T, o, nullptr, st);
+    return cudaGetLastError() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
 }
 
 bcu_status bcu_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,

@@ -35,7 +35,8 @@ typedef enum {
     BCU_ERR_TIMEOUT = 4,   /* a bounded host or device wait ran out */
     BCU_ERR_CANCELLED = 5, /* the cancel flag was raised between steps (ext.rs:21-42) */
     BCU_ERR_STATE = 6,     /* call out of order (e.g. verify before finalize, context full) */
-    BCU_ERR_NOT_FOUND = 7  /* unknown or missing tensor name */
+    BCU_ERR_NOT_FOUND = 7, /* unknown or missing tensor name */
+    BCU_ERR_TOO_LARGE = 8  /* sizes beyond a fixed capacity (the static scratch of bcu_linear_rotate_forward_static) */
 } bcu_status;
 
 /* Tensor element types of bcu_load_tensor. */
@@ -206,6 +207,17 @@ bcu_status bcu_linear_rotate_forward(bcu_linear* l, const uint16_t* x_bf16_dev, 
                                      const float* signs_dev, float* y_dev, void* stream);
 /* Y = W . X for an already rotated fp32 X (device pointers). */
 bcu_status bcu_linear_forward(bcu_linear* l, const float* x_dev, int32_t T, float* y_dev, void* stream);
+
+/* bcu_linear_rotate_forward for callers that may not allocate device memory when they run it: a host that hands
+ * all of its device memory to its own pool, or a decode loop that must not stall on the device synchronisation a
+ * cudaMalloc/cudaFree can cause. No counterpart in the reference (its backends have no such caller). Same
+ * arguments, same result; it allocates nothing: the split-K partial sums, per-row-block counters and error word
+ * live in one static device array of 1 MiB + 4 KiB + 256 B in the library, so calls whose splits x T x O exceed
+ * 262144 floats or whose O exceeds 131072 rows return BCU_ERR_TOO_LARGE. The first call on a device looks up that
+ * array's address (make it before any stream capture). Every call shares the array and clears the counters it
+ * needs on `stream` first; calls that overlap on the GPU (other streams, other threads) race on it. */
+bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf16_dev, int32_t T, int32_t hadamard,
+                                            const float* signs_dev, float* y_dev, void* stream);
 
 /* Config 2: one GatedDeltaNet verify step with rollback. q,k [T, NK, 128] and v [T, NV, 128] fp32 (q, k already
  * normalised as gdn_conv leaves them), a_in/b_in [T, NV] gate logits, A_log/dt_bias [NV], state [NV, 128, 128]
