@@ -54,7 +54,8 @@ struct __align__(16) GdnSmem {
     float k[RMAX][128];
     float v[RMAX][16];
     float g[RMAX], beta[RMAX];
-    float red[2][4][VMAX];
+    float red[4][32];      // per-warp row sums of squares: slots 0..15 q rows, 16..31 k rows
+    float rs[32];          // their norm scales
 };
 
 __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
@@ -78,63 +79,34 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
     pdl_trigger();
     pdl_wait();
     const int par = a.ctl->parity, prev = par ^ 1, rn = a.ctl->replay_n;
-    // recurrent state rows of this warp (issued first, they overlap the conv work)
+
+    // ---- every load of the layer in flight at once: the state rows of this warp, the replayed rows (conv outputs
+    // of the previous pass), the committed conv state, the previous pass's raw rows, this pass's rows, gate inputs
     float* S = a.gdn_state + ((size_t)hd * 128 + dv0 + w * 4) * 128 + lane * 4;
     float4 st[4];
 #pragma unroll
     for (int r = 0; r < 4; r++) st[r] = *(const float4*)(S + (size_t)r * 128);
-
-    // ---- stage the replayed rows (conv outputs + gates of the previous pass)
     const float* pqc = a.pend_qkvc + (size_t)prev * VMAX * C;
-    const float* pab = a.pend_ab + (size_t)prev * VMAX * 2 * NV;
-    {  // all replay loads in flight together
-        float lq[VMAX], lk[VMAX], lv[VMAX];
+    float lq[VMAX], lk[VMAX], lv[VMAX];
 #pragma unroll
-        for (int r = 0; r < VMAX; r++)
-            if (r < rn) {
-                lq[r] = pqc[(size_t)r * C + cq];
-                lk[r] = pqc[(size_t)r * C + ck];
-                lv[r] = has_v ? pqc[(size_t)r * C + cv] : 0.0f;
-            }
-#pragma unroll
-        for (int r = 0; r < VMAX; r++)
-            if (r < rn) {
-                sm.q[r][tid] = lq[r];
-                sm.k[r][tid] = lk[r];
-                if (has_v) sm.v[r][tid] = lv[r];
-            }
-    }
-    if (tid < rn) gates(pab[(size_t)tid * 2 * NV + hd], pab[(size_t)tid * 2 * NV + NV + hd], ea, dtb, sm.g[tid], sm.beta[tid]);
-    if (tid >= 32 && tid - 32 < T) {
-        int t = tid - 32;
-        const float* ab = a.pend_ab + ((size_t)par * VMAX + t) * 2 * NV;
-        gates(ab[hd], ab[NV + hd], ea, dtb, sm.g[rn + t], sm.beta[rn + t]);
-    }
-
-    // ---- conv: commit the previous pass's rows, then this pass's rows
+    for (int r = 0; r < VMAX; r++)
+        if (r < rn) {
+            lq[r] = pqc[(size_t)r * C + cq];
+            lk[r] = pqc[(size_t)r * C + ck];
+            lv[r] = has_v ? pqc[(size_t)r * C + cv] : 0.0f;
+        }
     const float* cs_in = a.conv_state + (size_t)prev * 3 * C;  // committed state lives at the previous parity
-    float* cs_out = a.conv_state + (size_t)par * 3 * C;
     const float* pq = a.pend_qkv + (size_t)prev * VMAX * C;
-    float* pq_out = a.pend_qkv + (size_t)par * VMAX * C;
-    float* pqc_out = a.pend_qkvc + (size_t)par * VMAX * C;
     const int ld = C + NV * 128;
+    // rows rn..rn+2 of [state(3); previous raw rows], then this pass's rows
     float rq[3 + VMAX], rk[3 + VMAX], rv[3 + VMAX];
-    {
-        float oq[3], ok[3], ov[3];
 #pragma unroll
-        for (int j = 0; j < 3; j++) {
-            oq[j] = cs_in[(size_t)j * C + cq];
-            ok[j] = cs_in[(size_t)j * C + ck];
-            ov[j] = has_v ? cs_in[(size_t)j * C + cv] : 0.0f;
-        }
-        // rows rn..rn+2 of [state(3); previous raw rows]
-#pragma unroll
-        for (int j = 0; j < 3; j++) {
-            int kk = rn + j;
-            rq[j] = kk < 3 ? oq[kk] : pq[(size_t)(kk - 3) * C + cq];
-            rk[j] = kk < 3 ? ok[kk] : pq[(size_t)(kk - 3) * C + ck];
-            rv[j] = kk < 3 ? ov[kk] : (has_v ? pq[(size_t)(kk - 3) * C + cv] : 0.0f);
-        }
+    for (int j = 0; j < 3; j++) {
+        const int kk = rn + j;
+        const float* src = kk < 3 ? cs_in + (size_t)kk * C : pq + (size_t)(kk - 3) * C;
+        rq[j] = src[cq];
+        rk[j] = src[ck];
+        rv[j] = has_v ? src[cv] : 0.0f;
     }
 #pragma unroll
     for (int t = 0; t < VMAX; t++)
@@ -143,6 +115,28 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
             rk[3 + t] = a.qkvz[(size_t)t * ld + ck];
             rv[3 + t] = has_v ? a.qkvz[(size_t)t * ld + cv] : 0.0f;
         }
+    float ga = 0.0f, gb = 0.0f;
+    if (tid < rn + T) {
+        const float* ab = tid < rn ? a.pend_ab + ((size_t)prev * VMAX + tid) * 2 * NV
+                                   : a.pend_ab + ((size_t)par * VMAX + tid - rn) * 2 * NV;
+        ga = ab[hd];
+        gb = ab[NV + hd];
+    }
+
+    // ---- stage the replayed rows and the gates of every row
+#pragma unroll
+    for (int r = 0; r < VMAX; r++)
+        if (r < rn) {
+            sm.q[r][tid] = lq[r];
+            sm.k[r][tid] = lk[r];
+            if (has_v) sm.v[r][tid] = lv[r];
+        }
+    if (tid < rn + T) gates(ga, gb, ea, dtb, sm.g[tid], sm.beta[tid]);
+
+    // ---- conv: commit the previous pass's rows, record this pass's raw rows
+    float* cs_out = a.conv_state + (size_t)par * 3 * C;
+    float* pq_out = a.pend_qkv + (size_t)par * VMAX * C;
+    float* pqc_out = a.pend_qkvc + (size_t)par * VMAX * C;
     if (qk_writer) {
 #pragma unroll
         for (int j = 0; j < 3; j++) {
@@ -166,7 +160,9 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
     // conv + SiLU; q, k rows then get the per-head RMS norm scaled by 1/128 and 1/sqrt(128)
     float cq_[VMAX], ck_[VMAX];
 #pragma unroll
-    for (int t = 0; t < VMAX; t++)
+    for (int t = 0; t < VMAX; t++) {
+        cq_[t] = 0.0f;
+        ck_[t] = 0.0f;
         if (t < T) {
             float aq = 0.0f, ak = 0.0f, av = 0.0f;
 #pragma unroll
@@ -183,23 +179,37 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
                 pqc_out[(size_t)t * C + cv] = vv;
             }
         }
+    }
+    {   // row sums of squares, q rows in slots 0..15 and k rows in 16..31: halving butterfly, lane l holds slot l
+        float v[32];
 #pragma unroll
-    for (int t = 0; t < VMAX; t++)
-        if (t < T) {
-            float sq = warp_sum(cq_[t] * cq_[t]), sk = warp_sum(ck_[t] * ck_[t]);
-            if (lane == 0) {
-                sm.red[0][w][t] = sq;
-                sm.red[1][w][t] = sk;
+        for (int t = 0; t < VMAX; t++) {
+            v[t] = cq_[t] * cq_[t];
+            v[VMAX + t] = ck_[t] * ck_[t];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < o; j++) {
+                const float send = up ? v[j] : v[j + o];
+                const float keep = up ? v[j + o] : v[j];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
             }
         }
+        sm.red[w][lane] = v[0];
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const float ss = ((sm.red[0][tid] + sm.red[1][tid]) + sm.red[2][tid]) + sm.red[3][tid];
+        sm.rs[tid] = rsqrtf(ss / 128.0f + EPS_G) * (tid < VMAX ? (1.0f / 128.0f) : 0.08838834764831845f);
+    }
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < VMAX; t++)
         if (t < T) {
-            float sq = ((sm.red[0][0][t] + sm.red[0][1][t]) + sm.red[0][2][t]) + sm.red[0][3][t];
-            float sk = ((sm.red[1][0][t] + sm.red[1][1][t]) + sm.red[1][2][t]) + sm.red[1][3][t];
-            float q = cq_[t] * rsqrtf(sq / 128.0f + EPS_G) * (1.0f / 128.0f);
-            float k = ck_[t] * rsqrtf(sk / 128.0f + EPS_G) * 0.08838834764831845f;
+            const float q = cq_[t] * sm.rs[t];
+            const float k = ck_[t] * sm.rs[VMAX + t];
             sm.q[rn + t][tid] = q;
             sm.k[rn + t][tid] = k;
             if (qk_writer) {
@@ -209,20 +219,47 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
         }
     __syncthreads();
 
-    // ---- gated delta rule: replay (commit), then this pass's rows
-    float o[4], vv[4];
+    // ---- gated delta rule: replay (commit), then this pass's rows. Per step one reduction round: with u = S.k and
+    // z = S.q of the state before the step, S' = g S + delta k with delta = (v - g u) beta, and the output
+    // S'.q = g z + delta (k.q) (kernels.metal:607-620 computes the same quantities in sequence).
     for (int r = 0; r < rn + T; r++) {
-        float4 q = *(const float4*)&sm.q[r][lane * 4];
-        float4 k = *(const float4*)&sm.k[r][lane * 4];
+        const float4 q = *(const float4*)&sm.q[r][lane * 4];
+        const float4 k = *(const float4*)&sm.k[r][lane * 4];
+        const float4 v4 = *(const float4*)&sm.v[r][w * 4];
+        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+        const float g = sm.g[r], beta = sm.beta[r];
+        float u[4], z[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) vv[i] = sm.v[r][w * 4 + i];
-        gdn_step4(st, q, k, vv, sm.g[r], sm.beta[r], o);
+        for (int i = 0; i < 4; i++) {
+            u[i] = st[i].x * k.x + st[i].y * k.y + st[i].z * k.z + st[i].w * k.w;
+            z[i] = st[i].x * q.x + st[i].y * q.y + st[i].z * q.z + st[i].w * q.w;
+        }
+        float kq = k.x * q.x + k.y * q.y + k.z * q.z + k.w * q.w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                u[i] += __shfl_xor_sync(0xffffffffu, u[i], o);
+                z[i] += __shfl_xor_sync(0xffffffffu, z[i], o);
+            }
+            kq += __shfl_xor_sync(0xffffffffu, kq, o);
+        }
+        float o4[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float delta = (vv[i] - g * u[i]) * beta;
+            st[i].x = g * st[i].x + k.x * delta;
+            st[i].y = g * st[i].y + k.y * delta;
+            st[i].z = g * st[i].z + k.z * delta;
+            st[i].w = g * st[i].w + k.w * delta;
+            o4[i] = g * z[i] + delta * kq;
+        }
         if (r == rn - 1) {
 #pragma unroll
             for (int i = 0; i < 4; i++) *(float4*)(S + (size_t)i * 128) = st[i];
         }
         if (r >= rn && lane < 4) {
-            float ov = lane == 0 ? o[0] : (lane == 1 ? o[1] : (lane == 2 ? o[2] : o[3]));
+            const float ov = lane == 0 ? o4[0] : (lane == 1 ? o4[1] : (lane == 2 ? o4[2] : o4[3]));
             a.y[(size_t)(r - rn) * NV * 128 + hd * 128 + dv0 + w * 4 + lane] = ov;
         }
     }
