@@ -100,6 +100,22 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def max_over_ranks(x, dist, device):
+    """The largest of a per-rank float over all ranks (the device time of the slowest replica); x itself at N=1."""
+    if dist is None:
+        return float(x)
+    import torch
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(ws, units_per_rank, seconds_max):
+    """Whole-job throughput of ws replicas that each processed units_per_rank in at most seconds_max."""
+    return ws * units_per_rank / seconds_max
+
+
 def cpu_baseline(cfg, ts, steps, warmup, quiet=False):
     """The oracle (C++ scalar restatement, OpenMP) on the host cores: one verify pass of 9 rows (planted drafts,
     100% accept) of the full model per step, from an empty context (a bounded sample of the workload)."""
@@ -244,14 +260,11 @@ def main():
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
     ck = clocks.stop()
-    ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
     if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
         dist.barrier()
     tokens_step = passes * T  # generated per request after the prefill's first token
-    value = ws * tokens_step * args.steps / (ms / 1000)
+    value = whole_job_rate(ws, tokens_step * args.steps, ms / 1000)
 
     # verify-pass roofline: the pass at the mean decode context, CUDA events on the model stream
     bytes_pass = m.pass_bytes(T)  # at the restored length; grows by KV only
@@ -271,8 +284,8 @@ def main():
     m.enqueue_passes(T, GEN - 1, 1)
     ev3.record(stream)
     m.sync()
-    rnd_ms = ev2.elapsed_time(ev3)
-    rnd_tok_s = (GEN - 1) / (rnd_ms / 1000)
+    rnd_ms = max_over_ranks(ev2.elapsed_time(ev3), dist, "cuda")
+    rnd_tok_s = whole_job_rate(ws, GEN - 1, rnd_ms / 1000)
 
     # e2e through the public decode loop (host buffers, H2D drafts + D2H accept per round)
     e2e_steps = max(1, min(args.steps, 5))
@@ -286,8 +299,9 @@ def main():
         out, st = m.decode(first, mode=_lib.DRAFT_PLANTED, planted=planted_host, max_tokens=gen_tokens, draft_max=8)
         n_tok += len(out) - 1
         rounds += st.verify_calls
-    e2e_s = time.perf_counter() - w0
-    e2e = {"value": ws * n_tok / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": int(rounds / e2e_steps * (T * 4 + 16)),
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - w0, dist, "cuda")
+    e2e = {"value": whole_job_rate(ws, n_tok, e2e_s), "unit": "tok/s", "h2d_bytes_per_step": int(rounds / e2e_steps * (T * 4 + 16)),
            "d2h_bytes_per_step": int(rounds / e2e_steps * 8), "steps": e2e_steps,
            "path": "bcu_decode (C ABI) planted drafts, host loop"}
 
@@ -301,12 +315,12 @@ def main():
                    "tokens_per_step": tokens_step, "parallelism": f"replicas x{ws}",
                    "l2": "inputs larger than L2 (1.6 GB of weights streamed per pass)"},
         "e2e": e2e,
-        "gpu_launches": launches * passes * args.steps,
+        "gpu_launches": ws * launches * passes * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": None, "kernel": "verify pass (T=9 graph: all kernels of one pass)",
                      "bytes_per_launch": bytes_pass, "ms_per_launch": pass_ms,
                      "frac_of_8TBs": achieved / 8000.0, "peak_source": "MEASURED_PEAKS.json" if pk else "fallback"},
-        "random_drafts": {"tok_s": ws * rnd_tok_s, "ms_per_pass": rnd_ms / (GEN - 1)},
+        "random_drafts": {"tok_s": rnd_tok_s, "ms_per_pass": rnd_ms / (GEN - 1)},
         "clocks": ck, "wall_s": wall, "setup_s": t_load,
     }
     if rank == 0 and not args.no_cpu and ws == 1:
