@@ -53,6 +53,24 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_
     return false;
 }
 
+// ----------------------------------------------------------------------------------------------- grid counters
+// Count one arrival (release: this thread's earlier writes, and those of the CTA ordered before it by a barrier, are
+// visible to whoever observes the count).
+__device__ __forceinline__ void arrive_release(unsigned* c) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
+}
+// Bounded wait until *c >= target (acquire). Only for CTAs of one grid that are all resident at once; false when it
+// gives up (about a second).
+__device__ __forceinline__ bool spin_until_geq(const unsigned* c, unsigned target, uint32_t limit = (1u << 20)) {
+    for (uint32_t i = 0; i < limit; i++) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+        if (v >= target) return true;
+        __nanosleep(32);
+    }
+    return false;
+}
+
 // ----------------------------------------------------------------------------------------------- clusters
 // Barrier halves over every thread of the cluster (all threads of a CTA execute both, arrive first).
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
@@ -77,7 +95,16 @@ __device__ __forceinline__ void bulk_s2peer(uint32_t dst_cluster, const void* sr
         "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
         : "memory");
 }
+// 1-D bulk copy of this CTA's shared memory to global memory (bulk async-group completion). src/dst 16-byte
+// aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until this thread's committed bulk copies are complete (their writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Waits until the source shared memory of this thread's committed bulk copies has been read.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) reads.

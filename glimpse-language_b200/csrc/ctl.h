@@ -6,7 +6,7 @@ namespace bcu {
 
 // Device error codes written to Ctl::err (bitwise OR). A kernel that gives up a bounded wait sets a bit and returns;
 // the host maps a non-zero value to BCU_ERR_TIMEOUT / BCU_ERR_CUDA.
-enum : int { ERR_MBAR_TIMEOUT = 1, ERR_BAD_TOKEN = 2, ERR_CTX_FULL = 4 };
+enum : int { ERR_MBAR_TIMEOUT = 1, ERR_BAD_TOKEN = 2, ERR_CTX_FULL = 4, ERR_SPIN_TIMEOUT = 8 };
 
 constexpr int VMAX = 16;   // largest pass (rows) the kernels take
 constexpr int NSPLIT_ATTN = 16;  // key splits per (kv head, query row) in attention

@@ -28,7 +28,7 @@ size_t ternary_sb_bytes(int O, int K, int group);
 // Converts MLX-packed device arrays (u32 [O][K/16], fp16 [O][K/group] scales, optional biases) into the layout above.
 void repack_ternary(const uint32_t* w_mlx, const uint16_t* s, const uint16_t* b, int O, int K, int group,
                     void* codes, uint32_t* sb, cudaStream_t st);
-void plan_ternary(TernaryMat& m, int num_sms);
+void plan_ternary(TernaryMat& m, int num_sms, int min_kslice = 512);
 
 // Where a GEMV's activation rows come from. Each CTA builds the tensor-core operand of its own K-slice in shared
 // memory: the pre-rotation value x_k of the mode, times the input's signs, Walsh-Hadamard transformed in blocks of
@@ -56,9 +56,29 @@ struct ActSrc {
     const Ctl* ctl = nullptr;      // EMBED: token ids
     float* h_out = nullptr;        // EMBED: residual rows (written by CTA 0)
     int HB = 512, vocab = 0;
+    // != null: the operand was built by the previous kernel (OpOut of that kernel) in this buffer; x, w and signs
+    // are then not read by the GEMV CTAs (the a/b gate CTAs still read x, w, ss). NORM: the per-token RMS scale is
+    // applied to the outputs (from ss) because the producer leaves it out.
+    const uint8_t* opbuf = nullptr;
+};
+
+// Where a kernel writes the activation operand of the GEMV that follows it: region (block b, tile nt) at
+// buf + (b * 4 + nt) * region bytes, a block being `HB` consecutive inputs of the next GEMV (the region layout of
+// ternary.cu). The producing kernel applies the next GEMV's producer (mode; NORM without the per-token RMS scale),
+// its signs and the Walsh-Hadamard transform.
+struct OpOut {
+    uint8_t* buf = nullptr;        // null: no operand produced
+    int mode = ACT_NORM;           // NORM (x = h), SWIGLU (x = gate/up halves), GATED, GATE
+    int K = 0, group = 64, HB = 512;
+    const float* w = nullptr;      // NORM: norm weight [K]; GATED: head norm weight [128]
+    const float* signs = nullptr;  // [K] or null
+    const float* x2 = nullptr;     // GATED: z rows (x2 + t * ld2 + off2); GATE: gate rows (q projection, ld2)
+    int ld2 = 0, off2 = 0;
+    unsigned* counters = nullptr;  // per block arrival counts (zero between launches)
 };
 
 struct GemvOut {
+    OpOut op;                    // the next GEMV's operand, built from the final rows (NORM or SWIGLU)
     float* out = nullptr;        // [T][O]
     int add = 0;                 // 1: out += W.x (residual)
     float* ss_out = nullptr;     // != null: [O/128][VMAX] sums of squares of the new out rows (next RMSNorm)
@@ -79,6 +99,8 @@ struct AbArgs {
 // y[T][O] (+)= W . rotate(x) for T <= 16 rows.
 void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const GemvOut& o, const AbArgs* ab,
                          cudaStream_t st);
+// Whether every CTA of the GEMV fits on the GPU at once (needed when it produces the next operand).
+bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms);
 
 // ------------------------------------------------------------------------------------------------ GatedDeltaNet
 // One launch per GDN layer: conv (with the deferred conv-state commit) + gated delta rule (with the deferred replay)
@@ -97,8 +119,11 @@ struct GdnArgs {
     float* pend_ab;        // [2][VMAX][2NV] gate inputs (replay; written by the qkvz GEMV)
     float* y;              // [T][NV*128]
     int C, NK, NV, T;
+    OpOut op;              // the output GEMV's operand (GATED), built by the CTA that completes each block
 };
 void launch_gdn_layer(const GdnArgs& a, cudaStream_t st);
+// Whether all CTAs of the layer kernel fit on the GPU at once (needed when it produces the next operand).
+bool gdn_coresident(const GdnArgs& a, int num_sms);
 
 // Standalone verify step with rollback (graded config 2).
 void launch_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
@@ -120,6 +145,7 @@ struct AttnArgs {
     unsigned* counters;    // [VMAX][KV] zero between launches
     float* out;            // [T][H*256]
     int H, KV, rot, T, ld, ctx;
+    OpOut op;              // the output GEMV's operand (GATE), each row's columns written by its merging CTAs
 };
 void launch_attn(const AttnArgs& a, cudaStream_t st);
 

@@ -79,6 +79,9 @@ struct bcu_model {
     float* partial = nullptr;
     unsigned* counters = nullptr;
     unsigned* head_counter = nullptr;
+    uint8_t* opbuf[2] = {nullptr, nullptr};  // GEMV operands built by the kernel before each GEMV (alternating)
+    unsigned* op_counters = nullptr;         // per-block arrival counts of the operand producers
+    size_t opbuf_bytes = 0;
     float* pv = nullptr;
     int* pi = nullptr;
     int head_grid = 0;

@@ -3,6 +3,7 @@
 // rows (T = 1 plain step, 2..16 verify, 16-row prefill chunks) is one CUDA graph captured once and replayed; its
 // parameters (input ids, KV offset, replay count, parity) live in a device control block, as the Vulkan backend's
 // recorded command buffers read per-step parameter slots (gpu_vk.rs:651-666, 778-838).
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -10,6 +11,7 @@
 #include <thread>
 
 #include "model.h"
+#include "operand.cuh"
 
 using namespace bcu;
 
@@ -176,7 +178,7 @@ bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* o
         CK(cudaGetLastError());
         row += p.O;
     }
-    plan_ternary(tm, m->num_sms);
+    plan_ternary(tm, m->num_sms, m->c.hadamard);
     out->m = tm;
     out->signs = nullptr;
     if (m->c.has_signs) {
@@ -230,13 +232,32 @@ GdnArgs gdn_args(bcu_model* m, const Layer& L, int T) {
 }
 
 // The kernels of one pass of T rows, in order (Text::encode_embed + encode_layers + encode_head, model.rs:641-985):
-// per layer the mixer's input GEMV (norm + rotation fused in; the GDN a/b gates ride along), the mixer core (GDN conv +
-// recurrence, or attention), the mixer's output GEMV (gated norm / gate + rotation fused in, residual add), the MLP
-// gate/up GEMV (norm + rotation fused in) and the down GEMV (SwiGLU + rotation fused in, residual add); then the head.
+// per layer the mixer's input GEMV (norm + rotation; the GDN a/b gates ride along), the mixer core (GDN conv +
+// recurrence, or attention), the mixer's output GEMV (gated norm / gate + rotation, residual add), the MLP gate/up
+// GEMV (norm + rotation) and the down GEMV (SwiGLU + rotation, residual add); then the head. Except for the first
+// GEMV (embedding rows), each GEMV's rotated operand is built once by the kernel before it (its epilogue: the down /
+// mixer-output / gate-up GEMV, the GDN layer, attention) into one of two alternating buffers.
 void enqueue_pass(bcu_model* m, int T) {
     const bcu_config& c = m->c;
     const int NT = (2 * T + 7) / 8, d = c.hidden;
     cudaStream_t st = m->st;
+    int nbuf = 0;
+    const uint8_t* pending = nullptr;  // the operand the last producer built for the next GEMV
+    auto producer = [&](OpOut& op, int mode, int K, const float* w, const float* signs) {
+        op.buf = m->opbuf[nbuf++ & 1];
+        op.mode = mode;
+        op.K = K;
+        op.group = c.group_size;
+        op.HB = c.hadamard;
+        op.w = w;
+        op.signs = signs;
+        op.counters = m->op_counters;
+        pending = op.buf;
+    };
+    auto consume = [&](ActSrc& s) {
+        s.opbuf = pending;
+        pending = nullptr;
+    };
     GemvOut store, resid;
     store.partial = resid.partial = m->partial;
     store.counters = resid.counters = m->counters;
@@ -259,6 +280,7 @@ void enqueue_pass(bcu_model* m, int T) {
         in.h_out = m->h;
         in.HB = c.hadamard;
         in.vocab = c.vocab;
+        consume(in);
         GemvOut mixo = store;
         mixo.out = m->mix;
         ActSrc out;
@@ -272,7 +294,18 @@ void enqueue_pass(bcu_model* m, int T) {
             ab.ctl = m->ctl;
             ab.nv = c.lin_v_heads;
             launch_ternary_gemv(L.mix_in.m, in, T, mixo, &ab, st);
-            launch_gdn_layer(gdn_args(m, L, T), st);
+            GdnArgs g = gdn_args(m, L, T);
+            GdnArgs probe = g;
+            probe.op.buf = m->opbuf[0];
+            probe.op.HB = c.hadamard;
+            probe.op.group = c.group_size;
+            if (gdn_coresident(probe, m->num_sms)) {
+                producer(g.op, ACT_GATED, c.lin_v_heads * 128, L.gnorm, L.mix_out.signs);
+                g.op.x2 = m->mix;
+                g.op.ld2 = m->C + m->gw;
+                g.op.off2 = m->C;
+            }
+            launch_gdn_layer(g, st);
             out.mode = ACT_GATED;
             out.x = m->y;
             out.x2 = m->mix;
@@ -298,26 +331,44 @@ void enqueue_pass(bcu_model* m, int T) {
             a.T = T;
             a.ld = 2 * m->aw + 2 * m->kvw;
             a.ctx = c.ctx;
+            if ((c.heads / c.kv_heads) * 256 % c.hadamard == 0) {  // each kv head's rows cover whole blocks
+                producer(a.op, ACT_GATE, m->aw, nullptr, L.mix_out.signs);
+                a.op.x2 = m->mix;
+                a.op.ld2 = a.ld;
+            }
             launch_attn(a, st);
             out.mode = ACT_GATE;
             out.x = m->y;
             out.x2 = m->mix;
             out.ld2 = a.ld;
         }
-        launch_ternary_gemv(L.mix_out.m, out, T, resid, nullptr, st);
+        consume(out);
+        GemvOut ro = resid;
+        if (gemv_coresident(L.mix_out.m, T, 0, c.hadamard, m->num_sms))
+            producer(ro.op, ACT_NORM, d, L.post_norm, L.gu.signs);
+        launch_ternary_gemv(L.mix_out.m, out, T, ro, nullptr, st);
         ActSrc post = in;
         post.mode = ACT_NORM;
         post.w = L.post_norm;
         post.signs = L.gu.signs;
+        consume(post);
         GemvOut guo = store;
         guo.out = m->gubuf;
+        if (gemv_coresident(L.gu.m, T, 0, c.hadamard, m->num_sms))
+            producer(guo.op, ACT_SWIGLU, c.intermediate, nullptr, L.down.signs);
         launch_ternary_gemv(L.gu.m, post, T, guo, nullptr, st);
         ActSrc sw;
         sw.mode = ACT_SWIGLU;
         sw.x = m->gubuf;
         sw.signs = L.down.signs;
         sw.HB = c.hadamard;
-        launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st);
+        consume(sw);
+        GemvOut dno = resid;
+        if (li + 1 < m->layers.size() && gemv_coresident(L.down.m, T, 0, c.hadamard, m->num_sms)) {
+            const Layer& N = m->layers[li + 1];
+            producer(dno.op, ACT_NORM, d, N.in_norm, N.mix_in.signs);
+        }
+        launch_ternary_gemv(L.down.m, sw, T, dno, nullptr, st);
     }
     HeadArgs ha{};
     ha.ctl = m->ctl;
@@ -363,6 +414,7 @@ bcu_status read_ctl(bcu_model* m) {
         int e = m->h_out->err;
         cudaMemsetAsync(&m->ctl->err, 0, 4, m->st);
         if (e & ERR_MBAR_TIMEOUT) return fail(m, BCU_ERR_TIMEOUT, "a kernel gave up waiting for its bulk copies");
+        if (e & ERR_SPIN_TIMEOUT) return fail(m, BCU_ERR_TIMEOUT, "a kernel gave up waiting for the other CTAs of its grid");
         if (e & ERR_BAD_TOKEN) return fail(m, BCU_ERR_ARG, "token id out of vocabulary range");
         if (e & ERR_CTX_FULL) return fail(m, BCU_ERR_STATE, "KV context full");
         return fail(m, BCU_ERR_CUDA, "device error " + std::to_string(e));
@@ -589,6 +641,14 @@ bcu_status bcu_finalize(bcu_model* m) {
     TRY(dmalloc(m, &m->counters, (size_t)maxrb * 4));
     m->head_grid = 2 * m->num_sms;
     TRY(dmalloc(m, &m->head_counter, 4));
+    {
+        // operand buffers: [K / HB blocks][4 tiles][region] for the widest GEMV input
+        const int kmax = std::max(std::max(c.hidden, c.intermediate), std::max(m->aw, c.lin_v_heads * 128));
+        m->opbuf_bytes = (size_t)(kmax / c.hadamard) * 4 * op_region_bytes(c.hadamard, c.group_size);
+        TRY(dmalloc(m, &m->opbuf[0], m->opbuf_bytes));
+        TRY(dmalloc(m, &m->opbuf[1], m->opbuf_bytes));
+        TRY(dmalloc(m, &m->op_counters, 512 * 4));
+    }
     TRY(dmalloc(m, &m->pv, (size_t)m->head_grid * VMAX * 4));
     TRY(dmalloc(m, &m->pi, (size_t)m->head_grid * VMAX * 4));
     TRY(dmalloc(m, &m->ctl, sizeof(Ctl)));
@@ -610,6 +670,7 @@ bcu_status bcu_reset(bcu_model* m) {
     CK(cudaMemsetAsync(m->gdn, 0, (size_t)m->n_gdn * NV * 128 * 128 * 4, m->st));
     CK(cudaMemsetAsync(m->conv, 0, (size_t)m->n_gdn * 2 * 3 * m->C * 4, m->st));
     CK(cudaMemsetAsync(m->attn_counters, 0, (size_t)VMAX * m->c.kv_heads * 4, m->st));
+    CK(cudaMemsetAsync(m->op_counters, 0, 512 * 4, m->st));
     Ctl z;
     memset(&z, 0, sizeof(z));
     memcpy(m->h_out, &z, sizeof(Ctl));
@@ -631,7 +692,8 @@ void bcu_destroy(bcu_model* m) {
     for (auto& kv : m->staged) cudaFree(kv.second.dev);
     void* bufs[] = {m->arena, m->gdn, m->conv, m->kc, m->vc, m->pend_qkv, m->pend_qkvc, m->pend_ab, m->h,
                     m->mix, m->gubuf, m->y, m->apart, m->ssbuf, m->attn_counters, m->logits,
-                    m->partial, m->counters, m->head_counter, m->pv, m->pi, m->ctl, m->planted_dev};
+                    m->partial, m->counters, m->head_counter, m->pv, m->pi, m->ctl, m->planted_dev,
+                    m->opbuf[0], m->opbuf[1], m->op_counters};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (m->h_in) cudaFreeHost(m->h_in);

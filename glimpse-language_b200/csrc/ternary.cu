@@ -1,31 +1,33 @@
-// ternary.cu — tensor-core ternary verify GEMV for T <= 16 rows with the activation producer fused in front (the
-// reference's qmvxm / qmvx / qmv_cm / qmvr / qmv4, kernels.metal:275-404 and 664-709, kernels/qmvx.comp,
-// kernels/qmv_cm.comp, and the rotation kernels of kernels.metal:118-226 that feed them).
+// ternary.cu — tensor-core ternary verify GEMV for T <= 16 rows (the reference's qmvxm / qmvx / qmv_cm / qmvr / qmv4,
+// kernels.metal:275-404 and 664-709, kernels/qmvx.comp, kernels/qmv_cm.comp, with the rotation kernels of
+// kernels.metal:118-226 that feed them).
 //
 // Why tensor cores at batch 1: a T = 9 verify does 9 multiply-adds per 2-bit weight. At the HBM rate of ~21 T
 // weights/s that is ~190 T FMA/s, five times what the CUDA cores can issue, so the products go to mma.m16n8k16 and
 // the CUDA cores only decode: per pair of weights one LOP3 ((w & mask) | 0x6400 gives fp16 1024 + c*4^j) and one
-// HFMA2 (x s, - 1024 s gives exactly c*s*4^j). The activation operand carries 4^-j and a per-(CTA, row) power of
+// HFMA2 (x s, - 1024 s gives exactly c*s*4^j). The activation operand carries 4^-j and a per-(token, block) power of
 // two and is split into fp16 hi + lo columns, so products are exact and sums fp32-accurate. The bias term
 // sum_g b_g * sum_k x_k is one more k16 MMA step per warp (A = 64 b, B = group sums / 64). Every output's reduction
 // order is fixed and independent of T: a row's result is bit-identical whether it is verified alone or among 16.
 //
 // CTA = 128 rows x kslice codes (8 warps = 2 row groups of 64 x 4 k-quarters). Before waiting on the previous kernel
 // (programmatic dependent launch) one thread streams the CTA's codes and scale/bias tiles into shared memory with
-// cp.async.bulk; after the wait every warp builds the operand of its tokens from the source rows (norm / SwiGLU /
-// gated norm / gate, signs, Walsh-Hadamard transform in registers). Split-K partials are summed in a fixed order by
-// the last CTA of each row block, which also applies the residual add and the sums of squares the next norm needs.
-#include <cooperative_groups.h>
+// cp.async.bulk. After the wait the activation operand (operand.cuh) comes either from the previous kernel, which
+// built it once for the whole GEMV (one more bulk copy), or is built here from the source rows (embedding rows,
+// standalone inputs). Split-K partials are summed in a fixed order by the last CTA of each row block, which applies
+// the residual add and the sums of squares the next norm needs and, when asked, contributes to the next GEMV's
+// operand: the CTA that completes a Hadamard block of the next GEMV's input builds the block's regions.
 #include <cstdio>
 #include "common.cuh"
 #include "kernels.h"
-
-namespace cg = cooperative_groups;
+#include "operand.cuh"
 
 namespace bcu {
 
 constexpr float EPS_T = 1e-6f;
-constexpr int GEMV_HDR = 384;  // shared-memory header: mbarrier at 0, exponents [16][4] at 128
+// shared-memory header: mbarriers at 0 (codes) and 8 (operand), per-token RMS scales [16] at 16, exponents [16][4]
+// at 128
+constexpr int GEMV_HDR = 384;
 
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
     cudaLaunchConfig_t cfg = {};
@@ -119,11 +121,13 @@ void repack_ternary(const uint32_t* w_mlx, const uint16_t* s, const uint16_t* b,
 // K-slice plan: the longest slice (fewest splits) that still puts CTAs on at least ~45% of the SMs. Fewer splits save
 // the split-K reduction (a dependent global round trip) and the duplicated operand build; one CTA per SM gets the
 // SM's whole issue rate for the decode, so ~70 CTAs of 2048-code slices finish as fast as ~140 of 1024.
-void plan_ternary(TernaryMat& m, int num_sms) {
+// min_kslice: slices never split a Hadamard block of an operand built by the previous kernel (its regions cover
+// whole blocks).
+void plan_ternary(TernaryMat& m, int num_sms, int min_kslice) {
     int rb = m.O / 128;
     int best = 0;
     for (int ks : {2048, 1024, 512}) {
-        if (m.K % ks) continue;
+        if (m.K % ks || (best && ks < min_kslice)) continue;
         best = ks;
         if (rb * (m.K / ks) * 20 >= num_sms * 9) break;
     }
@@ -139,10 +143,8 @@ struct GemvParams {
     GemvOut o;
     AbArgs ab;
     int O, K, group, kslice, nsplit, T, n_main, ab_rows;
-    int nrb;  // row blocks; CTA = ks * nrb + rb, so a cluster holds consecutive row blocks of one K-slice
+    int nrb;  // row blocks; CTA = ks * nrb + rb
 };
-
-__device__ __forceinline__ float sigm(float z) { return 1.0f / (1.0f + expf(-z)); }
 
 __device__ __forceinline__ uint32_t resolve_id(const Ctl* ctl, int t) {
     int feed = ctl->in.feed;
@@ -242,165 +244,233 @@ __device__ __forceinline__ void act_values(const ActSrc& s, int t, int base, int
     }
 }
 
-__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }  // |e| <= 126
 
-// Activation operand layout in shared memory: one region per (column tile nt of 4 tokens, block b of the K-slice),
-// region index nt * nb + b. A block is the part of a Walsh-Hadamard block inside the slice (sb = min(HB, kslice)
-// elements). Region = sb/16 main k16 steps of B fragments (256 B each: 4 tokens x fp16 hi, lo columns), then the
-// block's bias k16 steps (group sums, group-in-block = k), then the power-of-two exponents of its 4 tokens (16 B).
-__host__ __device__ inline int op_bias_steps(int sb, int group) { return (sb / group + 15) / 16; }
-__host__ __device__ inline int op_region_bytes(int sb, int group) { return (sb / 16 + op_bias_steps(sb, group)) * 256 + 16; }
+// ------------------------------------------------------------------------------------------------ operand
+// Raw source values of one token for elements blk0 + lane + 32 e (every load of the token issued together).
+template <int VPL>
+struct RawTok {
+    float a[VPL], b[VPL];
+    float ss;  // NORM: this lane's part of the row's sum of squares (from the per-row-block partials)
+};
 
-// Builds token t's columns of region (t / 4, b) of K-slice ks in this CTA's shared memory (one warp). Lane l holds
-// element blk0 + l + 32 e (e < VPL = HB / 32) of the Hadamard block, the layout of fwht512 (kernels.metal:32-51), so
-// the transform's strides 1..16 run across lanes and 32.. inside the lane, in ascending order (bit-identical to an
-// in-memory radix-2 transform). Tokens t >= T write zero columns.
-template <int VPL, int GPC>
-__device__ void build_token(const GemvParams& p, int t, int b, int ks, int sbsz, uint8_t* reg, bool writer) {
-    constexpr int G = 128 / GPC, EPG = G / 32, HBe = VPL * 32, NGH = HBe / G;
+template <int VPL>
+__device__ __forceinline__ void load_raw(const ActSrc& s, int t, int blk0, int K, RawTok<VPL>& R) {
     const int lane = threadIdx.x & 31;
-    const int nsteps = sbsz / 16, nbs = op_bias_steps(sbsz, G);
-    uint32_t* rw = (uint32_t*)reg;
-    int* r_e = (int*)(reg + (nsteps + nbs) * 256);
-    const int col = (t & 3) * 2;  // hi column of the token in its tile; lo = col + 1
-    if (t >= p.T) {
-        // per k16 step the columns col, col + 1 are the 16 words [8 col, 8 col + 16)
-        for (int i = lane; i < (nsteps + nbs) * 16; i += 32) rw[(i >> 4) * 64 + col * 8 + (i & 15)] = 0u;
-        if (lane == 0) r_e[t & 3] = 0;
-        return;
-    }
-    const ActSrc& s = p.src;
-    const int K = p.K, kslice = p.kslice;
-    const int k0 = ks * kslice;
-    const int blk0 = HBe <= kslice ? k0 + b * HBe : (k0 / HBe) * HBe;
-    float v[VPL];
-    uint32_t id = 0;
-    float r = row_scale(s, t, K, &id, writer);
-    if (s.mode == ACT_GATED) {
-        float zz[VPL];
+    switch (s.mode) {
+        case ACT_NORM:
 #pragma unroll
-        for (int e = 0; e < VPL; e++) {
-            int k = blk0 + lane + 32 * e;
-            v[e] = s.x[(size_t)t * K + k];
-            zz[e] = s.x2[(size_t)t * s.ld2 + s.off2 + k];
-        }
-        float wv[4];  // norm weight at (lane + 32 e) & 127: period 4 in e
-#pragma unroll
-        for (int i = 0; i < 4; i++) wv[i] = s.w[(lane + 32 * i) & 127];
-#pragma unroll
-        for (int c = 0; c < VPL / 4; c++) {
-            float ss = 0.0f;
-#pragma unroll
-            for (int e = 4 * c; e < 4 * c + 4; e++) ss += v[e] * v[e];
-            float rh = rsqrtf(warp_sum(ss) / 128.0f + EPS_T);
-#pragma unroll
-            for (int e = 4 * c; e < 4 * c + 4; e++) v[e] = (((zz[e] * v[e]) * rh) * wv[e & 3]) * sigm(zz[e]);
-        }
-    } else {
-        act_values<VPL>(s, t, blk0, K, r, id, v);
-    }
-    if (s.signs) {
-        float sg[VPL];
-#pragma unroll
-        for (int e = 0; e < VPL; e++) sg[e] = s.signs[blk0 + lane + 32 * e];
-#pragma unroll
-        for (int e = 0; e < VPL; e++) v[e] *= sg[e];
-    }
-    if (s.HB > 0) {  // Walsh-Hadamard transform of the block (HB = 0: the input is already rotated)
-#pragma unroll
-        for (int m = 1; m < 32; m <<= 1) {
-            bool up = (lane & m) != 0;
+            for (int e = 0; e < VPL; e++) R.a[e] = s.x[(size_t)t * K + blk0 + lane + 32 * e];
+            R.ss = 0.0f;
+            for (int i = lane; i < s.nss; i += 32) R.ss += s.ss[i * VMAX + t];
+            break;
+        case ACT_GATED:
 #pragma unroll
             for (int e = 0; e < VPL; e++) {
-                float o = __shfl_xor_sync(0xffffffffu, v[e], m);
-                v[e] = up ? o - v[e] : v[e] + o;
+                const int k = blk0 + lane + 32 * e;
+                R.a[e] = s.x[(size_t)t * K + k];
+                R.b[e] = s.x2[(size_t)t * s.ld2 + s.off2 + k];
+            }
+            break;
+        case ACT_SWIGLU:
+#pragma unroll
+            for (int e = 0; e < VPL; e++) {
+                R.a[e] = s.x[(size_t)t * 2 * K + blk0 + lane + 32 * e];
+                R.b[e] = s.x[(size_t)t * 2 * K + K + blk0 + lane + 32 * e];
+            }
+            break;
+        case ACT_GATE:
+#pragma unroll
+            for (int e = 0; e < VPL; e++) {
+                const int k = blk0 + lane + 32 * e;
+                R.a[e] = s.x[(size_t)t * K + k];
+                R.b[e] = s.x2[(size_t)t * s.ld2 + (k >> 8) * 512 + 256 + (k & 255)];
+            }
+            break;
+        default:
+            if (s.xb) {
+#pragma unroll
+                for (int e = 0; e < VPL; e++)
+                    R.a[e] = __bfloat162float(__ushort_as_bfloat16(s.xb[(size_t)t * K + blk0 + lane + 32 * e]));
+            } else {
+#pragma unroll
+                for (int e = 0; e < VPL; e++) R.a[e] = s.x[(size_t)t * K + blk0 + lane + 32 * e];
+            }
+    }
+}
+
+// The producer (RMSNorm, gated RMSNorm, SwiGLU, sigmoid gate; kernels.metal:118-226) applied to raw values; wn: NORM
+// weights of the block (VPL) or GATED head-norm weights (4, period 128).
+template <int VPL>
+__device__ __forceinline__ void transform(const ActSrc& s, int K, const RawTok<VPL>& R, const float* wn, float* v) {
+    switch (s.mode) {
+        case ACT_NORM: {
+            const float r = rsqrtf(warp_sum(R.ss) / (float)K + EPS_T);
+#pragma unroll
+            for (int e = 0; e < VPL; e++) v[e] = (R.a[e] * r) * wn[e];
+            break;
+        }
+        case ACT_GATED:
+            gated_values<VPL>(R.a, R.b, wn, v);
+            break;
+        case ACT_SWIGLU:
+#pragma unroll
+            for (int e = 0; e < VPL; e++) v[e] = (R.a[e] * R.b[e]) * sigm(R.a[e]);
+            break;
+        case ACT_GATE:
+#pragma unroll
+            for (int e = 0; e < VPL; e++) v[e] = R.a[e] * sigm(R.b[e]);
+            break;
+        default:
+#pragma unroll
+            for (int e = 0; e < VPL; e++) v[e] = R.a[e];
+    }
+}
+
+// This CTA's operand for K-slice ks, built by its own warps (sources without a producing kernel: the embedding
+// rows of the first layer, standalone inputs): warp w takes block w % nb of the slice and the token slots w / nb,
+// w / nb + 8 / nb, ...; the next token's loads are in flight while the current one is built. Regions [nb][NT].
+template <int VPL, int GPC>
+__device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int NT, uint8_t* s_op, int rsz) {
+    constexpr int HBe = VPL * 32, G = 128 / GPC;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const ActSrc& s = p.src;
+    const int K = p.K, kslice = p.kslice, T = p.T, ntok = 4 * NT;
+    const int k0 = ks * kslice;
+    const int b = warp % nb, js = 8 / nb;
+    const int blk0 = HBe <= kslice ? k0 + b * HBe : (k0 / HBe) * HBe;
+    OpGeo geo;
+    geo.sbsz = sbsz;
+    geo.e_lo = HBe <= kslice ? 0 : (k0 - blk0) / 32;
+    geo.e_hi = HBe <= kslice ? VPL : geo.e_lo + kslice / 32;
+    geo.kr0 = HBe <= kslice ? 0 : blk0 - k0;
+    geo.rotate = s.HB > 0;
+    auto region = [&](int t) { return s_op + (size_t)(b * NT + (t >> 2)) * rsz; };
+    float sg[VPL];
+    if (s.signs) {
+#pragma unroll
+        for (int e = 0; e < VPL; e++) sg[e] = s.signs[blk0 + lane + 32 * e];
+    }
+    if (s.mode == ACT_EMBED) {  // the row scale needs the whole gathered row: one token at a time
+        for (int t = warp / nb; t < ntok; t += js) {
+            if (t >= T) {
+                zero_token(t, sbsz, G, region(t));
+                continue;
+            }
+            float v[VPL];
+            uint32_t id = 0;
+            const float r = row_scale(s, t, K, &id, blockIdx.x == 0 && b == 0);
+            act_values<VPL>(s, t, blk0, K, r, id, v);
+            emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
+        }
+        return;
+    }
+    float wn[VPL];
+    if (s.mode == ACT_NORM) {
+#pragma unroll
+        for (int e = 0; e < VPL; e++) wn[e] = s.w[blk0 + lane + 32 * e];
+    } else if (s.mode == ACT_GATED) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) wn[i] = s.w[(lane + 32 * i) & 127];
+    }
+    if constexpr (VPL <= 32) {
+        RawTok<VPL> cur, nxt;
+        int t = warp / nb;
+        if (t < T) load_raw<VPL>(s, t, blk0, K, cur);
+        for (; t < ntok; t += js) {
+            const int tn = t + js;
+            if (tn < T) load_raw<VPL>(s, tn, blk0, K, nxt);
+            if (t < T) {
+                float v[VPL];
+                transform<VPL>(s, K, cur, wn, v);
+                emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
+            } else {
+                zero_token(t, sbsz, G, region(t));
+            }
+            cur = nxt;
+        }
+    } else {  // 2048-point blocks: one token's values at a time (registers)
+        for (int t = warp / nb; t < ntok; t += js) {
+            if (t < T) {
+                RawTok<VPL> cur;
+                load_raw<VPL>(s, t, blk0, K, cur);
+                float v[VPL];
+                transform<VPL>(s, K, cur, wn, v);
+                emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
+            } else {
+                zero_token(t, sbsz, G, region(t));
             }
         }
-#pragma unroll
-        for (int h = 1; h < VPL; h <<= 1)
-#pragma unroll
-            for (int e = 0; e < VPL; e++)
-                if ((e & h) == 0) {
-                    float a = v[e], c = v[e + h];
-                    v[e] = a + c;
-                    v[e + h] = a - c;
-                }
-        const float inv = VPL == 16 ? 0.044194173824159216f : (VPL == 64 ? 0.02209708691207961f : 0.03125f);
-#pragma unroll
-        for (int e = 0; e < VPL; e++) v[e] *= inv;
     }
-    // the part of the Hadamard block inside the slice: e in [e_lo, e_hi); region-relative k = kr0 + lane + 32 e
-    const int e_lo = HBe <= kslice ? 0 : (k0 - blk0) / 32;
-    const int e_hi = HBe <= kslice ? VPL : e_lo + kslice / 32;
-    const int kr0 = HBe <= kslice ? 0 : blk0 - k0;
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < VPL; e++)
-        if (e >= e_lo && e < e_hi) amax = fmaxf(amax, fabsf(v[e]));
-    amax = warp_max(amax);
-    int E = 0;
-    if (amax > 0.0f && amax < INFINITY) {
-        int ex;
-        frexpf(amax, &ex);  // amax < 2^ex
-        E = min(max(14 - ex, -60), 100);
+}
+
+// The next GEMV's operand from this GEMV's final rows (GemvOut::op), called by the CTA that finalised row block rb
+// after its output is stored. NORM: x = h, the next GEMV's input is this GEMV's output (block b = HB/128 row blocks);
+// SWIGLU: x = silu(g) u with g, u the two halves of this GEMV's rows (block b = HB/128 row blocks of each half). The
+// `need` CTAs that finalise a block's row blocks share its tokens: contributor ci builds tokens ci, ci + need, ...
+// (one warp each) once every contributor has arrived, and stores those tokens' columns of the block's regions.
+// Every CTA of the grid is resident at once (the host checks), so the bounded wait ends. NORM leaves out the
+// per-token RMS scale: the next GEMV multiplies its outputs by it (the products are linear in it).
+template <int VPL, int GPC>
+__device__ void produce_operand(const GemvParams& p, int rb, uint8_t* scratch, int* s_ok) {
+    constexpr int HBe = VPL * 32, G = 128 / GPC;
+    const OpOut& op = p.o.op;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = HBe / 128;
+    const bool swiglu = op.mode == ACT_SWIGLU;
+    const int half_rb = p.nrb / 2;
+    const int b = swiglu ? (rb % half_rb) / per : rb / per;
+    const int need = swiglu ? 2 * per : per;
+    const int ci = swiglu ? (rb / half_rb) * per + (rb % half_rb) % per : rb % per;
+    const int T = p.T, O = p.O, k0 = b * HBe;
+    unsigned* arrive = op.counters + b;
+    unsigned* done = op.counters + 256 + b;
+    __syncthreads();  // every output row of this CTA is stored
+    if (tid == 0) {
+        arrive_release(arrive);
+        *s_ok = ci < T ? spin_until_geq(arrive, (unsigned)need) : 1;
+        if (!*s_ok) atomicOr(p.o.err, ERR_SPIN_TIMEOUT);
     }
-    if (lane == 0) r_e[t & 3] = E;
-    // x * 2^E * 4^-j in fp16 hi + lo, j = (k % 32) / 8 = lane / 8; each lane stores its element's two halves
-    {
-        const int j = lane >> 3;
-        const int t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
-        const int E1 = E - 2 * j;
-        const float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
-        uint16_t* r16 = (uint16_t*)reg;
-        const int h_hi = ((col * 4 + t4) * 2 + which) * 2 + (lane & 1), h_lo = h_hi + 16;
-        const int step0 = (kr0 >> 4) + (lane >> 4);
+    __syncthreads();
+    const int t = ci + need * warp;
+    if (*s_ok && t < T) {
+        const int rsz = op_region_bytes(HBe, G);
+        const OpGeo geo{HBe, 0, VPL, 0, true};
+        float v[VPL], sg[VPL];
+        if (swiglu) {
+            float g[VPL], u[VPL];
 #pragma unroll
-        for (int e = 0; e < VPL; e++) {
-            if (e >= e_lo && e < e_hi) {
-                const float a = v[e] * f;
-                const __half h = __float2half_rn(a);
-                const __half l = __float2half_rn(a - __half2float(h));
-                r16[(step0 + 2 * e) * 128 + h_hi] = __half_as_ushort(h);
-                r16[(step0 + 2 * e) * 128 + h_lo] = __half_as_ushort(l);
+            for (int e = 0; e < VPL; e++) {
+                g[e] = __ldcg(p.o.out + (size_t)t * O + k0 + lane + 32 * e);
+                u[e] = __ldcg(p.o.out + (size_t)t * O + O / 2 + k0 + lane + 32 * e);
             }
+#pragma unroll
+            for (int e = 0; e < VPL; e++) v[e] = (g[e] * u[e]) * sigm(g[e]);
+        } else {
+            float wn[VPL];
+#pragma unroll
+            for (int e = 0; e < VPL; e++) {
+                v[e] = __ldcg(p.o.out + (size_t)t * O + k0 + lane + 32 * e);
+                wn[e] = op.w[k0 + lane + 32 * e];
+            }
+#pragma unroll
+            for (int e = 0; e < VPL; e++) v[e] *= wn[e];
         }
+        if (op.signs) {
+#pragma unroll
+            for (int e = 0; e < VPL; e++) sg[e] = op.signs[k0 + lane + 32 * e];
+        }
+        uint8_t* reg = scratch + (size_t)warp * rsz;
+        emit_token<VPL, GPC>(geo, t, reg, v, op.signs ? sg : nullptr);
+        __syncwarp();
+        store_token_columns(t, HBe, G, reg, op.buf + ((size_t)b * 4 + (t >> 2)) * rsz);
     }
-    // group sums of the block's part for the bias steps (x 2^(E-6)); all lanes hold every sum after the reduction
-    float gs[NGH];
-#pragma unroll
-    for (int g = 0; g < NGH; g++) {
-        float a = 0.0f;
-#pragma unroll
-        for (int e = g * EPG; e < (g + 1) * EPG; e++) a += v[e];
-        gs[g] = a;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int g = 0; g < NGH; g++) gs[g] += __shfl_xor_sync(0xffffffffu, gs[g], o);
-    if (lane < 16) {
-        // lane -> column col + lane / 8, word (t4, which) of the bias step: k rows kk0, kk0 + 1
-        const int hl = lane >> 3, t4 = (lane >> 1) & 3, wh = lane & 1;
-        const int kk0 = wh * 8 + t4 * 2;
-        const int g_lo = e_lo / EPG, ngs = (e_hi - e_lo) / EPG;
-        const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
-        for (int bs = 0; bs < nbs; bs++) {
-            float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-            for (int g = 0; g < NGH; g++) {
-                const int gr = g - g_lo;  // block-relative group
-                if (gr >= 0 && gr < ngs) {
-                    if (gr == bs * 16 + kk0) s0 = gs[g];
-                    if (gr == bs * 16 + kk0 + 1) s1 = gs[g];
-                }
-            }
-            float a0 = s0 * fb, a1 = s1 * fb;
-            __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
-            if (hl) {
-                h0 = __float2half_rn(a0 - __half2float(h0));
-                h1 = __float2half_rn(a1 - __half2float(h1));
-            }
-            rw[(nsteps + bs) * 64 + ((col + hl) * 4 + t4) * 2 + wh] = pack_half2(h0, h1);
+    __syncthreads();
+    if (tid == 0) {  // the last contributor to finish resets the block's counts for the next producer
+        unsigned old;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(done) : "memory");
+        if (old == (unsigned)(need - 1)) {
+            *arrive = 0;
+            *done = 0;
         }
     }
 }
@@ -519,7 +589,8 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
     constexpr int G = 128 / GPC;
     uint64_t* bar = (uint64_t*)smem;           // codes + scales of this CTA
-    uint64_t* bar_op = (uint64_t*)(smem + 8);  // operand regions sent by the other CTAs of the cluster
+    uint64_t* bar_op = (uint64_t*)(smem + 8);  // operand regions from the producing kernel
+    float* s_r = (float*)(smem + 16);          // [16] per-token RMS scale (operand without it), else 1
     int* s_e = (int*)(smem + 128);             // [token][block] exponents, kept for the reduction
     const int kslice = p.kslice, nkc = kslice / 128;
     const int sbsz = min(VPL * 32, kslice), nb = kslice / sbsz;
@@ -528,33 +599,31 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     const size_t sb_bytes = (size_t)nkc * 8 * 2 * GPC * 32;
     uint8_t* s_codes = smem + GEMV_HDR;
     uint32_t* s_sb = (uint32_t*)(smem + GEMV_HDR + codes_bytes);
-    uint8_t* s_op = smem + GEMV_HDR + codes_bytes + sb_bytes;
+    uint8_t* s_op = smem + GEMV_HDR + codes_bytes + sb_bytes;  // regions [nb][NT]
+    const bool prebuilt = p.src.opbuf != nullptr;
 
     const int rb = blockIdx.x % p.nrb, ks = blockIdx.x / p.nrb;
     const int nkc_all = p.K / 128;
-    // operand tasks (nt, b) = region index i: built by CTA (i % 2 ncs) / 2 of the cluster, warps 4 (i % 2) .. + 3
-    const int ncs = (int)cg::this_cluster().num_blocks(), rank = (int)cg::this_cluster().block_rank();
-    const int ntask = NT * nb, nslot = 2 * ncs;
-    int mine = 0;
-    for (int i = 0; i < ntask; i++) mine += (i % nslot) / 2 == rank;
     if (tid == 0) {
         mbar_init(bar, 1);
         mbar_init(bar_op, 1);
-        fence_mbar_init_cluster();
         fence_proxy_async_smem();
     }
     __syncthreads();
-    cluster_arrive();
     pdl_trigger();
     if (tid == 0) {
         mbar_expect_tx(bar, (uint32_t)(codes_bytes + sb_bytes));
         bulk_g2s(s_codes, p.codes + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 512, (uint32_t)codes_bytes, bar);
         bulk_g2s(s_sb, (const uint8_t*)p.sb + ((size_t)rb * nkc_all + (size_t)ks * nkc) * 8 * 2 * GPC * 32,
                  (uint32_t)sb_bytes, bar);
-        mbar_expect_tx(bar_op, (uint32_t)((ntask - mine) * rsz));
     }
-    cluster_wait();  // every mbarrier of the cluster is initialised before any region is sent
     pdl_wait();
+    if (prebuilt && tid == 0) {  // the slice's regions: nb blocks of NT tiles (the buffer holds 4 tiles per block)
+        mbar_expect_tx(bar_op, (uint32_t)(nb * NT * rsz));
+        for (int b = 0; b < nb; b++)
+            bulk_g2s(s_op + (size_t)b * NT * rsz, p.src.opbuf + ((size_t)(ks * nb + b) * 4) * rsz, (uint32_t)(NT * rsz),
+                     bar_op);
+    }
     float res[8];  // residual rows of this row block (element e = tid + 256 i of [T][128]), read early
     if (p.o.add) {
 #pragma unroll
@@ -563,35 +632,28 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             res[i] = e < 128 * p.T ? p.o.out[(size_t)(e >> 7) * p.O + rb * 128 + (e & 127)] : 0.0f;
         }
     }
-    {
-        const int half = warp >> 2, tw = warp & 3;
-        const bool first_cluster = (int)blockIdx.x < ncs;  // ks == 0 and the first row blocks
-        for (int i = 2 * rank + half; i < ntask; i += nslot) {
-            const int nt = i / nb, b = i % nb;
-            uint8_t* reg = s_op + (size_t)i * rsz;
-            build_token<VPL, GPC>(p, nt * 4 + tw, b, ks, sbsz, reg, first_cluster && b == 0);
-            fence_proxy_async_smem();  // each writer orders its region writes before the bulk copies that read them
-            named_sync(1 + half, 128);
-            if (tw == 0 && lane == 0 && ncs > 1) {
-                const uint32_t src = smem_u32(reg), mb = smem_u32(bar_op);
-                for (int rk = 0; rk < ncs; rk++)
-                    if (rk != rank) bulk_s2peer(peer_addr(src, rk), reg, (uint32_t)rsz, peer_addr(mb, rk));
-                bulk_commit();
-            }
-        }
+    if (warp < 2) {  // per-token output scale: the RMS scale when the producer left it out
+        const int t = warp * 8 + (lane >> 2);
+        float a = 0.0f;
+        const bool norm = prebuilt && p.src.mode == ACT_NORM;
+        if (norm && t < p.T)
+            for (int i = lane & 3; i < p.src.nss; i += 4) a += p.src.ss[i * VMAX + t];
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        if ((lane & 3) == 0) s_r[t] = norm ? rsqrtf(a / (float)p.K + EPS_T) : 1.0f;
     }
+    if (!prebuilt) build_operand<VPL, GPC>(p, ks, sbsz, nb, NT, s_op, rsz);
     __syncthreads();
-    bool ok = mbar_wait_bounded(bar, 0) && mbar_wait_cluster_bounded(bar_op, 0);
+    const bool ok = mbar_wait_bounded(bar, 0) && (!prebuilt || mbar_wait_bounded(bar_op, 0));
     if (__syncthreads_or(!ok)) {
         if (tid == 0) atomicOr(p.o.err, ERR_MBAR_TIMEOUT);
-        if ((warp & 3) == 0 && lane == 0) bulk_wait_read();
         mbar_wait_bounded(bar, 0, 1u << 20);
-        mbar_wait_cluster_bounded(bar_op, 0, 1u << 20);
+        if (prebuilt) mbar_wait_bounded(bar_op, 0, 1u << 20);
         return;
     }
     if (tid < p.T * nb) {  // exponents to the header (the regions are overwritten by the reduction)
         const int t = tid / nb, b = tid % nb;
-        s_e[t * 4 + b] = ((const int*)(s_op + (size_t)((t >> 2) * nb + b) * rsz + (nsteps + nbs) * 256))[t & 3];
+        s_e[t * 4 + b] = ((const int*)(s_op + (size_t)(b * NT + (t >> 2)) * rsz + (nsteps + nbs) * 256))[t & 3];
     }
 
     const int rg = warp >> 2, kw = warp & 3;
@@ -607,9 +669,9 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             for (int i = 0; i < 4; i++) acc[m][n][i] = 0.0f;
 
     const uint32_t MAGIC = 0x64006400u, NEG1024 = 0xE400E400u;
-    // B fragments of k16 step (slice-local) st for tile n: regions (n, bw), step st - bw * nsteps
-    const uint2* s_b2 = (const uint2*)(s_op + (size_t)bw * rsz) - (size_t)bw * nsteps * 32;
-    const size_t tile_stride = (size_t)nb * rsz / 8;  // uint2 between tiles
+    // B fragments of k16 step (slice-local) st for tile n: region (bw, n), step st - bw * nsteps
+    const uint2* s_b2 = (const uint2*)(s_op + (size_t)bw * NT * rsz) - (size_t)bw * nsteps * 32;
+    const size_t tile_stride = (size_t)rsz / 8;  // uint2 between tiles
     for (int c = 0; c < nkc_w; c++) {
         const int kcl = kw * nkc_w + c;
         uint4 cw[4];
@@ -661,7 +723,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         uint2 bb[NT];
 #pragma unroll
         for (int n = 0; n < NT; n++)
-            bb[n] = ((const uint2*)(s_op + (size_t)(n * nb + bw) * rsz + (size_t)(nsteps + bs) * 256))[lane];
+            bb[n] = ((const uint2*)(s_op + (size_t)(bw * NT + n) * rsz + (size_t)(nsteps + bs) * 256))[lane];
         const int cols[4] = {2 * t4, 2 * t4 + 1, 2 * t4 + 8, 2 * t4 + 9};
 #pragma unroll
         for (int m = 0; m < 4; m++) {
@@ -682,9 +744,6 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             for (int n = 0; n < NT; n++) mma_f16(acc[m][n], a0, a1, a2, a3, bb[n].x, bb[n].y);
         }
     }
-    // the regions' last readers: this CTA's warps (above) and the bulk copies it sent
-    if ((warp & 3) == 0 && lane == 0) bulk_wait_read();
-
     // in-CTA reduction over the 4 k-quarters, fixed order; partials in units of x (2^-E applied)
     __syncthreads();
     float* red = (float*)(smem + GEMV_HDR);  // [kw 4][rg 2][m 4][NT][2][32]
@@ -721,6 +780,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         v += red[quarter + e] * pow2f(-et[blk_of_q[1]]);
         v += red[2 * quarter + e] * pow2f(-et[blk_of_q[2]]);
         v += red[3 * quarter + e] * pow2f(-et[blk_of_q[3]]);
+        v *= s_r[token];
         if (p.nsplit == 1) fin[token * 128 + rloc] = v;
         else p.o.partial[((size_t)ks * T + token) * O + rb * 128 + rloc] = v;
     }
@@ -776,24 +836,20 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             if (lane == 0) p.o.ss_out[rb * VMAX + token] = a;
         }
     }
+    if (p.o.op.buf) produce_operand<VPL, GPC>(p, rb, smem + GEMV_HDR, &s_last);
 }
 
-static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb) {
+static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb, bool produce) {
     int gpc = 128 / group;
     int sbsz = hb < kslice ? hb : kslice;
     size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
                   (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
     size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
     size_t abs_ = ab ? ((size_t)(AB_ROWS + T) * K + 8 * 64 + 32) * 4 : 0;
+    size_t prod = produce ? GEMV_HDR + (size_t)4 * op_region_bytes(hb, group) : 0;  // <= 4 tokens per CTA
     size_t s = main > red ? main : red;
-    return s > abs_ ? s : abs_;
-}
-
-// Cluster size: the largest of 8, 4, 2, 1 that divides the row-block count (clusters never straddle K-slices).
-static int gemv_cluster(int nrb) {
-    for (int c = 8; c > 1; c >>= 1)
-        if (nrb % c == 0) return c;
-    return 1;
+    s = s > abs_ ? s : abs_;
+    return s > prod ? s : prod;
 }
 
 template <int NT, int GPC, int VPL>
@@ -806,24 +862,35 @@ static void launch_gemv_t(const GemvParams& p, size_t smem, cudaStream_t st) {
     }
     GemvParams pp = p;
     void* args[] = {&pp};
-    const int cs = gemv_cluster(p.nrb);
-    int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
-    n_ab = (n_ab + cs - 1) / cs * cs;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(p.n_main + n_ab));
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = (unsigned)cs;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    cudaLaunchKernelExC(&cfg, (const void*)fn, args);
+    const int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
+    launch_pdl((const void*)fn, dim3((unsigned)(p.n_main + n_ab)), dim3(256), smem, st, args);
+}
+
+template <int NT, int GPC>
+static const void* gemv_fn_vpl(int hb) {
+    if (hb == 512) return (const void*)ternary_gemv_kernel<NT, GPC, 16>;
+    if (hb == 1024) return (const void*)ternary_gemv_kernel<NT, GPC, 32>;
+    return (const void*)ternary_gemv_kernel<NT, GPC, 64>;
+}
+template <int NT>
+static const void* gemv_fn_gpc(int group, int hb) {
+    return group == 64 ? gemv_fn_vpl<NT, 2>(hb) : gemv_fn_vpl<NT, 1>(hb);
+}
+
+// Whether every CTA of this GEMV's grid can be resident at once (required when it produces the next operand: its
+// CTAs wait for one another).
+bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms) {
+    const int nt = (2 * T + 7) / 8;
+    const void* fn = nt == 1 ? gemv_fn_gpc<1>(m.group, hb)
+                   : nt == 2 ? gemv_fn_gpc<2>(m.group, hb)
+                   : nt == 3 ? gemv_fn_gpc<3>(m.group, hb)
+                             : gemv_fn_gpc<4>(m.group, hb);
+    const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, true);
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess) return false;
+    const long grid = (long)(m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS;
+    return grid <= (long)per_sm * num_sms;
 }
 
 template <int NT, int GPC>
@@ -858,7 +925,7 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     p.nrb = m.O / 128;
     int hb = src.HB > 0 ? src.HB : 512;  // unrotated sources use 512-element blocks for their exponents
     int nt = (2 * T + 7) / 8;
-    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb);
+    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb, o.op.buf != nullptr);
     if (nt == 1) launch_gpc<1>(p, hb, smem, st);
     else if (nt == 2) launch_gpc<2>(p, hb, smem, st);
     else if (nt == 3) launch_gpc<3>(p, hb, smem, st);
