@@ -38,21 +38,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return false;
 }
 
-// Wait for a phase whose bytes were delivered by other CTAs of the cluster (acquire at cluster scope), bounded.
-__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 22)) {
-    for (uint32_t i = 0; i < limit; i++) {
-        uint32_t ok;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-            " selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        if (ok) return true;
-    }
-    return false;
-}
-
 // ----------------------------------------------------------------------------------------------- grid counters
 // Count one arrival (release: this thread's earlier writes, and those of the CTA ordered before it by a barrier, are
 // visible to whoever observes the count).
@@ -71,30 +56,7 @@ __device__ __forceinline__ bool spin_until_geq(const unsigned* c, unsigned targe
     return false;
 }
 
-// ----------------------------------------------------------------------------------------------- clusters
-// Barrier halves over every thread of the cluster (all threads of a CTA execute both, arrive first).
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-// Makes this CTA's mbarrier initialisations visible to the other CTAs of the cluster.
-__device__ __forceinline__ void fence_mbar_init_cluster() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-// Address in CTA `rank`'s shared memory of the variable at shared address `a` in this CTA (shared::cluster window).
-__device__ __forceinline__ uint32_t peer_addr(uint32_t a, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
-    return r;
-}
-// 1-D bulk copy of this CTA's shared memory into another CTA's shared memory (point to point, no multicast); the
-// bytes complete on the destination CTA's mbarrier. Both addresses 16-byte aligned, bytes % 16 == 0.
-__device__ __forceinline__ void bulk_s2peer(uint32_t dst_cluster, const void* src, uint32_t bytes,
-                                            uint32_t bar_cluster) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            dst_cluster),
-        "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
-        : "memory");
-}
+// ----------------------------------------------------------------------------------------------- bulk copies
 // 1-D bulk copy of this CTA's shared memory to global memory (bulk async-group completion). src/dst 16-byte
 // aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
@@ -105,8 +67,6 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until this thread's committed bulk copies are complete (their writes performed).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// Waits until the source shared memory of this thread's committed bulk copies has been read.
-__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // 16-byte asynchronous global -> shared copies (L2 only) and the wait for all of this thread's.
@@ -118,10 +78,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 // Waits until at most N of this thread's committed cp.async groups are still pending.
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// Named barrier over `count` threads (ids 1..15; id 0 is __syncthreads).
-__device__ __forceinline__ void named_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 
 // 1-D bulk copy global -> shared (TMA engine, no tensor map, no multicast). dst/src 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
