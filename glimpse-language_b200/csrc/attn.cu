@@ -103,11 +103,8 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             }
             cp_async_commit();
         };
-        if (nst > 0) issue(0);
-        if (nst > 1) issue(1);
-
         // rows to prepare: the qper query heads of row t, then this pass's keys in range (positions >= off),
-        // all loaded at once
+        // all loaded at once, ahead of the cached blocks
         const int u0 = max(j0, off) - off, u1 = j1 - off, nkeys = max(u1 - u0, 0);
         const int nrows = qper + nkeys;  // <= 16 + 16
         float x[32], vvals[16];
@@ -120,6 +117,8 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
 #pragma unroll
         for (int i = 0; i < 16; i++)
             if (i < nkeys) vvals[i] = a.qkv[(size_t)(u0 + i) * a.ld + 2 * aw + kvw + kh * 256 + d];
+        if (nst > 0) issue(0);
+        if (nst > 1) issue(1);
         for (int e = threadIdx.x; e < (1 + nkeys) * half; e += 256) {
             const int pi = e / half, f = e - pi * half;
             const int pos = pi == 0 ? off + t : off + u0 + pi - 1;
@@ -337,20 +336,24 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
     if (!s_last) return;
     const float* p0 = a.part + ((size_t)t * H + kh * qper) * NSPLIT_ATTN * 258;
     float* mls = qs;  // [qper][NSPLIT][2]
+    float av[2][NSPLIT_ATTN], an[2][NSPLIT_ATTN];
+    auto load_av = [&](int h0, float (*dst)[NSPLIT_ATTN]) {
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+            for (int q = 0; q < NSPLIT_ATTN; q++)
+                dst[hh][q] = h0 + hh < qper ? __ldcg(p0 + (size_t)(h0 + hh) * NSPLIT_ATTN * 258 + q * 258 + 2 + d) : 0.0f;
+    };
+    load_av(0, av);
     for (int e = threadIdx.x; e < qper * NSPLIT_ATTN * 2; e += 256) {
         const int h = e / (2 * NSPLIT_ATTN), r = e - h * 2 * NSPLIT_ATTN;
         mls[e] = __ldcg(p0 + (size_t)h * NSPLIT_ATTN * 258 + (r >> 1) * 258 + (r & 1));
     }
     __syncthreads();
-    for (int h0 = 0; h0 < qper; h0 += 4) {
-        float av[4][NSPLIT_ATTN];
+    for (int h0 = 0; h0 < qper; h0 += 2) {
+        if (h0 + 2 < qper) load_av(h0 + 2, an);  // the next heads' loads in flight while these are merged
 #pragma unroll
-        for (int hh = 0; hh < 4; hh++)
-#pragma unroll
-            for (int q = 0; q < NSPLIT_ATTN; q++)
-                av[hh][q] = h0 + hh < qper ? __ldcg(p0 + (size_t)(h0 + hh) * NSPLIT_ATTN * 258 + q * 258 + 2 + d) : 0.0f;
-#pragma unroll
-        for (int hh = 0; hh < 4; hh++) {
+        for (int hh = 0; hh < 2; hh++) {
             const int h = h0 + hh;
             if (h >= qper) break;
             const float* m2 = mls + h * NSPLIT_ATTN * 2;
@@ -368,6 +371,10 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             a.out[(size_t)t * aw + (kh * qper + h) * 256 + d] = o / L;
             if (a.op.buf) ks[h * 256 + d] = o / L;
         }
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+            for (int q = 0; q < NSPLIT_ATTN; q++) av[hh][q] = an[hh][q];
     }
     if (d == 0) a.counters[t * KV + kh] = 0;
     if (a.op.buf) {

@@ -74,6 +74,19 @@ __device__ void gdn_produce(const GdnArgs& a, uint8_t* scratch, int* s_ok) {
     const int T = a.T, t = ci, k0 = b * HBe, ldy = a.NV * 128;
     unsigned* arrive = op.counters + b;
     unsigned* done = op.counters + 256 + b;
+    // inputs that do not depend on the other CTAs, loaded before the wait
+    float wn[4], sg[VPL], ya[VPL], zb[VPL], v[VPL];
+    const bool builder = t < T && warp == 0;
+    if (builder) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) wn[i] = op.w[(lane + 32 * i) & 127];
+#pragma unroll
+        for (int e = 0; e < VPL; e++) zb[e] = op.x2[(size_t)t * op.ld2 + op.off2 + k0 + lane + 32 * e];
+        if (op.signs) {
+#pragma unroll
+            for (int e = 0; e < VPL; e++) sg[e] = op.signs[k0 + lane + 32 * e];
+        }
+    }
     __syncthreads();  // every output row of this CTA is stored
     if (tid == 0) {
         arrive_release(arrive);
@@ -81,22 +94,11 @@ __device__ void gdn_produce(const GdnArgs& a, uint8_t* scratch, int* s_ok) {
         if (!*s_ok) atomicOr(&((Ctl*)a.ctl)->err, ERR_SPIN_TIMEOUT);
     }
     __syncthreads();
-    if (*s_ok && t < T && warp == 0) {
+    if (*s_ok && builder) {
         const int rsz = op_region_bytes(HBe, G);
         const OpGeo geo{HBe, 0, VPL, 0, true};
-        float wn[4], sg[VPL], ya[VPL], zb[VPL], v[VPL];
 #pragma unroll
-        for (int i = 0; i < 4; i++) wn[i] = op.w[(lane + 32 * i) & 127];
-#pragma unroll
-        for (int e = 0; e < VPL; e++) {
-            const int k = k0 + lane + 32 * e;
-            ya[e] = __ldcg(a.y + (size_t)t * ldy + k);
-            zb[e] = op.x2[(size_t)t * op.ld2 + op.off2 + k];
-        }
-        if (op.signs) {
-#pragma unroll
-            for (int e = 0; e < VPL; e++) sg[e] = op.signs[k0 + lane + 32 * e];
-        }
+        for (int e = 0; e < VPL; e++) ya[e] = __ldcg(a.y + (size_t)t * ldy + k0 + lane + 32 * e);
         gated_values<VPL>(ya, zb, wn, v);
         emit_token<VPL, GPC>(geo, t, scratch, v, op.signs ? sg : nullptr);
         __syncwarp();

@@ -79,11 +79,14 @@ __device__ void emit_token(const OpGeo& geo, int t, uint8_t* reg, float* v, cons
 #pragma unroll
         for (int e = 0; e < VPL; e++) v[e] *= inv;
     }
-    float amax = 0.0f;
+    float am[VPL];  // |v| over the region's part, reduced as a tree
 #pragma unroll
-    for (int e = 0; e < VPL; e++)
-        if (e >= e_lo && e < e_hi) amax = fmaxf(amax, fabsf(v[e]));
-    amax = warp_max(amax);
+    for (int e = 0; e < VPL; e++) am[e] = (e >= e_lo && e < e_hi) ? fabsf(v[e]) : 0.0f;
+#pragma unroll
+    for (int h = VPL / 2; h > 0; h >>= 1)
+#pragma unroll
+        for (int e = 0; e < h; e++) am[e] = fmaxf(am[e], am[e + h]);
+    const float amax = warp_max(am[0]);
     int E = 0;
     if (amax > 0.0f && amax < INFINITY) {
         int ex;
