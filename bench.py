@@ -34,6 +34,9 @@ for p in (PKG, ROOT):
 import numpy as np  # noqa: E402
 
 METRIC = "decode tok/s/GPU with speculation (Bonsai-2B shape); verify-pass HBM GB/s"
+# DRAM bytes (read + write) of one 9-row verify pass of this workload's model, summed over its 121 kernels from one
+# ncu launch-list capture (profiles/verify_pass_2b_launches.md; context ~70, so ~35 MB less K/V than the timed passes)
+VERIFY_PASS_DRAM_BYTES = 1654.0e6
 PREFIX, USER, GEN, K_DRAFT = 1024, 256, 300, 8
 WORKLOAD = ("config3: Bonsai-2B shape random-init, 1024-token cached prefix + 256 Zipf(1.1) user tokens, "
             "300+ generated tokens, k=8 planted drafts (100% accept)")
@@ -317,7 +320,7 @@ def main():
         "e2e": e2e,
         "gpu_launches": ws * launches * passes * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": None, "kernel": "verify pass (T=9 graph: all kernels of one pass)",
+                     "traffic": VERIFY_PASS_DRAM_BYTES, "kernel": "verify pass (T=9 graph: all kernels of one pass)",
                      "bytes_per_launch": bytes_pass, "ms_per_launch": pass_ms,
                      "frac_of_8TBs": achieved / 8000.0, "peak_source": "MEASURED_PEAKS.json" if pk else "fallback"},
         "random_drafts": {"tok_s": rnd_tok_s, "ms_per_pass": rnd_ms / (GEN - 1)},
