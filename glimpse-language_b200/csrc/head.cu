@@ -2,8 +2,9 @@
 // model.rs:941-985; argmax1/argmax2, kernels.metal:802-842; the accept length of decode_spec, runtime/mod.rs:866-868).
 //
 // The 248320 x 2048 bf16 table is 62% of a verify pass's bytes, so this kernel is a pure stream: the table is
-// stored in mma fragment order (one LDG.128 per lane per 16x16 tile), the normed rows are a bf16 hi/lo operand kept in
-// shared memory, and mma.m16n8k16 does the T-row products (fp32 accumulate). Logits never go to HBM: every warp keeps
+// stored in mma fragment order (one 16-byte A fragment per lane per 16x16 tile), streamed through shared memory by
+// bulk copies, the normed rows are a bf16 hi/lo operand kept in shared memory, and mma.m16n8k16 does the T-row
+// products (fp32 accumulate). Logits never go to HBM: every warp keeps
 // a running (max, lowest index) per row; CTAs publish partials, and the last CTA to finish merges them in CTA order,
 // computes the accept length m on the device and advances the control block (KV offset, replay count, parity), so only
 // m and the bonus token need to reach the host.
@@ -65,9 +66,23 @@ __device__ void head_operand(const HeadArgs& a, int t, uint32_t* s_b) {
     }
 }
 
+constexpr int HEAD_KCH = 8;         // k-steps per staged unit: 8 x 512 B = 4 KB per warp
 template <int NT>
-__global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
+__host__ __device__ constexpr int head_stages() { return NT >= 4 ? 3 : 4; }  // units in flight per warp
+
+// Shared memory: the operand [d/16][NT][32 lanes][2 words], then per warp a ring of head_stages() 4-KB units of the
+// table, then their mbarriers.
+__host__ __device__ inline size_t head_smem_bytes(int d, int nt, int stages) {
+    return (size_t)(d / 16) * nt * 256 + (size_t)8 * stages * 4096 + (size_t)8 * stages * 8;
+}
+
+// One CTA per SM, 8 warps; warp w streams a contiguous range of 16-row m-tiles (a contiguous byte range of the
+// repacked table) through its shared-memory ring with 4-KB bulk copies (cp.async.bulk, no multicast), so each warp
+// keeps head_stages() x 4 KB of the table in flight while its tensor-core products run.
+template <int NT>
+__global__ void __launch_bounds__(256, 1) head_kernel(HeadArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int S = head_stages<NT>();
     uint2* s_b = (uint2*)smem;
     __shared__ float wbv[8][16];
     __shared__ int wbi[8][16];
@@ -79,13 +94,20 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
     const int gw = blockIdx.x * 8 + warp, W = gridDim.x * 8;
     // contiguous m-tile range per warp (rows visited in increasing order)
     const int per = (nmt + W - 1) / W;
-    const int mt0 = gw * per, mt1 = min(nmt, mt0 + per);
+    const int mt0 = min(nmt, gw * per), mt1 = min(nmt, mt0 + per);
+    const int upm = nks / HEAD_KCH;  // units per m-tile
+    const int nunits = (mt1 - mt0) * upm;
+    uint8_t* ring = smem + (size_t)nks * NT * 256 + (size_t)warp * S * 4096;
+    uint64_t* bars = (uint64_t*)(smem + (size_t)nks * NT * 256 + (size_t)8 * S * 4096) + warp * S;
+    const uint8_t* src = (const uint8_t*)a.w + (size_t)mt0 * nks * 512;
     // the table does not depend on the previous kernel: start streaming it before the dependency wait
-    uint4 buf0[8], buf1[8];
-    if (mt0 < mt1) {
-        const uint4* wp = (const uint4*)a.w + (size_t)mt0 * nks * 32 + lane;
-#pragma unroll
-        for (int i = 0; i < 8; i++) buf0[i] = __ldcs(wp + (size_t)i * 32);
+    if (lane == 0) {
+        for (int i = 0; i < S; i++) mbar_init(&bars[i], 1);
+        fence_proxy_async_smem();
+        for (int u = 0; u < S && u < nunits; u++) {
+            mbar_expect_tx(&bars[u], 4096);
+            bulk_g2s(ring + u * 4096, src + (size_t)u * 4096, 4096, &bars[u]);
+        }
     }
     for (size_t i = tid; i < (size_t)nks * NT * 256 / 16; i += 256) ((uint4*)smem)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
@@ -102,55 +124,52 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
         bv[n] = -INFINITY;
         bi[n] = 0x7fffffff;
     }
-    for (int mt = mt0; mt < mt1; mt++) {
-        const uint4* wp = (const uint4*)a.w + (size_t)mt * nks * 32 + lane;
-        float acc[NT][4];
+    float acc[NT][4];
 #pragma unroll
-        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-        if (mt != mt0) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) buf0[i] = __ldcs(wp + (size_t)i * 32);
-        }
-        for (int kb = 0; kb < nks; kb += 16) {
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-                if (kb + 8 + i < nks) buf1[i] = __ldcs(wp + (size_t)(kb + 8 + i) * 32);
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                int ks = kb + i;
-#pragma unroll
-                for (int n = 0; n < NT; n++) {
-                    uint2 b = s_b[((size_t)ks * NT + n) * 32 + lane];
-                    mma_bf16(acc[n], buf0[i].x, buf0[i].y, buf0[i].z, buf0[i].w, b.x, b.y);
-                }
+    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+    int mt = mt0;
+    for (int u = 0; u < nunits; u++) {
+        const int slot = u % S;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[slot], (u / S) & 1));
+        if (!ok) {  // give up: wait (bounded) for the copies in flight, report, stop streaming
+            if (lane == 0) {
+                atomicOr(&a.ctl->err, ERR_MBAR_TIMEOUT);
+                for (int v = u; v < u + S && v < nunits; v++) mbar_wait_bounded(&bars[v % S], (v / S) & 1, 1u << 20);
             }
-            if (kb + 8 >= nks) break;
+            break;
+        }
+        const uint4* wk = (const uint4*)(ring + slot * 4096) + lane;
+        const int kb = (u % upm) * HEAD_KCH;
 #pragma unroll
-            for (int i = 0; i < 8; i++)
-                if (kb + 16 + i < nks) buf0[i] = __ldcs(wp + (size_t)(kb + 16 + i) * 32);
+        for (int i = 0; i < HEAD_KCH; i++) {
+            const uint4 w = wk[i * 32];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                int ks = kb + 8 + i;
-                if (ks < nks) {
-#pragma unroll
-                    for (int n = 0; n < NT; n++) {
-                        uint2 b = s_b[((size_t)ks * NT + n) * 32 + lane];
-                        mma_bf16(acc[n], buf1[i].x, buf1[i].y, buf1[i].z, buf1[i].w, b.x, b.y);
-                    }
-                }
+            for (int n = 0; n < NT; n++) {
+                const uint2 b = s_b[((size_t)(kb + i) * NT + n) * 32 + lane];
+                mma_bf16(acc[n], w.x, w.y, w.z, w.w, b.x, b.y);
             }
         }
+        __syncwarp();
+        if (lane == 0 && u + S < nunits) {  // the slot's data is consumed: refill it with unit u + S
+            fence_proxy_async_smem();
+            mbar_expect_tx(&bars[slot], 4096);
+            bulk_g2s(ring + slot * 4096, src + (size_t)(u + S) * 4096, 4096, &bars[slot]);
+        }
+        if ((u + 1) % upm == 0) {  // m-tile done: its 16 rows' logits into the running argmax
 #pragma unroll
-        for (int n = 0; n < NT; n++) {
-            int token = n * 4 + t4;
-            float v0 = acc[n][0] + acc[n][1], v1 = acc[n][2] + acc[n][3];
-            int r0 = mt * 16 + g, r1 = r0 + 8;
-            if (keep && token < T) {
-                a.logits[(size_t)token * a.V + r0] = v0;
-                a.logits[(size_t)token * a.V + r1] = v1;
+            for (int n = 0; n < NT; n++) {
+                int token = n * 4 + t4;
+                float v0 = acc[n][0] + acc[n][1], v1 = acc[n][2] + acc[n][3];
+                int r0 = mt * 16 + g, r1 = r0 + 8;
+                if (keep && token < T) {
+                    a.logits[(size_t)token * a.V + r0] = v0;
+                    a.logits[(size_t)token * a.V + r1] = v1;
+                }
+                argmax_merge(bv[n], bi[n], v0, r0);
+                argmax_merge(bv[n], bi[n], v1, r1);
+                acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
             }
-            argmax_merge(bv[n], bi[n], v0, r0);
-            argmax_merge(bv[n], bi[n], v1, r1);
+            mt++;
         }
     }
     // lanes with the same t4 hold the same token: merge over g
@@ -213,10 +232,11 @@ __global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
 
 template <int NT>
 static void launch_head_t(const HeadArgs& a, int grid, cudaStream_t st) {
-    size_t smem = (size_t)(a.d / 16) * NT * 256;
+    size_t smem = head_smem_bytes(a.d, NT, head_stages<NT>());
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        // the per-block opt-in limit (227 KB) minus this kernel's static shared memory (~1.2 KB)
+        cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
         attr = true;
     }
     HeadArgs aa = a;

@@ -639,7 +639,7 @@ bcu_status bcu_finalize(bcu_model* m) {
     m->partial_floats = pf;
     TRY(dmalloc(m, &m->partial, pf * 4));
     TRY(dmalloc(m, &m->counters, (size_t)maxrb * 4));
-    m->head_grid = 2 * m->num_sms;
+    m->head_grid = m->num_sms;  // one CTA per SM (head.cu)
     TRY(dmalloc(m, &m->head_counter, 4));
     {
         // operand buffers: [K / HB blocks][4 tiles][region] for the widest GEMV input
