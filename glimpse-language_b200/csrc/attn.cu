@@ -10,7 +10,6 @@
 // (cp.async, every copy of a block in flight at once), and the softmax is accumulated online block by block.
 #include "common.cuh"
 #include "kernels.h"
-#include "operand.cuh"
 
 namespace bcu {
 
@@ -23,37 +22,6 @@ constexpr int KST = 16;  // cached keys per staged block
 __host__ __device__ inline size_t attn_smem_floats(int qp, int rot) {
     return (size_t)qp * 256 + 4 * KST * 256 + 2 * VMAX * 256 + 2 * (size_t)qp * KST + 288 + 4 * (size_t)qp +
            (size_t)(1 + VMAX) * rot;
-}
-
-// The output GEMV's operand columns of row t (GATE: sigmoid-gated attention output, its signs, Walsh-Hadamard) for
-// the Hadamard blocks of kv head kh's query heads: warp i < qper * 256 / HB builds block i of them from the merged
-// rows `xo` ([qper][256] in shared memory) in its scratch region and stores the row's columns to the buffer.
-template <int VPL, int GPC>
-__device__ void attn_produce(const AttnArgs& a, int t, int kh, const float* xo, uint8_t* scratch) {
-    constexpr int HBe = VPL * 32, G = 128 / GPC;
-    const OpOut& op = a.op;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int qper = a.H / a.KV, nblk = qper * 256 / HBe;
-    const int rsz = op_region_bytes(HBe, G);
-    const OpGeo geo{HBe, 0, VPL, 0, true};
-    for (int i = warp; i < nblk; i += 8) {
-        const int k0 = kh * qper * 256 + i * HBe;  // first input of the block (GEMV input index)
-        float v[VPL], sg[VPL];
-#pragma unroll
-        for (int e = 0; e < VPL; e++) {
-            const int k = k0 + lane + 32 * e;
-            const float gate = op.x2[(size_t)t * op.ld2 + (k >> 8) * 512 + 256 + (k & 255)];
-            v[e] = xo[i * HBe + lane + 32 * e] * sigm(gate);
-        }
-        if (op.signs) {
-#pragma unroll
-            for (int e = 0; e < VPL; e++) sg[e] = op.signs[k0 + lane + 32 * e];
-        }
-        uint8_t* reg = scratch + (size_t)warp * rsz;
-        emit_token<VPL, GPC>(geo, t, reg, v, op.signs ? sg : nullptr);
-        __syncwarp();
-        store_token_columns(t, HBe, G, reg, op.buf + ((size_t)(k0 / HBe) * 4 + (t >> 2)) * rsz);
-    }
 }
 
 // QP = query heads per kv head rounded up to a power of two (heads qper..QP-1 are zero padding).
@@ -369,7 +337,6 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
                 o += av[hh][q] * wgt;
             }
             a.out[(size_t)t * aw + (kh * qper + h) * 256 + d] = o / L;
-            if (a.op.buf) ks[h * 256 + d] = o / L;
         }
 #pragma unroll
         for (int hh = 0; hh < 2; hh++)
@@ -377,17 +344,6 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             for (int q = 0; q < NSPLIT_ATTN; q++) av[hh][q] = an[hh][q];
     }
     if (d == 0) a.counters[t * KV + kh] = 0;
-    if (a.op.buf) {
-        __syncthreads();
-        uint8_t* scratch = (uint8_t*)(ks + qper * 256);
-        if (a.op.HB == 512) {
-            if (a.op.group == 64) attn_produce<16, 2>(a, t, kh, ks, scratch);
-            else attn_produce<16, 1>(a, t, kh, ks, scratch);
-        } else {
-            if (a.op.group == 64) attn_produce<32, 2>(a, t, kh, ks, scratch);
-            else attn_produce<32, 1>(a, t, kh, ks, scratch);
-        }
-    }
 }
 
 template <int QP>

@@ -15,7 +15,6 @@
 // memory first, so the sequential steps run without global loads on the critical path.
 #include "common.cuh"
 #include "kernels.h"
-#include "operand.cuh"
 
 namespace bcu {
 
@@ -59,76 +58,11 @@ struct __align__(16) GdnSmem {
     float rs[32];          // their norm scales
 };
 
-// The output GEMV's operand (GATED: gated RMSNorm of y with the z rows, its signs, Walsh-Hadamard) for the Hadamard
-// block of heads [b * HB/128, (b + 1) * HB/128): its CTAs (every dv block of each of those heads) share the tokens,
-// contributor ci building token ci once all of them have arrived, and store its columns of the block's regions.
-// Every CTA of the grid is resident at once (the host checks), so the bounded wait ends.
-template <int VPL, int GPC>
-__device__ void gdn_produce(const GdnArgs& a, uint8_t* scratch, int* s_ok) {
-    constexpr int HBe = VPL * 32, G = 128 / GPC;
-    const OpOut& op = a.op;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int hpb = HBe / 128;
-    const int b = blockIdx.x / hpb, need = hpb * gridDim.y;
-    const int ci = (blockIdx.x % hpb) * gridDim.y + blockIdx.y;
-    const int T = a.T, t = ci, k0 = b * HBe, ldy = a.NV * 128;
-    unsigned* arrive = op.counters + b;
-    unsigned* done = op.counters + 256 + b;
-    // inputs that do not depend on the other CTAs, loaded before the wait
-    float wn[4], sg[VPL], ya[VPL], zb[VPL], v[VPL];
-    const bool builder = t < T && warp == 0;
-    if (builder) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) wn[i] = op.w[(lane + 32 * i) & 127];
-#pragma unroll
-        for (int e = 0; e < VPL; e++) zb[e] = op.x2[(size_t)t * op.ld2 + op.off2 + k0 + lane + 32 * e];
-        if (op.signs) {
-#pragma unroll
-            for (int e = 0; e < VPL; e++) sg[e] = op.signs[k0 + lane + 32 * e];
-        }
-    }
-    __syncthreads();  // every output row of this CTA is stored
-    if (tid == 0) {
-        arrive_release(arrive);
-        *s_ok = t < T ? spin_until_geq(arrive, (unsigned)need) : 1;
-        if (!*s_ok) atomicOr(&((Ctl*)a.ctl)->err, ERR_SPIN_TIMEOUT);
-    }
-    __syncthreads();
-    if (*s_ok && builder) {
-        const int rsz = op_region_bytes(HBe, G);
-        const OpGeo geo{HBe, 0, VPL, 0, true};
-#pragma unroll
-        for (int e = 0; e < VPL; e++) ya[e] = __ldcg(a.y + (size_t)t * ldy + k0 + lane + 32 * e);
-        gated_values<VPL>(ya, zb, wn, v);
-        emit_token<VPL, GPC>(geo, t, scratch, v, op.signs ? sg : nullptr);
-        __syncwarp();
-        store_token_columns(t, HBe, G, scratch, op.buf + ((size_t)b * 4 + (t >> 2)) * rsz);
-    }
-    __syncthreads();
-    if (tid == 0) {  // the last contributor to finish resets the block's counts for the next producer
-        unsigned old;
-        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(done) : "memory");
-        if (old == (unsigned)(need - 1)) {
-            *arrive = 0;
-            *done = 0;
-        }
-    }
-}
-
-// Shared memory of the layer kernel: the staging of the rows, or (after the steps) the produced operand's regions.
-__host__ __device__ inline size_t gdn_smem_bytes(const OpOut& op, int T) {
-    size_t r = sizeof(GdnSmem);
-    if (op.buf) {
-        size_t p = (size_t)op_region_bytes(op.HB, op.group);
-        r = r > p ? r : p;
-    }
-    return r;
-}
+__host__ __device__ inline size_t gdn_smem_bytes() { return sizeof(GdnSmem); }
 
 __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
     extern __shared__ __align__(16) uint8_t gsm[];
     GdnSmem& sm = *(GdnSmem*)gsm;
-    __shared__ int s_flag;
     const int hd = blockIdx.x, blk = blockIdx.y, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int NK = a.NK, NV = a.NV, C = a.C, T = a.T;
     const int hk = hd / (NV / NK);
@@ -332,25 +266,6 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
             a.y[(size_t)(r - rn) * NV * 128 + hd * 128 + dv0 + w * 4 + lane] = ov;
         }
     }
-    if (a.op.buf && T > 0) {
-        __syncthreads();  // the staging is dead: the regions reuse its shared memory
-        if (a.op.HB == 512) {
-            if (a.op.group == 64) gdn_produce<16, 2>(a, gsm, &s_flag);
-            else gdn_produce<16, 1>(a, gsm, &s_flag);
-        } else {
-            if (a.op.group == 64) gdn_produce<32, 2>(a, gsm, &s_flag);
-            else gdn_produce<32, 1>(a, gsm, &s_flag);
-        }
-    }
-}
-
-bool gdn_coresident(const GdnArgs& a, int num_sms) {
-    cudaFuncSetAttribute(gdn_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn_layer_kernel, 128, gdn_smem_bytes(a.op, a.T)) !=
-        cudaSuccess)
-        return false;
-    return (long)a.NV * 8 <= (long)per_sm * num_sms;
 }
 
 void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
@@ -361,7 +276,7 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
     }
     GdnArgs aa = a;
     void* args[] = {&aa};
-    launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(128), gdn_smem_bytes(a.op, a.T), st, args);
+    launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(128), gdn_smem_bytes(), st, args);
 }
 
 // Graded config 2: T rows from explicit q/k/v/gate inputs, outputs for every row, and the state written back as it

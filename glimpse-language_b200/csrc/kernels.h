@@ -56,29 +56,15 @@ struct ActSrc {
     const Ctl* ctl = nullptr;      // EMBED: token ids
     float* h_out = nullptr;        // EMBED: residual rows (written by CTA 0)
     int HB = 512, vocab = 0;
-    // != null: the operand was built by the previous kernel (OpOut of that kernel) in this buffer; x, w and signs
-    // are then not read by the GEMV CTAs (the a/b gate CTAs still read x, w, ss). NORM: the per-token RMS scale is
-    // applied to the outputs (from ss) because the producer leaves it out.
-    const uint8_t* opbuf = nullptr;
+    // != null: the GEMV's CTAs build the whole operand once, together, in this global buffer ([K / HB blocks]
+    // [4 tiles][region]) and then copy their slices from it; op_counters: 2 zeroed words. Needs every CTA of the
+    // grid resident at once (gemv_coresident). Null: each CTA builds its own slice's operand.
+    uint8_t* opbuf = nullptr;
+    unsigned* op_counters = nullptr;
 };
 
-// Where a kernel writes the activation operand of the GEMV that follows it: region (block b, tile nt) at
-// buf + (b * 4 + nt) * region bytes, a block being `HB` consecutive inputs of the next GEMV (the region layout of
-// ternary.cu). The producing kernel applies the next GEMV's producer (mode; NORM without the per-token RMS scale),
-// its signs and the Walsh-Hadamard transform.
-struct OpOut {
-    uint8_t* buf = nullptr;        // null: no operand produced
-    int mode = ACT_NORM;           // NORM (x = h), SWIGLU (x = gate/up halves), GATED, GATE
-    int K = 0, group = 64, HB = 512;
-    const float* w = nullptr;      // NORM: norm weight [K]; GATED: head norm weight [128]
-    const float* signs = nullptr;  // [K] or null
-    const float* x2 = nullptr;     // GATED: z rows (x2 + t * ld2 + off2); GATE: gate rows (q projection, ld2)
-    int ld2 = 0, off2 = 0;
-    unsigned* counters = nullptr;  // per block arrival counts (zero between launches)
-};
 
 struct GemvOut {
-    OpOut op;                    // the next GEMV's operand, built from the final rows (NORM or SWIGLU)
     float* out = nullptr;        // [T][O]
     int add = 0;                 // 1: out += W.x (residual)
     float* ss_out = nullptr;     // != null: [O/128][VMAX] sums of squares of the new out rows (next RMSNorm)
@@ -99,7 +85,8 @@ struct AbArgs {
 // y[T][O] (+)= W . rotate(x) for T <= 16 rows.
 void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const GemvOut& o, const AbArgs* ab,
                          cudaStream_t st);
-// Whether every CTA of the GEMV fits on the GPU at once (needed when it produces the next operand).
+int gemv_grid(const TernaryMat& m, int ab_rows);
+// Whether every CTA of the GEMV fits on the GPU at once (needed when its CTAs build the operand together).
 bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms);
 
 // ------------------------------------------------------------------------------------------------ GatedDeltaNet
@@ -119,11 +106,8 @@ struct GdnArgs {
     float* pend_ab;        // [2][VMAX][2NV] gate inputs (replay; written by the qkvz GEMV)
     float* y;              // [T][NV*128]
     int C, NK, NV, T;
-    OpOut op;              // the output GEMV's operand (GATED), built by the CTA that completes each block
 };
 void launch_gdn_layer(const GdnArgs& a, cudaStream_t st);
-// Whether all CTAs of the layer kernel fit on the GPU at once (needed when it produces the next operand).
-bool gdn_coresident(const GdnArgs& a, int num_sms);
 
 // Standalone verify step with rollback (graded config 2).
 void launch_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
@@ -145,7 +129,6 @@ struct AttnArgs {
     unsigned* counters;    // [VMAX][KV] zero between launches
     float* out;            // [T][H*256]
     int H, KV, rot, T, ld, ctx;
-    OpOut op;              // the output GEMV's operand (GATE), each row's columns written by its merging CTAs
 };
 void launch_attn(const AttnArgs& a, cudaStream_t st);
 

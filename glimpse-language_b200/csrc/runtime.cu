@@ -234,29 +234,18 @@ GdnArgs gdn_args(bcu_model* m, const Layer& L, int T) {
 // The kernels of one pass of T rows, in order (Text::encode_embed + encode_layers + encode_head, model.rs:641-985):
 // per layer the mixer's input GEMV (norm + rotation; the GDN a/b gates ride along), the mixer core (GDN conv +
 // recurrence, or attention), the mixer's output GEMV (gated norm / gate + rotation, residual add), the MLP gate/up
-// GEMV (norm + rotation) and the down GEMV (SwiGLU + rotation, residual add); then the head. Except for the first
-// GEMV (embedding rows), each GEMV's rotated operand is built once by the kernel before it (its epilogue: the down /
-// mixer-output / gate-up GEMV, the GDN layer, attention) into one of two alternating buffers.
+// GEMV (norm + rotation) and the down GEMV (SwiGLU + rotation, residual add); then the head. Each GEMV's CTAs build
+// its rotated operand once, together, in a global buffer and copy their slices from it.
 void enqueue_pass(bcu_model* m, int T) {
     const bcu_config& c = m->c;
     const int NT = (2 * T + 7) / 8, d = c.hidden;
     cudaStream_t st = m->st;
-    int nbuf = 0;
-    const uint8_t* pending = nullptr;  // the operand the last producer built for the next GEMV
-    auto producer = [&](OpOut& op, int mode, int K, const float* w, const float* signs) {
-        op.buf = m->opbuf[nbuf++ & 1];
-        op.mode = mode;
-        op.K = K;
-        op.group = c.group_size;
-        op.HB = c.hadamard;
-        op.w = w;
-        op.signs = signs;
-        op.counters = m->op_counters;
-        pending = op.buf;
-    };
-    auto consume = [&](ActSrc& s) {
-        s.opbuf = pending;
-        pending = nullptr;
+    // the GEMV's CTAs build its operand together when they all fit on the GPU at once (grid_build, ternary.cu)
+    auto grid_built = [&](ActSrc& src, const TernaryMat& mat, int ab_rows) {
+        if (gemv_coresident(mat, T, ab_rows, c.hadamard, m->num_sms)) {
+            src.opbuf = m->opbuf[0];
+            src.op_counters = m->op_counters;
+        }
     };
     GemvOut store, resid;
     store.partial = resid.partial = m->partial;
@@ -280,7 +269,6 @@ void enqueue_pass(bcu_model* m, int T) {
         in.h_out = m->h;
         in.HB = c.hadamard;
         in.vocab = c.vocab;
-        consume(in);
         GemvOut mixo = store;
         mixo.out = m->mix;
         ActSrc out;
@@ -293,19 +281,9 @@ void enqueue_pass(bcu_model* m, int T) {
             ab.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * c.lin_v_heads;
             ab.ctl = m->ctl;
             ab.nv = c.lin_v_heads;
+            grid_built(in, L.mix_in.m, 2 * c.lin_v_heads);
             launch_ternary_gemv(L.mix_in.m, in, T, mixo, &ab, st);
-            GdnArgs g = gdn_args(m, L, T);
-            GdnArgs probe = g;
-            probe.op.buf = m->opbuf[0];
-            probe.op.HB = c.hadamard;
-            probe.op.group = c.group_size;
-            if (gdn_coresident(probe, m->num_sms)) {
-                producer(g.op, ACT_GATED, c.lin_v_heads * 128, L.gnorm, L.mix_out.signs);
-                g.op.x2 = m->mix;
-                g.op.ld2 = m->C + m->gw;
-                g.op.off2 = m->C;
-            }
-            launch_gdn_layer(g, st);
+            launch_gdn_layer(gdn_args(m, L, T), st);
             out.mode = ACT_GATED;
             out.x = m->y;
             out.x2 = m->mix;
@@ -313,6 +291,7 @@ void enqueue_pass(bcu_model* m, int T) {
             out.off2 = m->C;
             out.w = L.gnorm;
         } else {
+            grid_built(in, L.mix_in.m, 0);
             launch_ternary_gemv(L.mix_in.m, in, T, mixo, nullptr, st);
             AttnArgs a{};
             a.ctl = m->ctl;
@@ -331,44 +310,31 @@ void enqueue_pass(bcu_model* m, int T) {
             a.T = T;
             a.ld = 2 * m->aw + 2 * m->kvw;
             a.ctx = c.ctx;
-            if ((c.heads / c.kv_heads) * 256 % c.hadamard == 0) {  // each kv head's rows cover whole blocks
-                producer(a.op, ACT_GATE, m->aw, nullptr, L.mix_out.signs);
-                a.op.x2 = m->mix;
-                a.op.ld2 = a.ld;
-            }
             launch_attn(a, st);
             out.mode = ACT_GATE;
             out.x = m->y;
             out.x2 = m->mix;
             out.ld2 = a.ld;
         }
-        consume(out);
-        GemvOut ro = resid;
-        if (gemv_coresident(L.mix_out.m, T, 0, c.hadamard, m->num_sms))
-            producer(ro.op, ACT_NORM, d, L.post_norm, L.gu.signs);
-        launch_ternary_gemv(L.mix_out.m, out, T, ro, nullptr, st);
+        grid_built(out, L.mix_out.m, 0);
+        launch_ternary_gemv(L.mix_out.m, out, T, resid, nullptr, st);
         ActSrc post = in;
         post.mode = ACT_NORM;
         post.w = L.post_norm;
         post.signs = L.gu.signs;
-        consume(post);
+        post.opbuf = nullptr;
+        post.op_counters = nullptr;
+        grid_built(post, L.gu.m, 0);
         GemvOut guo = store;
         guo.out = m->gubuf;
-        if (gemv_coresident(L.gu.m, T, 0, c.hadamard, m->num_sms))
-            producer(guo.op, ACT_SWIGLU, c.intermediate, nullptr, L.down.signs);
         launch_ternary_gemv(L.gu.m, post, T, guo, nullptr, st);
         ActSrc sw;
         sw.mode = ACT_SWIGLU;
         sw.x = m->gubuf;
         sw.signs = L.down.signs;
         sw.HB = c.hadamard;
-        consume(sw);
-        GemvOut dno = resid;
-        if (li + 1 < m->layers.size() && gemv_coresident(L.down.m, T, 0, c.hadamard, m->num_sms)) {
-            const Layer& N = m->layers[li + 1];
-            producer(dno.op, ACT_NORM, d, N.in_norm, N.mix_in.signs);
-        }
-        launch_ternary_gemv(L.down.m, sw, T, dno, nullptr, st);
+        grid_built(sw, L.down.m, 0);
+        launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st);
     }
     HeadArgs ha{};
     ha.ctl = m->ctl;

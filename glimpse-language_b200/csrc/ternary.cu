@@ -25,8 +25,7 @@
 namespace bcu {
 
 constexpr float EPS_T = 1e-6f;
-// shared-memory header: mbarriers at 0 (codes) and 8 (operand), per-token RMS scales [16] at 16, exponents [16][4]
-// at 128
+// shared-memory header: mbarriers at 0 (codes) and 8 (operand), exponents [16][4] at 128
 constexpr int GEMV_HDR = 384;
 
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
@@ -403,76 +402,65 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
     }
 }
 
-// The next GEMV's operand from this GEMV's final rows (GemvOut::op), called by the CTA that finalised row block rb
-// after its output is stored. NORM: x = h, the next GEMV's input is this GEMV's output (block b = HB/128 row blocks);
-// SWIGLU: x = silu(g) u with g, u the two halves of this GEMV's rows (block b = HB/128 row blocks of each half). The
-// `need` CTAs that finalise a block's row blocks share its tokens: contributor ci builds tokens ci, ci + need, ...
-// (one warp each) once every contributor has arrived, and stores those tokens' columns of the block's regions.
-// Every CTA of the grid is resident at once (the host checks), so the bounded wait ends. NORM leaves out the
-// per-token RMS scale: the next GEMV multiplies its outputs by it (the products are linear in it).
+// The whole operand of the GEMV, built once by its CTAs together into the global buffer src.opbuf: task i = (token
+// i / nblk, Hadamard block i % nblk of the K inputs) is built by warp i / n_main of CTA i % n_main (load, producer,
+// signs, Walsh-Hadamard, fp16 hi/lo, exponent, group sums) into a scratch region in shared memory, whose columns for
+// the token are then stored to the buffer. Then every CTA waits (bounded) until all builder CTAs have counted
+// themselves; the grid is resident at once (the host checks), so the wait ends. counters[0] counts builders,
+// counters[1] the CTAs past the wait (the last resets both for the next GEMV).
 template <int VPL, int GPC>
-__device__ void produce_operand(const GemvParams& p, int rb, uint8_t* scratch, int* s_ok) {
+__device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
     constexpr int HBe = VPL * 32, G = 128 / GPC;
-    const OpOut& op = p.o.op;
+    const ActSrc& s = p.src;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = HBe / 128;
-    const bool swiglu = op.mode == ACT_SWIGLU;
-    const int half_rb = p.nrb / 2;
-    const int b = swiglu ? (rb % half_rb) / per : rb / per;
-    const int need = swiglu ? 2 * per : per;
-    const int ci = swiglu ? (rb / half_rb) * per + (rb % half_rb) % per : rb % per;
-    const int T = p.T, O = p.O, k0 = b * HBe;
-    unsigned* arrive = op.counters + b;
-    unsigned* done = op.counters + 256 + b;
-    __syncthreads();  // every output row of this CTA is stored
-    if (tid == 0) {
-        arrive_release(arrive);
-        *s_ok = ci < T ? spin_until_geq(arrive, (unsigned)need) : 1;
-        if (!*s_ok) atomicOr(p.o.err, ERR_SPIN_TIMEOUT);
-    }
-    __syncthreads();
-    const int t = ci + need * warp;
-    if (*s_ok && t < T) {
-        const int rsz = op_region_bytes(HBe, G);
-        const OpGeo geo{HBe, 0, VPL, 0, true};
+    const int T = p.T, K = p.K, nblk = K / HBe, ntask = T * nblk;
+    const int c = blockIdx.x, ncta = p.n_main;
+    const int nbuild = ntask < ncta ? ntask : ncta;  // CTAs with at least one task
+    const int rsz = op_region_bytes(HBe, G);
+    const OpGeo geo{HBe, 0, VPL, 0, s.HB > 0};
+    const int i = c + ncta * warp;
+    if (i < ntask) {
+        const int t = i / nblk, b = i % nblk, blk0 = b * HBe;
+        uint8_t* reg = scratch + (size_t)warp * rsz;
         float v[VPL], sg[VPL];
-        if (swiglu) {
-            float g[VPL], u[VPL];
+        if (s.signs) {
 #pragma unroll
-            for (int e = 0; e < VPL; e++) {
-                g[e] = __ldcg(p.o.out + (size_t)t * O + k0 + lane + 32 * e);
-                u[e] = __ldcg(p.o.out + (size_t)t * O + O / 2 + k0 + lane + 32 * e);
-            }
-#pragma unroll
-            for (int e = 0; e < VPL; e++) v[e] = (g[e] * u[e]) * sigm(g[e]);
+            for (int e = 0; e < VPL; e++) sg[e] = s.signs[blk0 + lane + 32 * e];
+        }
+        if (s.mode == ACT_EMBED) {
+            uint32_t id = 0;
+            const float r = row_scale(s, t, K, &id, b == 0);  // the builder of block 0 writes the residual row
+            act_values<VPL>(s, t, blk0, K, r, id, v);
         } else {
             float wn[VPL];
+            if (s.mode == ACT_NORM) {
 #pragma unroll
-            for (int e = 0; e < VPL; e++) {
-                v[e] = __ldcg(p.o.out + (size_t)t * O + k0 + lane + 32 * e);
-                wn[e] = op.w[k0 + lane + 32 * e];
+                for (int e = 0; e < VPL; e++) wn[e] = s.w[blk0 + lane + 32 * e];
+            } else if (s.mode == ACT_GATED) {
+#pragma unroll
+                for (int q = 0; q < 4; q++) wn[q] = s.w[(lane + 32 * q) & 127];
             }
-#pragma unroll
-            for (int e = 0; e < VPL; e++) v[e] *= wn[e];
+            RawTok<VPL> R;
+            load_raw<VPL>(s, t, blk0, K, R);
+            transform<VPL>(s, K, R, wn, v);
         }
-        if (op.signs) {
-#pragma unroll
-            for (int e = 0; e < VPL; e++) sg[e] = op.signs[k0 + lane + 32 * e];
-        }
-        uint8_t* reg = scratch + (size_t)warp * rsz;
-        emit_token<VPL, GPC>(geo, t, reg, v, op.signs ? sg : nullptr);
+        emit_token<VPL, GPC>(geo, t, reg, v, s.signs ? sg : nullptr);
         __syncwarp();
-        store_token_columns(t, HBe, G, reg, op.buf + ((size_t)b * 4 + (t >> 2)) * rsz);
+        store_token_columns(t, HBe, G, reg, s.opbuf + ((size_t)b * 4 + (t >> 2)) * rsz);
+    }
+    __syncthreads();  // this CTA's tasks are stored
+    if (tid == 0) {
+        if (c < nbuild) arrive_release(s.op_counters);
+        *s_ok = spin_until_geq(s.op_counters, (unsigned)nbuild);
+        if (!*s_ok) atomicOr(p.o.err, ERR_SPIN_TIMEOUT);
+        unsigned old;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(s.op_counters + 1) : "memory");
+        if (old == (unsigned)(ncta - 1)) {  // every CTA is past the wait
+            s.op_counters[0] = 0;
+            s.op_counters[1] = 0;
+        }
     }
     __syncthreads();
-    if (tid == 0) {  // the last contributor to finish resets the block's counts for the next producer
-        unsigned old;
-        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(done) : "memory");
-        if (old == (unsigned)(need - 1)) {
-            *arrive = 0;
-            *done = 0;
-        }
-    }
 }
 
 // GDN a/b gate rows (dense fp32, gdn_ab_row kernels.metal:265-273): rows [r0, r0 + nr) of [Wa; Wb], nr <= AB_ROWS,
@@ -589,8 +577,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
     constexpr int G = 128 / GPC;
     uint64_t* bar = (uint64_t*)smem;           // codes + scales of this CTA
-    uint64_t* bar_op = (uint64_t*)(smem + 8);  // operand regions from the producing kernel
-    float* s_r = (float*)(smem + 16);          // [16] per-token RMS scale (operand without it), else 1
+    uint64_t* bar_op = (uint64_t*)(smem + 8);  // this slice's regions of the grid-built operand
     int* s_e = (int*)(smem + 128);             // [token][block] exponents, kept for the reduction
     const int kslice = p.kslice, nkc = kslice / 128;
     const int sbsz = min(VPL * 32, kslice), nb = kslice / sbsz;
@@ -600,7 +587,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     uint8_t* s_codes = smem + GEMV_HDR;
     uint32_t* s_sb = (uint32_t*)(smem + GEMV_HDR + codes_bytes);
     uint8_t* s_op = smem + GEMV_HDR + codes_bytes + sb_bytes;  // regions [nb][NT]
-    const bool prebuilt = p.src.opbuf != nullptr;
+    const bool prebuilt = p.src.opbuf != nullptr;  // operand built by the whole grid (grid_build)
 
     const int rb = blockIdx.x % p.nrb, ks = blockIdx.x / p.nrb;
     const int nkc_all = p.K / 128;
@@ -618,12 +605,6 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
                  (uint32_t)sb_bytes, bar);
     }
     pdl_wait();
-    if (prebuilt && tid == 0) {  // the slice's regions: nb blocks of NT tiles (the buffer holds 4 tiles per block)
-        mbar_expect_tx(bar_op, (uint32_t)(nb * NT * rsz));
-        for (int b = 0; b < nb; b++)
-            bulk_g2s(s_op + (size_t)b * NT * rsz, p.src.opbuf + ((size_t)(ks * nb + b) * 4) * rsz, (uint32_t)(NT * rsz),
-                     bar_op);
-    }
     float res[8];  // residual rows of this row block (element e = tid + 256 i of [T][128]), read early
     if (p.o.add) {
 #pragma unroll
@@ -632,15 +613,15 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             res[i] = e < 128 * p.T ? p.o.out[(size_t)(e >> 7) * p.O + rb * 128 + (e & 127)] : 0.0f;
         }
     }
-    if (warp < 2) {  // per-token output scale: the RMS scale when the producer left it out
-        const int t = warp * 8 + (lane >> 2);
-        float a = 0.0f;
-        const bool norm = prebuilt && p.src.mode == ACT_NORM;
-        if (norm && t < p.T)
-            for (int i = lane & 3; i < p.src.nss; i += 4) a += p.src.ss[i * VMAX + t];
-        a += __shfl_xor_sync(0xffffffffu, a, 1);
-        a += __shfl_xor_sync(0xffffffffu, a, 2);
-        if ((lane & 3) == 0) s_r[t] = norm ? rsqrtf(a / (float)p.K + EPS_T) : 1.0f;
+    if (prebuilt) {
+        __shared__ int s_ok;
+        grid_build<VPL, GPC>(p, s_op, &s_ok);
+        if (tid == 0) {  // the slice's regions: nb blocks of NT tiles (the buffer holds 4 tiles per block)
+            mbar_expect_tx(bar_op, (uint32_t)(nb * NT * rsz));
+            for (int b = 0; b < nb; b++)
+                bulk_g2s(s_op + (size_t)b * NT * rsz, p.src.opbuf + ((size_t)(ks * nb + b) * 4) * rsz,
+                         (uint32_t)(NT * rsz), bar_op);
+        }
     }
     if (!prebuilt) build_operand<VPL, GPC>(p, ks, sbsz, nb, NT, s_op, rsz);
     __syncthreads();
@@ -780,7 +761,6 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         v += red[quarter + e] * pow2f(-et[blk_of_q[1]]);
         v += red[2 * quarter + e] * pow2f(-et[blk_of_q[2]]);
         v += red[3 * quarter + e] * pow2f(-et[blk_of_q[3]]);
-        v *= s_r[token];
         if (p.nsplit == 1) fin[token * 128 + rloc] = v;
         else p.o.partial[((size_t)ks * T + token) * O + rb * 128 + rloc] = v;
     }
@@ -836,20 +816,24 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             if (lane == 0) p.o.ss_out[rb * VMAX + token] = a;
         }
     }
-    if (p.o.op.buf) produce_operand<VPL, GPC>(p, rb, smem + GEMV_HDR, &s_last);
 }
 
-static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb, bool produce) {
+// tpc: grid-build tasks per CTA (their scratch regions share the operand's space), 0 without a grid build.
+static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb, int tpc) {
     int gpc = 128 / group;
     int sbsz = hb < kslice ? hb : kslice;
-    size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 +
-                  (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
+    size_t ops = (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
+    size_t scratch = (size_t)tpc * op_region_bytes(hb, group);
+    size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 + (ops > scratch ? ops : scratch);
     size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
     size_t abs_ = ab ? ((size_t)(AB_ROWS + T) * K + 8 * 64 + 32) * 4 : 0;
-    size_t prod = produce ? GEMV_HDR + (size_t)4 * op_region_bytes(hb, group) : 0;  // <= 4 tokens per CTA
     size_t s = main > red ? main : red;
-    s = s > abs_ ? s : abs_;
-    return s > prod ? s : prod;
+    return s > abs_ ? s : abs_;
+}
+
+static int grid_build_tpc(const TernaryMat& m, int T, int hb) {
+    const int ntask = T * (m.K / hb), ncta = (m.O / 128) * m.nsplit;
+    return (ntask + ncta - 1) / ncta;
 }
 
 template <int NT, int GPC, int VPL>
@@ -877,20 +861,24 @@ static const void* gemv_fn_gpc(int group, int hb) {
     return group == 64 ? gemv_fn_vpl<NT, 2>(hb) : gemv_fn_vpl<NT, 1>(hb);
 }
 
-// Whether every CTA of this GEMV's grid can be resident at once (required when it produces the next operand: its
-// CTAs wait for one another).
+int gemv_grid(const TernaryMat& m, int ab_rows) { return (m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS; }
+
+// Whether this GEMV's CTAs can build its operand together (grid_build): every CTA of the grid resident at once
+// (they wait for one another) and at most 8 tasks (one per warp) per CTA.
 bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms) {
     const int nt = (2 * T + 7) / 8;
+    const int tpc = grid_build_tpc(m, T, hb);
+    if (tpc > 8 || hb <= 0) return false;
     const void* fn = nt == 1 ? gemv_fn_gpc<1>(m.group, hb)
                    : nt == 2 ? gemv_fn_gpc<2>(m.group, hb)
                    : nt == 3 ? gemv_fn_gpc<3>(m.group, hb)
                              : gemv_fn_gpc<4>(m.group, hb);
-    const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, true);
+    const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, tpc);
+    if (smem > 220 * 1024) return false;
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess) return false;
-    const long grid = (long)(m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS;
-    return grid <= (long)per_sm * num_sms;
+    return (long)gemv_grid(m, ab_rows) <= (long)per_sm * num_sms;
 }
 
 template <int NT, int GPC>
@@ -925,7 +913,8 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     p.nrb = m.O / 128;
     int hb = src.HB > 0 ? src.HB : 512;  // unrotated sources use 512-element blocks for their exponents
     int nt = (2 * T + 7) / 8;
-    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb, o.op.buf != nullptr);
+    size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb,
+                            src.opbuf ? grid_build_tpc(m, T, hb) : 0);
     if (nt == 1) launch_gpc<1>(p, hb, smem, st);
     else if (nt == 2) launch_gpc<2>(p, hb, smem, st);
     else if (nt == 3) launch_gpc<3>(p, hb, smem, st);
