@@ -13,8 +13,8 @@ MAX_LAYERS = 64
 VMAX = 16
 
 # bcu_status
-OK, ERR_CUDA, ERR_ARG, ERR_OOM, ERR_TIMEOUT, ERR_CANCELLED, ERR_STATE, ERR_NOT_FOUND, ERR_TOO_LARGE = range(9)
-STATUS_NAMES = ["OK", "CUDA", "ARG", "OOM", "TIMEOUT", "CANCELLED", "STATE", "NOT_FOUND", "TOO_LARGE"]
+OK, ERR_CUDA, ERR_ARG, ERR_OOM, ERR_TIMEOUT, ERR_CANCELLED, ERR_STATE, ERR_NOT_FOUND, ERR_TOO_LARGE, ERR_IO = range(10)
+STATUS_NAMES = ["OK", "CUDA", "ARG", "OOM", "TIMEOUT", "CANCELLED", "STATE", "NOT_FOUND", "TOO_LARGE", "IO"]
 # bcu_dtype
 U32, F16, BF16, F32 = range(4)
 # draft modes
@@ -103,6 +103,16 @@ SIGNATURES = {
     "bcu_state_read": (I32, [P, P, I32, P, U64]),
     "bcu_state_write": (I32, [P, P, I32, P, U64, I32]),
     "bcu_state_new": (I32, [P, I32, ctypes.POINTER(P)]),
+    "bcu_hash_bytes": (U64, [U64, P, U64]),
+    "bcu_kernel_hash": (U64, []),
+    "bcu_prefix_identity": (I32, [P, U64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, P, U64,
+                                  ctypes.POINTER(U64)]),
+    "bcu_prefix_path": (I32, [ctypes.c_char_p, P, U64, PU32, I32, ctypes.c_char_p, U64]),
+    "bcu_prefix_save": (I32, [P, P, ctypes.c_char_p, P, U64, PU32, I32, I32]),
+    "bcu_prefix_wait_saves": (I32, []),
+    "bcu_prefix_load": (I32, [P, ctypes.c_char_p, P, U64, PU32, I32, ctypes.POINTER(P)]),
+    "bcu_prefix_file_write": (I32, [ctypes.c_char_p, P, U64, PU32, I32, ctypes.POINTER(P), ctypes.POINTER(U64)]),
+    "bcu_prefix_file_read": (I32, [ctypes.c_char_p, P, U64, PU32, I32, ctypes.POINTER(P), ctypes.POINTER(U64), PI32]),
     "bcu_set_vocab_bytes": (I32, [P, P, ctypes.POINTER(U64), I32]),
     "bcu_decode": (
         I32,

@@ -13,6 +13,9 @@ class BackendError(RuntimeError):
         self.message = message
 
 
+PREFIX_SLOTS = 3  # runtime/mod.rs:213
+
+
 def _u32(a):
     return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
 
@@ -21,6 +24,11 @@ class Model:
     def __init__(self, cfg, device=0):
         self.L = _lib.lib()
         self.cfg = cfg
+        # prefix cache (runtime/mod.rs:213-223, 455-485): newest first, (ids, adapter, Snapshot)
+        self.prefixes = []
+        self.adapter = 0
+        self.prefix_dir = None
+        self.identity = None
         self.h = ctypes.c_void_p()
         s = self.L.bcu_create(ctypes.byref(cfg), device, ctypes.byref(self.h))
         if s != _lib.OK:
@@ -120,6 +128,63 @@ class Model:
         s = ctypes.c_void_p()
         self._ck(self.L.bcu_state_new(self.h, length, ctypes.byref(s)))
         return Snapshot(self, s)
+
+    # ---------------------------------------------------------------- saved prefix files (BNSPFX01)
+    def prefix_identity(self, adapter, weights, config, exe=None):
+        """Model::prefix_identity (runtime/mod.rs:494-510); None when a file cannot be read."""
+        n = ctypes.c_uint64()
+        args = (self.h, adapter, exe.encode() if exe else None, weights.encode(), config.encode())
+        s = self.L.bcu_prefix_identity(*args, None, 0, ctypes.byref(n))
+        if s == _lib.ERR_NOT_FOUND:
+            return None
+        self._ck(s)
+        buf = ctypes.create_string_buffer(n.value)
+        self._ck(self.L.bcu_prefix_identity(*args, buf, n.value, ctypes.byref(n)))
+        return buf.raw[: n.value]
+
+    def save_prefix(self, snap, directory, identity, ids, background=False):
+        """Model::save_prefix (runtime/mod.rs:549-578)."""
+        ids = _u32(ids)
+        self._ck(self.L.bcu_prefix_save(self.h, snap.h, directory.encode(), identity, len(identity),
+                                        ids.ctypes.data_as(_lib.PU32), len(ids), 1 if background else 0))
+
+    def load_prefix(self, directory, identity, ids):
+        """Model::load_prefix (runtime/mod.rs:517-546): a Snapshot, or None when there is no usable file."""
+        ids = _u32(ids)
+        s = ctypes.c_void_p()
+        self._ck(self.L.bcu_prefix_load(self.h, directory.encode(), identity, len(identity),
+                                        ids.ctypes.data_as(_lib.PU32), len(ids), ctypes.byref(s)))
+        return Snapshot(self, s) if s.value else None
+
+    def set_prefix_files(self, directory, identity):
+        """Model::prefix_dir plus the identity its files are saved under (None: memory slots only)."""
+        self.prefix_dir, self.identity = directory, identity
+
+    def start_prefix(self, prefix):
+        """Model::start_prefix (runtime/mod.rs:455-485): restores the state after `prefix` from a memory slot or a
+        saved file, or prefills it, keeps it in a slot and saves it. Returns the number of tokens served from a
+        cache."""
+        prefix = [int(t) for t in prefix]
+        if not prefix:
+            self.reset()
+            return 0
+        hit = next((i for i, (ids, ad, _) in enumerate(self.prefixes) if ids == prefix and ad == self.adapter), None)
+        snap = self.prefixes.pop(hit)[2] if hit is not None else None
+        files = self.prefix_dir is not None and self.identity is not None
+        if snap is None and files:
+            snap = self.load_prefix(self.prefix_dir, self.identity, prefix)
+        if snap is not None:
+            self.restore(snap)
+            self.prefixes.insert(0, (prefix, self.adapter, snap))
+            return len(prefix)
+        self.reset()
+        self.prefill(prefix)
+        snap = self.snapshot()
+        if files:
+            self.save_prefix(snap, self.prefix_dir, self.identity, prefix, background=True)
+        self.prefixes.insert(0, (prefix, self.adapter, snap))
+        del self.prefixes[PREFIX_SLOTS:]
+        return 0
 
     # ---------------------------------------------------------------- decoding
     def decode(self, first, user=(), *, speculate=True, mode=_lib.DRAFT_LOOKUP, planted=None, seed=0, eos=(),
@@ -224,3 +289,54 @@ class Snapshot:
             self.free()
         except Exception:
             pass
+
+
+# -------------------------------------------------------------------- prefix files, host only
+def hash_bytes(h, data):
+    """hash_bytes (runtime/mod.rs:225-235)."""
+    data = bytes(data)
+    return _lib.lib().bcu_hash_bytes(h, data, len(data))
+
+
+def kernel_hash():
+    return _lib.lib().bcu_kernel_hash()
+
+
+def prefix_path(directory, identity, ids):
+    """Model::prefix_path (runtime/mod.rs:512-515)."""
+    ids = _u32(ids)
+    buf = ctypes.create_string_buffer(len(directory) + 64)
+    s = _lib.lib().bcu_prefix_path(directory.encode(), identity, len(identity), ids.ctypes.data_as(_lib.PU32),
+                                   len(ids), buf, len(buf))
+    if s != _lib.OK:
+        raise BackendError(s, "prefix path")
+    return buf.value.decode()
+
+
+def wait_saves():
+    """Joins the background prefix writers."""
+    _lib.lib().bcu_prefix_wait_saves()
+
+
+def file_write(directory, identity, ids, parts):
+    """The prefix file writer on host buffers (uint8 arrays), as bcu_prefix_save writes it."""
+    ids = _u32(ids)
+    parts = [np.ascontiguousarray(np.frombuffer(bytes(p), np.uint8)) for p in parts]
+    ptrs = (ctypes.c_void_p * 4)(*[p.ctypes.data if p.size else None for p in parts])
+    sizes = (ctypes.c_uint64 * 4)(*[p.size for p in parts])
+    return _lib.lib().bcu_prefix_file_write(directory.encode(), identity, len(identity),
+                                            ids.ctypes.data_as(_lib.PU32), len(ids), ptrs, sizes)
+
+
+def file_read(directory, identity, ids, sizes):
+    """The prefix file reader on host buffers: the parts as bytes, or None when there is no usable file."""
+    ids = _u32(ids)
+    bufs = [np.zeros(max(int(n), 1), np.uint8) for n in sizes]
+    ptrs = (ctypes.c_void_p * 4)(*[b.ctypes.data for b in bufs])
+    sz = (ctypes.c_uint64 * 4)(*[int(n) for n in sizes])
+    found = ctypes.c_int32()
+    s = _lib.lib().bcu_prefix_file_read(directory.encode(), identity, len(identity), ids.ctypes.data_as(_lib.PU32),
+                                        len(ids), ptrs, sz, ctypes.byref(found))
+    if s != _lib.OK:
+        raise BackendError(s, "prefix file read")
+    return [b[: int(n)].tobytes() for b, n in zip(bufs, sizes)] if found.value else None

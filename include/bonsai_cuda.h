@@ -36,7 +36,8 @@ typedef enum {
     BCU_ERR_CANCELLED = 5, /* the cancel flag was raised between steps (ext.rs:21-42) */
     BCU_ERR_STATE = 6,     /* call out of order (e.g. verify before finalize, context full) */
     BCU_ERR_NOT_FOUND = 7, /* unknown or missing tensor name */
-    BCU_ERR_TOO_LARGE = 8  /* sizes beyond a fixed capacity (the static scratch of bcu_linear_rotate_forward_static) */
+    BCU_ERR_TOO_LARGE = 8, /* sizes beyond a fixed capacity (the static scratch of bcu_linear_rotate_forward_static) */
+    BCU_ERR_IO = 9         /* a prefix file could not be written (save_prefix drops it silently, mod.rs:562-565) */
 } bcu_status;
 
 /* Tensor element types of bcu_load_tensor. */
@@ -156,6 +157,42 @@ bcu_status bcu_state_parts(const bcu_model* m, const bcu_state* s, uint64_t size
 bcu_status bcu_state_read(const bcu_model* m, const bcu_state* s, int32_t part, void* host, uint64_t bytes);
 bcu_status bcu_state_write(bcu_model* m, bcu_state* s, int32_t part, const void* host, uint64_t bytes, int32_t len);
 bcu_status bcu_state_new(bcu_model* m, int32_t len, bcu_state** out);
+
+/* ------------------------------------------------------------------ saved prefix files (BNSPFX01) */
+
+/* Layout (runtime/mod.rs:494-578; all integers little-endian): identity | ids u32[n] | len u64 (= n) | pos i64 (= n,
+ * text only) | state parts gdn, conv, K, V as bcu_state_parts sizes them. identity = "BNSPFX01" | u64 words [kernel
+ * hash, adapter, exe size, exe mtime ns, weights size, weights mtime ns, hash(config bytes), n_gdn, n_attn, hidden,
+ * kv_width, conv_dim] | device name bytes. File "{dir}/{h:016x}.prefix", h = hash(hash(FNV, identity), ids bytes). */
+
+/* hash_bytes (runtime/mod.rs:225-235): FNV-1a style over little-endian 8-byte words, then tail bytes, ^ length. */
+uint64_t bcu_hash_bytes(uint64_t h, const void* data, uint64_t n);
+/* Stands in for hash_bytes(FNV, gpu::KERNEL_BLOB) (runtime/mod.rs:501): the first 64 bits of the SHA-256 of the
+ * CUDA sources and nvcc flags this library was built from. */
+uint64_t bcu_kernel_hash(void);
+/* Model::prefix_identity (runtime/mod.rs:494-510). exe_path NULL = the running executable. BCU_ERR_NOT_FOUND when
+ * a file cannot be read (the reference returns None: nothing is saved or loaded). out NULL: *len only. */
+bcu_status bcu_prefix_identity(const bcu_model* m, uint64_t adapter, const char* exe_path, const char* weights_path,
+                               const char* config_path, uint8_t* out, uint64_t cap, uint64_t* len);
+/* Model::prefix_path (runtime/mod.rs:512-515), NUL-terminated into out. */
+bcu_status bcu_prefix_path(const char* dir, const uint8_t* identity, uint64_t identity_len, const uint32_t* ids,
+                           int32_t n, char* out, uint64_t out_len);
+/* Model::save_prefix (runtime/mod.rs:549-578): reads the snapshot's parts to the host on this thread, then writes
+ * {h}.tmp, renames it to {h}.prefix and keeps the newest 3 .prefix files of dir (PREFIX_SLOTS, mod.rs:213), on a
+ * background thread when background != 0 (failures there are dropped, as in the reference). s's length must be n. */
+bcu_status bcu_prefix_save(bcu_model* m, const bcu_state* s, const char* dir, const uint8_t* identity,
+                           uint64_t identity_len, const uint32_t* ids, int32_t n, int32_t background);
+/* Joins the background writers started by bcu_prefix_save. (No counterpart: the reference detaches them.) */
+bcu_status bcu_prefix_wait_saves(void);
+/* Model::load_prefix (runtime/mod.rs:517-546): *out = a new snapshot of n tokens when {dir}/{h}.prefix has exactly
+ * this identity and these ids, len = n and exactly the parts' bytes; NULL (status BCU_OK) for any other file or none. */
+bcu_status bcu_prefix_load(bcu_model* m, const char* dir, const uint8_t* identity, uint64_t identity_len,
+                           const uint32_t* ids, int32_t n, bcu_state** out);
+/* The file writer and reader alone, on host buffers (no device): the same bytes as bcu_prefix_save / _load. */
+bcu_status bcu_prefix_file_write(const char* dir, const uint8_t* identity, uint64_t identity_len, const uint32_t* ids,
+                                 int32_t n, const void* const parts[4], const uint64_t sizes[4]);
+bcu_status bcu_prefix_file_read(const char* dir, const uint8_t* identity, uint64_t identity_len, const uint32_t* ids,
+                                int32_t n, void* const parts[4], const uint64_t sizes[4], int32_t* found);
 
 /* ------------------------------------------------------------------ decode driver (runtime/mod.rs:774-956) */
 
