@@ -50,6 +50,17 @@ class BcuConfig(ctypes.Structure):
     ]
 
 
+class BcuLoraLinear(ctypes.Structure):
+    _fields_ = [
+        ("layer", ctypes.c_int32),
+        ("module", ctypes.c_char_p),
+        ("a", ctypes.POINTER(ctypes.c_float)),
+        ("b", ctypes.POINTER(ctypes.c_float)),
+        ("a_shape", ctypes.c_int64 * 2),
+        ("b_shape", ctypes.c_int64 * 2),
+    ]
+
+
 class BcuSpec(ctypes.Structure):
     _fields_ = [("ngram_max", ctypes.c_int32), ("ngram_min", ctypes.c_int32), ("draft_max", ctypes.c_int32)]
 
@@ -103,6 +114,8 @@ SIGNATURES = {
     "bcu_state_read": (I32, [P, P, I32, P, U64]),
     "bcu_state_write": (I32, [P, P, I32, P, U64, I32]),
     "bcu_state_new": (I32, [P, I32, ctypes.POINTER(P)]),
+    "bcu_set_lora": (I32, [P, ctypes.POINTER(BcuLoraLinear), I32, ctypes.c_float]),
+    "bcu_lora_info": (I32, [P, PI32, PI32]),
     "bcu_hash_bytes": (U64, [U64, P, U64]),
     "bcu_kernel_hash": (U64, []),
     "bcu_prefix_identity": (I32, [P, U64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, P, U64,
@@ -135,7 +148,8 @@ SIGNATURES = {
     "bcu_enqueue_passes": (I32, [P, I32, I32, I32]),
     "bcu_sync": (I32, [P]),
     "bcu_stream": (I32, [P, ctypes.POINTER(P)]),
-    # host-logic exports (not in the ABI header: test hooks of the decode driver)
+    # host-logic exports (not in the ABI header: test hooks of the decode driver and the operand build)
+    "bcu_set_local_build": (I32, [P, I32]),
     "bcu_token_key": (U64, [P, U64]),
     "bcu_lookup": (I32, [PU32, I32, PU32, I32, ctypes.POINTER(U64), I32, I32, I32, I32, I32, I32, PU32, PI32]),
     "bcu_policy_choose": (I32, [ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_double), I32, I32,

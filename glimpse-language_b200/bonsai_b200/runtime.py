@@ -129,6 +129,50 @@ class Model:
         self._ck(self.L.bcu_state_new(self.h, length, ctypes.byref(s)))
         return Snapshot(self, s)
 
+    # ---------------------------------------------------------------- LoRA
+    def set_lora_linears(self, linears, fold):
+        """Text::set_lora with lora::load's tensors: linears = [(layer, module, A [r, in], B [out, r])] (empty
+        removes the adapter); fold = alpha / r x scale."""
+        arrs, items = [], (_lib.BcuLoraLinear * max(len(linears), 1))()
+        for i, (layer, module, a, b) in enumerate(linears):
+            a = np.ascontiguousarray(a, np.float32)
+            b = np.ascontiguousarray(b, np.float32)
+            mod = module.encode()
+            arrs += [a, b, mod]
+            it = items[i]
+            it.layer = layer
+            it.module = mod
+            it.a = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            it.b = b.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            it.a_shape[:] = list(a.shape) if a.ndim == 2 else [a.size, 1]
+            it.b_shape[:] = list(b.shape) if b.ndim == 2 else [b.size, 1]
+        self._ck(self.L.bcu_set_lora(self.h, items, len(linears), ctypes.c_float(fold)))
+
+    def set_lora(self, path=None, scale=1.0):
+        """Model::set_lora (runtime/mod.rs:328-337): loads the adapter file (or removes it: no path or scale 0),
+        records its id and drops the cached prefixes of other adapters."""
+        from . import lora
+
+        if path is not None and scale != 0.0:
+            linears, fold = lora.parse(path)
+            self.set_lora_linears(linears, float(np.float32(fold) * np.float32(scale)))
+            ident = lora.adapter_id(path, scale)
+        else:
+            self.set_lora_linears([], 1.0)
+            ident = 0
+        self.adapter = ident
+        self.prefixes = [p for p in self.prefixes if p[1] == ident]
+
+    def set_local_build(self, local=True):
+        """Test hook: every GEMV builds its operand per CTA instead of once across its grid."""
+        self._ck(self.L.bcu_set_local_build(self.h, 1 if local else 0))
+
+    def lora_info(self):
+        """Text::lora_info (model.rs:399-402): (adapted linears, rank), or None."""
+        n, r = ctypes.c_int32(), ctypes.c_int32()
+        self._ck(self.L.bcu_lora_info(self.h, ctypes.byref(n), ctypes.byref(r)))
+        return (n.value, r.value) if n.value else None
+
     # ---------------------------------------------------------------- saved prefix files (BNSPFX01)
     def prefix_identity(self, adapter, weights, config, exe=None):
         """Model::prefix_identity (runtime/mod.rs:494-510); None when a file cannot be read."""

@@ -110,3 +110,31 @@ def zipf_tokens(seed, n, vocab, s=1.1):
     out = np.empty(n, np.uint32)
     _lib.lib().bcu_synth_zipf(seed, s, vocab, out.ctypes.data_as(_lib.PU32), n)
     return out
+
+
+def lora_modules(cfg, layer):
+    """Text::linears (model.rs:372-385) of one layer: [(module, out, in)]."""
+    d, ff = cfg.hidden, cfg.intermediate
+    dm = dims(cfg)
+    if cfg.layer_is_attn[layer]:
+        mods = [("self_attn.q_proj", 2 * dm["aw"], d), ("self_attn.k_proj", dm["kvw"], d),
+                ("self_attn.v_proj", dm["kvw"], d), ("self_attn.o_proj", d, dm["aw"])]
+    else:
+        mods = [("linear_attn.in_proj_qkv", dm["C"], d), ("linear_attn.in_proj_z", dm["gw"], d),
+                ("linear_attn.out_proj", d, dm["gw"])]
+    return mods + [("mlp.gate_proj", ff, d), ("mlp.up_proj", ff, d), ("mlp.down_proj", d, ff)]
+
+
+def lora_linears(cfg, rank, seed=77, std_a=0.02, std_b=0.01, modules=None):
+    """A seeded adapter on every linear of every layer (or those whose module name is in `modules`): A ~ N(0, std_a)
+    [rank, in], B ~ N(0, std_b) [out, rank] (the graded 4B adapter: rank 16, A 0.02, B 0.01, alpha 32)."""
+    out, stream = [], 0
+    for layer in range(cfg.n_layers):
+        for mod, o, k in lora_modules(cfg, layer):
+            if modules is not None and mod not in modules:
+                continue
+            a = fill(1, seed, stream, 0.0, std_a, (rank, k), np.float32)
+            b = fill(1, seed, stream + 1, 0.0, std_b, (o, rank), np.float32)
+            stream += 2
+            out.append((layer, mod, a, b))
+    return out

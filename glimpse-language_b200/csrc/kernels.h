@@ -82,12 +82,24 @@ struct AbArgs {
     int nv = 0;
 };
 
-// y[T][O] (+)= W . rotate(x) for T <= 16 rows.
+// LoRA of one packed linear (lora.rs:1-5; fused like norm_rotate's A rows and the matmuls' B epilogue,
+// kernels.metal:70-116, 251-262): y += B . (A . x) on the linear's unrotated input x. A of the members stacked
+// (R = members x r rows), fp16, in the operand builders' lane order [K / HB][R][32 lanes][HB / 32]; B fp16 [O][r]
+// (alpha / r and the scale folded in); member i owns rows [m[i], m[i + 1]) of O and u rows [i r, (i + 1) r).
+struct LoraArgs {
+    const uint16_t* a = nullptr;  // null: no LoRA
+    const uint16_t* b = nullptr;
+    float* upart = nullptr;       // [VMAX][K / HB][R] partial A . x per (token, Hadamard block)
+    int R = 0, r = 0;             // r a multiple of 8 (the adapter's rank, zero-padded)
+    int m1 = 0, m2 = 0;           // member starts 1, 2 (O when absent)
+};
+
+// y[T][O] (+)= W . rotate(x) (+ LoRA) for T <= 16 rows.
 void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const GemvOut& o, const AbArgs* ab,
-                         cudaStream_t st);
+                         cudaStream_t st, const LoraArgs* lora = nullptr);
 int gemv_grid(const TernaryMat& m, int ab_rows);
 // Whether every CTA of the GEMV fits on the GPU at once (needed when its CTAs build the operand together).
-bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms);
+bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms, int lora_r = 0);
 
 // ------------------------------------------------------------------------------------------------ GatedDeltaNet
 // One launch per GDN layer: conv (with the deferred conv-state commit) + gated delta rule (with the deferred replay)

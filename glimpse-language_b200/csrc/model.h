@@ -23,6 +23,7 @@ struct DevTensor {
 struct Lin {
     TernaryMat m;
     const float* signs = nullptr;
+    LoraArgs lora;  // a == null: no adapter on this linear
 };
 
 struct Layer {
@@ -79,8 +80,9 @@ struct bcu_model {
     float* partial = nullptr;
     unsigned* counters = nullptr;
     unsigned* head_counter = nullptr;
-    uint8_t* opbuf[2] = {nullptr, nullptr};  // GEMV operands built by the kernel before each GEMV (alternating)
-    unsigned* op_counters = nullptr;         // per-block arrival counts of the operand producers
+    bool local_build = false;         // test hook: every GEMV builds its operand per CTA (no grid-wide build)
+    uint8_t* opbuf = nullptr;         // a GEMV's rotated operand, built by its CTAs together (grid_build)
+    unsigned* op_counters = nullptr;  // 2 words: builder CTAs arrived, CTAs past the grid-wide wait
     size_t opbuf_bytes = 0;
     float* pv = nullptr;
     int* pi = nullptr;
@@ -108,6 +110,12 @@ struct bcu_model {
     int len = 0;          // committed tokens including the pending commit (= ctl->off)
     int last_t = 0;       // rows of the last pass
     int pending_n = 0;    // rows of the last pass still to be committed on the device
+
+    // LoRA adapter (lora.rs, Text::set_lora model.rs:392-397): one device buffer of every group's A and B, and the
+    // partial products of the GEMV that runs
+    void* lora_buf = nullptr;
+    float* lora_upart = nullptr;
+    int lora_rank = 0, lora_linears = 0;
 
     // drafting
     std::vector<uint64_t> keys;   // token_key per vocab id

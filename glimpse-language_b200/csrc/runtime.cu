@@ -241,12 +241,13 @@ void enqueue_pass(bcu_model* m, int T) {
     const int NT = (2 * T + 7) / 8, d = c.hidden;
     cudaStream_t st = m->st;
     // the GEMV's CTAs build its operand together when they all fit on the GPU at once (grid_build, ternary.cu)
-    auto grid_built = [&](ActSrc& src, const TernaryMat& mat, int ab_rows) {
-        if (gemv_coresident(mat, T, ab_rows, c.hadamard, m->num_sms)) {
-            src.opbuf = m->opbuf[0];
+    auto grid_built = [&](ActSrc& src, const Lin& ln, int ab_rows) {
+        if (!m->local_build && gemv_coresident(ln.m, T, ab_rows, c.hadamard, m->num_sms, ln.lora.a ? ln.lora.r : 0)) {
+            src.opbuf = m->opbuf;
             src.op_counters = m->op_counters;
         }
     };
+    auto lora_of = [](const Lin& ln) { return ln.lora.a ? &ln.lora : nullptr; };
     GemvOut store, resid;
     store.partial = resid.partial = m->partial;
     store.counters = resid.counters = m->counters;
@@ -281,8 +282,8 @@ void enqueue_pass(bcu_model* m, int T) {
             ab.pend_ab = m->pend_ab + (size_t)L.gi * 2 * VMAX * 2 * c.lin_v_heads;
             ab.ctl = m->ctl;
             ab.nv = c.lin_v_heads;
-            grid_built(in, L.mix_in.m, 2 * c.lin_v_heads);
-            launch_ternary_gemv(L.mix_in.m, in, T, mixo, &ab, st);
+            grid_built(in, L.mix_in, 2 * c.lin_v_heads);
+            launch_ternary_gemv(L.mix_in.m, in, T, mixo, &ab, st, lora_of(L.mix_in));
             launch_gdn_layer(gdn_args(m, L, T), st);
             out.mode = ACT_GATED;
             out.x = m->y;
@@ -291,8 +292,8 @@ void enqueue_pass(bcu_model* m, int T) {
             out.off2 = m->C;
             out.w = L.gnorm;
         } else {
-            grid_built(in, L.mix_in.m, 0);
-            launch_ternary_gemv(L.mix_in.m, in, T, mixo, nullptr, st);
+            grid_built(in, L.mix_in, 0);
+            launch_ternary_gemv(L.mix_in.m, in, T, mixo, nullptr, st, lora_of(L.mix_in));
             AttnArgs a{};
             a.ctl = m->ctl;
             a.qkv = m->mix;
@@ -316,25 +317,25 @@ void enqueue_pass(bcu_model* m, int T) {
             out.x2 = m->mix;
             out.ld2 = a.ld;
         }
-        grid_built(out, L.mix_out.m, 0);
-        launch_ternary_gemv(L.mix_out.m, out, T, resid, nullptr, st);
+        grid_built(out, L.mix_out, 0);
+        launch_ternary_gemv(L.mix_out.m, out, T, resid, nullptr, st, lora_of(L.mix_out));
         ActSrc post = in;
         post.mode = ACT_NORM;
         post.w = L.post_norm;
         post.signs = L.gu.signs;
         post.opbuf = nullptr;
         post.op_counters = nullptr;
-        grid_built(post, L.gu.m, 0);
+        grid_built(post, L.gu, 0);
         GemvOut guo = store;
         guo.out = m->gubuf;
-        launch_ternary_gemv(L.gu.m, post, T, guo, nullptr, st);
+        launch_ternary_gemv(L.gu.m, post, T, guo, nullptr, st, lora_of(L.gu));
         ActSrc sw;
         sw.mode = ACT_SWIGLU;
         sw.x = m->gubuf;
         sw.signs = L.down.signs;
         sw.HB = c.hadamard;
-        grid_built(sw, L.down.m, 0);
-        launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st);
+        grid_built(sw, L.down, 0);
+        launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st, lora_of(L.down));
     }
     HeadArgs ha{};
     ha.ctl = m->ctl;
@@ -608,11 +609,10 @@ bcu_status bcu_finalize(bcu_model* m) {
     m->head_grid = m->num_sms;  // one CTA per SM (head.cu)
     TRY(dmalloc(m, &m->head_counter, 4));
     {
-        // operand buffers: [K / HB blocks][4 tiles][region] for the widest GEMV input
+        // operand buffer: [K / HB blocks][4 tiles][region] for the widest GEMV input
         const int kmax = std::max(std::max(c.hidden, c.intermediate), std::max(m->aw, c.lin_v_heads * 128));
         m->opbuf_bytes = (size_t)(kmax / c.hadamard) * 4 * op_region_bytes(c.hadamard, c.group_size);
-        TRY(dmalloc(m, &m->opbuf[0], m->opbuf_bytes));
-        TRY(dmalloc(m, &m->opbuf[1], m->opbuf_bytes));
+        TRY(dmalloc(m, &m->opbuf, m->opbuf_bytes));
         TRY(dmalloc(m, &m->op_counters, 512 * 4));
     }
     TRY(dmalloc(m, &m->pv, (size_t)m->head_grid * VMAX * 4));
@@ -659,7 +659,7 @@ void bcu_destroy(bcu_model* m) {
     void* bufs[] = {m->arena, m->gdn, m->conv, m->kc, m->vc, m->pend_qkv, m->pend_qkvc, m->pend_ab, m->h,
                     m->mix, m->gubuf, m->y, m->apart, m->ssbuf, m->attn_counters, m->logits,
                     m->partial, m->counters, m->head_counter, m->pv, m->pi, m->ctl, m->planted_dev,
-                    m->opbuf[0], m->opbuf[1], m->op_counters};
+                    m->opbuf, m->op_counters, m->lora_buf, m->lora_upart};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (m->h_in) cudaFreeHost(m->h_in);
@@ -1005,6 +1005,21 @@ bcu_status bcu_time_pass(bcu_model* m, int32_t t, int32_t iters, float* ms_per_p
     TRY(wait_stream(m, WAIT_S));
     bcu_state_free(snap);
     *ms_per_pass = total / iters;
+    return BCU_OK;
+}
+
+// Test hook (not in the ABI header): local != 0 makes every GEMV build its operand per CTA (build_operand) instead of
+// once across the grid, so tests cover both paths; the pass graphs are recaptured.
+bcu_status bcu_set_local_build(bcu_model* m, int32_t local) {
+    if (!m || !m->finalized) return BCU_ERR_ARG;
+    TRY(wait_stream(m, WAIT_S));
+    for (int t = 0; t <= VMAX; t++) {
+        if (m->graphs[t]) cudaGraphExecDestroy(m->graphs[t]);
+        m->graphs[t] = nullptr;
+        m->graph_nodes[t] = 0;
+    }
+    m->local_build = local != 0;
+    m->cost_ready = false;
     return BCU_OK;
 }
 

@@ -18,6 +18,8 @@
 // the residual add and the sums of squares the next norm needs and, when asked, contributes to the next GEMV's
 // operand: the CTA that completes a Hadamard block of the next GEMV's input builds the block's regions.
 #include <cstdio>
+#include <mutex>
+#include <set>
 #include "common.cuh"
 #include "kernels.h"
 #include "operand.cuh"
@@ -141,6 +143,7 @@ struct GemvParams {
     ActSrc src;
     GemvOut o;
     AbArgs ab;
+    LoraArgs lora;
     int O, K, group, kslice, nsplit, T, n_main, ab_rows;
     int nrb;  // row blocks; CTA = ks * nrb + rb
 };
@@ -325,10 +328,60 @@ __device__ __forceinline__ void transform(const ActSrc& s, int K, const RawTok<V
     }
 }
 
+// LoRA A of one (token t, Hadamard block b) (norm_rotate's fused A rows, kernels.metal:70-116): each lane's dot
+// products of its VPL unrotated values with the stacked A rows, 8 rows at a time (few registers: this runs inside the
+// GEMV), summed across the warp in a fixed order: a halving butterfly over offsets 16, 8, 4 leaves lane l with row
+// (l >> 2) & 7 of the chunk, then offsets 2 and 1 complete the sum. Stored to upart[t][b][row]; the order does not
+// depend on T.
+template <int VPL>
+__device__ __forceinline__ void lora_partial(const LoraArgs& L, int t, int b, int nblk, const float* v) {
+    const int lane = threadIdx.x & 31, R = L.R;
+    float* dst = L.upart + ((size_t)t * nblk + b) * R;
+#pragma unroll 1
+    for (int c0 = 0; c0 < R; c0 += 8) {
+        float acc[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            acc[q] = 0.0f;
+            const uint4* ap = (const uint4*)(L.a + (((size_t)b * R + c0 + q) * 32 + lane) * VPL);
+#pragma unroll
+            for (int u = 0; u < VPL / 8; u++) {
+                const uint4 w = __ldg(ap + u);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    const float2 f = __half22float2(*(const __half2*)&ws[h]);
+                    acc[q] = fmaf(f.x, v[8 * u + 2 * h], acc[q]);
+                    acc[q] = fmaf(f.y, v[8 * u + 2 * h + 1], acc[q]);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16, n = 4; o >= 4; o >>= 1, n >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < n; j++) {
+                const float send = up ? acc[j] : acc[j + n];
+                const float keep = up ? acc[j + n] : acc[j];
+                acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        float a = acc[0];
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        if ((lane & 3) == 0) dst[c0 + (lane >> 2)] = a;
+    }
+}
+
+template <int VPL, bool LORA>
+__device__ __forceinline__ void lora_partial_if(const GemvParams& p, int t, int b, const float* v) {
+    if constexpr (LORA) lora_partial<VPL>(p.lora, t, b, p.K / (VPL * 32), v);
+}
+
 // This CTA's operand for K-slice ks, built by its own warps (sources without a producing kernel: the embedding
 // rows of the first layer, standalone inputs): warp w takes block w % nb of the slice and the token slots w / nb,
 // w / nb + 8 / nb, ...; the next token's loads are in flight while the current one is built. Regions [nb][NT].
-template <int VPL, int GPC>
+template <int VPL, int GPC, bool LORA>
 __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int NT, uint8_t* s_op, int rsz) {
     constexpr int HBe = VPL * 32, G = 128 / GPC;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -359,6 +412,7 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
             uint32_t id = 0;
             const float r = row_scale(s, t, K, &id, blockIdx.x == 0 && b == 0);
             act_values<VPL>(s, t, blk0, K, r, id, v);
+            lora_partial_if<VPL, LORA>(p, t, blk0 / HBe, v);
             emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
         }
         return;
@@ -381,6 +435,7 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
             if (t < T) {
                 float v[VPL];
                 transform<VPL>(s, K, cur, wn, v);
+                lora_partial_if<VPL, LORA>(p, t, blk0 / HBe, v);
                 emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
             } else {
                 zero_token(t, sbsz, G, region(t));
@@ -394,6 +449,7 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
                 load_raw<VPL>(s, t, blk0, K, cur);
                 float v[VPL];
                 transform<VPL>(s, K, cur, wn, v);
+                lora_partial_if<VPL, LORA>(p, t, blk0 / HBe, v);
                 emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
             } else {
                 zero_token(t, sbsz, G, region(t));
@@ -408,7 +464,7 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
 // the token are then stored to the buffer. Then every CTA waits (bounded) until all builder CTAs have counted
 // themselves; the grid is resident at once (the host checks), so the wait ends. counters[0] counts builders,
 // counters[1] the CTAs past the wait (the last resets both for the next GEMV).
-template <int VPL, int GPC>
+template <int VPL, int GPC, bool LORA>
 __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
     constexpr int HBe = VPL * 32, G = 128 / GPC;
     const ActSrc& s = p.src;
@@ -444,6 +500,7 @@ __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
             load_raw<VPL>(s, t, blk0, K, R);
             transform<VPL>(s, K, R, wn, v);
         }
+        lora_partial_if<VPL, LORA>(p, t, b, v);
         emit_token<VPL, GPC>(geo, t, reg, v, s.signs ? sg : nullptr);
         __syncwarp();
         store_token_columns(t, HBe, G, reg, s.opbuf + ((size_t)b * 4 + (t >> 2)) * rsz);
@@ -565,7 +622,7 @@ __device__ void ab_rows(const GemvParams& p, int r0, int nr, uint8_t* smem) {
     }
 }
 
-template <int NT, int GPC, int VPL>
+template <int NT, int GPC, int VPL, bool LORA>
 __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -615,7 +672,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
     if (prebuilt) {
         __shared__ int s_ok;
-        grid_build<VPL, GPC>(p, s_op, &s_ok);
+        grid_build<VPL, GPC, LORA>(p, s_op, &s_ok);
         if (tid == 0) {  // the slice's regions: nb blocks of NT tiles (the buffer holds 4 tiles per block)
             mbar_expect_tx(bar_op, (uint32_t)(nb * NT * rsz));
             for (int b = 0; b < nb; b++)
@@ -623,7 +680,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
                          (uint32_t)(NT * rsz), bar_op);
         }
     }
-    if (!prebuilt) build_operand<VPL, GPC>(p, ks, sbsz, nb, NT, s_op, rsz);
+    if (!prebuilt) build_operand<VPL, GPC, LORA>(p, ks, sbsz, nb, NT, s_op, rsz);
     __syncthreads();
     const bool ok = mbar_wait_bounded(bar, 0) && (!prebuilt || mbar_wait_bounded(bar_op, 0));
     if (__syncthreads_or(!ok)) {
@@ -792,13 +849,48 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         if (tid == 0) p.o.counters[rb] = 0;
     }
     __syncthreads();
-    // output (store or residual add) and the sums of squares of the new rows
+    // LoRA: u = A . x of this row block's member (u[t][j] = sum over the Hadamard blocks of the builders' partials,
+    // in block order; every partial was stored before the grid-wide wait or this row block's split-K count)
+    const LoraArgs& L = p.lora;
+    const int lr = L.r;
+    float* s_u = fin + 128 * T;  // [T][lr]
+    const uint16_t* lb = nullptr;
+    if (LORA) {
+        const int row0 = rb * 128, mem = (row0 >= L.m1) + (row0 >= L.m2), nblk = p.K / (VPL * 32);
+        for (int i = tid; i < T * lr; i += 256) {
+            const int t = i / lr, j = i % lr;
+            const float* src = L.upart + (size_t)t * nblk * L.R + mem * lr + j;
+            float a = 0.0f;
+            for (int b = 0; b < nblk; b++) a += __ldcg(src + (size_t)b * L.R);
+            s_u[i] = a;
+        }
+        lb = L.b + (size_t)row0 * lr;
+        __syncthreads();
+    }
+    // output (store or residual add, then the LoRA up projection, as store_post kernels.metal:257-262) and the sums
+    // of squares of the new rows
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int e = tid + 256 * i;
         if (e < 128 * T) {
             float v = fin[e];
             if (p.o.add) v = res[i] + v;
+            if (LORA) {
+                const uint4* bp = (const uint4*)(lb + (size_t)(e & 127) * lr);
+                const float* ut = s_u + (e >> 7) * lr;
+                float a = 0.0f;
+                for (int j0 = 0; j0 < lr; j0 += 8) {
+                    const uint4 w = __ldg(bp + j0 / 8);
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float2 f = __half22float2(*(const __half2*)&ws[h]);
+                        a = fmaf(ut[j0 + 2 * h], f.x, a);
+                        a = fmaf(ut[j0 + 2 * h + 1], f.y, a);
+                    }
+                }
+                v = v + a;
+            }
             p.o.out[(size_t)(e >> 7) * O + rb * 128 + (e & 127)] = v;
             fin[e] = v;
         }
@@ -819,13 +911,13 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
 }
 
 // tpc: grid-build tasks per CTA (their scratch regions share the operand's space), 0 without a grid build.
-static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb, int tpc) {
+static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int hb, int tpc, int lora_r) {
     int gpc = 128 / group;
     int sbsz = hb < kslice ? hb : kslice;
     size_t ops = (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
     size_t scratch = (size_t)tpc * op_region_bytes(hb, group);
     size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 + (ops > scratch ? ops : scratch);
-    size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * 128 * 4;
+    size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * (128 + lora_r) * 4;
     size_t abs_ = ab ? ((size_t)(AB_ROWS + T) * K + 8 * 64 + 32) * 4 : 0;
     size_t s = main > red ? main : red;
     return s > abs_ ? s : abs_;
@@ -836,72 +928,57 @@ static int grid_build_tpc(const TernaryMat& m, int T, int hb) {
     return (ntask + ncta - 1) / ncta;
 }
 
-template <int NT, int GPC, int VPL>
-static void launch_gemv_t(const GemvParams& p, size_t smem, cudaStream_t st) {
-    auto fn = ternary_gemv_kernel<NT, GPC, VPL>;
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-        attr_done = true;
-    }
-    GemvParams pp = p;
-    void* args[] = {&pp};
-    const int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
-    launch_pdl((const void*)fn, dim3((unsigned)(p.n_main + n_ab)), dim3(256), smem, st, args);
-}
-
 template <int NT, int GPC>
-static const void* gemv_fn_vpl(int hb) {
-    if (hb == 512) return (const void*)ternary_gemv_kernel<NT, GPC, 16>;
-    if (hb == 1024) return (const void*)ternary_gemv_kernel<NT, GPC, 32>;
-    return (const void*)ternary_gemv_kernel<NT, GPC, 64>;
+static const void* gemv_fn_vpl(int hb, bool lora) {
+    if (lora)  // LoRA variants: 512- and 1024-point blocks (bcu_set_lora checks)
+        return hb == 512 ? (const void*)ternary_gemv_kernel<NT, GPC, 16, true>
+                         : (const void*)ternary_gemv_kernel<NT, GPC, 32, true>;
+    if (hb == 512) return (const void*)ternary_gemv_kernel<NT, GPC, 16, false>;
+    if (hb == 1024) return (const void*)ternary_gemv_kernel<NT, GPC, 32, false>;
+    return (const void*)ternary_gemv_kernel<NT, GPC, 64, false>;
 }
 template <int NT>
-static const void* gemv_fn_gpc(int group, int hb) {
-    return group == 64 ? gemv_fn_vpl<NT, 2>(hb) : gemv_fn_vpl<NT, 1>(hb);
+static const void* gemv_fn_gpc(int group, int hb, bool lora) {
+    return group == 64 ? gemv_fn_vpl<NT, 2>(hb, lora) : gemv_fn_vpl<NT, 1>(hb, lora);
+}
+// The kernel for nt column tiles, its shared-memory limit raised once.
+static const void* gemv_fn(int nt, int group, int hb, bool lora) {
+    const void* fn = nt == 1 ? gemv_fn_gpc<1>(group, hb, lora)
+                   : nt == 2 ? gemv_fn_gpc<2>(group, hb, lora)
+                   : nt == 3 ? gemv_fn_gpc<3>(group, hb, lora)
+                             : gemv_fn_gpc<4>(group, hb, lora);
+    static std::mutex mu;
+    static std::set<const void*> raised;
+    std::lock_guard<std::mutex> g(mu);
+    if (raised.insert(fn).second) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    return fn;
 }
 
 int gemv_grid(const TernaryMat& m, int ab_rows) { return (m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS; }
 
 // Whether this GEMV's CTAs can build its operand together (grid_build): every CTA of the grid resident at once
 // (they wait for one another) and at most 8 tasks (one per warp) per CTA.
-bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms) {
+bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms, int lora_r) {
     const int nt = (2 * T + 7) / 8;
     const int tpc = grid_build_tpc(m, T, hb);
     if (tpc > 8 || hb <= 0) return false;
-    const void* fn = nt == 1 ? gemv_fn_gpc<1>(m.group, hb)
-                   : nt == 2 ? gemv_fn_gpc<2>(m.group, hb)
-                   : nt == 3 ? gemv_fn_gpc<3>(m.group, hb)
-                             : gemv_fn_gpc<4>(m.group, hb);
-    const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, tpc);
+    const void* fn = gemv_fn(nt, m.group, hb, lora_r > 0);
+    const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, tpc, lora_r);
     if (smem > 220 * 1024) return false;
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess) return false;
     return (long)gemv_grid(m, ab_rows) <= (long)per_sm * num_sms;
 }
 
-template <int NT, int GPC>
-static void launch_vpl(const GemvParams& p, int hb, size_t smem, cudaStream_t st) {
-    if (hb == 512) launch_gemv_t<NT, GPC, 16>(p, smem, st);
-    else if (hb == 1024) launch_gemv_t<NT, GPC, 32>(p, smem, st);
-    else launch_gemv_t<NT, GPC, 64>(p, smem, st);
-}
-
-template <int NT>
-static void launch_gpc(const GemvParams& p, int hb, size_t smem, cudaStream_t st) {
-    if (p.group == 64) launch_vpl<NT, 2>(p, hb, smem, st);
-    else launch_vpl<NT, 1>(p, hb, smem, st);
-}
-
 void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const GemvOut& o, const AbArgs* ab,
-                         cudaStream_t st) {
+                         cudaStream_t st, const LoraArgs* lora) {
     GemvParams p;
     p.codes = (const uint8_t*)m.codes;
     p.sb = m.sb;
     p.src = src;
     p.o = o;
     p.ab = ab ? *ab : AbArgs();
+    p.lora = lora ? *lora : LoraArgs();
     p.O = m.O;
     p.K = m.K;
     p.group = m.group;
@@ -914,11 +991,11 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     int hb = src.HB > 0 ? src.HB : 512;  // unrotated sources use 512-element blocks for their exponents
     int nt = (2 * T + 7) / 8;
     size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb,
-                            src.opbuf ? grid_build_tpc(m, T, hb) : 0);
-    if (nt == 1) launch_gpc<1>(p, hb, smem, st);
-    else if (nt == 2) launch_gpc<2>(p, hb, smem, st);
-    else if (nt == 3) launch_gpc<3>(p, hb, smem, st);
-    else launch_gpc<4>(p, hb, smem, st);
+                            src.opbuf ? grid_build_tpc(m, T, hb) : 0, p.lora.a ? p.lora.r : 0);
+    const void* fn = gemv_fn(nt, m.group, hb, p.lora.a != nullptr);
+    void* args[] = {&p};
+    const int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
+    launch_pdl(fn, dim3((unsigned)(p.n_main + n_ab)), dim3(256), smem, st, args);
 }
 
 }  // namespace bcu

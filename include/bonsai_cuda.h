@@ -103,6 +103,29 @@ bcu_status bcu_finalize(bcu_model* m);
 /* Text::reset (model.rs:404-409): empty KV, zero GDN/conv state, no pending accept. */
 bcu_status bcu_reset(bcu_model* m);
 
+/* ------------------------------------------------------------------ LoRA adapter (lora.rs, config 4) */
+
+/* One adapted linear of lora::load (lora.rs:89-174) after the safetensors file is read: y = base(x) + (x A^T) B^T on
+ * the linear's unrotated input. module is a Text::linears name (model.rs:372-385): "self_attn.q_proj" (q with its
+ * gate rows), "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj", "linear_attn.in_proj_qkv",
+ * "linear_attn.in_proj_z", "linear_attn.out_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj". */
+typedef struct {
+    int32_t layer;
+    const char* module;
+    const float* a;      /* lora_A [a_shape[0] = r][a_shape[1] = in], rounded to fp16 on load (lora.rs:111-118) */
+    const float* b;      /* lora_B [b_shape[0] = out][b_shape[1] = r], times fold, then rounded to fp16 */
+    int64_t a_shape[2];
+    int64_t b_shape[2];
+} bcu_lora_linear;
+/* Text::set_lora (model.rs:392-397) with lora::load's grouping: linears that share an input share one stacked A (a
+ * member the adapter lacks gets zero A and B rows). n == 0 removes the adapter. fold = alpha / r for PEFT keys
+ * (peft_scaling, lora.rs:73-86) times the caller's scale. Errors as lora.rs: unknown module, shape mismatch, mixed
+ * ranks; also Hadamard blocks above 1024 inputs. Recaptures the pass graphs and drops the verify-cost table; the
+ * caller drops cached prefix states of another adapter (Model::set_lora, mod.rs:328-337). */
+bcu_status bcu_set_lora(bcu_model* m, const bcu_lora_linear* lins, int32_t n, float fold);
+/* Text::lora_info (model.rs:399-402): adapted linears and rank, 0 and 0 without an adapter. */
+bcu_status bcu_lora_info(const bcu_model* m, int32_t* linears, int32_t* rank);
+
 const char* bcu_last_error(const bcu_model* m);
 void bcu_destroy(bcu_model* m);
 

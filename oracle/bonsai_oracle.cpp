@@ -203,7 +203,30 @@ struct Lin {
     const uint16_t* b = nullptr;
     const float* signs = nullptr;
     int O = 0, K = 0;
+    // LoRA (lora.rs:89-174): A [lr][K] and B [O][lr] as the device holds them (fp16 values; B with alpha / r folded)
+    std::vector<float> la, lb;
+    int lr = 0;
 };
+
+// y[t] += B (A xu[t]) for T rows (lora.rs:1-3: on the linear's unrotated input), sums in index order: u as
+// norm_rotate's A rows (kernels.metal:70-116), the up projection as lora_acc (:251-255).
+void lora_add(const Lin& l, const float* xu, int T, float* y) {
+    if (!l.lr) return;
+    std::vector<float> u(l.lr);
+    for (int t = 0; t < T; t++) {
+        const float* x = xu + (size_t)t * l.K;
+        for (int j = 0; j < l.lr; j++) {
+            float a = 0;
+            for (int k = 0; k < l.K; k++) a += l.la[(size_t)j * l.K + k] * x[k];
+            u[j] = a;
+        }
+        for (int o = 0; o < l.O; o++) {
+            float a = 0;
+            for (int j = 0; j < l.lr; j++) a += u[j] * l.lb[(size_t)o * l.lr + j];
+            y[(size_t)t * l.O + o] += a;
+        }
+    }
+}
 
 struct Layer {
     bool attn = false;
@@ -334,6 +357,8 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
             // recurrent (gdn_recurrent :566-622), gated norm + rotate (:199-226), out_proj with add (model.rs:813)
             ternary_linear(L.qkv.w, L.qkv.s, L.qkv.b, C, d, c.group_size, xr.data(), T, a1.data());
             ternary_linear(L.z.w, L.z.s, L.z.b, gw, d, c.group_size, xr.data(), T, a2.data());
+            lora_add(L.qkv, xn.data(), T, a1.data());
+            lora_add(L.z, xn.data(), T, a2.data());
             std::vector<float> ab((size_t)T * 2 * NV);
             for (int t = 0; t < T; t++)
                 for (int r = 0; r < 2 * NV; r++) {
@@ -390,8 +415,9 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
                     }
                 }
             }
+            std::vector<float> xu((size_t)T * gw);
             for (int t = 0; t < T; t++) {
-                float* xo = tmp.data() + (size_t)t * gw;
+                float* xo = xu.data() + (size_t)t * gw;
                 for (int hd = 0; hd < NV; hd++) {
                     const float* yh = y.data() + (size_t)t * gw + hd * 128;
                     float r = rms_scale(yh, 128);
@@ -404,6 +430,7 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
             }
             ternary_linear(L.out.w, L.out.s, L.out.b, d, gw, c.group_size, xr.data(), T, tmp.data());
             for (size_t i = 0; i < (size_t)T * d; i++) h[i] += tmp[i];
+            lora_add(L.out, xu.data(), T, h.data());
         } else {
             // q (with gate) / k / v (model.rs:825), attn_prep (:828-851), split attention + combine
             // (kernels.metal:713-799) as one exact softmax, gate_rotate (:170-188), o_proj with add (model.rs:894)
@@ -411,6 +438,9 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
             ternary_linear(L.q.w, L.q.s, L.q.b, 2 * aw, d, c.group_size, xr.data(), T, qp.data());
             ternary_linear(L.k.w, L.k.s, L.k.b, kvw, d, c.group_size, xr.data(), T, kp.data());
             ternary_linear(L.v.w, L.v.s, L.v.b, kvw, d, c.group_size, xr.data(), T, vp.data());
+            lora_add(L.q, xn.data(), T, qp.data());
+            lora_add(L.k, xn.data(), T, kp.data());
+            lora_add(L.v, xn.data(), T, vp.data());
             float* kc = m->kc.data() + (size_t)L.ai * c.ctx * kvw;
             float* vc = m->vc.data() + (size_t)L.ai * c.ctx * kvw;
             std::vector<float> qr((size_t)T * H * 256);
@@ -451,8 +481,9 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
                 }
                 for (int dd = 0; dd < 256; dd++) y[(size_t)t * aw + hh * 256 + dd] = acc[dd] / l;
             }
+            std::vector<float> xu((size_t)T * aw);
             for (int t = 0; t < T; t++) {
-                float* xo = tmp.data() + (size_t)t * aw;
+                float* xo = xu.data() + (size_t)t * aw;
                 for (int e = 0; e < aw; e++) {
                     int hd = e >> 8, dd = e & 255;
                     float gt = qp[(size_t)t * 2 * aw + hd * 512 + 256 + dd];
@@ -462,13 +493,17 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
             }
             ternary_linear(L.o.w, L.o.s, L.o.b, d, aw, c.group_size, xr.data(), T, tmp.data());
             for (size_t i = 0; i < (size_t)T * d; i++) h[i] += tmp[i];
+            lora_add(L.o, xu.data(), T, h.data());
         }
         // MLP (model.rs:897-932): norm_rotate, gate/up, swiglu_rotate (kernels.metal:147-164), down with add
         norm_rotate(m, h.data(), L.post_norm, L.gate.signs, T, xn.data(), xr.data());
         ternary_linear(L.gate.w, L.gate.s, L.gate.b, ff, d, c.group_size, xr.data(), T, a1.data());
         ternary_linear(L.up.w, L.up.s, L.up.b, ff, d, c.group_size, xr.data(), T, a2.data());
+        lora_add(L.gate, xn.data(), T, a1.data());
+        lora_add(L.up, xn.data(), T, a2.data());
+        std::vector<float> xu((size_t)T * ff);
         for (int t = 0; t < T; t++) {
-            float* xo = tmp.data() + (size_t)t * ff;
+            float* xo = xu.data() + (size_t)t * ff;
             for (int e = 0; e < ff; e++) {
                 float a = a1[(size_t)t * ff + e];
                 xo[e] = (a * a2[(size_t)t * ff + e]) * (1.0f / (1.0f + std::exp(-a)));
@@ -477,6 +512,7 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
         }
         ternary_linear(L.down.w, L.down.s, L.down.b, d, ff, c.group_size, xr.data(), T, tmp.data());
         for (size_t i = 0; i < (size_t)T * d; i++) h[i] += tmp[i];
+        lora_add(L.down, xu.data(), T, h.data());
     }
     // head (model.rs:941-985): final norm, tied table, argmax with ties to the lowest index (kernels.metal:802-842)
     int V = c.vocab;
@@ -735,6 +771,56 @@ void orc_model_restore(void* mp, const void* sp) {
 }
 
 void orc_state_free(void* sp) { delete (Snap*)sp; }
+
+// One adapted linear (lora.rs:89-174): A [r][K] rounded to fp16, B [O][r] times fold rounded to fp16. Returns 0, or
+// -1 for an unknown layer/module or a shape mismatch. r = 0 removes it.
+int orc_model_set_lora(void* mp, int layer, const char* module, const float* a, const float* b, int r, float fold) {
+    Model* m = (Model*)mp;
+    if (layer < 0 || layer >= (int)m->layers.size()) return -1;
+    Layer& L = m->layers[layer];
+    const std::string mod(module);
+    Lin* l = nullptr;
+    if (L.attn) {
+        if (mod == "self_attn.q_proj") l = &L.q;
+        if (mod == "self_attn.k_proj") l = &L.k;
+        if (mod == "self_attn.v_proj") l = &L.v;
+        if (mod == "self_attn.o_proj") l = &L.o;
+    } else {
+        if (mod == "linear_attn.in_proj_qkv") l = &L.qkv;
+        if (mod == "linear_attn.in_proj_z") l = &L.z;
+        if (mod == "linear_attn.out_proj") l = &L.out;
+    }
+    if (mod == "mlp.gate_proj") l = &L.gate;
+    if (mod == "mlp.up_proj") l = &L.up;
+    if (mod == "mlp.down_proj") l = &L.down;
+    if (!l) return -1;
+    l->lr = r;
+    l->la.assign((size_t)r * l->K, 0.0f);
+    l->lb.assign((size_t)l->O * r, 0.0f);
+    for (size_t i = 0; i < l->la.size(); i++) l->la[i] = f16_to_f32(f32_to_f16(a[i]));
+    for (size_t i = 0; i < l->lb.size(); i++) l->lb[i] = f16_to_f32(f32_to_f16(b[i] * fold));
+    return 0;
+}
+
+// lora_add on its own: y [T][O] += B (A xu) with A [r][K], B [O][r] taken as given (no rounding).
+void orc_lora_add(const float* a, const float* b, int r, int O, int K, const float* xu, int T, float* y) {
+    Lin l;
+    l.O = O;
+    l.K = K;
+    l.lr = r;
+    l.la.assign(a, a + (size_t)r * K);
+    l.lb.assign(b, b + (size_t)O * r);
+    lora_add(l, xu, T, y);
+}
+
+void orc_model_clear_lora(void* mp) {
+    for (Layer& L : ((Model*)mp)->layers)
+        for (Lin* l : {&L.qkv, &L.z, &L.out, &L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) {
+            l->lr = 0;
+            l->la.clear();
+            l->lb.clear();
+        }
+}
 void orc_model_destroy(void* mp) { delete (Model*)mp; }
 
 // Greedy decoding, one token per step (decode_plain semantics, runtime/mod.rs:901-956): out[0] = first.

@@ -54,6 +54,9 @@ def lib():
             "orc_state_free": (None, [P]),
             "orc_model_destroy": (None, [P]),
             "orc_greedy": (I, [P, ctypes.c_uint32, I, PU32, I, PU32]),
+            "orc_model_set_lora": (I, [P, I, ctypes.c_char_p, P, P, I, ctypes.c_float]),
+            "orc_model_clear_lora": (None, [P]),
+            "orc_lora_add": (None, [P, P, I, I, I, P, I, P]),
             "orc_token_key": (ctypes.c_uint64, [P, I]),
             "orc_lookup": (I, [PU32, I, PU32, I, ctypes.POINTER(ctypes.c_uint64), I, I, I, I, I, I, PU32, ctypes.POINTER(I)]),
             "orc_policy_choose": (I, [ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_double), I, I,
@@ -113,6 +116,14 @@ def gdn_verify(q, k, v, a, b, a_log, dt_bias, state, n):
     return y, st
 
 
+def lora_add(a, b, xu, y):
+    """y [T, O] + B (A xu) per row (the oracle's LoRA arithmetic); returns a new array."""
+    a, b, xu = (np.ascontiguousarray(x, np.float32) for x in (a, b, xu))
+    out = np.ascontiguousarray(y, np.float32).copy()
+    lib().orc_lora_add(ptr(a), ptr(b), a.shape[0], b.shape[0], a.shape[1], ptr(xu), xu.shape[0], ptr(out))
+    return out
+
+
 class OracleModel:
     """The oracle's Model: same tensor names and pass semantics as the product's bcu_model."""
 
@@ -126,6 +137,18 @@ class OracleModel:
             L.orc_model_load_tensor(self.h, name.encode(), code, shape, arr.ndim, ptr(arr))
         if L.orc_model_finalize(self.h) != 0:
             raise RuntimeError("oracle: missing or mis-shaped tensor")
+
+    def set_lora(self, linears, fold):
+        """linears: (layer, module, A [r, in], B [out, r]) as lora.rs reads them; fold = alpha / r x scale."""
+        lib().orc_model_clear_lora(self.h)
+        for layer, module, a, b in linears:
+            a = np.ascontiguousarray(a, np.float32)
+            b = np.ascontiguousarray(b, np.float32)
+            if lib().orc_model_set_lora(self.h, layer, module.encode(), ptr(a), ptr(b), a.shape[0], fold) != 0:
+                raise ValueError(f"oracle: no linear layers.{layer}.{module}")
+
+    def clear_lora(self):
+        lib().orc_model_clear_lora(self.h)
 
     def forward(self, ids, logits=False):
         ids = np.ascontiguousarray(ids, np.uint32)
