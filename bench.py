@@ -40,6 +40,13 @@ VERIFY_PASS_DRAM_BYTES = 1654.0e6
 PREFIX, USER, GEN, K_DRAFT = 1024, 256, 300, 8
 WORKLOAD = ("config3: Bonsai-2B shape random-init, 1024-token cached prefix + 256 Zipf(1.1) user tokens, "
             "300+ generated tokens, k=8 planted drafts (100% accept)")
+# --workload config4: the Bonsai-4B shape with a rank-16 LoRA on q/k/v/o and gate/up/down (A ~ N(0, 0.02),
+# B ~ N(0, 0.01), alpha 32), a 4096-token Zipf(1.1) prefill, then the same decode step
+PROMPT_4B, LORA_RANK, LORA_ALPHA = 4096, 16, 32
+LORA_MODULES = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj", "mlp.gate_proj",
+                "mlp.up_proj", "mlp.down_proj"}
+WORKLOAD_4B = ("config4: Bonsai-4B shape random-init + rank-16 LoRA (q/k/v/o, gate/up/down; alpha 32), 4096-token "
+               "Zipf(1.1) prefill, 300+ generated tokens, k=8 planted drafts (100% accept)")
 
 
 def dist_env():
@@ -193,6 +200,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="profiling run for ncu: prefill --profile-prefix tokens, then this many 9-row verify passes")
     ap.add_argument("--profile-prefix", type=int, default=256)
+    ap.add_argument("--workload", default="config3", choices=["config3", "config4"],
+                    help="config3 (default, the headline) or config4 (4B shape + LoRA)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
 
@@ -217,21 +226,39 @@ def main():
     from bonsai_b200 import _lib, config, synth
     from bonsai_b200.runtime import Model
 
-    cfg = config.bonsai_2b_graded(ctx=2048)
+    lora4 = args.workload == "config4"
+    cfg = config.bonsai_4b_graded(ctx=4608) if lora4 else config.bonsai_2b_graded(ctx=2048)
     t_gen = time.time()
     ts = synth.model_tensors(cfg, args.seed)
     m = Model(cfg, device=local).load(ts)
+    prefill_info = None
+    if lora4:
+        m.set_lora_linears(synth.lora_linears(cfg, LORA_RANK, seed=args.seed + 3, modules=LORA_MODULES),
+                           LORA_ALPHA / LORA_RANK)
     t_load = time.time() - t_gen
-    prefix = synth.zipf_tokens(args.seed + 1, PREFIX, cfg.vocab)
-    user = synth.zipf_tokens(args.seed + 2, USER, cfg.vocab)
-    m.prefill(prefix)
-    snap_prefix = m.snapshot()
-    first = m.prefill(user)
+    if lora4:
+        prompt = synth.zipf_tokens(args.seed + 1, PROMPT_4B, cfg.vocab)
+        m.prefill(prompt[:32])  # graphs captured outside the timed prefill
+        m.reset()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        first = m.prefill(prompt)
+        torch.cuda.synchronize()
+        t_pf = max_over_ranks(time.perf_counter() - t0, dist, "cuda")
+        prefill_info = {"tokens": PROMPT_4B, "s": t_pf, "tok_s": whole_job_rate(ws, PROMPT_4B, t_pf),
+                        "path": "bcu_prefill (16-row verify passes), wall clock with synchronisation"}
+        base_len = PROMPT_4B
+    else:
+        prefix = synth.zipf_tokens(args.seed + 1, PREFIX, cfg.vocab)
+        user = synth.zipf_tokens(args.seed + 2, USER, cfg.vocab)
+        m.prefill(prefix)
+        first = m.prefill(user)
+        base_len = PREFIX + USER
     snap = m.snapshot()
     passes = -(-(GEN - 1) // (K_DRAFT + 1))  # verify passes per request
     gen_tokens = 1 + passes * (K_DRAFT + 1)
     greedy, _ = m.decode(first, speculate=False, max_tokens=gen_tokens + K_DRAFT + 1)
-    m.set_planted(greedy, PREFIX + USER)
+    m.set_planted(greedy, base_len)
     T = K_DRAFT + 1
     stream = torch.cuda.ExternalStream(m.stream())
 
@@ -246,7 +273,7 @@ def main():
     m.restore(snap)
     m.enqueue_passes(T, passes, 2)
     m.sync()
-    assert m.length == PREFIX + USER + passes * T, "planted decode did not accept every draft"
+    assert m.length == base_len + passes * T, "planted decode did not accept every draft"
 
     clocks = Clocks(local)
     if dist:
@@ -310,23 +337,26 @@ def main():
 
     launches = m.pass_launches(T)
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+        "metric": METRIC.replace("Bonsai-2B shape", "Bonsai-4B shape + LoRA") if lora4 else METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded random-init weights, Zipf(1.1) prompts)",
-        "config": {"workload": WORKLOAD, "draft_k": K_DRAFT, "verify_rows": T, "passes_per_step": passes,
+        "config": {"workload": WORKLOAD_4B if lora4 else WORKLOAD, "draft_k": K_DRAFT, "verify_rows": T, "passes_per_step": passes,
                    "tokens_per_step": tokens_step, "parallelism": f"replicas x{ws}",
                    "l2": "inputs larger than L2 (1.6 GB of weights streamed per pass)"},
         "e2e": e2e,
         "gpu_launches": ws * launches * passes * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": VERIFY_PASS_DRAM_BYTES, "kernel": "verify pass (T=9 graph: all kernels of one pass)",
+                     "traffic": None if lora4 else VERIFY_PASS_DRAM_BYTES,
+                     "kernel": "verify pass (T=9 graph: all kernels of one pass)",
                      "bytes_per_launch": bytes_pass, "ms_per_launch": pass_ms,
                      "frac_of_8TBs": achieved / 8000.0, "peak_source": "MEASURED_PEAKS.json" if pk else "fallback"},
         "random_drafts": {"tok_s": rnd_tok_s, "ms_per_pass": rnd_ms / (GEN - 1)},
         "clocks": ck, "wall_s": wall, "setup_s": t_load,
     }
-    if rank == 0 and not args.no_cpu and ws == 1:
+    if prefill_info:
+        line["prefill"] = prefill_info
+    if rank == 0 and not args.no_cpu and ws == 1 and not lora4:
         cb, _ = cpu_baseline(cfg, ts, 1, 0)
         line["cpu_baseline"] = cb
     if rank == 0:

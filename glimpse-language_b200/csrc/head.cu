@@ -68,7 +68,8 @@ __device__ void head_operand(const HeadArgs& a, int t, uint32_t* s_b) {
 
 constexpr int HEAD_KCH = 8;         // k-steps per staged unit: 8 x 512 B = 4 KB per warp
 template <int NT>
-__host__ __device__ constexpr int head_stages() { return NT >= 4 ? 3 : 4; }  // units in flight per warp
+__host__ __device__ constexpr int head_stages() { return NT >= 4 ? 3 : 4; }  // units in flight per warp (at most)
+constexpr size_t HEAD_SMEM_MAX = 225 * 1024;  // the per-block opt-in limit (227 KB) minus the static arrays
 
 // Shared memory: the operand [d/16][NT][32 lanes][2 words], then per warp a ring of head_stages() 4-KB units of the
 // table, then their mbarriers.
@@ -78,11 +79,12 @@ __host__ __device__ inline size_t head_smem_bytes(int d, int nt, int stages) {
 
 // One CTA per SM, 8 warps; warp w streams a contiguous range of 16-row m-tiles (a contiguous byte range of the
 // repacked table) through its shared-memory ring with 4-KB bulk copies (cp.async.bulk, no multicast), so each warp
-// keeps head_stages() x 4 KB of the table in flight while its tensor-core products run.
+// keeps a.stages x 4 KB of the table in flight while its tensor-core products run (head_stages(), fewer when the
+// operand of a wide hidden size leaves less room).
 template <int NT>
 __global__ void __launch_bounds__(256, 1) head_kernel(HeadArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int S = head_stages<NT>();
+    const int S = a.stages;
     uint2* s_b = (uint2*)smem;
     __shared__ float wbv[8][16];
     __shared__ int wbi[8][16];
@@ -232,14 +234,16 @@ __global__ void __launch_bounds__(256, 1) head_kernel(HeadArgs a) {
 
 template <int NT>
 static void launch_head_t(const HeadArgs& a, int grid, cudaStream_t st) {
-    size_t smem = head_smem_bytes(a.d, NT, head_stages<NT>());
+    int stages = head_stages<NT>();
+    while (stages > 1 && head_smem_bytes(a.d, NT, stages) > HEAD_SMEM_MAX) stages--;
+    size_t smem = head_smem_bytes(a.d, NT, stages);
     static bool attr = false;
     if (!attr) {
-        // the per-block opt-in limit (227 KB) minus this kernel's static shared memory (~1.2 KB)
-        cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
+        cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)HEAD_SMEM_MAX);
         attr = true;
     }
     HeadArgs aa = a;
+    aa.stages = stages;
     void* args[] = {&aa};
     launch_pdl((const void*)head_kernel<NT>, dim3(grid), dim3(256), smem, st, args);
 }

@@ -160,8 +160,11 @@ struct HeadArgs {
     int* pi;                 // [grid][T]
     unsigned* counter;       // 1 zeroed uint
     int V, d, T;
+    int stages = 0;          // 4-KB table units in flight per warp (set by launch_head)
 };
 void launch_head(const HeadArgs& a, int NT, int grid, cudaStream_t st);
+// Largest hidden size whose head operand fits beside one ring stage (16-row tiles of 4 tokens, 16 rows at T = 16).
+constexpr int HEAD_MAX_HIDDEN = 3072;
 
 // Generic launch helper (PDL attribute on).
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args);

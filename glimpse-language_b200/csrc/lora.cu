@@ -53,6 +53,7 @@ void clear(bcu_model* m) {
     m->lora_buf = nullptr;
     m->lora_upart = nullptr;
     m->lora_rank = m->lora_linears = 0;
+    m->lora_bytes = 0;
 }
 
 // Pass graphs hold the GEMV parameters by value: drop them (recaptured on next use), and the verify costs measured
@@ -200,6 +201,7 @@ bcu_status bcu_set_lora(bcu_model* m, const bcu_lora_linear* lins, int32_t n, fl
     m->lora_upart = upart;
     m->lora_rank = rank;
     m->lora_linears = n;
+    m->lora_bytes = img.size() * 2;
     for (const Placed& pl : placed) {
         LoraArgs& la = group_lin(m->layers[pl.li], pl.gi)->lora;
         la.a = (const uint16_t*)buf + pl.a_off;

@@ -51,6 +51,7 @@ struct bcu_model {
     int device = 0, num_sms = 148;
     cudaStream_t st = nullptr;
     std::string err;
+    std::string launch_err;  // the first kernel launch that failed while capturing a pass
     bool finalized = false;
     volatile int cancel = 0;
     std::map<std::string, bcu::DevTensor> staged;
@@ -116,6 +117,7 @@ struct bcu_model {
     void* lora_buf = nullptr;
     float* lora_upart = nullptr;
     int lora_rank = 0, lora_linears = 0;
+    size_t lora_bytes = 0;  // fp16 A and B of every adapted group, read once per pass
 
     // drafting
     std::vector<uint64_t> keys;   // token_key per vocab id

@@ -88,6 +88,7 @@ bcu_status check_config(const bcu_config* c, std::string* why) {
     if (c->heads / c->kv_heads > 16) return bad("more than 16 q heads per kv head");
     if (c->lin_k_heads < 1 || c->lin_v_heads % c->lin_k_heads != 0) return bad("v heads not divisible by k heads");
     if (c->hidden % 512 || c->intermediate % 512) return bad("hidden/intermediate must be multiples of 512");
+    if (c->hidden > HEAD_MAX_HIDDEN) return bad("hidden above 3072 is not supported (the head's operand lives in shared memory)");
     if (c->group_size != 64 && c->group_size != 128) return bad("group_size must be 64 or 128");
     if (c->hadamard != 512 && c->hadamard != 1024 && c->hadamard != 2048) return bad("hadamard block must be 512/1024/2048");
     int C = 2 * c->lin_k_heads * 128 + c->lin_v_heads * 128, gw = c->lin_v_heads * 128, aw = c->heads * 256;
@@ -248,6 +249,14 @@ void enqueue_pass(bcu_model* m, int T) {
         }
     };
     auto lora_of = [](const Lin& ln) { return ln.lora.a ? &ln.lora : nullptr; };
+    // the first launch that failed (a capture only reports that one did)
+    m->launch_err.clear();
+    auto note = [&](const char* what, size_t li) {
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess && m->launch_err.empty())
+            m->launch_err = std::string(what) + (li != (size_t)-1 ? " of layer " + std::to_string(li) : "") +
+                            " (T = " + std::to_string(T) + "): " + cudaGetErrorString(e);
+    };
     GemvOut store, resid;
     store.partial = resid.partial = m->partial;
     store.counters = resid.counters = m->counters;
@@ -284,7 +293,9 @@ void enqueue_pass(bcu_model* m, int T) {
             ab.nv = c.lin_v_heads;
             grid_built(in, L.mix_in, 2 * c.lin_v_heads);
             launch_ternary_gemv(L.mix_in.m, in, T, mixo, &ab, st, lora_of(L.mix_in));
+            note("mixer input GEMV", li);
             launch_gdn_layer(gdn_args(m, L, T), st);
+            note("GDN layer", li);
             out.mode = ACT_GATED;
             out.x = m->y;
             out.x2 = m->mix;
@@ -294,6 +305,7 @@ void enqueue_pass(bcu_model* m, int T) {
         } else {
             grid_built(in, L.mix_in, 0);
             launch_ternary_gemv(L.mix_in.m, in, T, mixo, nullptr, st, lora_of(L.mix_in));
+            note("mixer input GEMV", li);
             AttnArgs a{};
             a.ctl = m->ctl;
             a.qkv = m->mix;
@@ -312,6 +324,7 @@ void enqueue_pass(bcu_model* m, int T) {
             a.ld = 2 * m->aw + 2 * m->kvw;
             a.ctx = c.ctx;
             launch_attn(a, st);
+            note("attention", li);
             out.mode = ACT_GATE;
             out.x = m->y;
             out.x2 = m->mix;
@@ -319,6 +332,7 @@ void enqueue_pass(bcu_model* m, int T) {
         }
         grid_built(out, L.mix_out, 0);
         launch_ternary_gemv(L.mix_out.m, out, T, resid, nullptr, st, lora_of(L.mix_out));
+        note("mixer output GEMV", li);
         ActSrc post = in;
         post.mode = ACT_NORM;
         post.w = L.post_norm;
@@ -329,6 +343,7 @@ void enqueue_pass(bcu_model* m, int T) {
         GemvOut guo = store;
         guo.out = m->gubuf;
         launch_ternary_gemv(L.gu.m, post, T, guo, nullptr, st, lora_of(L.gu));
+        note("gate/up GEMV", li);
         ActSrc sw;
         sw.mode = ACT_SWIGLU;
         sw.x = m->gubuf;
@@ -336,6 +351,7 @@ void enqueue_pass(bcu_model* m, int T) {
         sw.HB = c.hadamard;
         grid_built(sw, L.down, 0);
         launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st, lora_of(L.down));
+        note("down GEMV", li);
     }
     HeadArgs ha{};
     ha.ctl = m->ctl;
@@ -352,6 +368,7 @@ void enqueue_pass(bcu_model* m, int T) {
     ha.d = d;
     ha.T = T;
     launch_head(ha, NT, m->head_grid, st);
+    note("head", -1);
 }
 
 bcu_status get_graph(bcu_model* m, int T, cudaGraphExec_t* out) {
@@ -363,7 +380,9 @@ bcu_status get_graph(bcu_model* m, int T, cudaGraphExec_t* out) {
     CK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
     enqueue_pass(m, T);
     cudaError_t e = cudaStreamEndCapture(m->st, &g);
-    if (e != cudaSuccess) return fail(m, BCU_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess)
+        return fail(m, BCU_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e) +
+                                         (m->launch_err.empty() ? "" : "; first failed launch: " + m->launch_err));
     size_t n = 0;
     cudaGraphGetNodes(g, nullptr, &n);
     m->graph_nodes[T] = (int)n;
@@ -925,6 +944,7 @@ bcu_status bcu_pass_bytes(const bcu_model* m, int32_t t, double* bytes) {
     b += (double)m->n_gdn * c.lin_v_heads * 128 * 128 * 4 * 2;                    // GDN state r+w
     b += (double)m->n_gdn * 3 * m->C * 4 * 2;                                     // conv state r+w
     b += (double)m->n_attn * (m->len + t / 2.0) * m->kvw * 4 * 2;                 // fp32 K+V read
+    b += (double)m->lora_bytes;                                                   // LoRA A and B (fp16)
     *bytes = b;
     return BCU_OK;
 }

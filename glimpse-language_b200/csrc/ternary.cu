@@ -328,60 +328,10 @@ __device__ __forceinline__ void transform(const ActSrc& s, int K, const RawTok<V
     }
 }
 
-// LoRA A of one (token t, Hadamard block b) (norm_rotate's fused A rows, kernels.metal:70-116): each lane's dot
-// products of its VPL unrotated values with the stacked A rows, 8 rows at a time (few registers: this runs inside the
-// GEMV), summed across the warp in a fixed order: a halving butterfly over offsets 16, 8, 4 leaves lane l with row
-// (l >> 2) & 7 of the chunk, then offsets 2 and 1 complete the sum. Stored to upart[t][b][row]; the order does not
-// depend on T.
-template <int VPL>
-__device__ __forceinline__ void lora_partial(const LoraArgs& L, int t, int b, int nblk, const float* v) {
-    const int lane = threadIdx.x & 31, R = L.R;
-    float* dst = L.upart + ((size_t)t * nblk + b) * R;
-#pragma unroll 1
-    for (int c0 = 0; c0 < R; c0 += 8) {
-        float acc[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-            acc[q] = 0.0f;
-            const uint4* ap = (const uint4*)(L.a + (((size_t)b * R + c0 + q) * 32 + lane) * VPL);
-#pragma unroll
-            for (int u = 0; u < VPL / 8; u++) {
-                const uint4 w = __ldg(ap + u);
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int h = 0; h < 4; h++) {
-                    const float2 f = __half22float2(*(const __half2*)&ws[h]);
-                    acc[q] = fmaf(f.x, v[8 * u + 2 * h], acc[q]);
-                    acc[q] = fmaf(f.y, v[8 * u + 2 * h + 1], acc[q]);
-                }
-            }
-        }
-#pragma unroll
-        for (int o = 16, n = 4; o >= 4; o >>= 1, n >>= 1) {
-            const bool up = (lane & o) != 0;
-#pragma unroll
-            for (int j = 0; j < n; j++) {
-                const float send = up ? acc[j] : acc[j + n];
-                const float keep = up ? acc[j + n] : acc[j];
-                acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
-        float a = acc[0];
-        a += __shfl_xor_sync(0xffffffffu, a, 2);
-        a += __shfl_xor_sync(0xffffffffu, a, 1);
-        if ((lane & 3) == 0) dst[c0 + (lane >> 2)] = a;
-    }
-}
-
-template <int VPL, bool LORA>
-__device__ __forceinline__ void lora_partial_if(const GemvParams& p, int t, int b, const float* v) {
-    if constexpr (LORA) lora_partial<VPL>(p.lora, t, b, p.K / (VPL * 32), v);
-}
-
 // This CTA's operand for K-slice ks, built by its own warps (sources without a producing kernel: the embedding
 // rows of the first layer, standalone inputs): warp w takes block w % nb of the slice and the token slots w / nb,
 // w / nb + 8 / nb, ...; the next token's loads are in flight while the current one is built. Regions [nb][NT].
-template <int VPL, int GPC, bool LORA>
+template <int VPL, int GPC>
 __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int NT, uint8_t* s_op, int rsz) {
     constexpr int HBe = VPL * 32, G = 128 / GPC;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -412,7 +362,6 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
             uint32_t id = 0;
             const float r = row_scale(s, t, K, &id, blockIdx.x == 0 && b == 0);
             act_values<VPL>(s, t, blk0, K, r, id, v);
-            lora_partial_if<VPL, LORA>(p, t, blk0 / HBe, v);
             emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
         }
         return;
@@ -435,7 +384,6 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
             if (t < T) {
                 float v[VPL];
                 transform<VPL>(s, K, cur, wn, v);
-                lora_partial_if<VPL, LORA>(p, t, blk0 / HBe, v);
                 emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
             } else {
                 zero_token(t, sbsz, G, region(t));
@@ -449,7 +397,6 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
                 load_raw<VPL>(s, t, blk0, K, cur);
                 float v[VPL];
                 transform<VPL>(s, K, cur, wn, v);
-                lora_partial_if<VPL, LORA>(p, t, blk0 / HBe, v);
                 emit_token<VPL, GPC>(geo, t, region(t), v, s.signs ? sg : nullptr);
             } else {
                 zero_token(t, sbsz, G, region(t));
@@ -464,7 +411,7 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
 // the token are then stored to the buffer. Then every CTA waits (bounded) until all builder CTAs have counted
 // themselves; the grid is resident at once (the host checks), so the wait ends. counters[0] counts builders,
 // counters[1] the CTAs past the wait (the last resets both for the next GEMV).
-template <int VPL, int GPC, bool LORA>
+template <int VPL, int GPC>
 __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
     constexpr int HBe = VPL * 32, G = 128 / GPC;
     const ActSrc& s = p.src;
@@ -500,7 +447,6 @@ __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
             load_raw<VPL>(s, t, blk0, K, R);
             transform<VPL>(s, K, R, wn, v);
         }
-        lora_partial_if<VPL, LORA>(p, t, b, v);
         emit_token<VPL, GPC>(geo, t, reg, v, s.signs ? sg : nullptr);
         __syncwarp();
         store_token_columns(t, HBe, G, reg, s.opbuf + ((size_t)b * 4 + (t >> 2)) * rsz);
@@ -518,6 +464,85 @@ __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
         }
     }
     __syncthreads();
+}
+
+// LoRA A of a GEMV's input (norm_rotate's fused A rows, kernels.metal:70-116), in a short kernel launched just before
+// the GEMV: u partials for every (token t, Hadamard block b) of the input, which the GEMV's output epilogue sums over
+// the blocks and multiplies by B. One warp per (t, b, chunk of 8 stacked A rows): the chunk's rows are loaded before
+// the dependency wait; after it the warp forms the block's unrotated input values (the producer of the GEMV's source
+// mode, without signs or rotation), takes 8 lane-local dot products and sums them across the warp in a fixed order
+// (a halving butterfly over offsets 16, 8, 4 leaves lane l with row (l >> 2) & 7, offsets 2 and 1 finish). Stored to
+// upart[t][b][row]; nothing depends on T.
+template <int VPL>
+__global__ void __launch_bounds__(256) lora_a_kernel(GemvParams p) {
+    constexpr int HBe = VPL * 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const ActSrc& s = p.src;
+    const LoraArgs& L = p.lora;
+    const int K = p.K, nblk = K / HBe, nch = L.R / 8;
+    const int i = blockIdx.x * 8 + warp;
+    pdl_trigger();
+    const bool active = i < p.T * nblk * nch;
+    const int c = active ? i % nch : 0, b = active ? (i / nch) % nblk : 0, t = active ? i / (nch * nblk) : 0;
+    const int blk0 = b * HBe;
+    uint4 w[8][VPL / 8];
+    float wn[VPL];
+    if (active) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const uint4* ap = (const uint4*)(L.a + (((size_t)b * L.R + c * 8 + q) * 32 + lane) * VPL);
+#pragma unroll
+            for (int u = 0; u < VPL / 8; u++) w[q][u] = __ldg(ap + u);
+        }
+        if (s.mode == ACT_NORM) {
+#pragma unroll
+            for (int e = 0; e < VPL; e++) wn[e] = s.w[blk0 + lane + 32 * e];
+        } else if (s.mode == ACT_GATED) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) wn[q] = s.w[(lane + 32 * q) & 127];
+        }
+    }
+    pdl_wait();
+    if (!active) return;
+    float v[VPL];
+    if (s.mode == ACT_EMBED) {
+        uint32_t id = 0;
+        const float r = row_scale(s, t, K, &id, false);
+        act_values<VPL>(s, t, blk0, K, r, id, v);
+    } else {
+        RawTok<VPL> R;
+        load_raw<VPL>(s, t, blk0, K, R);
+        transform<VPL>(s, K, R, wn, v);
+    }
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        acc[q] = 0.0f;
+#pragma unroll
+        for (int u = 0; u < VPL / 8; u++) {
+            const uint32_t ws[4] = {w[q][u].x, w[q][u].y, w[q][u].z, w[q][u].w};
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const float2 f = __half22float2(*(const __half2*)&ws[h]);
+                acc[q] = fmaf(f.x, v[8 * u + 2 * h], acc[q]);
+                acc[q] = fmaf(f.y, v[8 * u + 2 * h + 1], acc[q]);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16, n = 4; o >= 4; o >>= 1, n >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < n; j++) {
+            const float send = up ? acc[j] : acc[j + n];
+            const float keep = up ? acc[j + n] : acc[j];
+            acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float a = acc[0];
+    a += __shfl_xor_sync(0xffffffffu, a, 2);
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    if ((lane & 3) == 0) L.upart[((size_t)t * nblk + b) * L.R + c * 8 + (lane >> 2)] = a;
 }
 
 // GDN a/b gate rows (dense fp32, gdn_ab_row kernels.metal:265-273): rows [r0, r0 + nr) of [Wa; Wb], nr <= AB_ROWS,
@@ -672,7 +697,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
     }
     if (prebuilt) {
         __shared__ int s_ok;
-        grid_build<VPL, GPC, LORA>(p, s_op, &s_ok);
+        grid_build<VPL, GPC>(p, s_op, &s_ok);
         if (tid == 0) {  // the slice's regions: nb blocks of NT tiles (the buffer holds 4 tiles per block)
             mbar_expect_tx(bar_op, (uint32_t)(nb * NT * rsz));
             for (int b = 0; b < nb; b++)
@@ -680,7 +705,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
                          (uint32_t)(NT * rsz), bar_op);
         }
     }
-    if (!prebuilt) build_operand<VPL, GPC, LORA>(p, ks, sbsz, nb, NT, s_op, rsz);
+    if (!prebuilt) build_operand<VPL, GPC>(p, ks, sbsz, nb, NT, s_op, rsz);
     __syncthreads();
     const bool ok = mbar_wait_bounded(bar, 0) && (!prebuilt || mbar_wait_bounded(bar_op, 0));
     if (__syncthreads_or(!ok)) {
@@ -849,8 +874,8 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
         if (tid == 0) p.o.counters[rb] = 0;
     }
     __syncthreads();
-    // LoRA: u = A . x of this row block's member (u[t][j] = sum over the Hadamard blocks of the builders' partials,
-    // in block order; every partial was stored before the grid-wide wait or this row block's split-K count)
+    // LoRA: u = A . x of this row block's member (u[t][j] = sum over the Hadamard blocks of lora_a_kernel's partials,
+    // in block order; that kernel completed before this one's dependency wait)
     const LoraArgs& L = p.lora;
     const int lr = L.r;
     float* s_u = fin + 128 * T;  // [T][lr]
@@ -992,6 +1017,12 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     int nt = (2 * T + 7) / 8;
     size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, p.ab_rows > 0, hb,
                             src.opbuf ? grid_build_tpc(m, T, hb) : 0, p.lora.a ? p.lora.r : 0);
+    if (p.lora.a) {  // the LoRA A partials first (lora_a_kernel); hb is 512 or 1024 here (bcu_set_lora checks)
+        const int tasks = T * (m.K / hb) * (p.lora.R / 8);
+        void* largs[] = {&p};
+        launch_pdl(hb == 512 ? (const void*)lora_a_kernel<16> : (const void*)lora_a_kernel<32>,
+                   dim3((unsigned)((tasks + 7) / 8)), dim3(256), 0, st, largs);
+    }
     const void* fn = gemv_fn(nt, m.group, hb, p.lora.a != nullptr);
     void* args[] = {&p};
     const int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;

@@ -23,6 +23,9 @@ CONFIGS = {
     "g128_ref_pack": dict(group_size=128, has_bias=False, hadamard=512, has_signs=True, kv_heads=1),
     "g64_h1024_nosigns": dict(group_size=64, has_bias=True, hadamard=1024, has_signs=False, hidden=1024,
                               intermediate=2048, heads=4, lin_v_heads=8),
+    # the 4B shape's hidden size (2560 = 5 rotation blocks; the head's ring has fewer stages) and kv heads
+    "g64_h2560_4b_widths": dict(group_size=64, has_bias=True, hadamard=512, has_signs=True, hidden=2560,
+                                intermediate=1536, heads=4, kv_heads=4, lin_v_heads=4),
 }
 
 
