@@ -168,6 +168,149 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+# --workload config5: the prefill linears of the Bonsai-2B shape for 32 sessions x 2048 tokens = 65536 rows per GPU
+# (ternary g64 + bias, synthetic weights), on the tcgen05 GEMM (bcu_linear_gemm). Per layer the reference's matmuls:
+# GDN [qkv; z] 12288 x 2048, out_proj 2048 x 4096; attention [q; k; v] 9216 x 2048, o_proj 2048 x 4096; MLP [gate;
+# up] 12288 x 2048, down 2048 x 6144; 18 GDN + 6 attention layers.
+PREFILL_M = 65536
+GEMM_SHAPES = {"gdn_in": (12288, 2048), "attn_in": (9216, 2048), "mix_out": (2048, 4096), "gate_up": (12288, 2048),
+               "down": (2048, 6144)}
+GEMM_COUNTS = {"gdn_in": 18, "attn_in": 6, "mix_out": 24, "gate_up": 24, "down": 24}
+WORKLOAD_5 = ("config5 (linears only): the 96 ternary GEMMs of the Bonsai-2B shape (g64 + bias) for 32 sessions x "
+              "2048 tokens = 65536 prefill rows per GPU, fp32 activations in HBM")
+
+
+def run_config5(args, ws, rank, local):
+    import ctypes
+
+    import torch
+
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    from bonsai_b200 import _lib, synth
+
+    L = _lib.lib()
+    rng = np.random.default_rng(args.seed)
+    lins, host_w = {}, {}
+    for name, (O, K) in GEMM_SHAPES.items():
+        W = synth.fill(3, args.seed, len(lins) * 3, 0, 0, (O, K // 16), np.uint32)
+        S = synth.fill(4, args.seed, len(lins) * 3 + 1, 0.01, 0.05, (O, K // 64), np.uint16)
+        B = synth.fill(6, args.seed, len(lins) * 3 + 1, 0.01, 0.05, (O, K // 64), np.uint16)
+        h = ctypes.c_void_p()
+        st = L.bcu_linear_prepare(W.ctypes.data_as(ctypes.c_void_p), S.ctypes.data_as(ctypes.c_void_p),
+                                  B.ctypes.data_as(ctypes.c_void_p), O, K, 64, local, ctypes.byref(h))
+        assert st == _lib.OK, st
+        lins[name] = h
+        host_w[name] = (W, S, B)
+    kmax = max(K for _, K in GEMM_SHAPES.values())
+    omax = max(O for O, _ in GEMM_SHAPES.values())
+    x = torch.randn(PREFILL_M * kmax, device="cuda", dtype=torch.float32)
+    y = torch.empty(PREFILL_M * omax, device="cuda", dtype=torch.float32)
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    xp, yp = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr())
+    launches = [name for name in GEMM_SHAPES for _ in range(GEMM_COUNTS[name])]
+
+    def step():
+        for name in launches:
+            assert L.bcu_linear_gemm(lins[name], xp, PREFILL_M, yp, sp) == _lib.OK
+
+    for _ in range(args.warmup):
+        step()
+    assert L.bcu_linear_sync(lins["down"], sp) == _lib.OK
+    # per-GEMM device time of one launch of each shape (CUDA events on the launching stream)
+    per = {}
+    for name in GEMM_SHAPES:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(3):
+            assert L.bcu_linear_gemm(lins[name], xp, PREFILL_M, yp, sp) == _lib.OK
+        e1.record(stream)
+        torch.cuda.synchronize()
+        O, K = GEMM_SHAPES[name]
+        ms = e0.elapsed_time(e1) / 3
+        per[name] = {"ms": ms, "tflops": 2.0 * PREFILL_M * O * K / (ms / 1000) / 1e12}
+    clocks = Clocks(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ck = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
+    for name in GEMM_SHAPES:
+        assert L.bcu_linear_sync(lins[name], sp) == _lib.OK, "a GEMM gave up a bounded wait"
+    flops_step = sum(2.0 * PREFILL_M * GEMM_SHAPES[n][0] * GEMM_SHAPES[n][1] for n in launches)
+    value = whole_job_rate(ws, PREFILL_M * args.steps, ms / 1000)
+    achieved = flops_step / (ms / args.steps / 1000) / 1e12
+    pk = peaks() or {}
+    peak = pk.get("bf16_tflops_sustained", 1400.0)
+
+    # e2e: the same step with the first GEMM's input copied from pinned host memory and the last output read back
+    xh = torch.empty(PREFILL_M * 2048, dtype=torch.float32, pin_memory=True).normal_()
+    yh = torch.empty(PREFILL_M * 2048, dtype=torch.float32, pin_memory=True)
+    e2e_steps = max(1, min(args.steps, 2))
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        x[: xh.numel()].copy_(xh, non_blocking=True)
+        step()
+        yh.copy_(y[: yh.numel()], non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - w0, dist, "cuda")
+    line = {
+        "metric": "prefill tok/s/GPU (linears only: the ternary GEMMs of the Bonsai-2B shape on tcgen05)",
+        "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 activations (fp16 hi + lo) x fp16 weights, fp32 accumulate",
+        "data": "synthetic (seeded ternary weights, N(0,1) activations)",
+        "config": {"workload": WORKLOAD_5, "rows_per_step": PREFILL_M, "gemms_per_step": len(launches),
+                   "parallelism": f"replicas x{ws}", "l2": "inputs larger than L2 (0.5-1.6 GB activations)"},
+        "e2e": {"value": whole_job_rate(ws, PREFILL_M * e2e_steps, e2e_s), "unit": "tok/s",
+                "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
+                "path": "bcu_linear_gemm (C ABI) x 96, input H2D from pinned host, last output D2H"},
+        "gpu_launches": ws * args.steps * len(launches) * 2,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "ternary_gemm_kernel (all 96 GEMMs of a step)",
+                     "flops_per_step": flops_step,
+                     "note": "algorithmic 2 M O K; the fp16 hi + lo split issues 2x that on the tensor cores",
+                     "peak_source": "MEASURED_PEAKS.json bf16 sustained" if pk else "fallback"},
+        "per_gemm": per, "clocks": ck,
+    }
+    if rank == 0 and not args.no_cpu and ws == 1:
+        from oracle.oracle import ternary_linear
+
+        sample, secs = 16, 0.0
+        xs = rng.standard_normal((sample, kmax)).astype(np.float32)
+        for name, (O, K) in GEMM_SHAPES.items():
+            W, S, B = host_w[name]
+            t0 = time.perf_counter()
+            ternary_linear(W, S, B, 64, xs[:, :K])
+            secs += (time.perf_counter() - t0) * GEMM_COUNTS[name]
+        line["cpu_baseline"] = {"value": sample / secs, "unit": "tok/s",
+                                "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": "port",
+                                "sample": f"the oracle's ternary linear on {sample} rows of each GEMM shape, times its "
+                                          "count per step"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for h in lins.values():
+        L.bcu_linear_free(h)
+    if dist:
+        dist.destroy_process_group()
+
+
 def run_profile(args, local):
     """A short run for kernel profiling: model load, a --profile-prefix token prefill (16-row passes), then
     --profile verify passes of 9 rows with planted drafts. Prints the kernel launches of one 9-row pass."""
@@ -200,8 +343,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="profiling run for ncu: prefill --profile-prefix tokens, then this many 9-row verify passes")
     ap.add_argument("--profile-prefix", type=int, default=256)
-    ap.add_argument("--workload", default="config3", choices=["config3", "config4"],
-                    help="config3 (default, the headline) or config4 (4B shape + LoRA)")
+    ap.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
+                    help="config3 (default, the headline), config4 (4B shape + LoRA) or config5 (prefill linears)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
 
@@ -210,6 +353,9 @@ def main():
         return
     if args.profile:
         run_profile(args, local)
+        return
+    if args.workload == "config5":
+        run_config5(args, ws, rank, local)
         return
 
     import torch

@@ -137,6 +137,8 @@ SIGNATURES = {
     "bcu_linear_free": (None, [P]),
     "bcu_linear_rotate_forward": (I32, [P, P, I32, I32, P, P, P]),
     "bcu_linear_forward": (I32, [P, P, I32, P, P]),
+    "bcu_linear_gemm": (I32, [P, P, I32, P, P]),
+    "bcu_linear_sync": (I32, [P, P]),
     "bcu_linear_rotate_forward_static": (I32, [P, P, I32, I32, P, P, P]),
     "bcu_gdn_verify": (I32, [P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
     "bcu_synth_fill": (I32, [I32, U64, U64, ctypes.c_double, ctypes.c_double, P, U64]),
@@ -150,6 +152,7 @@ SIGNATURES = {
     "bcu_stream": (I32, [P, ctypes.POINTER(P)]),
     # host-logic exports (not in the ABI header: test hooks of the decode driver and the operand build)
     "bcu_set_local_build": (I32, [P, I32]),
+    "bcu_gemm_prep_debug": (I32, [P, P, I32, P, P]),
     "bcu_token_key": (U64, [P, U64]),
     "bcu_lookup": (I32, [PU32, I32, PU32, I32, ctypes.POINTER(U64), I32, I32, I32, I32, I32, I32, PU32, PI32]),
     "bcu_policy_choose": (I32, [ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_double), I32, I32,

@@ -1,0 +1,382 @@
+// gemm.cu — ternary GEMM for batched prefill (graded config 5; the reference's prefill matmul qmm,
+// kernels.metal:437-500, and its Vulkan coopmat form qmm_cm.comp) on the 5th-generation tensor cores:
+// y[M][O] = W . x for M tokens, W the MLX 2-bit pack (w = c s + b per group of G inputs).
+//
+// Per CTA tile: 128 weight rows x 128 tokens, accumulated in tensor memory (TMEM, 256 fp32 columns: the tokens' fp16
+// hi parts in columns 0..127 and lo parts in 128..255, so one tcgen05.mma of N = 256 multiplies both halves by the
+// same weight tile). K runs in chunks of 64 inputs through a 3-stage shared-memory pipeline:
+//   - one thread issues 1-D bulk copies (the TMA engine, cp.async.bulk, no tensor map, no multicast) of the chunk's
+//     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's canonical layout) and of its packed codes and
+//     scales (2.3 KB), completing on the stage's mbarrier;
+//   - all 128 threads decode the codes into fp16 weights c s (exact for ternary codes: one fma of (1024 + c) s -
+//     1024 s) in the canonical K-major layout (8-row x 16-byte core matrices, no swizzle);
+//   - one thread issues 4 tcgen05.mma.kind::f16 (128 x 256 x 16) and commits them to the stage's second mbarrier,
+//     which frees the stage for the loads two chunks ahead.
+// The bias term sum_g b_g sum_{k in g} x_k rides as extra chunks: A = G b (prepared tiles), B = the group sums of the
+// token times 2^-log2(G) (prepared with the activations). Activations are fp32 split as x 2^E = hi + lo (fp16 each,
+// E per token from its row maximum), so every product is exact and sums are fp32: y = (D_hi + D_lo) 2^-E.
+// Every wait is bounded; on a timeout the kernel records ERR_MBAR_TIMEOUT, waits (bounded) for its copies and MMAs
+// in flight, frees its tensor memory and returns.
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "operand.cuh"  // pow2f
+
+namespace bcu {
+
+constexpr int GM_ROWS = 128, GM_TOK = 128, GM_KC = 64;  // tile rows, tile tokens, inputs per chunk
+constexpr int GM_STAGES = 3;
+constexpr int GM_A_BYTES = GM_ROWS * GM_KC * 2;           // 16 KB decoded weights
+constexpr int GM_B_BYTES = 2 * GM_TOK * GM_KC * 2;        // 32 KB activations (hi and lo)
+constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // codes [128][4 u32] + scales [128] fp16
+constexpr int GM_STAGE = 52224;                           // A | B | W (51456 B), 1024-aligned
+static_assert(GM_A_BYTES + GM_B_BYTES + GM_W_BYTES <= GM_STAGE, "a stage's buffers overlap the next stage");
+constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 1024;      // + barriers, TMEM address, exponents
+constexpr uint32_t GM_TMEM_COLS = 256;
+// kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B f16 (0), both K-major, N = 256 (bits 17-22 =
+// N / 8), M = 128 (bits 24-28 = M / 16)
+constexpr uint32_t GM_IDESC = (1u << 4) | ((256u / 8) << 17) | ((128u / 16) << 24);
+
+// ----------------------------------------------------------------------------------------------- tcgen05 / TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D (TMEM) (+)= A (smem) . B (smem)^T, both K-major; accumulate = 0 overwrites D.
+__device__ __forceinline__ void umma_f16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// Arrives on bar once every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 TMEM lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane (lane field of taddr) + i.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor, no swizzle: core matrices of 8 rows x 16 bytes; lbo = bytes between core matrices
+// adjacent in K, sbo = bytes between core matrices adjacent in M/N; version 1 (bit 46).
+__device__ __forceinline__ uint64_t umma_desc(const void* p, uint32_t lbo, uint32_t sbo) {
+    const uint64_t a = smem_u32(p);
+    return ((a >> 4) & 0x3FFFull) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) |
+           (1ull << 46);
+}
+
+// ----------------------------------------------------------------------------------------------- weights
+// Main chunks: per (row tile rt, chunk c) [128 rows][4 u32 codes of inputs 64 c .. 64 c + 63, MLX order] then [128]
+// fp16 scales of the chunk's group. One thread per (rt, c, row).
+__global__ void gemm_pack_w_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s, int O, int K, int G,
+                                   uint8_t* __restrict__ out) {
+    const int nmain = K / GM_KC;
+    const size_t n = (size_t)(O / GM_ROWS) * nmain * GM_ROWS;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int r = i % GM_ROWS, c = (i / GM_ROWS) % nmain, rt = i / ((size_t)GM_ROWS * nmain);
+    const size_t row = (size_t)rt * GM_ROWS + r;
+    uint8_t* base = out + ((size_t)rt * nmain + c) * GM_W_BYTES;
+    const uint4 v = *(const uint4*)(w + row * (K / 16) + 4 * c);
+    ((uint4*)base)[r] = v;
+    ((uint16_t*)(base + GM_ROWS * 16))[r] = s[row * (K / G) + (GM_KC * c) / G];
+}
+
+// Bias chunks: per (rt, bias chunk cb) the canonical A tile [8 k-chunks][16 row groups][8 rows][8 fp16] of
+// G b[row][g], g = 64 cb + k (zero past K / G); b = -s for the implicit bias of the reference pack. One thread per
+// (rt, cb, row, k-chunk).
+__global__ void gemm_pack_bias_kernel(const uint16_t* __restrict__ s, const uint16_t* __restrict__ b, int O, int K,
+                                      int G, int nbias, uint8_t* __restrict__ out) {
+    const size_t n = (size_t)(O / GM_ROWS) * nbias * GM_ROWS * 8;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int kk = i % 8, r = (i / 8) % GM_ROWS, cb = (i / (8 * GM_ROWS)) % nbias, rt = i / ((size_t)8 * GM_ROWS * nbias);
+    const size_t row = (size_t)rt * GM_ROWS + r;
+    const int ng = K / G;
+    uint16_t v[8];
+    for (int e = 0; e < 8; e++) {
+        const int g = GM_KC * cb + 8 * kk + e;
+        float x = 0.0f;
+        if (g < ng) {
+            const float bb = b ? __half2float(__ushort_as_half(b[row * ng + g])) : -__half2float(__ushort_as_half(s[row * ng + g]));
+            x = bb * (float)G;
+        }
+        v[e] = __half_as_ushort(__float2half_rn(x));
+    }
+    uint8_t* tile = out + ((size_t)rt * nbias + cb) * GM_A_BYTES;
+    *(uint4*)(tile + kk * (GM_ROWS * 16) + r * 16) = *(const uint4*)v;
+}
+
+// ----------------------------------------------------------------------------------------------- activations
+// One warp per token: exponent E = clamp(14 - ceil-exponent(max |x|)), then x 2^E split into fp16 hi + lo written to
+// the token tile's chunks in the canonical K-major layout of the B operand ([8 k-chunks][32 row groups][8 rows]
+// [8 fp16]; rows 0..127 hi, 128..255 lo), and the group sums x 2^(E - log2 G) (hi + lo) to the bias chunks.
+__global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int G, int nmain, int nbias,
+                                 uint8_t* __restrict__ bop, int* __restrict__ ex) {
+    const int lane = threadIdx.x & 31, t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= M) return;
+    const float* row = x + (size_t)t * K;
+    float am = 0.0f;
+    for (int k = lane * 4; k < K; k += 128) {
+        const float4 v = *(const float4*)(row + k);
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    am = warp_max(am);
+    int E = 0;
+    if (am > 0.0f && am < INFINITY) {
+        int e2;
+        frexpf(am, &e2);
+        E = min(max(14 - e2, -60), 100);
+    }
+    if (lane == 0) ex[t] = E;
+    const float f = E > 60 ? pow2f(60) * pow2f(E - 60) : (E < -60 ? pow2f(-60) * pow2f(E + 60) : pow2f(E));
+    const int nch = nmain + nbias, tt = t / GM_TOK, tl = t % GM_TOK;
+    uint8_t* tile0 = bop + (size_t)tt * nch * GM_B_BYTES;
+    const int hi_off = (tl / 8) * 128 + (tl % 8) * 16, lo_off = ((GM_TOK + tl) / 8) * 128 + (tl % 8) * 16;
+    const int lg = G == 64 ? 6 : 7, lanes_per_group = G / 8;
+    const float fb = pow2f(E - lg > 100 ? 100 : E - lg);
+    for (int q0 = 0; q0 < K / 8; q0 += 32) {
+        const int q = q0 + lane;  // 8 inputs 8 q .. 8 q + 7
+        float gs = 0.0f;
+        if (q < K / 8) {
+            const float4 a = *(const float4*)(row + 8 * q), b = *(const float4*)(row + 8 * q + 4);
+            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            uint16_t h[8], l[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float s = v[e] * f;
+                const __half hh = __float2half_rn(s);
+                h[e] = __half_as_ushort(hh);
+                l[e] = __half_as_ushort(__float2half_rn(s - __half2float(hh)));
+                gs += v[e];
+            }
+            uint8_t* chunk = tile0 + (size_t)(q / 8) * GM_B_BYTES + (q % 8) * (2 * GM_TOK * 16);
+            *(uint4*)(chunk + hi_off) = *(const uint4*)h;
+            *(uint4*)(chunk + lo_off) = *(const uint4*)l;
+        }
+        // group sums: the lanes of one group are consecutive (G / 8 of them), summed in a fixed tree
+        for (int o = 1; o < lanes_per_group; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        if (q < K / 8 && (lane % lanes_per_group) == 0) {
+            const int g = q / lanes_per_group;
+            const float s = gs * fb;
+            const __half hh = __float2half_rn(s);
+            const __half ll = __float2half_rn(s - __half2float(hh));
+            uint8_t* chunk = tile0 + (size_t)(nmain + g / GM_KC) * GM_B_BYTES + ((g % GM_KC) / 8) * (2 * GM_TOK * 16);
+            ((__half*)(chunk + hi_off))[g % 8] = hh;
+            ((__half*)(chunk + lo_off))[g % 8] = ll;
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------------------------- GEMM
+struct GemmParams {
+    const uint8_t* wt;     // main chunks (gemm_pack_w_kernel)
+    const uint8_t* abias;  // bias chunks (gemm_pack_bias_kernel)
+    const uint8_t* bop;    // activation chunks (gemm_prep_kernel)
+    const int* ex;         // [M] exponents
+    float* y;              // [M][O]
+    int* err;
+    int M, O, nmain, nbias, n_rt, n_tiles;
+};
+
+__global__ void __launch_bounds__(128, 1) ternary_gemm_kernel(GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint64_t* load_bar = (uint64_t*)(smem + GM_STAGES * GM_STAGE);
+    uint64_t* mma_bar = load_bar + GM_STAGES;
+    uint32_t* s_tmem = (uint32_t*)(mma_bar + GM_STAGES);
+    __shared__ int s_bad;
+    const int nch = p.nmain + p.nbias;
+    const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_tiles * nch;  // chunks this CTA runs, in order
+    if (tid == 0) {
+        s_bad = 0;
+        for (int i = 0; i < GM_STAGES; i++) {
+            mbar_init(&load_bar[i], 1);
+            mbar_init(&mma_bar[i], 1);
+        }
+        fence_proxy_async_smem();
+    }
+    if (warp == 0) {
+        tmem_alloc(s_tmem, GM_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+
+    auto stage_of = [&](int q) { return smem + (q % GM_STAGES) * GM_STAGE; };
+    auto issue_load = [&](int q) {  // thread 0
+        const int j = q / nch, c = q % nch;
+        const int tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
+        uint8_t* st = stage_of(q);
+        uint64_t* bar = &load_bar[q % GM_STAGES];
+        const uint8_t* bsrc = p.bop + ((size_t)tt * nch + c) * GM_B_BYTES;
+        if (c < p.nmain) {
+            mbar_expect_tx(bar, GM_B_BYTES + GM_W_BYTES);
+            bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, bar);
+            bulk_g2s(st + GM_A_BYTES + GM_B_BYTES, p.wt + ((size_t)rt * p.nmain + c) * GM_W_BYTES, GM_W_BYTES, bar);
+        } else {
+            mbar_expect_tx(bar, GM_B_BYTES + GM_A_BYTES);
+            bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, bar);
+            bulk_g2s(st, p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * GM_A_BYTES, GM_A_BYTES, bar);
+        }
+    };
+    if (tid == 0)
+        for (int q = 0; q < 2 && q < total; q++) issue_load(q);
+
+    int issued = total < 2 ? total : 2;  // loads issued
+    int committed = 0;                   // chunks whose MMAs were committed
+    for (int q = 0; q < total; q++) {
+        const int s = q % GM_STAGES, c = q % nch;
+        uint8_t* st = stage_of(q);
+        bool bad = !mbar_wait_bounded(&load_bar[s], (q / GM_STAGES) & 1);
+        if (__syncthreads_or(bad)) {
+            if (tid == 0) atomicOr(p.err, ERR_MBAR_TIMEOUT);
+            break;
+        }
+        if (c < p.nmain) {  // decode row tid's 64 codes into the canonical A tile
+            const uint4 cw = ((const uint4*)(st + GM_A_BYTES + GM_B_BYTES))[tid];
+            const uint16_t sc = ((const uint16_t*)(st + GM_A_BYTES + GM_B_BYTES + GM_ROWS * 16))[tid];
+            const uint32_t s2 = (uint32_t)sc * 0x10001u;
+            uint32_t n2;
+            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(n2) : "r"(s2), "r"(0xE400E400u));  // -1024 s
+            const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                const uint32_t wd = words[kk >> 1] >> (16 * (kk & 1));  // codes 8 kk .. 8 kk + 7 in bits 0..15
+                uint32_t o[4];
+#pragma unroll
+                for (int pr = 0; pr < 4; pr++) {
+                    const uint32_t x = wd >> (4 * pr);
+                    const uint32_t h = (x & 3u) | ((x << 14) & 0x30000u) | 0x64006400u;  // fp16 (1024 + c) pair
+                    o[pr] = hfma2_u32(h, s2, n2);                                     // c s, exact for c <= 2
+                }
+                *(uint4*)(st + kk * (GM_ROWS * 16) + tid * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                const uint64_t ad = umma_desc(st + 2 * ks * (GM_ROWS * 16), GM_ROWS * 16, 128);
+                const uint64_t bd = umma_desc(st + GM_A_BYTES + 2 * ks * (2 * GM_TOK * 16), 2 * GM_TOK * 16, 128);
+                umma_f16(tmem, ad, bd, GM_IDESC, (c > 0 || ks > 0) ? 1u : 0u);
+            }
+            umma_commit(&mma_bar[s]);
+            // the stage of chunk q - 1 is free once its MMAs are done: load chunk q + 2 into it
+            if (q + 2 < total) {
+                if (q >= 1 && !mbar_wait_bounded(&mma_bar[(q - 1) % GM_STAGES], ((q - 1) / GM_STAGES) & 1)) {
+                    atomicOr(p.err, ERR_MBAR_TIMEOUT);
+                    s_bad = 1;
+                } else {
+                    issue_load(q + 2);
+                    issued = q + 3;
+                }
+            }
+        }
+        committed = q + 1;
+        if (c == nch - 1) {  // tile done: TMEM -> registers -> y
+            const int j = q / nch, tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
+            bad = !mbar_wait_bounded(&mma_bar[s], (q / GM_STAGES) & 1);
+            if (__syncthreads_or(bad || s_bad)) {
+                if (tid == 0) atomicOr(p.err, ERR_MBAR_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const int row = rt * GM_ROWS + warp * 32 + lane;
+#pragma unroll 1
+            for (int cb = 0; cb < GM_TOK / 32; cb++) {
+                uint32_t hi[32], lo[32];
+                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb * 32, hi);
+                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + GM_TOK + cb * 32, lo);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const int t = tt * GM_TOK + cb * 32 + i;
+                    if (t < p.M)
+                        p.y[(size_t)t * p.O + row] = (__uint_as_float(hi[i]) + __uint_as_float(lo[i])) * pow2f(-p.ex[t]);
+                }
+            }
+            tc_fence_before();
+        } else if (__syncthreads_or(s_bad)) {
+            break;
+        }
+    }
+    // drain: copies and MMAs still in flight (bounded), then free the tensor memory
+    if (tid == 0) {
+        for (int q = committed; q < issued; q++) mbar_wait_bounded(&load_bar[q % GM_STAGES], (q / GM_STAGES) & 1, 1u << 20);
+        if (committed > 0)
+            mbar_wait_bounded(&mma_bar[(committed - 1) % GM_STAGES], ((committed - 1) / GM_STAGES) & 1, 1u << 20);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, GM_TMEM_COLS);
+}
+
+// ----------------------------------------------------------------------------------------------- host
+size_t gemm_w_bytes(int O, int K) { return (size_t)(O / GM_ROWS) * (K / GM_KC) * GM_W_BYTES; }
+int gemm_bias_chunks(int K, int G) { return (K / G + GM_KC - 1) / GM_KC; }
+size_t gemm_bias_bytes(int O, int K, int G) { return (size_t)(O / GM_ROWS) * gemm_bias_chunks(K, G) * GM_A_BYTES; }
+size_t gemm_act_bytes(int M, int K, int G) {
+    return (size_t)((M + GM_TOK - 1) / GM_TOK) * (K / GM_KC + gemm_bias_chunks(K, G)) * GM_B_BYTES;
+}
+
+void gemm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int O, int K, int G, uint8_t* wt,
+               uint8_t* abias, cudaStream_t st) {
+    const size_t n1 = (size_t)(O / GM_ROWS) * (K / GM_KC) * GM_ROWS;
+    gemm_pack_w_kernel<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(w, s, O, K, G, wt);
+    const int nb = gemm_bias_chunks(K, G);
+    const size_t n2 = (size_t)(O / GM_ROWS) * nb * GM_ROWS * 8;
+    gemm_pack_bias_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(s, b, O, K, G, nb, abias);
+}
+
+void gemm_prep_only(const float* x, int M, int K, int G, uint8_t* bop, int* ex, cudaStream_t st) {
+    gemm_prep_kernel<<<(unsigned)((M + 7) / 8), 256, 0, st>>>(x, M, K, G, K / GM_KC, gemm_bias_chunks(K, G), bop, ex);
+}
+
+cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int G, const float* x, int M, uint8_t* bop,
+                     int* ex, float* y, int* err, int num_sms, cudaStream_t st) {
+    const int nmain = K / GM_KC, nbias = gemm_bias_chunks(K, G);
+    gemm_prep_kernel<<<(unsigned)((M + 7) / 8), 256, 0, st>>>(x, M, K, G, nmain, nbias, bop, ex);
+    GemmParams p;
+    p.wt = wt;
+    p.abias = abias;
+    p.bop = bop;
+    p.ex = ex;
+    p.y = y;
+    p.err = err;
+    p.M = M;
+    p.O = O;
+    p.nmain = nmain;
+    p.nbias = nbias;
+    p.n_rt = O / GM_ROWS;
+    p.n_tiles = p.n_rt * ((M + GM_TOK - 1) / GM_TOK);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(ternary_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
+    });
+    const int grid = p.n_tiles < num_sms ? p.n_tiles : num_sms;
+    ternary_gemm_kernel<<<grid, 128, GM_SMEM, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace bcu

@@ -166,6 +166,17 @@ void launch_head(const HeadArgs& a, int NT, int grid, cudaStream_t st);
 // Largest hidden size whose head operand fits beside one ring stage (16-row tiles of 4 tokens, 16 rows at T = 16).
 constexpr int HEAD_MAX_HIDDEN = 3072;
 
+// Prefill GEMM on tcgen05 (gemm.cu): y[M][O] = W . x for any M. gemm_pack converts the MLX pack (device arrays) once;
+// gemm_run prepares the activation tiles (bop: gemm_act_bytes, ex: M ints) and runs the GEMM on the stream.
+size_t gemm_w_bytes(int O, int K);
+size_t gemm_bias_bytes(int O, int K, int G);
+size_t gemm_act_bytes(int M, int K, int G);
+void gemm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int O, int K, int G, uint8_t* wt,
+               uint8_t* abias, cudaStream_t st);
+void gemm_prep_only(const float* x, int M, int K, int G, uint8_t* bop, int* ex, cudaStream_t st);
+cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int G, const float* x, int M, uint8_t* bop,
+                     int* ex, float* y, int* err, int num_sms, cudaStream_t st);
+
 // Generic launch helper (PDL attribute on).
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args);
 

@@ -11,7 +11,7 @@
 using namespace bcu;
 
 struct bcu_linear {
-    int device = 0;
+    int device = 0, sms = 148;
     TernaryMat m;
     void* codes = nullptr;
     uint32_t* sb = nullptr;
@@ -19,6 +19,11 @@ struct bcu_linear {
     float* partial = nullptr;
     unsigned* counters = nullptr;
     int* err = nullptr;
+    // prefill GEMM (gemm.cu): packed weights and bias tiles; activation tiles and exponents grown on demand
+    uint8_t *gwt = nullptr, *gbias = nullptr, *gbop = nullptr;
+    int* gex = nullptr;
+    size_t gbop_bytes = 0;
+    int gex_n = 0;
 };
 
 extern "C" {
@@ -41,8 +46,11 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
              cudaMemcpy(ds, scales_host, sb, cudaMemcpyHostToDevice) == cudaSuccess &&
              (!biases_host || cudaMemcpy(db, biases_host, sb, cudaMemcpyHostToDevice) == cudaSuccess);
     }
+    ok = ok && cudaMalloc(&l->gwt, gemm_w_bytes(O, K)) == cudaSuccess &&
+         cudaMalloc(&l->gbias, gemm_bias_bytes(O, K, group)) == cudaSuccess;
     if (ok) {
         repack_ternary(dw, ds, db, O, K, group, l->codes, l->sb, 0);
+        gemm_pack(dw, ds, db, O, K, group, l->gwt, l->gbias, 0);
         ok = cudaDeviceSynchronize() == cudaSuccess;
     }
     cudaFree(dw);
@@ -55,6 +63,7 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
     l->m.group = group;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    l->sms = sms;
     plan_ternary(l->m, sms);
     ok = ok && cudaMalloc(&l->partial, (size_t)l->m.nsplit * VMAX * O * 4) == cudaSuccess &&
          cudaMalloc(&l->counters, (size_t)(O / 128) * 4) == cudaSuccess && cudaMalloc(&l->err, 4) == cudaSuccess &&
@@ -71,7 +80,7 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
 void bcu_linear_free(bcu_linear* l) {
     if (!l) return;
     cudaSetDevice(l->device);
-    void* p[] = {l->codes, l->sb, l->partial, l->counters, l->err};
+    void* p[] = {l->codes, l->sb, l->partial, l->counters, l->err, l->gwt, l->gbias, l->gbop, l->gex};
     for (void* q : p)
         if (q) cudaFree(q);
     delete l;
@@ -110,6 +119,52 @@ bcu_status bcu_linear_forward(bcu_linear* l, const float* x_dev, int32_t T, floa
     if (!l) return BCU_ERR_ARG;
     cudaSetDevice(l->device);
     return linear_run(l, nullptr, x_dev, T, 0, nullptr, y_dev, stream);
+}
+
+bcu_status bcu_linear_gemm(bcu_linear* l, const float* x_dev, int32_t M, float* y_dev, void* stream) {
+    if (!l || !x_dev || !y_dev || M < 1) return BCU_ERR_ARG;
+    cudaSetDevice(l->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t need = gemm_act_bytes(M, l->m.K, l->m.group);
+    if (need > l->gbop_bytes || M > l->gex_n) {  // grow the activation tiles (outside any capture)
+        if (cudaStreamSynchronize(st) != cudaSuccess) return BCU_ERR_CUDA;
+        cudaFree(l->gbop);
+        cudaFree(l->gex);
+        l->gbop = nullptr;
+        l->gex = nullptr;
+        l->gbop_bytes = 0;
+        l->gex_n = 0;
+        if (cudaMalloc(&l->gbop, need) != cudaSuccess || cudaMalloc(&l->gex, (size_t)M * 4) != cudaSuccess)
+            return BCU_ERR_OOM;
+        l->gbop_bytes = need;
+        l->gex_n = M;
+    }
+    if (gemm_run(l->gwt, l->gbias, l->m.O, l->m.K, l->m.group, x_dev, M, l->gbop, l->gex, y_dev, l->err, l->sms, st) !=
+        cudaSuccess)
+        return BCU_ERR_CUDA;
+    return BCU_OK;
+}
+
+// Test hook (not in the ABI header): the GEMM's activation tiles and exponents for x [M][K] (device pointers; bop
+// sized by the same rule as bcu_linear_gemm's scratch), so tests can check their layout byte for byte.
+bcu_status bcu_gemm_prep_debug(bcu_linear* l, const float* x_dev, int32_t M, void* bop_dev, int32_t* ex_dev) {
+    if (!l || !x_dev || !bop_dev || !ex_dev || M < 1) return BCU_ERR_ARG;
+    cudaSetDevice(l->device);
+    gemm_prep_only(x_dev, M, l->m.K, l->m.group, (uint8_t*)bop_dev, ex_dev, 0);
+    return cudaDeviceSynchronize() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
+}
+
+bcu_status bcu_linear_sync(bcu_linear* l, void* stream) {
+    if (!l) return BCU_ERR_ARG;
+    cudaSetDevice(l->device);
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return BCU_ERR_CUDA;
+    int e = 0;
+    if (cudaMemcpy(&e, l->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return BCU_ERR_CUDA;
+    if (e) {
+        cudaMemset(l->err, 0, 4);
+        return BCU_ERR_TIMEOUT;
+    }
+    return BCU_OK;
 }
 
 // ------------------------------------------------------------------------------------------ no-allocation variant

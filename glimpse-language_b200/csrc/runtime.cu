@@ -368,7 +368,7 @@ void enqueue_pass(bcu_model* m, int T) {
     ha.d = d;
     ha.T = T;
     launch_head(ha, NT, m->head_grid, st);
-    note("head", -1);
+    note("head", (size_t)-1);
 }
 
 bcu_status get_graph(bcu_model* m, int T, cudaGraphExec_t* out) {

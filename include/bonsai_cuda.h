@@ -267,6 +267,13 @@ bcu_status bcu_linear_rotate_forward(bcu_linear* l, const uint16_t* x_bf16_dev, 
                                      const float* signs_dev, float* y_dev, void* stream);
 /* Y = W . X for an already rotated fp32 X (device pointers). */
 bcu_status bcu_linear_forward(bcu_linear* l, const float* x_dev, int32_t T, float* y_dev, void* stream);
+/* Batched prefill matmul (the reference's qmm, kernels.metal:437-500 / qmm_cm.comp; graded config 5): y[M][O] = W x
+ * for any M, fp32 x (already rotated) and y on the device, on 5th-generation tensor cores (tcgen05.mma, tensor
+ * memory accumulators, bulk-copy staging). Grows its activation scratch on the first call of a larger M (outside any
+ * stream capture). Asynchronous: bcu_linear_sync waits and reports a device timeout. */
+bcu_status bcu_linear_gemm(bcu_linear* l, const float* x_dev, int32_t M, float* y_dev, void* stream);
+/* Waits for `stream` and returns BCU_ERR_TIMEOUT (clearing it) if a kernel of this handle gave up a bounded wait. */
+bcu_status bcu_linear_sync(bcu_linear* l, void* stream);
 
 /* bcu_linear_rotate_forward for callers that may not allocate device memory when they run it: a host that hands
  * all of its device memory to its own pool, or a decode loop that must not stall on the device synchronisation a
