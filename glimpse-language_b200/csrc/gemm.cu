@@ -2,21 +2,24 @@
 // kernels.metal:437-500, and its Vulkan coopmat form qmm_cm.comp) on the 5th-generation tensor cores:
 // y[M][O] = W . x for M tokens, W the MLX 2-bit pack (w = c s + b per group of G inputs).
 //
-// Per CTA tile: 128 weight rows x 128 tokens, accumulated in tensor memory (TMEM, 256 fp32 columns: the tokens' fp16
-// hi parts in columns 0..127 and lo parts in 128..255, so one tcgen05.mma of N = 256 multiplies both halves by the
-// same weight tile). K runs in chunks of 64 inputs through a 3-stage shared-memory pipeline:
-//   - one thread issues 1-D bulk copies (the TMA engine, cp.async.bulk, no tensor map, no multicast) of the chunk's
+// Per CTA tile: 128 weight rows x 128 tokens, accumulated in tensor memory (TMEM: the tokens' fp16 hi parts in columns
+// 0..127 and lo parts in 128..255 of a 256-column accumulator, so one tcgen05.mma of N = 256 multiplies both halves by
+// the same weight tile; two accumulators, so a tile's epilogue overlaps the next tile's MMAs). K runs in chunks of 64
+// inputs through a 4-stage shared-memory pipeline with warp roles:
+//   - a loader warp issues 1-D bulk copies (the TMA engine, cp.async.bulk, no tensor map, no multicast) of the chunk's
 //     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's canonical layout) and of its packed codes and
 //     scales (2.3 KB), completing on the stage's mbarrier;
-//   - all 128 threads decode the codes into fp16 weights c s (exact for ternary codes: one fma of (1024 + c) s -
-//     1024 s) in the canonical K-major layout (8-row x 16-byte core matrices, no swizzle);
-//   - one thread issues 4 tcgen05.mma.kind::f16 (128 x 256 x 16) and commits them to the stage's second mbarrier,
-//     which frees the stage for the loads two chunks ahead.
+//   - 4 decoder warps (thread = weight row) turn the codes into fp16 weights c s (one LOP3 per pair of codes gives
+//     fp16 1024 + c, one fma with s and -1024 s gives c s, exact for ternary codes) in the canonical K-major layout
+//     (8-row x 16-byte core matrices, no swizzle);
+//   - an MMA warp issues 4 tcgen05.mma.kind::f16 (128 x 256 x 16) per chunk and commits them to the stage's mbarrier,
+//     which frees the stage;
+//   - 4 epilogue warps read the accumulator (tcgen05.ld) and write y.
 // The bias term sum_g b_g sum_{k in g} x_k rides as extra chunks: A = G b (prepared tiles), B = the group sums of the
 // token times 2^-log2(G) (prepared with the activations). Activations are fp32 split as x 2^E = hi + lo (fp16 each,
 // E per token from its row maximum), so every product is exact and sums are fp32: y = (D_hi + D_lo) 2^-E.
-// Every wait is bounded; on a timeout the kernel records ERR_MBAR_TIMEOUT, waits (bounded) for its copies and MMAs
-// in flight, frees its tensor memory and returns.
+// Every wait is bounded; on a timeout the kernel records ERR_MBAR_TIMEOUT, every role stops, the MMA issuer waits
+// (bounded) for its last MMAs, and the tensor memory is freed.
 #include <mutex>
 
 #include "common.cuh"
@@ -26,7 +29,7 @@
 namespace bcu {
 
 constexpr int GM_ROWS = 128, GM_TOK = 128, GM_KC = 64;  // tile rows, tile tokens, inputs per chunk
-constexpr int GM_STAGES = 3;
+constexpr int GM_STAGES = 4;
 constexpr int GM_A_BYTES = GM_ROWS * GM_KC * 2;           // 16 KB decoded weights
 constexpr int GM_B_BYTES = 2 * GM_TOK * GM_KC * 2;        // 32 KB activations (hi and lo)
 constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // codes [128][4 u32] + scales [128] fp16
@@ -122,9 +125,16 @@ __global__ void gemm_pack_bias_kernel(const uint16_t* __restrict__ s, const uint
 }
 
 // ----------------------------------------------------------------------------------------------- activations
-// One warp per token: exponent E = clamp(14 - ceil-exponent(max |x|)), then x 2^E split into fp16 hi + lo written to
-// the token tile's chunks in the canonical K-major layout of the B operand ([8 k-chunks][32 row groups][8 rows]
-// [8 fp16]; rows 0..127 hi, 128..255 lo), and the group sums x 2^(E - log2 G) (hi + lo) to the bias chunks.
+// Order of the inputs inside a chunk: the weight decode takes two codes of one packed word per LOP3, codes i and i + 8
+// (i < 8) of word w (inputs 16 w + i, 16 w + i + 8), so half p of 16-byte row kk of a chunk holds input
+// 16 (kk / 2) + 4 (kk % 2) + p / 2 + 8 (p % 2). The activations use the same order (any order of the inputs gives
+// the same dot products, as long as A and B agree).
+__host__ __device__ inline int gemm_k_of(int kk, int p) { return 16 * (kk >> 1) + 4 * (kk & 1) + (p >> 1) + 8 * (p & 1); }
+
+// One warp per token: exponent E = clamp(14 - frexp exponent of max |x|), then x 2^E split into fp16 hi + lo written
+// to the token tile's chunks in the canonical K-major layout of the B operand ([8 k-rows][32 row groups][8 rows]
+// [8 fp16], rows 0..127 hi, 128..255 lo, inputs in the decode order above), and the group sums x 2^(E - log2 G)
+// (hi + lo) to the bias chunks. Lane l takes packed word w = l + 32 i: inputs 16 w .. 16 w + 15, two k-rows.
 __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int G, int nmain, int nbias,
                                  uint8_t* __restrict__ bop, int* __restrict__ ex) {
     const int lane = threadIdx.x & 31, t = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -147,31 +157,43 @@ __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int 
     const int nch = nmain + nbias, tt = t / GM_TOK, tl = t % GM_TOK;
     uint8_t* tile0 = bop + (size_t)tt * nch * GM_B_BYTES;
     const int hi_off = (tl / 8) * 128 + (tl % 8) * 16, lo_off = ((GM_TOK + tl) / 8) * 128 + (tl % 8) * 16;
-    const int lg = G == 64 ? 6 : 7, lanes_per_group = G / 8;
+    const int lg = G == 64 ? 6 : 7, lanes_per_group = G / 16;
     const float fb = pow2f(E - lg > 100 ? 100 : E - lg);
-    for (int q0 = 0; q0 < K / 8; q0 += 32) {
-        const int q = q0 + lane;  // 8 inputs 8 q .. 8 q + 7
+    for (int w0 = 0; w0 < K / 16; w0 += 32) {
+        const int w = w0 + lane;  // inputs 16 w .. 16 w + 15
         float gs = 0.0f;
-        if (q < K / 8) {
-            const float4 a = *(const float4*)(row + 8 * q), b = *(const float4*)(row + 8 * q + 4);
-            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            uint16_t h[8], l[8];
+        if (w < K / 16) {
+            float v[16];
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const float s = v[e] * f;
-                const __half hh = __float2half_rn(s);
-                h[e] = __half_as_ushort(hh);
-                l[e] = __half_as_ushort(__float2half_rn(s - __half2float(hh)));
-                gs += v[e];
+            for (int i = 0; i < 4; i++) {
+                const float4 a = *(const float4*)(row + 16 * w + 4 * i);
+                v[4 * i] = a.x;
+                v[4 * i + 1] = a.y;
+                v[4 * i + 2] = a.z;
+                v[4 * i + 3] = a.w;
             }
-            uint8_t* chunk = tile0 + (size_t)(q / 8) * GM_B_BYTES + (q % 8) * (2 * GM_TOK * 16);
-            *(uint4*)(chunk + hi_off) = *(const uint4*)h;
-            *(uint4*)(chunk + lo_off) = *(const uint4*)l;
+#pragma unroll
+            for (int e = 0; e < 16; e++) gs += v[e];
+            uint8_t* chunk = tile0 + (size_t)(w / 4) * GM_B_BYTES;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int kk = 2 * (w % 4) + h;
+                uint16_t hv[8], lv[8];
+#pragma unroll
+                for (int p = 0; p < 8; p++) {
+                    const float s = v[4 * h + (p >> 1) + 8 * (p & 1)] * f;
+                    const __half hh = __float2half_rn(s);
+                    hv[p] = __half_as_ushort(hh);
+                    lv[p] = __half_as_ushort(__float2half_rn(s - __half2float(hh)));
+                }
+                *(uint4*)(chunk + kk * (2 * GM_TOK * 16) + hi_off) = *(const uint4*)hv;
+                *(uint4*)(chunk + kk * (2 * GM_TOK * 16) + lo_off) = *(const uint4*)lv;
+            }
         }
-        // group sums: the lanes of one group are consecutive (G / 8 of them), summed in a fixed tree
+        // group sums: the G / 16 consecutive lanes of one group, summed in a fixed tree
         for (int o = 1; o < lanes_per_group; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
-        if (q < K / 8 && (lane % lanes_per_group) == 0) {
-            const int g = q / lanes_per_group;
+        if (w < K / 16 && (lane % lanes_per_group) == 0) {
+            const int g = w / lanes_per_group;
             const float s = gs * fb;
             const __half hh = __float2half_rn(s);
             const __half ll = __float2half_rn(s - __half2float(hh));
@@ -193,120 +215,152 @@ struct GemmParams {
     int M, O, nmain, nbias, n_rt, n_tiles;
 };
 
-__global__ void __launch_bounds__(128, 1) ternary_gemm_kernel(GemmParams p) {
+// Warp roles (320 threads): warps 0-3 epilogue (tensor memory -> y; warp w reads lanes 32 w .. 32 w + 31), warps 4-7
+// decode (thread = weight row), warp 8 issues the bulk copies, warp 9 issues the MMAs. Stages: GM_STAGES buffers of
+// A | B | W; barriers load_full (copies landed), a_full (128 decoder arrivals), mma_done (the stage's MMAs finished:
+// the stage is free); accumulators: two 256-column buffers in tensor memory with acc_full (the tile's MMAs finished)
+// and acc_empty (128 epilogue arrivals), so the epilogue of one tile overlaps the MMAs of the next.
+constexpr int GM_THREADS = 320;
+
+__global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint64_t* load_bar = (uint64_t*)(smem + GM_STAGES * GM_STAGE);
-    uint64_t* mma_bar = load_bar + GM_STAGES;
-    uint32_t* s_tmem = (uint32_t*)(mma_bar + GM_STAGES);
-    __shared__ int s_bad;
+    uint64_t* load_full = (uint64_t*)(smem + GM_STAGES * GM_STAGE);
+    uint64_t* a_full = load_full + GM_STAGES;
+    uint64_t* mma_done = a_full + GM_STAGES;
+    uint64_t* acc_full = mma_done + GM_STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* s_tmem = (uint32_t*)(acc_empty + 2);
+    volatile int* s_abort = (volatile int*)(s_tmem + 1);
     const int nch = p.nmain + p.nbias;
     const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int total = my_tiles * nch;  // chunks this CTA runs, in order
+    const int total = my_tiles * nch;
     if (tid == 0) {
-        s_bad = 0;
         for (int i = 0; i < GM_STAGES; i++) {
-            mbar_init(&load_bar[i], 1);
-            mbar_init(&mma_bar[i], 1);
+            mbar_init(&load_full[i], 1);
+            mbar_init(&a_full[i], 128);
+            mbar_init(&mma_done[i], 1);
         }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
+        *s_abort = 0;
         fence_proxy_async_smem();
     }
     if (warp == 0) {
-        tmem_alloc(s_tmem, GM_TMEM_COLS);
+        tmem_alloc(s_tmem, 2 * GM_TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-
-    auto stage_of = [&](int q) { return smem + (q % GM_STAGES) * GM_STAGE; };
-    auto issue_load = [&](int q) {  // thread 0
-        const int j = q / nch, c = q % nch;
-        const int tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
-        uint8_t* st = stage_of(q);
-        uint64_t* bar = &load_bar[q % GM_STAGES];
-        const uint8_t* bsrc = p.bop + ((size_t)tt * nch + c) * GM_B_BYTES;
-        if (c < p.nmain) {
-            mbar_expect_tx(bar, GM_B_BYTES + GM_W_BYTES);
-            bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, bar);
-            bulk_g2s(st + GM_A_BYTES + GM_B_BYTES, p.wt + ((size_t)rt * p.nmain + c) * GM_W_BYTES, GM_W_BYTES, bar);
-        } else {
-            mbar_expect_tx(bar, GM_B_BYTES + GM_A_BYTES);
-            bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, bar);
-            bulk_g2s(st, p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * GM_A_BYTES, GM_A_BYTES, bar);
-        }
+    auto fail = [&]() {
+        atomicOr(p.err, ERR_MBAR_TIMEOUT);
+        *s_abort = 1;
     };
-    if (tid == 0)
-        for (int q = 0; q < 2 && q < total; q++) issue_load(q);
+    auto stage_of = [&](int q) { return smem + (q % GM_STAGES) * GM_STAGE; };
+    // parity of the n-th completion (0-based) of a barrier used once per GM_STAGES chunks
+    auto par = [](int q) { return (uint32_t)((q / GM_STAGES) & 1); };
 
-    int issued = total < 2 ? total : 2;  // loads issued
-    int committed = 0;                   // chunks whose MMAs were committed
-    for (int q = 0; q < total; q++) {
-        const int s = q % GM_STAGES, c = q % nch;
-        uint8_t* st = stage_of(q);
-        bool bad = !mbar_wait_bounded(&load_bar[s], (q / GM_STAGES) & 1);
-        if (__syncthreads_or(bad)) {
-            if (tid == 0) atomicOr(p.err, ERR_MBAR_TIMEOUT);
-            break;
-        }
-        if (c < p.nmain) {  // decode row tid's 64 codes into the canonical A tile
-            const uint4 cw = ((const uint4*)(st + GM_A_BYTES + GM_B_BYTES))[tid];
-            const uint16_t sc = ((const uint16_t*)(st + GM_A_BYTES + GM_B_BYTES + GM_ROWS * 16))[tid];
-            const uint32_t s2 = (uint32_t)sc * 0x10001u;
-            uint32_t n2;
-            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(n2) : "r"(s2), "r"(0xE400E400u));  // -1024 s
-            const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-#pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                const uint32_t wd = words[kk >> 1] >> (16 * (kk & 1));  // codes 8 kk .. 8 kk + 7 in bits 0..15
-                uint32_t o[4];
-#pragma unroll
-                for (int pr = 0; pr < 4; pr++) {
-                    const uint32_t x = wd >> (4 * pr);
-                    const uint32_t h = (x & 3u) | ((x << 14) & 0x30000u) | 0x64006400u;  // fp16 (1024 + c) pair
-                    o[pr] = hfma2_u32(h, s2, n2);                                     // c s, exact for c <= 2
+    if (warp == 8) {  // ------------------------------------------------------------------ bulk copies
+        if (lane == 0) {
+            for (int q = 0; q < total && !*s_abort; q++) {
+                const int s = q % GM_STAGES, c = q % nch, j = q / nch;
+                const int tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
+                if (q >= GM_STAGES && !mbar_wait_bounded(&mma_done[s], par(q - GM_STAGES))) {
+                    fail();
+                    break;
                 }
-                *(uint4*)(st + kk * (GM_ROWS * 16) + tid * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-            }
-        }
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            for (int ks = 0; ks < 4; ks++) {
-                const uint64_t ad = umma_desc(st + 2 * ks * (GM_ROWS * 16), GM_ROWS * 16, 128);
-                const uint64_t bd = umma_desc(st + GM_A_BYTES + 2 * ks * (2 * GM_TOK * 16), 2 * GM_TOK * 16, 128);
-                umma_f16(tmem, ad, bd, GM_IDESC, (c > 0 || ks > 0) ? 1u : 0u);
-            }
-            umma_commit(&mma_bar[s]);
-            // the stage of chunk q - 1 is free once its MMAs are done: load chunk q + 2 into it
-            if (q + 2 < total) {
-                if (q >= 1 && !mbar_wait_bounded(&mma_bar[(q - 1) % GM_STAGES], ((q - 1) / GM_STAGES) & 1)) {
-                    atomicOr(p.err, ERR_MBAR_TIMEOUT);
-                    s_bad = 1;
+                uint8_t* st = stage_of(q);
+                const uint8_t* bsrc = p.bop + ((size_t)tt * nch + c) * GM_B_BYTES;
+                if (c < p.nmain) {
+                    mbar_expect_tx(&load_full[s], GM_B_BYTES + GM_W_BYTES);
+                    bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, &load_full[s]);
+                    bulk_g2s(st + GM_A_BYTES + GM_B_BYTES, p.wt + ((size_t)rt * p.nmain + c) * GM_W_BYTES, GM_W_BYTES,
+                             &load_full[s]);
                 } else {
-                    issue_load(q + 2);
-                    issued = q + 3;
+                    mbar_expect_tx(&load_full[s], GM_B_BYTES + GM_A_BYTES);
+                    bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, &load_full[s]);
+                    bulk_g2s(st, p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * GM_A_BYTES, GM_A_BYTES,
+                             &load_full[s]);
                 }
             }
         }
-        committed = q + 1;
-        if (c == nch - 1) {  // tile done: TMEM -> registers -> y
-            const int j = q / nch, tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
-            bad = !mbar_wait_bounded(&mma_bar[s], (q / GM_STAGES) & 1);
-            if (__syncthreads_or(bad || s_bad)) {
-                if (tid == 0) atomicOr(p.err, ERR_MBAR_TIMEOUT);
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {  // ------------------------------------------------- decode
+        const int r = tid - 128;  // weight row of the tile
+        for (int q = 0; q < total && !*s_abort; q++) {
+            const int s = q % GM_STAGES, c = q % nch;
+            uint8_t* st = stage_of(q);
+            if (c < p.nmain) {
+                // A[s] is free once the MMAs of chunk q - GM_STAGES are done; the codes of chunk q have landed
+                if ((q >= GM_STAGES && !mbar_wait_bounded(&mma_done[s], par(q - GM_STAGES))) ||
+                    !mbar_wait_bounded(&load_full[s], par(q))) {
+                    fail();
+                    break;
+                }
+                const uint4 cw = ((const uint4*)(st + GM_A_BYTES + GM_B_BYTES))[r];
+                const uint16_t sc = ((const uint16_t*)(st + GM_A_BYTES + GM_B_BYTES + GM_ROWS * 16))[r];
+                const uint32_t s2 = (uint32_t)sc * 0x10001u;
+                uint32_t n2;
+                asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(n2) : "r"(s2), "r"(0xE400E400u));  // -1024 s
+                const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+                for (int wi = 0; wi < 4; wi++) {
+                    uint32_t o[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++)  // codes i, i + 8: fp16 (1024 + c) pair, then c s (exact for c <= 2)
+                        o[i] = hfma2_u32(lop_and_or(words[wi] >> (2 * i), 0x00030003u, 0x64006400u), s2, n2);
+                    *(uint4*)(st + (2 * wi) * (GM_ROWS * 16) + r * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *(uint4*)(st + (2 * wi + 1) * (GM_ROWS * 16) + r * 16) = make_uint4(o[4], o[5], o[6], o[7]);
+                }
+                fence_proxy_async_smem();
+            }
+            mbar_arrive(&a_full[s]);
+        }
+    } else if (warp == 9) {  // ----------------------------------------------------------- MMA
+        if (lane == 0) {
+            for (int q = 0; q < total && !*s_abort; q++) {
+                const int s = q % GM_STAGES, c = q % nch, j = q / nch, a = j & 1;
+                if (c == 0 && j >= 2 && !mbar_wait_bounded(&acc_empty[a], (uint32_t)(((j >> 1) - 1) & 1))) {
+                    fail();
+                    break;
+                }
+                if (!mbar_wait_bounded(&load_full[s], par(q)) || !mbar_wait_bounded(&a_full[s], par(q))) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                uint8_t* st = stage_of(q);
+                const uint32_t d = tmem + a * GM_TMEM_COLS;
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++) {
+                    const uint64_t ad = umma_desc(st + 2 * ks * (GM_ROWS * 16), GM_ROWS * 16, 128);
+                    const uint64_t bd = umma_desc(st + GM_A_BYTES + 2 * ks * (2 * GM_TOK * 16), 2 * GM_TOK * 16, 128);
+                    umma_f16(d, ad, bd, GM_IDESC, (c > 0 || ks > 0) ? 1u : 0u);
+                }
+                umma_commit(&mma_done[s]);
+                if (c == nch - 1) umma_commit(&acc_full[a]);
+            }
+        }
+        __syncwarp();
+    } else {  // ------------------------------------------------------------------ epilogue (warps 0-3)
+        for (int j = 0; j < my_tiles && !*s_abort; j++) {
+            const int a = j & 1, tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
+            if (!mbar_wait_bounded(&acc_full[a], (uint32_t)((j >> 1) & 1))) {
+                fail();
                 break;
             }
             tc_fence_after();
             const int row = rt * GM_ROWS + warp * 32 + lane;
+            const uint32_t base = tmem + a * GM_TMEM_COLS + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
             for (int cb = 0; cb < GM_TOK / 32; cb++) {
                 uint32_t hi[32], lo[32];
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb * 32, hi);
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + GM_TOK + cb * 32, lo);
+                tmem_ld32(base + cb * 32, hi);
+                tmem_ld32(base + GM_TOK + cb * 32, lo);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
@@ -316,20 +370,16 @@ __global__ void __launch_bounds__(128, 1) ternary_gemm_kernel(GemmParams p) {
                 }
             }
             tc_fence_before();
-        } else if (__syncthreads_or(s_bad)) {
-            break;
+            mbar_arrive(&acc_empty[a]);
         }
     }
-    // drain: copies and MMAs still in flight (bounded), then free the tensor memory
-    if (tid == 0) {
-        for (int q = committed; q < issued; q++) mbar_wait_bounded(&load_bar[q % GM_STAGES], (q / GM_STAGES) & 1, 1u << 20);
-        if (committed > 0)
-            mbar_wait_bounded(&mma_bar[(committed - 1) % GM_STAGES], ((committed - 1) / GM_STAGES) & 1, 1u << 20);
-    }
+    // drain: the MMA issuer waits (bounded) for its last commit, the loader for copies that nobody consumed
+    if (warp == 9 && lane == 0 && total > 0) mbar_wait_bounded(&mma_done[(total - 1) % GM_STAGES], par(total - 1), 1u << 20);
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, GM_TMEM_COLS);
+    if (warp == 0) tmem_dealloc(tmem, 2 * GM_TMEM_COLS);
 }
 
 // ----------------------------------------------------------------------------------------------- host
@@ -375,7 +425,7 @@ cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int 
         cudaFuncSetAttribute(ternary_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
     });
     const int grid = p.n_tiles < num_sms ? p.n_tiles : num_sms;
-    ternary_gemm_kernel<<<grid, 128, GM_SMEM, st>>>(p);
+    ternary_gemm_kernel<<<grid, GM_THREADS, GM_SMEM, st>>>(p);
     return cudaGetLastError();
 }
 

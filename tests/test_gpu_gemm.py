@@ -89,8 +89,9 @@ def test_gemm_rows_do_not_depend_on_batch(gpu):
 
 def test_activation_tiles_layout(gpu):
     """gemm_prep_kernel's output byte for byte against a restatement of the layout: per token tile and chunk of 64
-    inputs, [8 k-chunks][32 row groups][8 rows][8 fp16] with rows 0..127 the hi parts and 128..255 the lo parts of
-    x 2^E, E = clamp(14 - frexp exponent of max |x|), then the bias chunks of group sums x 2^(E - 6)."""
+    inputs, [8 k-rows][32 row groups][8 rows][8 fp16] with rows 0..127 the hi parts and 128..255 the lo parts of
+    x 2^E, E = clamp(14 - frexp exponent of max |x|), inputs in the weight decode's order, then the bias chunks of
+    group sums x 2^(E - 6)."""
     torch = pytest.importorskip("torch")
     O, K, M, G = 128, 512, 130, 64
     W, S, B, X = ternary_case(O, K, G, M, "neg", 5)
@@ -107,21 +108,22 @@ def test_activation_tiles_layout(gpu):
     E = np.array([min(max(14 - np.frexp(np.abs(r).max())[1], -60), 100) for r in X])
     assert np.array_equal(ex.cpu().numpy(), E)
     want = np.zeros_like(got)
+    # half p of k-row kk of a chunk holds input 16 (kk / 2) + 4 (kk % 2) + p / 2 + 8 (p % 2) (the decode's order)
+    order = np.array([16 * (kk // 2) + 4 * (kk % 2) + p // 2 + 8 * (p % 2) for kk in range(8) for p in range(8)])
     for t in range(M):
         tt, tl = divmod(t, 128)
         v = X[t].astype(np.float32) * np.float32(2.0 ** E[t])
         hi = v.astype(np.float16)
         lo = (v - hi.astype(np.float32)).astype(np.float16)
-        # each lane sums its 8 inputs in order, then the group's 8 lanes are summed as a butterfly tree
-        ls = np.cumsum(X[t].reshape(-1, 8), axis=1, dtype=np.float32)[:, -1].reshape(-1, 8)
-        pair = [ls[:, 2 * i] + ls[:, 2 * i + 1] for i in range(4)]
-        gs = ((pair[0] + pair[1]) + (pair[2] + pair[3])) * np.float32(2.0 ** (E[t] - 6))
+        # each lane sums its 16 inputs in order, then the group's 4 lanes are summed as a butterfly tree
+        ls = np.cumsum(X[t].reshape(-1, 16), axis=1, dtype=np.float32)[:, -1].reshape(-1, 4)
+        gs = ((ls[:, 0] + ls[:, 1]) + (ls[:, 2] + ls[:, 3])) * np.float32(2.0 ** (E[t] - 6))
         ghi = gs.astype(np.float16)
         glo = (gs - ghi.astype(np.float32)).astype(np.float16)
         for c in range(nmain):
-            blk = slice(64 * c, 64 * c + 64)
-            want[tt, c, :, tl // 8, tl % 8, :] = hi[blk].reshape(8, 8).view(np.uint16)
-            want[tt, c, :, (128 + tl) // 8, tl % 8, :] = lo[blk].reshape(8, 8).view(np.uint16)
+            ks = 64 * c + order
+            want[tt, c, :, tl // 8, tl % 8, :] = hi[ks].reshape(8, 8).view(np.uint16)
+            want[tt, c, :, (128 + tl) // 8, tl % 8, :] = lo[ks].reshape(8, 8).view(np.uint16)
         ng = K // G
         for gi in range(ng):
             want[tt, nmain, gi // 8, tl // 8, tl % 8, gi % 8] = ghi[gi].view(np.uint16)
