@@ -7,11 +7,11 @@
 // the same weight tile; two accumulators, so a tile's epilogue overlaps the next tile's MMAs). K runs in chunks of 64
 // inputs through a 4-stage shared-memory pipeline with warp roles:
 //   - a loader warp issues 1-D bulk copies (the TMA engine, cp.async.bulk, no tensor map, no multicast) of the chunk's
-//     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's canonical layout) and of its packed codes and
+//     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's shared-memory layout) and of its packed codes and
 //     scales (2.3 KB), completing on the stage's mbarrier;
 //   - 4 decoder warps (thread = weight row) turn the codes into fp16 weights c s (one LOP3 per pair of codes gives
-//     fp16 1024 + c, one fma with s and -1024 s gives c s, exact for ternary codes) in the canonical K-major layout
-//     (8-row x 16-byte core matrices, no swizzle);
+//     fp16 1024 + c, one fma with s and -1024 s gives c s, exact for ternary codes) in the K-major layout with the
+//     128-byte swizzle;
 //   - an MMA warp issues 4 tcgen05.mma.kind::f16 (128 x 256 x 16) per chunk and commits them to the stage's mbarrier,
 //     which frees the stage;
 //   - 4 epilogue warps read the accumulator (tcgen05.ld) and write y.
@@ -35,7 +35,7 @@ constexpr int GM_B_BYTES = 2 * GM_TOK * GM_KC * 2;        // 32 KB activations (
 constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // codes [128][4 u32] + scales [128] fp16
 constexpr int GM_STAGE = 52224;                           // A | B | W (51456 B), 1024-aligned
 static_assert(GM_A_BYTES + GM_B_BYTES + GM_W_BYTES <= GM_STAGE, "a stage's buffers overlap the next stage");
-constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 1024;      // + barriers, TMEM address, exponents
+constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 2048;      // + barriers, TMEM address; + 1024 to align the base
 constexpr uint32_t GM_TMEM_COLS = 256;
 // kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B f16 (0), both K-major, N = 256 (bits 17-22 =
 // N / 8), M = 128 (bits 24-28 = M / 16)
@@ -74,12 +74,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
                  : "r"(taddr));
 }
 
-// Shared-memory matrix descriptor, no swizzle: core matrices of 8 rows x 16 bytes; lbo = bytes between core matrices
-// adjacent in K, sbo = bytes between core matrices adjacent in M/N; version 1 (bit 46).
-__device__ __forceinline__ uint64_t umma_desc(const void* p, uint32_t lbo, uint32_t sbo) {
-    const uint64_t a = smem_u32(p);
-    return ((a >> 4) & 0x3FFFull) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) |
-           (1ull << 46);
+// Operand tiles in shared memory: K-major with the 128-byte swizzle. A row of a tile is one chunk of 64 fp16 inputs
+// (128 bytes); rows are contiguous; 16-byte piece j of row r sits at r * 128 + ((j ^ (r % 8)) * 16), so 8 rows form a
+// 1024-byte swizzle atom (tiles start on 1024-byte boundaries).
+__host__ __device__ inline int sw128(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
+// Its matrix descriptor for the k16 step at byte offset koff (0, 32, 64, 96) of the rows: start address, leading
+// byte offset 16 (unused by swizzled K-major layouts), stride byte offset 1024 (8-row groups), version 1 (bit 46),
+// layout SWIZZLE_128B (2 in bits 61-63).
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile, uint32_t koff) {
+    const uint64_t a = smem_u32(tile) + koff;
+    return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
 // ----------------------------------------------------------------------------------------------- weights
@@ -99,7 +103,7 @@ __global__ void gemm_pack_w_kernel(const uint32_t* __restrict__ w, const uint16_
     ((uint16_t*)(base + GM_ROWS * 16))[r] = s[row * (K / G) + (GM_KC * c) / G];
 }
 
-// Bias chunks: per (rt, bias chunk cb) the canonical A tile [8 k-chunks][16 row groups][8 rows][8 fp16] of
+// Bias chunks: per (rt, bias chunk cb) the A tile (128 rows of 64 fp16, 128-byte swizzle) of
 // G b[row][g], g = 64 cb + k (zero past K / G); b = -s for the implicit bias of the reference pack. One thread per
 // (rt, cb, row, k-chunk).
 __global__ void gemm_pack_bias_kernel(const uint16_t* __restrict__ s, const uint16_t* __restrict__ b, int O, int K,
@@ -121,20 +125,20 @@ __global__ void gemm_pack_bias_kernel(const uint16_t* __restrict__ s, const uint
         v[e] = __half_as_ushort(__float2half_rn(x));
     }
     uint8_t* tile = out + ((size_t)rt * nbias + cb) * GM_A_BYTES;
-    *(uint4*)(tile + kk * (GM_ROWS * 16) + r * 16) = *(const uint4*)v;
+    *(uint4*)(tile + sw128(r, kk)) = *(const uint4*)v;
 }
 
 // ----------------------------------------------------------------------------------------------- activations
 // Order of the inputs inside a chunk: the weight decode takes two codes of one packed word per LOP3, codes i and i + 8
-// (i < 8) of word w (inputs 16 w + i, 16 w + i + 8), so half p of 16-byte row kk of a chunk holds input
+// (i < 8) of word w (inputs 16 w + i, 16 w + i + 8), so half p of 16-byte piece kk of a chunk row holds input
 // 16 (kk / 2) + 4 (kk % 2) + p / 2 + 8 (p % 2). The activations use the same order (any order of the inputs gives
 // the same dot products, as long as A and B agree).
 __host__ __device__ inline int gemm_k_of(int kk, int p) { return 16 * (kk >> 1) + 4 * (kk & 1) + (p >> 1) + 8 * (p & 1); }
 
 // One warp per token: exponent E = clamp(14 - frexp exponent of max |x|), then x 2^E split into fp16 hi + lo written
-// to the token tile's chunks in the canonical K-major layout of the B operand ([8 k-rows][32 row groups][8 rows]
-// [8 fp16], rows 0..127 hi, 128..255 lo, inputs in the decode order above), and the group sums x 2^(E - log2 G)
-// (hi + lo) to the bias chunks. Lane l takes packed word w = l + 32 i: inputs 16 w .. 16 w + 15, two k-rows.
+// to the token tile's chunks in the B operand's layout (256 rows of 64 fp16 with the 128-byte swizzle, rows 0..127
+// hi, 128..255 lo, inputs in the decode order above), and the group sums x 2^(E - log2 G) (hi + lo) to the bias
+// chunks. Lane l takes packed word w = l + 32 i: inputs 16 w .. 16 w + 15, two 16-byte pieces of each row.
 __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int G, int nmain, int nbias,
                                  uint8_t* __restrict__ bop, int* __restrict__ ex) {
     const int lane = threadIdx.x & 31, t = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -156,7 +160,7 @@ __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int 
     const float f = E > 60 ? pow2f(60) * pow2f(E - 60) : (E < -60 ? pow2f(-60) * pow2f(E + 60) : pow2f(E));
     const int nch = nmain + nbias, tt = t / GM_TOK, tl = t % GM_TOK;
     uint8_t* tile0 = bop + (size_t)tt * nch * GM_B_BYTES;
-    const int hi_off = (tl / 8) * 128 + (tl % 8) * 16, lo_off = ((GM_TOK + tl) / 8) * 128 + (tl % 8) * 16;
+    const int n_hi = tl, n_lo = GM_TOK + tl;  // rows of the B tile
     const int lg = G == 64 ? 6 : 7, lanes_per_group = G / 16;
     const float fb = pow2f(E - lg > 100 ? 100 : E - lg);
     for (int w0 = 0; w0 < K / 16; w0 += 32) {
@@ -186,8 +190,8 @@ __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int 
                     hv[p] = __half_as_ushort(hh);
                     lv[p] = __half_as_ushort(__float2half_rn(s - __half2float(hh)));
                 }
-                *(uint4*)(chunk + kk * (2 * GM_TOK * 16) + hi_off) = *(const uint4*)hv;
-                *(uint4*)(chunk + kk * (2 * GM_TOK * 16) + lo_off) = *(const uint4*)lv;
+                *(uint4*)(chunk + sw128(n_hi, kk)) = *(const uint4*)hv;
+                *(uint4*)(chunk + sw128(n_lo, kk)) = *(const uint4*)lv;
             }
         }
         // group sums: the G / 16 consecutive lanes of one group, summed in a fixed tree
@@ -197,9 +201,10 @@ __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int 
             const float s = gs * fb;
             const __half hh = __float2half_rn(s);
             const __half ll = __float2half_rn(s - __half2float(hh));
-            uint8_t* chunk = tile0 + (size_t)(nmain + g / GM_KC) * GM_B_BYTES + ((g % GM_KC) / 8) * (2 * GM_TOK * 16);
-            ((__half*)(chunk + hi_off))[g % 8] = hh;
-            ((__half*)(chunk + lo_off))[g % 8] = ll;
+            uint8_t* chunk = tile0 + (size_t)(nmain + g / GM_KC) * GM_B_BYTES;
+            const int kk = (g % GM_KC) / 8;
+            ((__half*)(chunk + sw128(n_hi, kk)))[g % 8] = hh;
+            ((__half*)(chunk + sw128(n_lo, kk)))[g % 8] = ll;
         }
     }
 }
@@ -223,7 +228,9 @@ struct GemmParams {
 constexpr int GM_THREADS = 320;
 
 __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams p) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // swizzle atoms need 1024-byte aligned tiles: align the base (the launch adds 1024 bytes of slack)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint64_t* load_full = (uint64_t*)(smem + GM_STAGES * GM_STAGE);
     uint64_t* a_full = load_full + GM_STAGES;
@@ -313,8 +320,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
 #pragma unroll
                     for (int i = 0; i < 8; i++)  // codes i, i + 8: fp16 (1024 + c) pair, then c s (exact for c <= 2)
                         o[i] = hfma2_u32(lop_and_or(words[wi] >> (2 * i), 0x00030003u, 0x64006400u), s2, n2);
-                    *(uint4*)(st + (2 * wi) * (GM_ROWS * 16) + r * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-                    *(uint4*)(st + (2 * wi + 1) * (GM_ROWS * 16) + r * 16) = make_uint4(o[4], o[5], o[6], o[7]);
+                    *(uint4*)(st + sw128(r, 2 * wi)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *(uint4*)(st + sw128(r, 2 * wi + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
                 }
                 fence_proxy_async_smem();
             }
@@ -337,8 +344,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
                 const uint32_t d = tmem + a * GM_TMEM_COLS;
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++) {
-                    const uint64_t ad = umma_desc(st + 2 * ks * (GM_ROWS * 16), GM_ROWS * 16, 128);
-                    const uint64_t bd = umma_desc(st + GM_A_BYTES + 2 * ks * (2 * GM_TOK * 16), 2 * GM_TOK * 16, 128);
+                    const uint64_t ad = umma_desc_sw128(st, 32 * ks);
+                    const uint64_t bd = umma_desc_sw128(st + GM_A_BYTES, 32 * ks);
                     umma_f16(d, ad, bd, GM_IDESC, (c > 0 || ks > 0) ? 1u : 0u);
                 }
                 umma_commit(&mma_done[s]);

@@ -89,7 +89,8 @@ def test_gemm_rows_do_not_depend_on_batch(gpu):
 
 def test_activation_tiles_layout(gpu):
     """gemm_prep_kernel's output byte for byte against a restatement of the layout: per token tile and chunk of 64
-    inputs, [8 k-rows][32 row groups][8 rows][8 fp16] with rows 0..127 the hi parts and 128..255 the lo parts of
+    inputs, 256 rows of 8 pieces of 8 fp16 (piece j of row r at position j ^ (r % 8)), rows 0..127 the hi parts and
+    128..255 the lo parts of
     x 2^E, E = clamp(14 - frexp exponent of max |x|), inputs in the weight decode's order, then the bias chunks of
     group sums x 2^(E - 6)."""
     torch = pytest.importorskip("torch")
@@ -104,7 +105,11 @@ def test_activation_tiles_layout(gpu):
     x = torch.from_numpy(X).cuda()
     assert g.L.bcu_gemm_prep_debug(g.h, ctypes.c_void_p(x.data_ptr()), M, ctypes.c_void_p(bop.data_ptr()),
                                    ctypes.c_void_p(ex.data_ptr())) == _lib.OK
-    got = bop.cpu().numpy().view(np.uint16).reshape(nt, nch, 8, 32, 8, 8)
+    # tiles of 256 rows x 8 pieces of 8 fp16, piece j of row r stored at position j ^ (r % 8) (128-byte swizzle)
+    raw = bop.cpu().numpy().view(np.uint16).reshape(nt, nch, 256, 8, 8)
+    sw = np.array([[j ^ (r % 8) for j in range(8)] for r in range(256)])
+    got = np.take_along_axis(raw, sw[None, None, :, :, None].repeat(8, -1).astype(np.int64), axis=3)
+    got = got.transpose(0, 1, 3, 2, 4).reshape(nt, nch, 8, 32, 8, 8)  # [tt][chunk][piece][row group][row][half]
     E = np.array([min(max(14 - np.frexp(np.abs(r).max())[1], -60), 100) for r in X])
     assert np.array_equal(ex.cpu().numpy(), E)
     want = np.zeros_like(got)
