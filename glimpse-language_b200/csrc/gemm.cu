@@ -2,19 +2,20 @@
 // kernels.metal:437-500, and its Vulkan coopmat form qmm_cm.comp) on the 5th-generation tensor cores:
 // y[M][O] = W . x for M tokens, W the MLX 2-bit pack (w = c s + b per group of G inputs).
 //
-// Per CTA tile: 128 weight rows x 128 tokens, accumulated in tensor memory (TMEM: the tokens' fp16 hi parts in columns
-// 0..127 and lo parts in 128..255 of a 256-column accumulator, so one tcgen05.mma of N = 256 multiplies both halves by
-// the same weight tile; two accumulators, so a tile's epilogue overlaps the next tile's MMAs). K runs in chunks of 64
-// inputs through a 4-stage shared-memory pipeline with warp roles:
+// Per CTA tile: 256 weight rows (two halves of 128) x 128 tokens, accumulated in tensor memory (TMEM, all 512 columns:
+// per half a 256-column accumulator with the tokens' fp16 hi parts in columns 0..127 and lo parts in 128..255, so
+// one tcgen05.mma of N = 256 multiplies both by the same weight tile, and the two halves' MMAs share the activation
+// tile, halving the activation bytes per flop). K runs in chunks of 64 inputs through a 3-stage shared-memory
+// pipeline with warp roles:
 //   - a loader warp issues 1-D bulk copies (the TMA engine, cp.async.bulk, no tensor map, no multicast) of the chunk's
-//     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's shared-memory layout) and of its packed codes and
-//     scales (2.3 KB), completing on the stage's mbarrier;
-//   - 4 decoder warps (thread = weight row) turn the codes into fp16 weights c s (one LOP3 per pair of codes gives
+//     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's shared-memory layout) and of its packed codes
+//     and scales (4.6 KB), completing on the stage's mbarrier;
+//   - 8 decoder warps (thread = weight row) turn the codes into fp16 weights c s (one LOP3 per pair of codes gives
 //     fp16 1024 + c, one fma with s and -1024 s gives c s, exact for ternary codes) in the K-major layout with the
 //     128-byte swizzle;
-//   - an MMA warp issues 4 tcgen05.mma.kind::f16 (128 x 256 x 16) per chunk and commits them to the stage's mbarrier,
+//   - an MMA warp issues 8 tcgen05.mma.kind::f16 (128 x 256 x 16) per chunk and commits them to the stage's mbarrier,
 //     which frees the stage;
-//   - 4 epilogue warps read the accumulator (tcgen05.ld) and write y.
+//   - 8 epilogue warps read the accumulators (tcgen05.ld) and write y.
 // The bias term sum_g b_g sum_{k in g} x_k rides as extra chunks: A = G b (prepared tiles), B = the group sums of the
 // token times 2^-log2(G) (prepared with the activations). Activations are fp32 split as x 2^E = hi + lo (fp16 each,
 // E per token from its row maximum), so every product is exact and sums are fp32: y = (D_hi + D_lo) 2^-E.
@@ -28,15 +29,17 @@
 
 namespace bcu {
 
-constexpr int GM_ROWS = 128, GM_TOK = 128, GM_KC = 64;  // tile rows, tile tokens, inputs per chunk
-constexpr int GM_STAGES = 4;
-constexpr int GM_A_BYTES = GM_ROWS * GM_KC * 2;           // 16 KB decoded weights
+// A tile is 256 weight rows (two halves of 128, one MMA each) x 128 tokens; a chunk is 64 inputs.
+constexpr int GM_ROWS = 128, GM_TOK = 128, GM_KC = 64;  // rows per half, tile tokens, inputs per chunk
+constexpr int GM_STAGES = 3;
+constexpr int GM_A_BYTES = GM_ROWS * GM_KC * 2;           // 16 KB decoded weights per half
 constexpr int GM_B_BYTES = 2 * GM_TOK * GM_KC * 2;        // 32 KB activations (hi and lo)
-constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // codes [128][4 u32] + scales [128] fp16
-constexpr int GM_STAGE = 52224;                           // A | B | W (51456 B), 1024-aligned
-static_assert(GM_A_BYTES + GM_B_BYTES + GM_W_BYTES <= GM_STAGE, "a stage's buffers overlap the next stage");
+constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // per half: codes [128][4 u32] + scales [128] fp16
+constexpr int GM_B_OFF = 2 * GM_A_BYTES, GM_W_OFF = GM_B_OFF + GM_B_BYTES;
+constexpr int GM_STAGE = 70656;                           // A0 | A1 | B | W0 | W1 (70144 B), 1024-aligned
+static_assert(GM_W_OFF + 2 * GM_W_BYTES <= GM_STAGE, "a stage's buffers overlap the next stage");
 constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 2048;      // + barriers, TMEM address; + 1024 to align the base
-constexpr uint32_t GM_TMEM_COLS = 256;
+constexpr uint32_t GM_TMEM_COLS = 256;                    // one accumulator (128 lanes x 256 columns) per half
 // kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B f16 (0), both K-major, N = 256 (bits 17-22 =
 // N / 8), M = 128 (bits 24-28 = M / 16)
 constexpr uint32_t GM_IDESC = (1u << 4) | ((256u / 8) << 17) | ((128u / 16) << 24);
@@ -87,44 +90,47 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile, uint32_t k
 }
 
 // ----------------------------------------------------------------------------------------------- weights
-// Main chunks: per (row tile rt, chunk c) [128 rows][4 u32 codes of inputs 64 c .. 64 c + 63, MLX order] then [128]
-// fp16 scales of the chunk's group. One thread per (rt, c, row).
+// Row tiles of 256 rows; O is padded to whole tiles with zero weights.
+__host__ __device__ inline int gemm_row_tiles(int O) { return (O + 2 * GM_ROWS - 1) / (2 * GM_ROWS); }
+
+// Main chunks: per (row tile rt, chunk c, half h) [128 rows][4 u32 codes of inputs 64 c .. 64 c + 63, MLX order] then
+// [128] fp16 scales of the chunk's group; the two halves of a (rt, c) are adjacent. One thread per (rt, c, h, row).
 __global__ void gemm_pack_w_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s, int O, int K, int G,
                                    uint8_t* __restrict__ out) {
     const int nmain = K / GM_KC;
-    const size_t n = (size_t)(O / GM_ROWS) * nmain * GM_ROWS;
+    const size_t n = (size_t)gemm_row_tiles(O) * nmain * 2 * GM_ROWS;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const int r = i % GM_ROWS, c = (i / GM_ROWS) % nmain, rt = i / ((size_t)GM_ROWS * nmain);
-    const size_t row = (size_t)rt * GM_ROWS + r;
-    uint8_t* base = out + ((size_t)rt * nmain + c) * GM_W_BYTES;
-    const uint4 v = *(const uint4*)(w + row * (K / 16) + 4 * c);
-    ((uint4*)base)[r] = v;
-    ((uint16_t*)(base + GM_ROWS * 16))[r] = s[row * (K / G) + (GM_KC * c) / G];
+    const int r = i % GM_ROWS, h = (i / GM_ROWS) % 2, c = (i / (2 * GM_ROWS)) % nmain;
+    const size_t rt = i / ((size_t)2 * GM_ROWS * nmain), row = rt * 2 * GM_ROWS + h * GM_ROWS + r;
+    uint8_t* base = out + (((size_t)rt * nmain + c) * 2 + h) * GM_W_BYTES;
+    const bool in = row < (size_t)O;
+    ((uint4*)base)[r] = in ? *(const uint4*)(w + row * (K / 16) + 4 * c) : make_uint4(0, 0, 0, 0);
+    ((uint16_t*)(base + GM_ROWS * 16))[r] = in ? s[row * (K / G) + (GM_KC * c) / G] : (uint16_t)0;
 }
 
-// Bias chunks: per (rt, bias chunk cb) the A tile (128 rows of 64 fp16, 128-byte swizzle) of
-// G b[row][g], g = 64 cb + k (zero past K / G); b = -s for the implicit bias of the reference pack. One thread per
-// (rt, cb, row, k-chunk).
+// Bias chunks: per (rt, bias chunk cb, half h) the A tile (128 rows of 64 fp16, 128-byte swizzle) of
+// G b[row][g], g = 64 cb + k (zero past K / G or O); b = -s for the implicit bias of the reference pack; the two
+// halves adjacent. One thread per (rt, cb, h, row, k-chunk).
 __global__ void gemm_pack_bias_kernel(const uint16_t* __restrict__ s, const uint16_t* __restrict__ b, int O, int K,
                                       int G, int nbias, uint8_t* __restrict__ out) {
-    const size_t n = (size_t)(O / GM_ROWS) * nbias * GM_ROWS * 8;
+    const size_t n = (size_t)gemm_row_tiles(O) * nbias * 2 * GM_ROWS * 8;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const int kk = i % 8, r = (i / 8) % GM_ROWS, cb = (i / (8 * GM_ROWS)) % nbias, rt = i / ((size_t)8 * GM_ROWS * nbias);
-    const size_t row = (size_t)rt * GM_ROWS + r;
+    const int kk = i % 8, r = (i / 8) % GM_ROWS, h = (i / (8 * GM_ROWS)) % 2, cb = (i / (16 * GM_ROWS)) % nbias;
+    const size_t rt = i / ((size_t)16 * GM_ROWS * nbias), row = rt * 2 * GM_ROWS + h * GM_ROWS + r;
     const int ng = K / G;
     uint16_t v[8];
     for (int e = 0; e < 8; e++) {
         const int g = GM_KC * cb + 8 * kk + e;
         float x = 0.0f;
-        if (g < ng) {
+        if (g < ng && row < (size_t)O) {
             const float bb = b ? __half2float(__ushort_as_half(b[row * ng + g])) : -__half2float(__ushort_as_half(s[row * ng + g]));
             x = bb * (float)G;
         }
         v[e] = __half_as_ushort(__float2half_rn(x));
     }
-    uint8_t* tile = out + ((size_t)rt * nbias + cb) * GM_A_BYTES;
+    uint8_t* tile = out + (((size_t)rt * nbias + cb) * 2 + h) * GM_A_BYTES;
     *(uint4*)(tile + sw128(r, kk)) = *(const uint4*)v;
 }
 
@@ -220,12 +226,12 @@ struct GemmParams {
     int M, O, nmain, nbias, n_rt, n_tiles;
 };
 
-// Warp roles (320 threads): warps 0-3 epilogue (tensor memory -> y; warp w reads lanes 32 w .. 32 w + 31), warps 4-7
-// decode (thread = weight row), warp 8 issues the bulk copies, warp 9 issues the MMAs. Stages: GM_STAGES buffers of
-// A | B | W; barriers load_full (copies landed), a_full (128 decoder arrivals), mma_done (the stage's MMAs finished:
-// the stage is free); accumulators: two 256-column buffers in tensor memory with acc_full (the tile's MMAs finished)
-// and acc_empty (128 epilogue arrivals), so the epilogue of one tile overlaps the MMAs of the next.
-constexpr int GM_THREADS = 320;
+// Warp roles (576 threads): warps 0-7 epilogue (tensor memory -> y; warp w reads half w / 4, lanes 32 (w % 4) ..
+// 32 (w % 4) + 31), warps 8-15 decode (thread = weight row of the tile), warp 16 issues the bulk copies, warp 17
+// issues the MMAs. Stages: GM_STAGES buffers of A0 | A1 | B | W; barriers load_full (copies landed), a_full (256
+// decoder arrivals), mma_done (the stage's MMAs finished: the stage is free); the two halves' accumulators fill the
+// 512 tensor-memory columns, with acc_full (the tile's MMAs finished) and acc_empty (256 epilogue arrivals).
+constexpr int GM_THREADS = 576;
 
 __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -236,8 +242,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
     uint64_t* a_full = load_full + GM_STAGES;
     uint64_t* mma_done = a_full + GM_STAGES;
     uint64_t* acc_full = mma_done + GM_STAGES;
-    uint64_t* acc_empty = acc_full + 2;
-    uint32_t* s_tmem = (uint32_t*)(acc_empty + 2);
+    uint64_t* acc_empty = acc_full + 1;
+    uint32_t* s_tmem = (uint32_t*)(acc_empty + 1);
     volatile int* s_abort = (volatile int*)(s_tmem + 1);
     const int nch = p.nmain + p.nbias;
     const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -245,13 +251,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
     if (tid == 0) {
         for (int i = 0; i < GM_STAGES; i++) {
             mbar_init(&load_full[i], 1);
-            mbar_init(&a_full[i], 128);
+            mbar_init(&a_full[i], 256);
             mbar_init(&mma_done[i], 1);
         }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 128);
-        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 256);
         *s_abort = 0;
         fence_proxy_async_smem();
     }
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
     // parity of the n-th completion (0-based) of a barrier used once per GM_STAGES chunks
     auto par = [](int q) { return (uint32_t)((q / GM_STAGES) & 1); };
 
-    if (warp == 8) {  // ------------------------------------------------------------------ bulk copies
+    if (warp == 16) {  // ----------------------------------------------------------------- bulk copies
         if (lane == 0) {
             for (int q = 0; q < total && !*s_abort; q++) {
                 const int s = q % GM_STAGES, c = q % nch, j = q / nch;
@@ -283,21 +287,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
                 uint8_t* st = stage_of(q);
                 const uint8_t* bsrc = p.bop + ((size_t)tt * nch + c) * GM_B_BYTES;
                 if (c < p.nmain) {
-                    mbar_expect_tx(&load_full[s], GM_B_BYTES + GM_W_BYTES);
-                    bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, &load_full[s]);
-                    bulk_g2s(st + GM_A_BYTES + GM_B_BYTES, p.wt + ((size_t)rt * p.nmain + c) * GM_W_BYTES, GM_W_BYTES,
+                    mbar_expect_tx(&load_full[s], GM_B_BYTES + 2 * GM_W_BYTES);
+                    bulk_g2s(st + GM_B_OFF, bsrc, GM_B_BYTES, &load_full[s]);
+                    bulk_g2s(st + GM_W_OFF, p.wt + ((size_t)rt * p.nmain + c) * 2 * GM_W_BYTES, 2 * GM_W_BYTES,
                              &load_full[s]);
                 } else {
-                    mbar_expect_tx(&load_full[s], GM_B_BYTES + GM_A_BYTES);
-                    bulk_g2s(st + GM_A_BYTES, bsrc, GM_B_BYTES, &load_full[s]);
-                    bulk_g2s(st, p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * GM_A_BYTES, GM_A_BYTES,
+                    mbar_expect_tx(&load_full[s], GM_B_BYTES + 2 * GM_A_BYTES);
+                    bulk_g2s(st + GM_B_OFF, bsrc, GM_B_BYTES, &load_full[s]);
+                    bulk_g2s(st, p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * 2 * GM_A_BYTES, 2 * GM_A_BYTES,
                              &load_full[s]);
                 }
             }
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {  // ------------------------------------------------- decode
-        const int r = tid - 128;  // weight row of the tile
+    } else if (warp >= 8 && warp < 16) {  // ----------------------------------------------- decode
+        const int r = tid - 256, h = r / GM_ROWS, rr = r % GM_ROWS;  // half and row of the tile
         for (int q = 0; q < total && !*s_abort; q++) {
             const int s = q % GM_STAGES, c = q % nch;
             uint8_t* st = stage_of(q);
@@ -308,30 +312,33 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
                     fail();
                     break;
                 }
-                const uint4 cw = ((const uint4*)(st + GM_A_BYTES + GM_B_BYTES))[r];
-                const uint16_t sc = ((const uint16_t*)(st + GM_A_BYTES + GM_B_BYTES + GM_ROWS * 16))[r];
+                const uint8_t* wh = st + GM_W_OFF + h * GM_W_BYTES;
+                const uint4 cw = ((const uint4*)wh)[rr];
+                const uint16_t sc = ((const uint16_t*)(wh + GM_ROWS * 16))[rr];
                 const uint32_t s2 = (uint32_t)sc * 0x10001u;
                 uint32_t n2;
                 asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(n2) : "r"(s2), "r"(0xE400E400u));  // -1024 s
                 const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+                uint8_t* ah = st + h * GM_A_BYTES;
 #pragma unroll
                 for (int wi = 0; wi < 4; wi++) {
                     uint32_t o[8];
 #pragma unroll
                     for (int i = 0; i < 8; i++)  // codes i, i + 8: fp16 (1024 + c) pair, then c s (exact for c <= 2)
                         o[i] = hfma2_u32(lop_and_or(words[wi] >> (2 * i), 0x00030003u, 0x64006400u), s2, n2);
-                    *(uint4*)(st + sw128(r, 2 * wi)) = make_uint4(o[0], o[1], o[2], o[3]);
-                    *(uint4*)(st + sw128(r, 2 * wi + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                    *(uint4*)(ah + sw128(rr, 2 * wi)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *(uint4*)(ah + sw128(rr, 2 * wi + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
                 }
                 fence_proxy_async_smem();
             }
             mbar_arrive(&a_full[s]);
         }
-    } else if (warp == 9) {  // ----------------------------------------------------------- MMA
+    } else if (warp == 17) {  // ---------------------------------------------------------- MMA
         if (lane == 0) {
             for (int q = 0; q < total && !*s_abort; q++) {
-                const int s = q % GM_STAGES, c = q % nch, j = q / nch, a = j & 1;
-                if (c == 0 && j >= 2 && !mbar_wait_bounded(&acc_empty[a], (uint32_t)(((j >> 1) - 1) & 1))) {
+                const int s = q % GM_STAGES, c = q % nch, j = q / nch;
+                // the accumulators are free once the epilogue of the previous tile has read them
+                if (c == 0 && j >= 1 && !mbar_wait_bounded(acc_empty, (uint32_t)((j - 1) & 1))) {
                     fail();
                     break;
                 }
@@ -341,47 +348,52 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
                 }
                 tc_fence_after();
                 uint8_t* st = stage_of(q);
-                const uint32_t d = tmem + a * GM_TMEM_COLS;
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++) {
-                    const uint64_t ad = umma_desc_sw128(st, 32 * ks);
-                    const uint64_t bd = umma_desc_sw128(st + GM_A_BYTES, 32 * ks);
-                    umma_f16(d, ad, bd, GM_IDESC, (c > 0 || ks > 0) ? 1u : 0u);
+                    const uint64_t bd = umma_desc_sw128(st + GM_B_OFF, 32 * ks);
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+                        umma_f16(tmem + h * GM_TMEM_COLS, umma_desc_sw128(st + h * GM_A_BYTES, 32 * ks), bd, GM_IDESC,
+                                 (c > 0 || ks > 0) ? 1u : 0u);
                 }
                 umma_commit(&mma_done[s]);
-                if (c == nch - 1) umma_commit(&acc_full[a]);
+                if (c == nch - 1) umma_commit(acc_full);
             }
         }
         __syncwarp();
-    } else {  // ------------------------------------------------------------------ epilogue (warps 0-3)
+    } else {  // ------------------------------------------------------------------ epilogue (warps 0-7)
+        const int h = warp >> 2, wq = warp & 3;
         for (int j = 0; j < my_tiles && !*s_abort; j++) {
-            const int a = j & 1, tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
-            if (!mbar_wait_bounded(&acc_full[a], (uint32_t)((j >> 1) & 1))) {
+            const int tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
+            if (!mbar_wait_bounded(acc_full, (uint32_t)(j & 1))) {
                 fail();
                 break;
             }
             tc_fence_after();
-            const int row = rt * GM_ROWS + warp * 32 + lane;
-            const uint32_t base = tmem + a * GM_TMEM_COLS + ((uint32_t)(warp * 32) << 16);
+            const int row = rt * 2 * GM_ROWS + h * GM_ROWS + wq * 32 + lane;
+            const uint32_t base = tmem + h * GM_TMEM_COLS + ((uint32_t)(wq * 32) << 16);
 #pragma unroll 1
             for (int cb = 0; cb < GM_TOK / 32; cb++) {
                 uint32_t hi[32], lo[32];
                 tmem_ld32(base + cb * 32, hi);
                 tmem_ld32(base + GM_TOK + cb * 32, lo);
                 tmem_wait_ld();
+                if (row < p.O) {
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int t = tt * GM_TOK + cb * 32 + i;
-                    if (t < p.M)
-                        p.y[(size_t)t * p.O + row] = (__uint_as_float(hi[i]) + __uint_as_float(lo[i])) * pow2f(-p.ex[t]);
+                    for (int i = 0; i < 32; i++) {
+                        const int t = tt * GM_TOK + cb * 32 + i;
+                        if (t < p.M)
+                            p.y[(size_t)t * p.O + row] =
+                                (__uint_as_float(hi[i]) + __uint_as_float(lo[i])) * pow2f(-p.ex[t]);
+                    }
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[a]);
+            mbar_arrive(acc_empty);
         }
     }
-    // drain: the MMA issuer waits (bounded) for its last commit, the loader for copies that nobody consumed
-    if (warp == 9 && lane == 0 && total > 0) mbar_wait_bounded(&mma_done[(total - 1) % GM_STAGES], par(total - 1), 1u << 20);
+    // drain: the MMA issuer waits (bounded) for its last commit
+    if (warp == 17 && lane == 0 && total > 0) mbar_wait_bounded(&mma_done[(total - 1) % GM_STAGES], par(total - 1), 1u << 20);
     __syncwarp();
     tc_fence_before();
     __syncthreads();
@@ -390,19 +402,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
 }
 
 // ----------------------------------------------------------------------------------------------- host
-size_t gemm_w_bytes(int O, int K) { return (size_t)(O / GM_ROWS) * (K / GM_KC) * GM_W_BYTES; }
+size_t gemm_w_bytes(int O, int K) { return (size_t)gemm_row_tiles(O) * (K / GM_KC) * 2 * GM_W_BYTES; }
 int gemm_bias_chunks(int K, int G) { return (K / G + GM_KC - 1) / GM_KC; }
-size_t gemm_bias_bytes(int O, int K, int G) { return (size_t)(O / GM_ROWS) * gemm_bias_chunks(K, G) * GM_A_BYTES; }
+size_t gemm_bias_bytes(int O, int K, int G) {
+    return (size_t)gemm_row_tiles(O) * gemm_bias_chunks(K, G) * 2 * GM_A_BYTES;
+}
 size_t gemm_act_bytes(int M, int K, int G) {
     return (size_t)((M + GM_TOK - 1) / GM_TOK) * (K / GM_KC + gemm_bias_chunks(K, G)) * GM_B_BYTES;
 }
 
 void gemm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int O, int K, int G, uint8_t* wt,
                uint8_t* abias, cudaStream_t st) {
-    const size_t n1 = (size_t)(O / GM_ROWS) * (K / GM_KC) * GM_ROWS;
+    const size_t n1 = (size_t)gemm_row_tiles(O) * (K / GM_KC) * 2 * GM_ROWS;
     gemm_pack_w_kernel<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(w, s, O, K, G, wt);
     const int nb = gemm_bias_chunks(K, G);
-    const size_t n2 = (size_t)(O / GM_ROWS) * nb * GM_ROWS * 8;
+    const size_t n2 = (size_t)gemm_row_tiles(O) * nb * 2 * GM_ROWS * 8;
     gemm_pack_bias_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(s, b, O, K, G, nb, abias);
 }
 
@@ -425,7 +439,7 @@ cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int 
     p.O = O;
     p.nmain = nmain;
     p.nbias = nbias;
-    p.n_rt = O / GM_ROWS;
+    p.n_rt = gemm_row_tiles(O);
     p.n_tiles = p.n_rt * ((M + GM_TOK - 1) / GM_TOK);
     static std::once_flag once;
     std::call_once(once, [] {
