@@ -5,8 +5,8 @@
 // Per CTA tile: 256 weight rows (two halves of 128) x 128 tokens, accumulated in tensor memory (TMEM, all 512 columns:
 // per half a 256-column accumulator with the tokens' fp16 hi parts in columns 0..127 and lo parts in 128..255, so
 // one tcgen05.mma of N = 256 multiplies both by the same weight tile, and the two halves' MMAs share the activation
-// tile, halving the activation bytes per flop). K runs in chunks of 64 inputs through a 3-stage shared-memory
-// pipeline with warp roles:
+// tile, halving the activation bytes per flop). K runs in chunks of 64 inputs through a shared-memory pipeline (4
+// activation/code stages, 2 decoded-weight buffers) with warp roles:
 //   - a loader warp issues 1-D bulk copies (the TMA engine, cp.async.bulk, no tensor map, no multicast) of the chunk's
 //     activation tile (32 KB, prepared by gemm_prep_kernel in the MMA's shared-memory layout) and of its packed codes
 //     and scales (4.6 KB), completing on the stage's mbarrier;
@@ -31,14 +31,17 @@ namespace bcu {
 
 // A tile is 256 weight rows (two halves of 128, one MMA each) x 128 tokens; a chunk is 64 inputs.
 constexpr int GM_ROWS = 128, GM_TOK = 128, GM_KC = 64;  // rows per half, tile tokens, inputs per chunk
-constexpr int GM_STAGES = 3;
+constexpr int GM_SB = 4;  // activation + code stages (the loader runs up to 3 chunks ahead of the MMAs)
+constexpr int GM_SA = 2;  // decoded-weight buffers (the decoders run 1 chunk ahead)
 constexpr int GM_A_BYTES = GM_ROWS * GM_KC * 2;           // 16 KB decoded weights per half
 constexpr int GM_B_BYTES = 2 * GM_TOK * GM_KC * 2;        // 32 KB activations (hi and lo)
 constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // per half: codes [128][4 u32] + scales [128] fp16
-constexpr int GM_B_OFF = 2 * GM_A_BYTES, GM_W_OFF = GM_B_OFF + GM_B_BYTES;
-constexpr int GM_STAGE = 70656;                           // A0 | A1 | B | W0 | W1 (70144 B), 1024-aligned
-static_assert(GM_W_OFF + 2 * GM_W_BYTES <= GM_STAGE, "a stage's buffers overlap the next stage");
-constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 2048;      // + barriers, TMEM address; + 1024 to align the base
+// shared memory: B[GM_SB] (32 KB each) | A[GM_SA] (two 16-KB halves each) | W[GM_SB] (two halves of codes + scales)
+// | barriers; tiles on 1024-byte boundaries
+constexpr int GM_A_OFF = GM_SB * GM_B_BYTES, GM_W_OFF = GM_A_OFF + GM_SA * 2 * GM_A_BYTES;
+constexpr int GM_BAR_OFF = GM_W_OFF + GM_SB * 2 * GM_W_BYTES;
+constexpr int GM_SMEM = GM_BAR_OFF + 2048;                // + barriers, TMEM address; + 1024 to align the base
+static_assert(GM_SMEM <= 227 * 1024, "shared memory of the prefill GEMM");
 constexpr uint32_t GM_TMEM_COLS = 256;                    // one accumulator (128 lanes x 256 columns) per half
 // kind::f16 instruction descriptor: D f32 (bits 4-5 = 1), A and B f16 (0), both K-major, N = 256 (bits 17-22 =
 // N / 8), M = 128 (bits 24-28 = M / 16)
@@ -228,8 +231,9 @@ struct GemmParams {
 
 // Warp roles (576 threads): warps 0-7 epilogue (tensor memory -> y; warp w reads half w / 4, lanes 32 (w % 4) ..
 // 32 (w % 4) + 31), warps 8-15 decode (thread = weight row of the tile), warp 16 issues the bulk copies, warp 17
-// issues the MMAs. Stages: GM_STAGES buffers of A0 | A1 | B | W; barriers load_full (copies landed), a_full (256
-// decoder arrivals), mma_done (the stage's MMAs finished: the stage is free); the two halves' accumulators fill the
+// issues the MMAs. Chunk q uses activation/code stage q % GM_SB and decoded-weight buffer q % GM_SA; barriers
+// load_full[GM_SB] (copies landed), a_full[GM_SA] (256 decoder arrivals), mma_done[GM_SB] (chunk q's MMAs finished,
+// which frees its stage and its weight buffer); the two halves' accumulators fill the
 // 512 tensor-memory columns, with acc_full (the tile's MMAs finished) and acc_empty (256 epilogue arrivals).
 constexpr int GM_THREADS = 576;
 
@@ -238,10 +242,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
     // swizzle atoms need 1024-byte aligned tiles: align the base (the launch adds 1024 bytes of slack)
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint64_t* load_full = (uint64_t*)(smem + GM_STAGES * GM_STAGE);
-    uint64_t* a_full = load_full + GM_STAGES;
-    uint64_t* mma_done = a_full + GM_STAGES;
-    uint64_t* acc_full = mma_done + GM_STAGES;
+    uint64_t* load_full = (uint64_t*)(smem + GM_BAR_OFF);
+    uint64_t* a_full = load_full + GM_SB;
+    uint64_t* mma_done = a_full + GM_SA;
+    uint64_t* acc_full = mma_done + GM_SB;
     uint64_t* acc_empty = acc_full + 1;
     uint32_t* s_tmem = (uint32_t*)(acc_empty + 1);
     volatile int* s_abort = (volatile int*)(s_tmem + 1);
@@ -249,11 +253,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
     const int my_tiles = p.n_tiles > (int)blockIdx.x ? (p.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int total = my_tiles * nch;
     if (tid == 0) {
-        for (int i = 0; i < GM_STAGES; i++) {
+        for (int i = 0; i < GM_SB; i++) {
             mbar_init(&load_full[i], 1);
-            mbar_init(&a_full[i], 256);
             mbar_init(&mma_done[i], 1);
         }
+        for (int i = 0; i < GM_SA; i++) mbar_init(&a_full[i], 256);
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, 256);
         *s_abort = 0;
@@ -271,30 +275,35 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
         atomicOr(p.err, ERR_MBAR_TIMEOUT);
         *s_abort = 1;
     };
-    auto stage_of = [&](int q) { return smem + (q % GM_STAGES) * GM_STAGE; };
-    // parity of the n-th completion (0-based) of a barrier used once per GM_STAGES chunks
-    auto par = [](int q) { return (uint32_t)((q / GM_STAGES) & 1); };
+    auto b_of = [&](int q) { return smem + (q % GM_SB) * GM_B_BYTES; };
+    auto a_of = [&](int q) { return smem + GM_A_OFF + (q % GM_SA) * 2 * GM_A_BYTES; };
+    auto w_of = [&](int q) { return smem + GM_W_OFF + (q % GM_SB) * 2 * GM_W_BYTES; };
+    // parity of chunk q's completion of a barrier used once per GM_SB (par) or GM_SA (para) chunks
+    auto par = [](int q) { return (uint32_t)((q / GM_SB) & 1); };
+    auto para = [](int q) { return (uint32_t)((q / GM_SA) & 1); };
 
     if (warp == 16) {  // ----------------------------------------------------------------- bulk copies
         if (lane == 0) {
             for (int q = 0; q < total && !*s_abort; q++) {
-                const int s = q % GM_STAGES, c = q % nch, j = q / nch;
+                const int s = q % GM_SB, c = q % nch, j = q / nch;
                 const int tile = blockIdx.x + j * gridDim.x, rt = tile % p.n_rt, tt = tile / p.n_rt;
-                if (q >= GM_STAGES && !mbar_wait_bounded(&mma_done[s], par(q - GM_STAGES))) {
+                // the stage is free once chunk q - GM_SB's MMAs are done; a bias chunk also writes weight buffer
+                // q % GM_SA, free once chunk q - GM_SA's MMAs are done
+                if ((q >= GM_SB && !mbar_wait_bounded(&mma_done[s], par(q - GM_SB))) ||
+                    (c >= p.nmain && q >= GM_SA &&
+                     !mbar_wait_bounded(&mma_done[(q - GM_SA) % GM_SB], par(q - GM_SA)))) {
                     fail();
                     break;
                 }
-                uint8_t* st = stage_of(q);
                 const uint8_t* bsrc = p.bop + ((size_t)tt * nch + c) * GM_B_BYTES;
                 if (c < p.nmain) {
                     mbar_expect_tx(&load_full[s], GM_B_BYTES + 2 * GM_W_BYTES);
-                    bulk_g2s(st + GM_B_OFF, bsrc, GM_B_BYTES, &load_full[s]);
-                    bulk_g2s(st + GM_W_OFF, p.wt + ((size_t)rt * p.nmain + c) * 2 * GM_W_BYTES, 2 * GM_W_BYTES,
-                             &load_full[s]);
+                    bulk_g2s(b_of(q), bsrc, GM_B_BYTES, &load_full[s]);
+                    bulk_g2s(w_of(q), p.wt + ((size_t)rt * p.nmain + c) * 2 * GM_W_BYTES, 2 * GM_W_BYTES, &load_full[s]);
                 } else {
                     mbar_expect_tx(&load_full[s], GM_B_BYTES + 2 * GM_A_BYTES);
-                    bulk_g2s(st + GM_B_OFF, bsrc, GM_B_BYTES, &load_full[s]);
-                    bulk_g2s(st, p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * 2 * GM_A_BYTES, 2 * GM_A_BYTES,
+                    bulk_g2s(b_of(q), bsrc, GM_B_BYTES, &load_full[s]);
+                    bulk_g2s(a_of(q), p.abias + ((size_t)rt * p.nbias + (c - p.nmain)) * 2 * GM_A_BYTES, 2 * GM_A_BYTES,
                              &load_full[s]);
                 }
             }
@@ -303,23 +312,26 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
     } else if (warp >= 8 && warp < 16) {  // ----------------------------------------------- decode
         const int r = tid - 256, h = r / GM_ROWS, rr = r % GM_ROWS;  // half and row of the tile
         for (int q = 0; q < total && !*s_abort; q++) {
-            const int s = q % GM_STAGES, c = q % nch;
-            uint8_t* st = stage_of(q);
+            const int s = q % GM_SB, c = q % nch;
+            // weight buffer q % GM_SA is free once chunk q - GM_SA's MMAs are done (waited for bias chunks too, whose
+            // buffer the loader fills: so no arrival on a_full can run ahead into the phase of an earlier chunk)
+            if (q >= GM_SA && !mbar_wait_bounded(&mma_done[(q - GM_SA) % GM_SB], par(q - GM_SA))) {
+                fail();
+                break;
+            }
             if (c < p.nmain) {
-                // A[s] is free once the MMAs of chunk q - GM_STAGES are done; the codes of chunk q have landed
-                if ((q >= GM_STAGES && !mbar_wait_bounded(&mma_done[s], par(q - GM_STAGES))) ||
-                    !mbar_wait_bounded(&load_full[s], par(q))) {
+                if (!mbar_wait_bounded(&load_full[s], par(q))) {  // the codes of chunk q have landed
                     fail();
                     break;
                 }
-                const uint8_t* wh = st + GM_W_OFF + h * GM_W_BYTES;
+                const uint8_t* wh = w_of(q) + h * GM_W_BYTES;
                 const uint4 cw = ((const uint4*)wh)[rr];
                 const uint16_t sc = ((const uint16_t*)(wh + GM_ROWS * 16))[rr];
                 const uint32_t s2 = (uint32_t)sc * 0x10001u;
                 uint32_t n2;
                 asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(n2) : "r"(s2), "r"(0xE400E400u));  // -1024 s
                 const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-                uint8_t* ah = st + h * GM_A_BYTES;
+                uint8_t* ah = a_of(q) + h * GM_A_BYTES;
 #pragma unroll
                 for (int wi = 0; wi < 4; wi++) {
                     uint32_t o[8];
@@ -331,29 +343,30 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
                 }
                 fence_proxy_async_smem();
             }
-            mbar_arrive(&a_full[s]);
+            mbar_arrive(&a_full[q % GM_SA]);
         }
     } else if (warp == 17) {  // ---------------------------------------------------------- MMA
         if (lane == 0) {
             for (int q = 0; q < total && !*s_abort; q++) {
-                const int s = q % GM_STAGES, c = q % nch, j = q / nch;
+                const int s = q % GM_SB, c = q % nch, j = q / nch;
                 // the accumulators are free once the epilogue of the previous tile has read them
                 if (c == 0 && j >= 1 && !mbar_wait_bounded(acc_empty, (uint32_t)((j - 1) & 1))) {
                     fail();
                     break;
                 }
-                if (!mbar_wait_bounded(&load_full[s], par(q)) || !mbar_wait_bounded(&a_full[s], par(q))) {
+                if (!mbar_wait_bounded(&load_full[s], par(q)) || !mbar_wait_bounded(&a_full[q % GM_SA], para(q))) {
                     fail();
                     break;
                 }
                 tc_fence_after();
-                uint8_t* st = stage_of(q);
+                const uint8_t* bt = b_of(q);
+                const uint8_t* at = a_of(q);
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++) {
-                    const uint64_t bd = umma_desc_sw128(st + GM_B_OFF, 32 * ks);
+                    const uint64_t bd = umma_desc_sw128(bt, 32 * ks);
 #pragma unroll
                     for (int h = 0; h < 2; h++)
-                        umma_f16(tmem + h * GM_TMEM_COLS, umma_desc_sw128(st + h * GM_A_BYTES, 32 * ks), bd, GM_IDESC,
+                        umma_f16(tmem + h * GM_TMEM_COLS, umma_desc_sw128(at + h * GM_A_BYTES, 32 * ks), bd, GM_IDESC,
                                  (c > 0 || ks > 0) ? 1u : 0u);
                 }
                 umma_commit(&mma_done[s]);
@@ -393,7 +406,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) ternary_gemm_kernel(GemmParams 
         }
     }
     // drain: the MMA issuer waits (bounded) for its last commit
-    if (warp == 17 && lane == 0 && total > 0) mbar_wait_bounded(&mma_done[(total - 1) % GM_STAGES], par(total - 1), 1u << 20);
+    if (warp == 17 && lane == 0 && total > 0) mbar_wait_bounded(&mma_done[(total - 1) % GM_SB], par(total - 1), 1u << 20);
     __syncwarp();
     tc_fence_before();
     __syncthreads();
