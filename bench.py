@@ -197,6 +197,7 @@ def run_config5(args, ws, rank, local):
     from bonsai_b200 import _lib, synth
 
     L = _lib.lib()
+    M = args.rows
     rng = np.random.default_rng(args.seed)
     lins, host_w = {}, {}
     for name, (O, K) in GEMM_SHAPES.items():
@@ -211,8 +212,8 @@ def run_config5(args, ws, rank, local):
         host_w[name] = (W, S, B)
     kmax = max(K for _, K in GEMM_SHAPES.values())
     omax = max(O for O, _ in GEMM_SHAPES.values())
-    x = torch.randn(PREFILL_M * kmax, device="cuda", dtype=torch.float32)
-    y = torch.empty(PREFILL_M * omax, device="cuda", dtype=torch.float32)
+    x = torch.randn(M * kmax, device="cuda", dtype=torch.float32)
+    y = torch.empty(M * omax, device="cuda", dtype=torch.float32)
     stream = torch.cuda.current_stream()
     sp = ctypes.c_void_p(stream.cuda_stream)
     xp, yp = ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr())
@@ -220,7 +221,7 @@ def run_config5(args, ws, rank, local):
 
     def step():
         for name in launches:
-            assert L.bcu_linear_gemm(lins[name], xp, PREFILL_M, yp, sp) == _lib.OK
+            assert L.bcu_linear_gemm(lins[name], xp, M, yp, sp) == _lib.OK
 
     for _ in range(args.warmup):
         step()
@@ -231,12 +232,12 @@ def run_config5(args, ws, rank, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(3):
-            assert L.bcu_linear_gemm(lins[name], xp, PREFILL_M, yp, sp) == _lib.OK
+            assert L.bcu_linear_gemm(lins[name], xp, M, yp, sp) == _lib.OK
         e1.record(stream)
         torch.cuda.synchronize()
         O, K = GEMM_SHAPES[name]
         ms = e0.elapsed_time(e1) / 3
-        per[name] = {"ms": ms, "tflops": 2.0 * PREFILL_M * O * K / (ms / 1000) / 1e12}
+        per[name] = {"ms": ms, "tflops": 2.0 * M * O * K / (ms / 1000) / 1e12}
     clocks = Clocks(local)
     if dist:
         dist.barrier()
@@ -252,15 +253,15 @@ def run_config5(args, ws, rank, local):
     ms = max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
     for name in GEMM_SHAPES:
         assert L.bcu_linear_sync(lins[name], sp) == _lib.OK, "a GEMM gave up a bounded wait"
-    flops_step = sum(2.0 * PREFILL_M * GEMM_SHAPES[n][0] * GEMM_SHAPES[n][1] for n in launches)
-    value = whole_job_rate(ws, PREFILL_M * args.steps, ms / 1000)
+    flops_step = sum(2.0 * M * GEMM_SHAPES[n][0] * GEMM_SHAPES[n][1] for n in launches)
+    value = whole_job_rate(ws, M * args.steps, ms / 1000)
     achieved = flops_step / (ms / args.steps / 1000) / 1e12
     pk = peaks() or {}
     peak = pk.get("bf16_tflops_sustained", 1400.0)
 
     # e2e: the same step with the first GEMM's input copied from pinned host memory and the last output read back
-    xh = torch.empty(PREFILL_M * 2048, dtype=torch.float32, pin_memory=True).normal_()
-    yh = torch.empty(PREFILL_M * 2048, dtype=torch.float32, pin_memory=True)
+    xh = torch.empty(M * 2048, dtype=torch.float32, pin_memory=True).normal_()
+    yh = torch.empty(M * 2048, dtype=torch.float32, pin_memory=True)
     e2e_steps = max(1, min(args.steps, 2))
     torch.cuda.synchronize()
     w0 = time.perf_counter()
@@ -276,9 +277,9 @@ def run_config5(args, ws, rank, local):
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp32 activations (fp16 hi + lo) x fp16 weights, fp32 accumulate",
         "data": "synthetic (seeded ternary weights, N(0,1) activations)",
-        "config": {"workload": WORKLOAD_5, "rows_per_step": PREFILL_M, "gemms_per_step": len(launches),
+        "config": {"workload": WORKLOAD_5, "rows_per_step": M, "gemms_per_step": len(launches),
                    "parallelism": f"replicas x{ws}", "l2": "inputs larger than L2 (0.5-1.6 GB activations)"},
-        "e2e": {"value": whole_job_rate(ws, PREFILL_M * e2e_steps, e2e_s), "unit": "tok/s",
+        "e2e": {"value": whole_job_rate(ws, M * e2e_steps, e2e_s), "unit": "tok/s",
                 "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4, "steps": e2e_steps,
                 "path": "bcu_linear_gemm (C ABI) x 96, input H2D from pinned host, last output D2H"},
         "gpu_launches": ws * args.steps * len(launches) * 2,
@@ -343,6 +344,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="profiling run for ncu: prefill --profile-prefix tokens, then this many 9-row verify passes")
     ap.add_argument("--profile-prefix", type=int, default=256)
+    ap.add_argument("--rows", type=int, default=PREFILL_M,
+                    help="config5 only: prefill rows per step (65536 = 32 sessions x 2048; smaller for profiling)")
     ap.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
                     help="config3 (default, the headline), config4 (4B shape + LoRA) or config5 (prefill linears)")
     args = ap.parse_args()
