@@ -1,6 +1,6 @@
 // operand.cuh — the activation operand of the ternary GEMV in tensor-core fragment order, and the device code that
-// writes it. Used by the GEMV itself (operand built in its own shared memory) and by the kernels that produce the
-// next GEMV's operand in their epilogue (GEMV: RMSNorm / SwiGLU inputs; GDN: gated norm; attention: sigmoid gate).
+// writes it (used by the GEMV's operand builders in ternary.cu: RMSNorm, gated RMSNorm, SwiGLU and sigmoid-gate
+// inputs, then signs, Walsh-Hadamard transform, exponent, fp16 hi/lo split and group sums).
 //
 // Layout: one region per (block b of HB consecutive inputs, column tile nt of 4 tokens). A region is sb/16 main k16
 // steps of B fragments (256 B each: 4 tokens x fp16 hi, lo columns; word (c * 4 + t4) * 2 + which of a step holds

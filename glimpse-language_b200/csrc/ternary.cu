@@ -12,11 +12,11 @@
 //
 // CTA = 128 rows x kslice codes (8 warps = 2 row groups of 64 x 4 k-quarters). Before waiting on the previous kernel
 // (programmatic dependent launch) one thread streams the CTA's codes and scale/bias tiles into shared memory with
-// cp.async.bulk. After the wait the activation operand (operand.cuh) comes either from the previous kernel, which
-// built it once for the whole GEMV (one more bulk copy), or is built here from the source rows (embedding rows,
-// standalone inputs). Split-K partials are summed in a fixed order by the last CTA of each row block, which applies
-// the residual add and the sums of squares the next norm needs and, when asked, contributes to the next GEMV's
-// operand: the CTA that completes a Hadamard block of the next GEMV's input builds the block's regions.
+// cp.async.bulk. After the wait the activation operand (operand.cuh) is built once for the whole GEMV by its CTAs
+// together (grid_build: one (token, Hadamard block) per warp into a global buffer, a bounded grid-wide wait, then one
+// bulk copy per block into each CTA), or, when the grid cannot be resident at once (and for standalone inputs), by
+// each CTA for its own K-slice (build_operand). Split-K partials are summed in a fixed order by the last CTA of each
+// row block, which applies the residual add, the LoRA up projection and the sums of squares the next norm needs.
 #include <cstdio>
 #include <mutex>
 #include <set>
@@ -118,12 +118,10 @@ void repack_ternary(const uint32_t* w_mlx, const uint16_t* s, const uint16_t* b,
     repack_sb_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(s, b, O, K, group, sb);
 }
 
-// Split-K plan: the fewest K-slices (512, 1024 or 2048 codes) that give at least one CTA per SM.
-// K-slice plan: the longest slice (fewest splits) that still puts CTAs on at least ~45% of the SMs. Fewer splits save
-// the split-K reduction (a dependent global round trip) and the duplicated operand build; one CTA per SM gets the
-// SM's whole issue rate for the decode, so ~70 CTAs of 2048-code slices finish as fast as ~140 of 1024.
-// min_kslice: slices never split a Hadamard block of an operand built by the previous kernel (its regions cover
-// whole blocks).
+// K-slice plan: the longest slice (512, 1024 or 2048 codes; fewest splits) that still puts CTAs on at least ~45% of
+// the SMs. Fewer splits save the split-K reduction (a dependent global round trip) and the duplicated operand build;
+// one CTA per SM gets the SM's whole issue rate for the decode, so ~70 CTAs of 2048-code slices finish as fast as
+// ~140 of 1024. min_kslice: slices never split a Hadamard block (the operand's regions cover whole blocks).
 void plan_ternary(TernaryMat& m, int num_sms, int min_kslice) {
     int rb = m.O / 128;
     int best = 0;
