@@ -167,6 +167,11 @@ class Model:
         """Test hook: every GEMV builds its operand per CTA instead of once across its grid."""
         self._ck(self.L.bcu_set_local_build(self.h, 1 if local else 0))
 
+    def debug_wait_timeout(self):
+        """Test hook: a device wait that runs out; returns (status, message)."""
+        st = self.L.bcu_debug_wait_timeout(self.h)
+        return st, (self.L.bcu_last_error(self.h).decode() if st != _lib.OK else "")
+
     def lora_info(self):
         """Text::lora_info (model.rs:399-402): (adapted linears, rank), or None."""
         n, r = ctypes.c_int32(), ctypes.c_int32()

@@ -393,6 +393,11 @@ bcu_status get_graph(bcu_model* m, int T, cudaGraphExec_t* out) {
     return BCU_OK;
 }
 
+// A bounded wait that nothing satisfies (bcu_debug_wait_timeout): flag stays 0.
+__global__ void wait_timeout_kernel(Ctl* ctl, const unsigned* flag, uint32_t limit) {
+    if (!spin_until_geq(flag, 1u, limit)) atomicOr(&ctl->err, ERR_SPIN_TIMEOUT);
+}
+
 bcu_status read_ctl(bcu_model* m) {
     CK(cudaMemcpyAsync(m->h_out, m->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost, m->st));
     TRY(wait_stream(m, WAIT_S));
@@ -1026,6 +1031,18 @@ bcu_status bcu_time_pass(bcu_model* m, int32_t t, int32_t iters, float* ms_per_p
     bcu_state_free(snap);
     *ms_per_pass = total / iters;
     return BCU_OK;
+}
+
+// Test hook (not in the ABI header): one thread waits, with the bounded spin the GEMV's grid-wide build uses (a short
+// limit here), on a zeroed word that nothing writes; the wait runs out, the kernel records ERR_SPIN_TIMEOUT in the
+// control block and returns, and the host reads it as BCU_ERR_TIMEOUT, with the context still usable.
+bcu_status bcu_debug_wait_timeout(bcu_model* m) {
+    if (!m || !m->finalized) return BCU_ERR_ARG;
+    CK(cudaSetDevice(m->device));
+    TRY(wait_stream(m, WAIT_S));
+    wait_timeout_kernel<<<1, 1, 0, m->st>>>(m->ctl, m->op_counters + 256, 1u << 14);
+    CK(cudaGetLastError());
+    return read_ctl(m);
 }
 
 // Test hook (not in the ABI header): local != 0 makes every GEMV build its operand per CTA (build_operand) instead of
