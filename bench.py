@@ -36,7 +36,7 @@ import numpy as np  # noqa: E402
 METRIC = "decode tok/s/GPU with speculation (Bonsai-2B shape); verify-pass HBM GB/s"
 # DRAM bytes (read + write) of one 9-row verify pass of this workload's model, summed over its 121 kernels from one
 # ncu launch-list capture (profiles/verify_pass_2b_launches.md; context ~70, so ~35 MB less K/V than the timed passes)
-VERIFY_PASS_DRAM_BYTES = 1654.0e6
+VERIFY_PASS_DRAM_BYTES = 1648.3e6
 PREFIX, USER, GEN, K_DRAFT = 1024, 256, 300, 8
 WORKLOAD = ("config3: Bonsai-2B shape random-init, 1024-token cached prefix + 256 Zipf(1.1) user tokens, "
             "300+ generated tokens, k=8 planted drafts (100% accept)")
