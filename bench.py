@@ -312,6 +312,138 @@ def run_config5(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+# --workload config1 / config2: the graded single-op configs, timed over ROT_COPIES copies of the weights / state
+# (more than L2 holds together) so every call streams from HBM; one call per step, back to back on one stream.
+ROT_COPIES = 64
+
+
+def run_small_op(args, local):
+    import ctypes
+
+    import torch
+
+    torch.cuda.set_device(local)
+    from bonsai_b200 import _lib, synth
+
+    L = _lib.lib()
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    if args.workload == "config1":
+        O, K, T = 6144, 2048, 9
+        hs = []
+        for r in range(ROT_COPIES):
+            W = synth.fill(3, args.seed, 3 * r, 0, 0, (O, K // 16), np.uint32)
+            S = synth.fill(4, args.seed, 3 * r + 1, 0.01, 0.05, (O, K // 64), np.uint16)
+            B = synth.fill(6, args.seed, 3 * r + 1, 0.01, 0.05, (O, K // 64), np.uint16)
+            h = ctypes.c_void_p()
+            assert L.bcu_linear_prepare(W.ctypes.data_as(ctypes.c_void_p), S.ctypes.data_as(ctypes.c_void_p),
+                                        B.ctypes.data_as(ctypes.c_void_p), O, K, 64, local, ctypes.byref(h)) == 0
+            hs.append(h)
+        x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+        y = torch.empty(T, O, device="cuda")
+        per_call = O * K / 4 + O * (K // 64) * 4 + T * K * 2 + T * O * 4  # codes, scale+bias, X bf16, Y fp32
+
+        def call(i):
+            assert L.bcu_linear_rotate_forward(hs[i % ROT_COPIES], vp(x), T, 2048, None, vp(y), sp) == 0
+
+        desc = ("config1: one ternary linear 9 x 2048 -> 6144 (g64 + bias, bf16 X, normalised 2048-point rotation), "
+                f"{ROT_COPIES} weight copies in rotation")
+        metric, unit = "ternary linear calls/s (config 1)", "calls/s"
+        host_in, host_out = T * K * 2, T * O * 4
+        cleanup = lambda: [L.bcu_linear_free(h) for h in hs]  # noqa: E731
+    else:
+        T, NK, NV = 9, 16, 32
+        g = torch.Generator(device="cuda").manual_seed(args.seed)
+
+        def l2n(t):
+            return t / t.norm(dim=-1, keepdim=True)
+
+        q = l2n(torch.randn(T, NK, 128, device="cuda", generator=g))
+        k = l2n(torch.randn(T, NK, 128, device="cuda", generator=g))
+        v = torch.randn(T, NV, 128, device="cuda", generator=g)
+        a = torch.randn(T, NV, device="cuda", generator=g)
+        b = torch.randn(T, NV, device="cuda", generator=g)
+        alog = torch.zeros(NV, device="cuda")
+        dtb = torch.zeros(NV, device="cuda")
+        states = torch.randn(ROT_COPIES, NV, 128, 128, device="cuda", generator=g) * 0.02
+        y = torch.empty(T, NV, 128, device="cuda")
+        ns = np.random.default_rng(args.seed).integers(0, T, ROT_COPIES)  # accept lengths U{0..8}
+        per_call = NV * 128 * 128 * 4 * 2 + (2 * NK + 2 * NV) * T * 128 * 4 + 2 * T * NV * 4
+
+        def call(i):
+            st = states[i % ROT_COPIES]
+            assert L.bcu_gdn_verify(vp(q), vp(k), vp(v), vp(a), vp(b), vp(alog), vp(dtb), vp(st), vp(y), T, NK, NV,
+                                    int(ns[i % ROT_COPIES]), sp) == 0
+
+        desc = ("config2: one GatedDeltaNet verify step, T = 9, 16 key / 32 value heads, accept length U{0..8} "
+                f"and rollback, {ROT_COPIES} states in rotation")
+        metric, unit = "GDN verify steps/s (config 2)", "calls/s"
+        host_in, host_out = (2 * NK + NV) * T * 128 * 4 + 2 * T * NV * 4, T * NV * 128 * 4
+        cleanup = lambda: None  # noqa: E731
+    calls = ROT_COPIES * 4
+    for i in range(ROT_COPIES):  # first calls outside the capture (one-time kernel attributes)
+        call(i)
+    torch.cuda.synchronize()
+    # one step = the calls replayed from one CUDA graph, so the host's per-call overhead is not timed
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        sp = ctypes.c_void_p(cap.cuda_stream)
+        graph.capture_begin()
+        for i in range(calls):
+            call(i)
+        graph.capture_end()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for step in range(args.steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ck = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    n = args.steps * calls
+    us_call = ms * 1000 / n
+    pk = peaks() or {}
+    hbm = pk.get("hbm_gbs", 6650.0)
+    achieved = per_call / (us_call * 1e-6) / 1e9
+    # e2e: each call's input copied from pinned host memory and its output read back
+    hin = torch.empty(host_in // 4, dtype=torch.float32, pin_memory=True)
+    hout = torch.empty(host_out // 4, dtype=torch.float32, pin_memory=True)
+    dev_in = torch.empty(host_in // 4, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    n2 = min(n, 512)
+    for i in range(n2):
+        dev_in.copy_(hin, non_blocking=True)
+        call(i)
+        hout.copy_(y.view(-1)[: hout.numel()], non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - w0
+    line = {
+        "metric": metric, "value": n / (ms / 1000), "unit": unit, "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+        "config": {"workload": desc, "calls_per_step": calls, "l2": f"{ROT_COPIES} copies in rotation, larger than L2"},
+        "e2e": {"value": n2 / e2e_s, "unit": unit, "h2d_bytes_per_step": host_in * calls,
+                "d2h_bytes_per_step": host_out * calls, "path": "C ABI call per step with its input H2D and output D2H"},
+        "gpu_launches": n,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None, "bytes_per_launch": per_call, "us_per_launch": us_call,
+                     "peak_source": "MEASURED_PEAKS.json" if pk else "fallback"},
+        "clocks": ck,
+    }
+    print(json.dumps(line), flush=True)
+    cleanup()
+
+
 def run_profile(args, local):
     """A short run for kernel profiling: model load, a --profile-prefix token prefill (16-row passes), then
     --profile verify passes of 9 rows with planted drafts. Prints the kernel launches of one 9-row pass."""
@@ -346,8 +478,9 @@ def main():
     ap.add_argument("--profile-prefix", type=int, default=256)
     ap.add_argument("--rows", type=int, default=PREFILL_M,
                     help="config5 only: prefill rows per step (65536 = 32 sessions x 2048; smaller for profiling)")
-    ap.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
-                    help="config3 (default, the headline), config4 (4B shape + LoRA) or config5 (prefill linears)")
+    ap.add_argument("--workload", default="config3", choices=["config1", "config2", "config3", "config4", "config5"],
+                    help="config3 (default, the headline); config1 / config2 (single ops), config4 (4B shape + LoRA), "
+                         "config5 (prefill linears)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
 
@@ -359,6 +492,10 @@ def main():
         return
     if args.workload == "config5":
         run_config5(args, ws, rank, local)
+        return
+    if args.workload in ("config1", "config2"):
+        if rank == 0:
+            run_small_op(args, local)
         return
 
     import torch

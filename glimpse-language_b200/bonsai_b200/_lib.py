@@ -152,6 +152,7 @@ SIGNATURES = {
     "bcu_stream": (I32, [P, ctypes.POINTER(P)]),
     # host-logic exports (not in the ABI header: test hooks of the decode driver and the operand build)
     "bcu_set_local_build": (I32, [P, I32]),
+    "bcu_linear_set_local_build": (I32, [P, I32]),
     "bcu_debug_wait_timeout": (I32, [P]),
     "bcu_gemm_prep_debug": (I32, [P, P, I32, P, P]),
     "bcu_token_key": (U64, [P, U64]),

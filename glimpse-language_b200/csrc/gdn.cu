@@ -280,14 +280,24 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
 }
 
 // Graded config 2: T rows from explicit q/k/v/gate inputs, outputs for every row, and the state written back as it
-// was after the first n rows (the checkpoint taken in registers while the rows run).
+// was after the first n rows (the checkpoint taken in registers while the rows run). Rows are staged in shared
+// memory GV_CHUNK at a time, every load of a chunk in flight at once, so the sequential steps wait on no global load.
+constexpr int GV_CHUNK = 16;
+struct __align__(16) GvSmem {
+    float q[GV_CHUNK][128];
+    float k[GV_CHUNK][128];
+    float v[GV_CHUNK][16];
+    float g[GV_CHUNK], beta[GV_CHUNK];
+};
+
 __global__ void __launch_bounds__(128) gdn_verify_kernel(const float* q, const float* k, const float* v,
                                                          const float* a_in, const float* b_in, const float* a_log,
                                                          const float* dt_bias, float* state, float* y, int T, int NK,
                                                          int NV, int n) {
-    const int hd = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __shared__ GvSmem sm;
+    const int hd = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int hk = hd / (NV / NK);
-    const int dv0 = blockIdx.y * 16 + w * 4;
+    const int dvb = blockIdx.y * 16, dv0 = dvb + w * 4;
     float4 st[4], keep[4];
     float* S = state + ((size_t)hd * 128 + dv0) * 128 + lane * 4;
     const float ea = expf(a_log[hd]), dtb = dt_bias[hd];
@@ -295,23 +305,48 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(const float* q, const f
     pdl_wait();
 #pragma unroll
     for (int r = 0; r < 4; r++) keep[r] = st[r] = *(const float4*)(S + (size_t)r * 128);
-    float o[4], vv[4];
-    for (int t = 0; t < T; t++) {
-        float g, beta;
-        gates(a_in[(size_t)t * NV + hd], b_in[(size_t)t * NV + hd], ea, dtb, g, beta);
-        float4 qq = *(const float4*)(q + ((size_t)t * NK + hk) * 128 + lane * 4);
-        float4 kk = *(const float4*)(k + ((size_t)t * NK + hk) * 128 + lane * 4);
+    for (int t0 = 0; t0 < T; t0 += GV_CHUNK) {
+        const int nr = min(GV_CHUNK, T - t0);
+        float lq[GV_CHUNK], lk[GV_CHUNK], lv[GV_CHUNK];
 #pragma unroll
-        for (int r = 0; r < 4; r++) vv[r] = v[((size_t)t * NV + hd) * 128 + dv0 + r];
-        gdn_step4(st, qq, kk, vv, g, beta, o);
-        if (lane < 4) {
-            float ov = lane == 0 ? o[0] : (lane == 1 ? o[1] : (lane == 2 ? o[2] : o[3]));
-            y[((size_t)t * NV + hd) * 128 + dv0 + lane] = ov;
+        for (int r = 0; r < GV_CHUNK; r++)
+            if (r < nr) {
+                const size_t t = (size_t)(t0 + r);
+                lq[r] = q[(t * NK + hk) * 128 + tid];
+                lk[r] = k[(t * NK + hk) * 128 + tid];
+                lv[r] = tid < 16 ? v[(t * NV + hd) * 128 + dvb + tid] : 0.0f;
+            }
+        float ga = 0.0f, gb = 0.0f;
+        if (tid < nr) {
+            ga = a_in[(size_t)(t0 + tid) * NV + hd];
+            gb = b_in[(size_t)(t0 + tid) * NV + hd];
         }
-        if (t + 1 == n) {
 #pragma unroll
-            for (int r = 0; r < 4; r++) keep[r] = st[r];
+        for (int r = 0; r < GV_CHUNK; r++)
+            if (r < nr) {
+                sm.q[r][tid] = lq[r];
+                sm.k[r][tid] = lk[r];
+                if (tid < 16) sm.v[r][tid] = lv[r];
+            }
+        if (tid < nr) gates(ga, gb, ea, dtb, sm.g[tid], sm.beta[tid]);
+        __syncthreads();
+        for (int r = 0; r < nr; r++) {
+            const float4 qq = *(const float4*)&sm.q[r][lane * 4];
+            const float4 kk = *(const float4*)&sm.k[r][lane * 4];
+            const float4 v4 = *(const float4*)&sm.v[r][w * 4];
+            const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+            float o[4];
+            gdn_step4(st, qq, kk, vv, sm.g[r], sm.beta[r], o);
+            if (lane < 4) {
+                const float ov = lane == 0 ? o[0] : (lane == 1 ? o[1] : (lane == 2 ? o[2] : o[3]));
+                y[((size_t)(t0 + r) * NV + hd) * 128 + dv0 + lane] = ov;
+            }
+            if (t0 + r + 1 == n) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) keep[i] = st[i];
+            }
         }
+        __syncthreads();  // the next chunk overwrites the rows
     }
 #pragma unroll
     for (int r = 0; r < 4; r++) *(float4*)(S + (size_t)r * 128) = keep[r];

@@ -1,5 +1,6 @@
 // ops.cu — standalone hot ops of the C ABI on caller-owned device buffers: the rotate-then-ternary-linear of graded
 // config 1 and the GatedDeltaNet verify step with rollback of graded config 2.
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -7,6 +8,7 @@
 #include "../../include/bonsai_cuda.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "operand.cuh"
 
 using namespace bcu;
 
@@ -19,6 +21,10 @@ struct bcu_linear {
     float* partial = nullptr;
     unsigned* counters = nullptr;
     int* err = nullptr;
+    // the rotated operand when the GEMV's CTAs build it together (grid_build): room for the largest block size
+    uint8_t* opbuf = nullptr;
+    unsigned* op_counters = nullptr;
+    bool local_build = false;  // test hook: every CTA builds its own slice
     // prefill GEMM (gemm.cu): packed weights and bias tiles; activation tiles and exponents grown on demand
     uint8_t *gwt = nullptr, *gbias = nullptr, *gbop = nullptr;
     int* gex = nullptr;
@@ -67,7 +73,12 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
     plan_ternary(l->m, sms);
     ok = ok && cudaMalloc(&l->partial, (size_t)l->m.nsplit * VMAX * O * 4) == cudaSuccess &&
          cudaMalloc(&l->counters, (size_t)(O / 128) * 4) == cudaSuccess && cudaMalloc(&l->err, 4) == cudaSuccess &&
-         cudaMemset(l->counters, 0, (size_t)(O / 128) * 4) == cudaSuccess && cudaMemset(l->err, 0, 4) == cudaSuccess &&
+         cudaMemset(l->counters, 0, (size_t)(O / 128) * 4) == cudaSuccess && cudaMemset(l->err, 0, 4) == cudaSuccess;
+    size_t opb = 0;
+    for (int hb : {512, 1024, 2048})
+        if (K % hb == 0) opb = std::max(opb, (size_t)(K / hb) * 4 * op_region_bytes(hb, group));
+    ok = ok && cudaMalloc(&l->opbuf, opb) == cudaSuccess && cudaMalloc(&l->op_counters, 8) == cudaSuccess &&
+         cudaMemset(l->opbuf, 0, opb) == cudaSuccess && cudaMemset(l->op_counters, 0, 8) == cudaSuccess &&
          cudaDeviceSynchronize() == cudaSuccess;  // callers may launch on a non-blocking stream
     if (!ok) {
         bcu_linear_free(l);
@@ -80,10 +91,20 @@ bcu_status bcu_linear_prepare(const uint32_t* w_host, const uint16_t* scales_hos
 void bcu_linear_free(bcu_linear* l) {
     if (!l) return;
     cudaSetDevice(l->device);
-    void* p[] = {l->codes, l->sb, l->partial, l->counters, l->err, l->gwt, l->gbias, l->gbop, l->gex};
+    void* p[] = {l->codes, l->sb,   l->partial, l->counters, l->err,  l->gwt,
+                 l->gbias, l->gbop, l->gex,     l->opbuf,    l->op_counters};
     for (void* q : p)
         if (q) cudaFree(q);
     delete l;
+}
+
+// The K-slice plan of a call rotating in HB-point blocks: slices of whole blocks (a slice that split a block would
+// have every CTA of the block transform all of it, and the grid-built operand holds whole blocks). The plan depends
+// on HB only, never on T or on how the operand is built, so a row's result is the same bits at every T.
+static TernaryMat rotate_plan(const bcu_linear* l, int HB) {
+    TernaryMat mm = l->m;
+    if (HB > mm.kslice) plan_ternary(mm, l->sms, HB);
+    return mm;
 }
 
 static bcu_status linear_run(bcu_linear* l, const uint16_t* xb, const float* xf, int T, int HB, const float* signs,
@@ -92,18 +113,23 @@ static bcu_status linear_run(bcu_linear* l, const uint16_t* xb, const float* xf,
     if (HB && (HB != 512 && HB != 1024 && HB != 2048)) return BCU_ERR_ARG;
     if (HB && l->m.K % HB) return BCU_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
+    const TernaryMat mm = rotate_plan(l, HB);
     ActSrc src;
     src.mode = ACT_EXT;
     src.x = xf;
     src.xb = xb;
     src.signs = signs;
     src.HB = HB;
+    if (HB && !l->local_build && gemv_coresident(mm, T, 0, HB, l->sms, 0)) {  // the CTAs build the operand together
+        src.opbuf = l->opbuf;
+        src.op_counters = l->op_counters;
+    }
     GemvOut o;
     o.out = y;
     o.partial = l->partial;
     o.counters = l->counters;
     o.err = l->err;
-    launch_ternary_gemv(l->m, src, T, o, nullptr, st);
+    launch_ternary_gemv(mm, src, T, o, nullptr, st);
     if (cudaGetLastError() != cudaSuccess) return BCU_ERR_CUDA;
     return BCU_OK;
 }
@@ -154,6 +180,14 @@ bcu_status bcu_gemm_prep_debug(bcu_linear* l, const float* x_dev, int32_t M, voi
     return cudaDeviceSynchronize() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
 }
 
+// Test hook (not in the ABI header): 1 = every CTA builds its own slice of the operand (the path taken when the
+// grid cannot hold all CTAs at once), 0 = the default choice.
+bcu_status bcu_linear_set_local_build(bcu_linear* l, int32_t on) {
+    if (!l) return BCU_ERR_ARG;
+    l->local_build = on != 0;
+    return BCU_OK;
+}
+
 bcu_status bcu_linear_sync(bcu_linear* l, void* stream) {
     if (!l) return BCU_ERR_ARG;
     cudaSetDevice(l->device);
@@ -201,9 +235,10 @@ bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf1
     if (!l || !x_bf16_dev || !y_dev || T < 1 || T > VMAX) return BCU_ERR_ARG;
     if (hadamard && (hadamard != 512 && hadamard != 1024 && hadamard != 2048)) return BCU_ERR_ARG;
     if (hadamard && l->m.K % hadamard) return BCU_ERR_ARG;
-    const int nrb = l->m.O / 128;
+    const TernaryMat mm = rotate_plan(l, hadamard);
+    const int nrb = mm.O / 128;
     if (nrb > STATIC_COUNTERS) return BCU_ERR_TOO_LARGE;
-    if (l->m.nsplit > 1 && (size_t)l->m.nsplit * T * l->m.O > STATIC_PARTIAL_FLOATS) return BCU_ERR_TOO_LARGE;
+    if (mm.nsplit > 1 && (size_t)mm.nsplit * T * mm.O > STATIC_PARTIAL_FLOATS) return BCU_ERR_TOO_LARGE;
     if (cudaSetDevice(l->device) != cudaSuccess) return BCU_ERR_CUDA;
     unsigned char* scratch = nullptr;
     bcu_status s = static_scratch(l->device, &scratch);
@@ -223,7 +258,7 @@ bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf1
     o.partial = (float*)scratch;
     o.counters = counters;
     o.err = err;
-    launch_ternary_gemv(l->m, src, T, o, nullptr, st);
+    launch_ternary_gemv(mm, src, T, o, nullptr, st);
     return cudaGetLastError() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
 }
 

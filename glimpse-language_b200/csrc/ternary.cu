@@ -984,7 +984,7 @@ int gemv_grid(const TernaryMat& m, int ab_rows) { return (m.O / 128) * m.nsplit 
 bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms, int lora_r) {
     const int nt = (2 * T + 7) / 8;
     const int tpc = grid_build_tpc(m, T, hb);
-    if (tpc > 8 || hb <= 0) return false;
+    if (tpc > 8 || hb <= 0 || hb > m.kslice) return false;  // the buffer's regions hold whole blocks
     const void* fn = gemv_fn(nt, m.group, hb, lora_r > 0);
     const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, tpc, lora_r);
     if (smem > 220 * 1024) return false;

@@ -92,6 +92,27 @@ def test_config1_full_shape_and_batch_invariance(gpu):
             assert np.array_equal(yT[t].view(np.uint32), alone[t].view(np.uint32)), (T, t)
 
 
+@pytest.mark.parametrize("O,K,group,HB,T", [(6144, 2048, 64, 2048, 9), (1024, 2048, 128, 512, 16),
+                                            (2048, 4096, 64, 1024, 5), (1024, 2048, 64, 2048, 1)])
+def test_rotate_linear_grid_and_local_build_agree(gpu, O, K, group, HB, T):
+    """The operand built by all CTAs together (the default when they fit at once) and by each CTA for its own slice:
+    the same plan and the same operand values, so the outputs are the same bits."""
+    torch = pytest.importorskip("torch")
+    W, S, B, X = ternary_case(O, K, group, T, "neg", 300 + HB)
+    xb = bf16_bits(torch, X)
+    signs = np.where(np.random.default_rng(HB).random(K) < 0.5, -1, 1).astype(np.float32)
+    lin = Linear(W, S, B, group)
+    grid = lin.rotate_forward(torch, xb, HB, signs)
+    assert lin.L.bcu_linear_set_local_build(lin.h, 1) == _lib.OK
+    local = lin.rotate_forward(torch, xb, HB, signs)
+    assert lin.L.bcu_linear_set_local_build(lin.h, 0) == _lib.OK
+    assert np.array_equal(grid.view(np.uint32), local.view(np.uint32))
+    want, xr = orc.rotate_ternary_linear(W, S, B, group, xb, HB, signs)
+    Wd = refimpl.dense_weights(W, S, B, group)
+    bound = 2e-5 * (np.abs(xr).astype(np.float64) @ np.abs(Wd).T) + 1e-5
+    assert np.all(np.abs(grid.astype(np.float64) - want) <= bound)
+
+
 @pytest.mark.parametrize("n", list(range(10)))
 def test_config2_gdn_verify_rollback(gpu, n):
     torch = pytest.importorskip("torch")
@@ -103,6 +124,22 @@ def test_config2_gdn_verify_rollback(gpu, n):
     y = torch.empty((T, NV, 128), dtype=torch.float32, device="cuda")
     s = _lib.lib().bcu_gdn_verify(*[vp(x) for x in t], vp(st), vp(y), T, NK, NV, n, None)
     assert s == _lib.OK
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(y.cpu().numpy(), want_y, rtol=2e-4, atol=2e-6)
+    np.testing.assert_allclose(st.cpu().numpy(), want_s, rtol=2e-4, atol=2e-6)
+
+
+@pytest.mark.parametrize("T,n", [(1, 0), (1, 1), (16, 16), (20, 0), (20, 17), (20, 20), (37, 33)])
+def test_gdn_verify_rows_past_one_chunk(gpu, T, n):
+    """Rows are staged 16 at a time: passes longer than one chunk, and checkpoints in the second or third chunk."""
+    torch = pytest.importorskip("torch")
+    NK, NV = 2, 4
+    q, k, v, a, b, alog, dtb, S = gdn_case(T, NK, NV, 100 + T)
+    want_y, want_s = orc.gdn_verify(q, k, v, a, b, alog, dtb, S, n)
+    t = [dev(torch, x) for x in (q, k, v, a, b, alog, dtb)]
+    st = dev(torch, S)
+    y = torch.empty((T, NV, 128), dtype=torch.float32, device="cuda")
+    assert _lib.lib().bcu_gdn_verify(*[vp(x) for x in t], vp(st), vp(y), T, NK, NV, n, None) == _lib.OK
     torch.cuda.synchronize()
     np.testing.assert_allclose(y.cpu().numpy(), want_y, rtol=2e-4, atol=2e-6)
     np.testing.assert_allclose(st.cpu().numpy(), want_s, rtol=2e-4, atol=2e-6)
