@@ -336,6 +336,8 @@ def run_small_op(args, local):
             W = synth.fill(3, args.seed, 3 * r, 0, 0, (O, K // 16), np.uint32)
             S = synth.fill(4, args.seed, 3 * r + 1, 0.01, 0.05, (O, K // 64), np.uint16)
             B = synth.fill(6, args.seed, 3 * r + 1, 0.01, 0.05, (O, K // 64), np.uint16)
+            if r == 0:
+                host0 = (W, S, B)
             h = ctypes.c_void_p()
             assert L.bcu_linear_prepare(W.ctypes.data_as(ctypes.c_void_p), S.ctypes.data_as(ctypes.c_void_p),
                                         B.ctypes.data_as(ctypes.c_void_p), O, K, 64, local, ctypes.byref(h)) == 0
@@ -352,6 +354,12 @@ def run_small_op(args, local):
         metric, unit = "ternary linear calls/s (config 1)", "calls/s"
         host_in, host_out = T * K * 2, T * O * 4
         cleanup = lambda: [L.bcu_linear_free(h) for h in hs]  # noqa: E731
+
+        def cpu_call():
+            from oracle.oracle import rotate_ternary_linear
+
+            xbits = x.view(torch.int16).cpu().numpy().view(np.uint16)
+            rotate_ternary_linear(*host0, 64, xbits, 2048)
     else:
         T, NK, NV = 9, 16, 32
         g = torch.Generator(device="cuda").manual_seed(args.seed)
@@ -381,6 +389,11 @@ def run_small_op(args, local):
         metric, unit = "GDN verify steps/s (config 2)", "calls/s"
         host_in, host_out = (2 * NK + NV) * T * 128 * 4 + 2 * T * NV * 4, T * NV * 128 * 4
         cleanup = lambda: None  # noqa: E731
+
+        def cpu_call():
+            from oracle.oracle import gdn_verify
+
+            gdn_verify(*[t.cpu().numpy() for t in (q, k, v, a, b, alog, dtb, states[0])], int(ns[0]))
     calls = ROT_COPIES * 4
     for i in range(ROT_COPIES):  # first calls outside the capture (one-time kernel attributes)
         call(i)
@@ -440,6 +453,16 @@ def run_small_op(args, local):
                      "peak_source": "MEASURED_PEAKS.json" if pk else "fallback"},
         "clocks": ck,
     }
+    if not args.no_cpu:  # the oracle port on the host cores, about two seconds of calls
+        cpu_call()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 2.0:
+            cpu_call()
+            reps += 1
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": reps / secs, "unit": unit,
+                                "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": "port",
+                                "sample": f"{reps} calls of the oracle on copy 0 (inputs copied to the host each call)"}
     print(json.dumps(line), flush=True)
     cleanup()
 

@@ -28,25 +28,37 @@ __device__ __forceinline__ void gates(float a_in, float b_in, float ea, float dt
     beta = 1.0f / (1.0f + expf(-b_in));
 }
 
-// One gated-delta step for the 4 dv rows of a warp (kernels.metal:607-620): S *= g; kv = S.k; delta = (v - kv) beta;
-// S += k delta; y = S.q.
-__device__ __forceinline__ void gdn_step4(float4* st, float4 q, float4 k, const float* v, float g, float beta, float* o) {
-    float kv[4];
+// One gated-delta step for the R dv rows of a warp (lane = 4 dk entries), with one reduction round: with u = S.k and
+// z = S.q of the state before the step, S' = g S + delta k with delta = (v - g u) beta, and the output
+// S'.q = g z + delta (k.q) (kernels.metal:607-620 computes the same quantities in sequence, with two rounds).
+template <int R>
+__device__ __forceinline__ void gdn_step_fused(float4* st, float4 q, float4 k, const float* vv, float g, float beta,
+                                               float* o4) {
+    float u[R], z[R];
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-        st[r].x *= g; st[r].y *= g; st[r].z *= g; st[r].w *= g;
-        kv[r] = st[r].x * k.x + st[r].y * k.y + st[r].z * k.z + st[r].w * k.w;
+    for (int i = 0; i < R; i++) {
+        u[i] = st[i].x * k.x + st[i].y * k.y + st[i].z * k.z + st[i].w * k.w;
+        z[i] = st[i].x * q.x + st[i].y * q.y + st[i].z * q.z + st[i].w * q.w;
+    }
+    float kq = k.x * q.x + k.y * q.y + k.z * q.z + k.w * q.w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            u[i] += __shfl_xor_sync(0xffffffffu, u[i], o);
+            z[i] += __shfl_xor_sync(0xffffffffu, z[i], o);
+        }
+        kq += __shfl_xor_sync(0xffffffffu, kq, o);
     }
 #pragma unroll
-    for (int r = 0; r < 4; r++) kv[r] = warp_sum(kv[r]);
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        float delta = (v[r] - kv[r]) * beta;
-        st[r].x += k.x * delta; st[r].y += k.y * delta; st[r].z += k.z * delta; st[r].w += k.w * delta;
-        o[r] = st[r].x * q.x + st[r].y * q.y + st[r].z * q.z + st[r].w * q.w;
+    for (int i = 0; i < R; i++) {
+        const float delta = (vv[i] - g * u[i]) * beta;
+        st[i].x = g * st[i].x + k.x * delta;
+        st[i].y = g * st[i].y + k.y * delta;
+        st[i].z = g * st[i].z + k.z * delta;
+        st[i].w = g * st[i].w + k.w * delta;
+        o4[i] = g * z[i] + delta * kq;
     }
-#pragma unroll
-    for (int r = 0; r < 4; r++) o[r] = warp_sum(o[r]);
 }
 
 struct __align__(16) GdnSmem {
@@ -222,41 +234,14 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
         }
     __syncthreads();
 
-    // ---- gated delta rule: replay (commit), then this pass's rows. Per step one reduction round: with u = S.k and
-    // z = S.q of the state before the step, S' = g S + delta k with delta = (v - g u) beta, and the output
-    // S'.q = g z + delta (k.q) (kernels.metal:607-620 computes the same quantities in sequence).
+    // ---- gated delta rule: replay (commit), then this pass's rows, one reduction round per step (gdn_step_fused)
     for (int r = 0; r < rn + T; r++) {
         const float4 q = *(const float4*)&sm.q[r][lane * 4];
         const float4 k = *(const float4*)&sm.k[r][lane * 4];
         const float4 v4 = *(const float4*)&sm.v[r][w * 4];
         const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-        const float g = sm.g[r], beta = sm.beta[r];
-        float u[4], z[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            u[i] = st[i].x * k.x + st[i].y * k.y + st[i].z * k.z + st[i].w * k.w;
-            z[i] = st[i].x * q.x + st[i].y * q.y + st[i].z * q.z + st[i].w * q.w;
-        }
-        float kq = k.x * q.x + k.y * q.y + k.z * q.z + k.w * q.w;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                u[i] += __shfl_xor_sync(0xffffffffu, u[i], o);
-                z[i] += __shfl_xor_sync(0xffffffffu, z[i], o);
-            }
-            kq += __shfl_xor_sync(0xffffffffu, kq, o);
-        }
         float o4[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float delta = (vv[i] - g * u[i]) * beta;
-            st[i].x = g * st[i].x + k.x * delta;
-            st[i].y = g * st[i].y + k.y * delta;
-            st[i].z = g * st[i].z + k.z * delta;
-            st[i].w = g * st[i].w + k.w * delta;
-            o4[i] = g * z[i] + delta * kq;
-        }
+        gdn_step_fused<4>(st, q, k, vv, sm.g[r], sm.beta[r], o4);
         if (r == rn - 1) {
 #pragma unroll
             for (int i = 0; i < 4; i++) *(float4*)(S + (size_t)i * 128) = st[i];
@@ -280,8 +265,10 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
 }
 
 // Graded config 2: T rows from explicit q/k/v/gate inputs, outputs for every row, and the state written back as it
-// was after the first n rows (the checkpoint taken in registers while the rows run). Rows are staged in shared
-// memory GV_CHUNK at a time, every load of a chunk in flight at once, so the sequential steps wait on no global load.
+// was after the first n rows (the checkpoint taken in registers while the rows run). CTA = (value head, 16 dv rows),
+// 256 threads: warp w owns dv rows 2w, 2w + 1 (short per-warp step chains: the steps are latency-bound). Rows are
+// staged in shared memory GV_CHUNK at a time, every load of a chunk in flight at once, so the sequential steps wait
+// on no global load.
 constexpr int GV_CHUNK = 16;
 struct __align__(16) GvSmem {
     float q[GV_CHUNK][128];
@@ -290,30 +277,32 @@ struct __align__(16) GvSmem {
     float g[GV_CHUNK], beta[GV_CHUNK];
 };
 
-__global__ void __launch_bounds__(128) gdn_verify_kernel(const float* q, const float* k, const float* v,
+__global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const float* k, const float* v,
                                                          const float* a_in, const float* b_in, const float* a_log,
                                                          const float* dt_bias, float* state, float* y, int T, int NK,
                                                          int NV, int n) {
     __shared__ GvSmem sm;
     const int hd = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int hk = hd / (NV / NK);
-    const int dvb = blockIdx.y * 16, dv0 = dvb + w * 4;
-    float4 st[4], keep[4];
+    const int dvb = blockIdx.y * 16, dv0 = dvb + w * 2;
+    const int ch = tid & 127;           // q channel (threads < 128) or k channel (the others) staged by this thread
+    const float* qk = tid < 128 ? q : k;
+    float (*sqk)[128] = tid < 128 ? sm.q : sm.k;
+    float4 st[2], keep[2];
     float* S = state + ((size_t)hd * 128 + dv0) * 128 + lane * 4;
     const float ea = expf(a_log[hd]), dtb = dt_bias[hd];
     pdl_trigger();
     pdl_wait();
 #pragma unroll
-    for (int r = 0; r < 4; r++) keep[r] = st[r] = *(const float4*)(S + (size_t)r * 128);
+    for (int r = 0; r < 2; r++) keep[r] = st[r] = *(const float4*)(S + (size_t)r * 128);
     for (int t0 = 0; t0 < T; t0 += GV_CHUNK) {
         const int nr = min(GV_CHUNK, T - t0);
-        float lq[GV_CHUNK], lk[GV_CHUNK], lv[GV_CHUNK];
+        float lqk[GV_CHUNK], lv[GV_CHUNK];
 #pragma unroll
         for (int r = 0; r < GV_CHUNK; r++)
             if (r < nr) {
                 const size_t t = (size_t)(t0 + r);
-                lq[r] = q[(t * NK + hk) * 128 + tid];
-                lk[r] = k[(t * NK + hk) * 128 + tid];
+                lqk[r] = qk[(t * NK + hk) * 128 + ch];
                 lv[r] = tid < 16 ? v[(t * NV + hd) * 128 + dvb + tid] : 0.0f;
             }
         float ga = 0.0f, gb = 0.0f;
@@ -324,8 +313,7 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(const float* q, const f
 #pragma unroll
         for (int r = 0; r < GV_CHUNK; r++)
             if (r < nr) {
-                sm.q[r][tid] = lq[r];
-                sm.k[r][tid] = lk[r];
+                sqk[r][ch] = lqk[r];
                 if (tid < 16) sm.v[r][tid] = lv[r];
             }
         if (tid < nr) gates(ga, gb, ea, dtb, sm.g[tid], sm.beta[tid]);
@@ -333,30 +321,27 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(const float* q, const f
         for (int r = 0; r < nr; r++) {
             const float4 qq = *(const float4*)&sm.q[r][lane * 4];
             const float4 kk = *(const float4*)&sm.k[r][lane * 4];
-            const float4 v4 = *(const float4*)&sm.v[r][w * 4];
-            const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-            float o[4];
-            gdn_step4(st, qq, kk, vv, sm.g[r], sm.beta[r], o);
-            if (lane < 4) {
-                const float ov = lane == 0 ? o[0] : (lane == 1 ? o[1] : (lane == 2 ? o[2] : o[3]));
-                y[((size_t)(t0 + r) * NV + hd) * 128 + dv0 + lane] = ov;
-            }
+            const float2 v2 = *(const float2*)&sm.v[r][w * 2];
+            const float vv[2] = {v2.x, v2.y};
+            float o[2];
+            gdn_step_fused<2>(st, qq, kk, vv, sm.g[r], sm.beta[r], o);
+            if (lane < 2) y[((size_t)(t0 + r) * NV + hd) * 128 + dv0 + lane] = lane == 0 ? o[0] : o[1];
             if (t0 + r + 1 == n) {
-#pragma unroll
-                for (int i = 0; i < 4; i++) keep[i] = st[i];
+                keep[0] = st[0];
+                keep[1] = st[1];
             }
         }
         __syncthreads();  // the next chunk overwrites the rows
     }
 #pragma unroll
-    for (int r = 0; r < 4; r++) *(float4*)(S + (size_t)r * 128) = keep[r];
+    for (int r = 0; r < 2; r++) *(float4*)(S + (size_t)r * 128) = keep[r];
 }
 
 void launch_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
                        const float* a_log, const float* dt_bias, float* state, float* y, int T, int NK, int NV,
                        int n, cudaStream_t st) {
     void* args[] = {&q, &k, &v, &a_in, &b_in, &a_log, &dt_bias, &state, &y, &T, &NK, &NV, &n};
-    launch_pdl((const void*)gdn_verify_kernel, dim3(NV, 8), dim3(128), 0, st, args);
+    launch_pdl((const void*)gdn_verify_kernel, dim3(NV, 8), dim3(256), 0, st, args);
 }
 
 }  // namespace bcu
