@@ -315,6 +315,10 @@ def run_config5(args, ws, rank, local):
 # --workload config1 / config2: the graded single-op configs, timed over ROT_COPIES copies of the weights / state
 # (more than L2 holds together) so every call streams from HBM; one call per step, back to back on one stream.
 ROT_COPIES = 64
+# DRAM bytes (read + write) of one call, from one ncu capture of the kernel on this workload
+# (profiles/ternary_gemv_config1_rot2048.md, profiles/gdn_verify_config2.md); the GDN state's 2.1 MB of writes are
+# still in L2 when the kernel ends, so that capture counts them as 0
+OP_DRAM_BYTES = {"config1": 4.3607e6, "config2": 2.4151e6}
 
 
 def run_small_op(args, local):
@@ -449,7 +453,7 @@ def run_small_op(args, local):
                 "d2h_bytes_per_step": host_out * calls, "path": "C ABI call per step with its input H2D and output D2H"},
         "gpu_launches": n,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": None, "bytes_per_launch": per_call, "us_per_launch": us_call,
+                     "traffic": OP_DRAM_BYTES[args.workload], "bytes_per_launch": per_call, "us_per_launch": us_call,
                      "peak_source": "MEASURED_PEAKS.json" if pk else "fallback"},
         "clocks": ck,
     }
