@@ -93,7 +93,8 @@ def test_config1_full_shape_and_batch_invariance(gpu):
 
 
 @pytest.mark.parametrize("O,K,group,HB,T", [(6144, 2048, 64, 2048, 9), (1024, 2048, 128, 512, 16),
-                                            (2048, 4096, 64, 1024, 5), (1024, 2048, 64, 2048, 1)])
+                                            (2048, 4096, 64, 1024, 5), (1024, 2048, 64, 2048, 1),
+                                            (6144, 2048, 64, 2048, 16), (1024, 4096, 128, 2048, 13)])
 def test_rotate_linear_grid_and_local_build_agree(gpu, O, K, group, HB, T):
     """The operand built by all CTAs together (the default when they fit at once) and by each CTA for its own slice:
     the same plan and the same operand values, so the outputs are the same bits."""
