@@ -10,9 +10,9 @@
 // whatever the accept length, and rollback costs nothing. The conv state is double-buffered by parity because several
 // CTAs read the q/k channels of a key head while one of them writes the new committed rows.
 //
-// CTA = (value head, 16 dv rows), 128 threads: warp w owns dv rows 4w..4w+3, lane = 4 dk entries. Thread c convolves
-// q and k channel c of the head's key head; threads < 16 also the CTA's 16 v channels. All rows are staged in shared
-// memory first, so the sequential steps run without global loads on the critical path.
+// CTA = (value head, 16 dv rows), 256 threads: warp w owns dv rows 2w, 2w + 1, lane = 4 dk entries. Thread t convolves
+// q channel t (t < 128) or k channel t - 128 of the head's key head; threads < 16 also the CTA's 16 v channels. All
+// rows are staged in shared memory first, so the sequential steps run without global loads on the critical path.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -66,28 +66,31 @@ struct __align__(16) GdnSmem {
     float k[RMAX][128];
     float v[RMAX][16];
     float g[RMAX], beta[RMAX];
-    float red[4][32];      // per-warp row sums of squares: slots 0..15 q rows, 16..31 k rows
+    float red[8][32];      // per-warp row sums of squares: slots 0..15 q rows, 16..31 k rows
     float rs[32];          // their norm scales
 };
 
 __host__ __device__ inline size_t gdn_smem_bytes() { return sizeof(GdnSmem); }
 
-__global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
+__global__ void __launch_bounds__(256, 2) gdn_layer_kernel(GdnArgs a) {
     extern __shared__ __align__(16) uint8_t gsm[];
     GdnSmem& sm = *(GdnSmem*)gsm;
     const int hd = blockIdx.x, blk = blockIdx.y, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int NK = a.NK, NV = a.NV, C = a.C, T = a.T;
     const int hk = hd / (NV / NK);
     const int dv0 = blk * 16;
-    // channels of this thread: q and k channel `tid` of key head hk, v channel dv0 + tid (tid < 16)
-    const int cq = hk * 128 + tid, ck = (NK + hk) * 128 + tid, cv = (2 * NK + hd) * 128 + dv0 + tid;
+    // channels of this thread: q channel c (threads < 128) or k channel c (the others) of key head hk, c = tid % 128;
+    // v channel dv0 + tid (tid < 16)
+    const int c = tid & 127;
+    const bool is_k = tid >= 128;
+    const int cx = (is_k ? NK + hk : hk) * 128 + c, cv = (2 * NK + hd) * 128 + dv0 + tid;
     const bool has_v = tid < 16;
     const bool qk_writer = (hd % (NV / NK)) == 0 && blk == 0;  // one CTA commits the shared q/k channels
-    float wq[4], wk[4], wv[4] = {0, 0, 0, 0};
+    float (*sx)[128] = is_k ? sm.k : sm.q;
+    float wx[4], wv[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        wq[i] = a.convw[(size_t)cq * 4 + i];
-        wk[i] = a.convw[(size_t)ck * 4 + i];
+        wx[i] = a.convw[(size_t)cx * 4 + i];
         if (has_v) wv[i] = a.convw[(size_t)cv * 4 + i];
     }
     const float ea = expf(a.a_log[hd]), dtb = a.dt_bias[hd];
@@ -97,37 +100,34 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
 
     // ---- every load of the layer in flight at once: the state rows of this warp, the replayed rows (conv outputs
     // of the previous pass), the committed conv state, the previous pass's raw rows, this pass's rows, gate inputs
-    float* S = a.gdn_state + ((size_t)hd * 128 + dv0 + w * 4) * 128 + lane * 4;
-    float4 st[4];
+    float* S = a.gdn_state + ((size_t)hd * 128 + dv0 + w * 2) * 128 + lane * 4;
+    float4 st[2];
 #pragma unroll
-    for (int r = 0; r < 4; r++) st[r] = *(const float4*)(S + (size_t)r * 128);
+    for (int r = 0; r < 2; r++) st[r] = *(const float4*)(S + (size_t)r * 128);
     const float* pqc = a.pend_qkvc + (size_t)prev * VMAX * C;
-    float lq[VMAX], lk[VMAX], lv[VMAX];
+    float lx[VMAX], lv[VMAX];
 #pragma unroll
     for (int r = 0; r < VMAX; r++)
         if (r < rn) {
-            lq[r] = pqc[(size_t)r * C + cq];
-            lk[r] = pqc[(size_t)r * C + ck];
+            lx[r] = pqc[(size_t)r * C + cx];
             lv[r] = has_v ? pqc[(size_t)r * C + cv] : 0.0f;
         }
     const float* cs_in = a.conv_state + (size_t)prev * 3 * C;  // committed state lives at the previous parity
     const float* pq = a.pend_qkv + (size_t)prev * VMAX * C;
     const int ld = C + NV * 128;
     // rows rn..rn+2 of [state(3); previous raw rows], then this pass's rows
-    float rq[3 + VMAX], rk[3 + VMAX], rv[3 + VMAX];
+    float rx[3 + VMAX], rv[3 + VMAX];
 #pragma unroll
     for (int j = 0; j < 3; j++) {
         const int kk = rn + j;
         const float* src = kk < 3 ? cs_in + (size_t)kk * C : pq + (size_t)(kk - 3) * C;
-        rq[j] = src[cq];
-        rk[j] = src[ck];
+        rx[j] = src[cx];
         rv[j] = has_v ? src[cv] : 0.0f;
     }
 #pragma unroll
     for (int t = 0; t < VMAX; t++)
         if (t < T) {
-            rq[3 + t] = a.qkvz[(size_t)t * ld + cq];
-            rk[3 + t] = a.qkvz[(size_t)t * ld + ck];
+            rx[3 + t] = a.qkvz[(size_t)t * ld + cx];
             rv[3 + t] = has_v ? a.qkvz[(size_t)t * ld + cv] : 0.0f;
         }
     float ga = 0.0f, gb = 0.0f;
@@ -142,8 +142,7 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
 #pragma unroll
     for (int r = 0; r < VMAX; r++)
         if (r < rn) {
-            sm.q[r][tid] = lq[r];
-            sm.k[r][tid] = lk[r];
+            sx[r][c] = lx[r];
             if (has_v) sm.v[r][tid] = lv[r];
         }
     if (tid < rn + T) gates(ga, gb, ea, dtb, sm.g[tid], sm.beta[tid]);
@@ -154,16 +153,10 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
     float* pqc_out = a.pend_qkvc + (size_t)par * VMAX * C;
     if (qk_writer) {
 #pragma unroll
-        for (int j = 0; j < 3; j++) {
-            cs_out[(size_t)j * C + cq] = rq[j];
-            cs_out[(size_t)j * C + ck] = rk[j];
-        }
+        for (int j = 0; j < 3; j++) cs_out[(size_t)j * C + cx] = rx[j];
 #pragma unroll
         for (int t = 0; t < VMAX; t++)
-            if (t < T) {
-                pq_out[(size_t)t * C + cq] = rq[3 + t];
-                pq_out[(size_t)t * C + ck] = rk[3 + t];
-            }
+            if (t < T) pq_out[(size_t)t * C + cx] = rx[3 + t];
     }
     if (has_v) {
 #pragma unroll
@@ -173,21 +166,18 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
             if (t < T) pq_out[(size_t)t * C + cv] = rv[3 + t];
     }
     // conv + SiLU; q, k rows then get the per-head RMS norm scaled by 1/128 and 1/sqrt(128)
-    float cq_[VMAX], ck_[VMAX];
+    float cx_[VMAX];
 #pragma unroll
     for (int t = 0; t < VMAX; t++) {
-        cq_[t] = 0.0f;
-        ck_[t] = 0.0f;
+        cx_[t] = 0.0f;
         if (t < T) {
-            float aq = 0.0f, ak = 0.0f, av = 0.0f;
+            float ax = 0.0f, av = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                aq += wq[i] * rq[t + i];
-                ak += wk[i] * rk[t + i];
+                ax += wx[i] * rx[t + i];
                 av += wv[i] * rv[t + i];
             }
-            cq_[t] = aq / (1.0f + expf(-aq));
-            ck_[t] = ak / (1.0f + expf(-ak));
+            cx_[t] = ax / (1.0f + expf(-ax));
             if (has_v) {
                 float vv = av / (1.0f + expf(-av));
                 sm.v[rn + t][tid] = vv;
@@ -195,12 +185,13 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
             }
         }
     }
-    {   // row sums of squares, q rows in slots 0..15 and k rows in 16..31: halving butterfly, lane l holds slot l
+    {   // row sums of squares, q rows in slots 0..15 (warps 0-3) and k rows in 16..31 (warps 4-7): halving butterfly,
+        // lane l holds slot l; the other kind's slots are zero
         float v[32];
 #pragma unroll
         for (int t = 0; t < VMAX; t++) {
-            v[t] = cq_[t] * cq_[t];
-            v[VMAX + t] = ck_[t] * ck_[t];
+            v[t] = is_k ? 0.0f : cx_[t] * cx_[t];
+            v[VMAX + t] = is_k ? cx_[t] * cx_[t] : 0.0f;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -215,41 +206,36 @@ __global__ void __launch_bounds__(128) gdn_layer_kernel(GdnArgs a) {
         sm.red[w][lane] = v[0];
     }
     __syncthreads();
-    if (tid < 32) {
-        const float ss = ((sm.red[0][tid] + sm.red[1][tid]) + sm.red[2][tid]) + sm.red[3][tid];
+    if (tid < 32) {  // slot tid: the four warps of its kind, in channel order
+        const int w0 = tid < VMAX ? 0 : 4;
+        const float ss = ((sm.red[w0][tid] + sm.red[w0 + 1][tid]) + sm.red[w0 + 2][tid]) + sm.red[w0 + 3][tid];
         sm.rs[tid] = rsqrtf(ss / 128.0f + EPS_G) * (tid < VMAX ? (1.0f / 128.0f) : 0.08838834764831845f);
     }
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < VMAX; t++)
         if (t < T) {
-            const float q = cq_[t] * sm.rs[t];
-            const float k = ck_[t] * sm.rs[VMAX + t];
-            sm.q[rn + t][tid] = q;
-            sm.k[rn + t][tid] = k;
-            if (qk_writer) {
-                pqc_out[(size_t)t * C + cq] = q;
-                pqc_out[(size_t)t * C + ck] = k;
-            }
+            const float x = cx_[t] * sm.rs[(is_k ? VMAX : 0) + t];
+            sx[rn + t][c] = x;
+            if (qk_writer) pqc_out[(size_t)t * C + cx] = x;
         }
     __syncthreads();
 
-    // ---- gated delta rule: replay (commit), then this pass's rows, one reduction round per step (gdn_step_fused)
+    // ---- gated delta rule: replay (commit), then this pass's rows, one reduction round per step (gdn_step_fused);
+    // warp w owns dv rows 2w, 2w + 1
     for (int r = 0; r < rn + T; r++) {
         const float4 q = *(const float4*)&sm.q[r][lane * 4];
         const float4 k = *(const float4*)&sm.k[r][lane * 4];
-        const float4 v4 = *(const float4*)&sm.v[r][w * 4];
-        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-        float o4[4];
-        gdn_step_fused<4>(st, q, k, vv, sm.g[r], sm.beta[r], o4);
+        const float2 v2 = *(const float2*)&sm.v[r][w * 2];
+        const float vv[2] = {v2.x, v2.y};
+        float o2[2];
+        gdn_step_fused<2>(st, q, k, vv, sm.g[r], sm.beta[r], o2);
         if (r == rn - 1) {
 #pragma unroll
-            for (int i = 0; i < 4; i++) *(float4*)(S + (size_t)i * 128) = st[i];
+            for (int i = 0; i < 2; i++) *(float4*)(S + (size_t)i * 128) = st[i];
         }
-        if (r >= rn && lane < 4) {
-            const float ov = lane == 0 ? o4[0] : (lane == 1 ? o4[1] : (lane == 2 ? o4[2] : o4[3]));
-            a.y[(size_t)(r - rn) * NV * 128 + hd * 128 + dv0 + w * 4 + lane] = ov;
-        }
+        if (r >= rn && lane < 2)
+            a.y[(size_t)(r - rn) * NV * 128 + hd * 128 + dv0 + w * 2 + lane] = lane == 0 ? o2[0] : o2[1];
     }
 }
 
@@ -261,7 +247,7 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
     }
     GdnArgs aa = a;
     void* args[] = {&aa};
-    launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(128), gdn_smem_bytes(), st, args);
+    launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(256), gdn_smem_bytes(), st, args);
 }
 
 // Graded config 2: T rows from explicit q/k/v/gate inputs, outputs for every row, and the state written back as it
