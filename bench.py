@@ -155,7 +155,8 @@ def run_reference(args, ws, rank):
 
     cfg = config.bonsai_2b_graded(ctx=2048)
     ts = synth.model_tensors(cfg, args.seed)
-    steps, warm = max(1, min(args.steps, 3)), min(args.warmup, 1)
+    # each step is one full-model CPU pass (1-3 s on the host cores): at most 20 timed and 5 warm-up steps
+    steps, warm = max(1, min(args.steps, 20)), min(args.warmup, 5)
     cb, times = cpu_baseline(cfg, ts, steps, warm)
     v = cb["value"]
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": ws, "steps": steps,
