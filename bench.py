@@ -35,7 +35,7 @@ import numpy as np  # noqa: E402
 
 METRIC = "decode tok/s/GPU with speculation (Bonsai-2B shape); verify-pass HBM GB/s"
 # DRAM bytes (read + write) of one 9-row verify pass of this workload's model, summed over its 121 kernels from one
-# ncu launch-list capture (profiles/verify_pass_2b_launches.md; context ~70, so ~35 MB less K/V than the timed passes)
+# ncu capture of the pass at context ~70 (so ~35 MB less K/V than the timed passes)
 VERIFY_PASS_DRAM_BYTES = 1648.3e6
 PREFIX, USER, GEN, K_DRAFT = 1024, 256, 300, 8
 WORKLOAD = ("config3: Bonsai-2B shape random-init, 1024-token cached prefix + 256 Zipf(1.1) user tokens, "
@@ -116,7 +116,8 @@ def max_over_ranks(x, dist, device):
         return float(x)
     import torch
 
-    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    # replicas exchange nothing on the data path: a host-side (gloo) reduction of one number per rank
+    t = torch.tensor([float(x)], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -126,16 +127,22 @@ def whole_job_rate(ws, units_per_rank, seconds_max):
     return ws * units_per_rank / seconds_max
 
 
+# the CPU sample's context: the middle of the GPU arm's 1280..1580 (prefix + user, then 300 generated tokens)
+CPU_SAMPLE_CONTEXT = PREFIX + USER + GEN // 2
+
+
 def cpu_baseline(cfg, ts, steps, warmup, quiet=False):
-    """The oracle (C++ scalar restatement, OpenMP) on the host cores: one verify pass of 9 rows (planted drafts,
-    100% accept) of the full model per step, from an empty context (a bounded sample of the workload)."""
+    """The oracle (C++ scalar restatement, OpenMP) on the host cores: one verify pass of 9 rows of the full model
+    per step, from a seeded committed state at the GPU arm's mean context (a bounded sample of the workload)."""
+    from bonsai_b200 import synth
     from oracle.oracle import OracleModel
 
     o = OracleModel(cfg, ts)
+    parts = synth.random_state(cfg, CPU_SAMPLE_CONTEXT, 5)
     ids = np.arange(9, dtype=np.uint32) * 7 + 11
     times = []
     for i in range(warmup + steps):
-        o.reset()
+        o.set_state(*parts, CPU_SAMPLE_CONTEXT)
         t0 = time.perf_counter()
         o.forward(ids)
         dt = time.perf_counter() - t0
@@ -144,8 +151,8 @@ def cpu_baseline(cfg, ts, steps, warmup, quiet=False):
     cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     tok_s = 9 / statistics.mean(times)
     return {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": "one 9-row verify pass (8 planted drafts accepted + bonus) of the full Bonsai-2B shape at "
-                      "context 0 per step; tok/s = 9 / pass time"}, times
+            "sample": f"one 9-row verify pass (8 planted drafts accepted + bonus) of the full Bonsai-2B shape at "
+                      f"context {CPU_SAMPLE_CONTEXT} (the GPU arm's mean) per step; tok/s = 9 / pass time"}, times
 
 
 def run_reference(args, ws, rank):
@@ -193,7 +200,7 @@ def run_config5(args, ws, rank, local):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     torch.cuda.set_device(local)
     from bonsai_b200 import _lib, synth
 
@@ -316,9 +323,8 @@ def run_config5(args, ws, rank, local):
 # --workload config1 / config2: the graded single-op configs, timed over ROT_COPIES copies of the weights / state
 # (more than L2 holds together) so every call streams from HBM; one call per step, back to back on one stream.
 ROT_COPIES = 64
-# DRAM bytes (read + write) of one call, from one ncu capture of the kernel on this workload
-# (profiles/ternary_gemv_config1_rot2048.md, profiles/gdn_verify_config2.md); the GDN state's 2.1 MB of writes are
-# still in L2 when the kernel ends, so that capture counts them as 0
+# DRAM bytes (read + write) of one call, from one ncu capture of the kernel on this workload; the GDN state's 2.1 MB
+# of writes are still in L2 when the kernel ends, so that capture counts them as 0
 OP_DRAM_BYTES = {"config1": 4.1388e6, "config2": 2.4151e6}
 
 
@@ -535,7 +541,7 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     torch.cuda.set_device(local)
     from bonsai_b200 import _lib, config, synth
     from bonsai_b200.runtime import Model

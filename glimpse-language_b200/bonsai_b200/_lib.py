@@ -141,8 +141,6 @@ SIGNATURES = {
     "bcu_linear_sync": (I32, [P, P]),
     "bcu_linear_rotate_forward_static": (I32, [P, P, I32, I32, P, P, P]),
     "bcu_gdn_verify": (I32, [P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
-    "bcu_synth_fill": (I32, [I32, U64, U64, ctypes.c_double, ctypes.c_double, P, U64]),
-    "bcu_synth_zipf": (I32, [U64, ctypes.c_double, I32, PU32, I32]),
     "bcu_pass_launches": (I32, [P, I32, PI32]),
     "bcu_pass_bytes": (I32, [P, I32, ctypes.POINTER(ctypes.c_double)]),
     "bcu_time_pass": (I32, [P, I32, I32, ctypes.POINTER(ctypes.c_float)]),
@@ -153,6 +151,7 @@ SIGNATURES = {
     # host-logic exports (not in the ABI header: test hooks of the decode driver and the operand build)
     "bcu_set_local_build": (I32, [P, I32]),
     "bcu_linear_set_local_build": (I32, [P, I32]),
+    "bcu_static_scratch_debug": (I32, [I32, I32]),
     "bcu_debug_wait_timeout": (I32, [P]),
     "bcu_gemm_prep_debug": (I32, [P, P, I32, P, P]),
     "bcu_token_key": (U64, [P, U64]),

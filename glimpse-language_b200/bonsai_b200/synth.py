@@ -4,14 +4,38 @@ Distributions follow the graded configs: ternary codes uniform in {0,1,2}, fp16 
 (or the implicit -s of the reference pack), bf16 embedding / lm_head N(0, 0.02). The rest (not specified by the
 configs) keeps activations O(1): norm weights U(0.8, 1.2), GDN a/b rows N(0, 1/sqrt(hidden)) so the gate logits are
 ~N(0, 1), A_log = dt_bias = 0 (decay exp(-softplus(a)) as config 2 states), conv taps N(0, 0.5).
-All values come from bcu_synth_fill, so the same seed gives the same bytes on every host.
+All values come from bcu_synth_fill (libbonsai_synth.so, include/bonsai_synth.h: a host-only library apart from the
+CUDA backend), so the same seed gives the same bytes on every host.
 """
 import ctypes
+import os
 
 import numpy as np
 
 from . import _lib
 from .config import dims
+
+SYNTH_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libbonsai_synth.so")
+SIGNATURES = {
+    "bcu_synth_fill": (_lib.I32, [_lib.I32, _lib.U64, _lib.U64, ctypes.c_double, ctypes.c_double, _lib.P, _lib.U64]),
+    "bcu_synth_zipf": (_lib.I32, [_lib.U64, ctypes.c_double, _lib.I32, _lib.PU32, _lib.I32]),
+}
+_S = None
+
+
+def lib():
+    """The generator library (built in-tree with the backend by `make -C glimpse-language_b200`)."""
+    global _S
+    if _S is None:
+        if not os.path.exists(SYNTH_PATH):
+            raise RuntimeError(f"{SYNTH_PATH} is missing: make -C glimpse-language_b200")
+        L = ctypes.CDLL(SYNTH_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _S = L
+    return _S
 
 PFX = "language_model.model."
 
@@ -21,7 +45,7 @@ def fill(kind, seed, stream, a, b, shape, dtype):
     n = arr.size // 16 if kind == 3 else arr.size
     if kind == 3:
         n = arr.size
-    s = _lib.lib().bcu_synth_fill(kind, seed, stream, a, b, arr.ctypes.data_as(ctypes.c_void_p), n)
+    s = lib().bcu_synth_fill(kind, seed, stream, a, b, arr.ctypes.data_as(ctypes.c_void_p), n)
     if s != _lib.OK:
         raise RuntimeError("bcu_synth_fill failed")
     return arr
@@ -106,9 +130,25 @@ def model_tensors(cfg, seed=1234):
     return ts
 
 
+def random_state(cfg, length, seed):
+    """A seeded committed state after `length` tokens, in the four state parts' layout (bcu_state_read): GDN
+    [gdn layer][NV][128][128] ~N(0, 0.02) (config 2's starting state), conv [gdn layer][3][C] ~N(0, 1), K and V
+    [attn layer][length][KV * 256] ~N(0, 1) (cached keys are RMS-normalised, so unit scale is their natural size).
+    Starts a pass at a long context without prefilling it (numpy's generator: same bytes on every host)."""
+    rng = np.random.default_rng(seed)
+    n_attn = sum(cfg.layer_is_attn[i] for i in range(cfg.n_layers))
+    n_gdn = cfg.n_layers - n_attn
+    d = dims(cfg)
+    gdn = rng.normal(0, 0.02, (n_gdn, cfg.lin_v_heads, 128, 128)).astype(np.float32)
+    conv = rng.normal(0, 1, (n_gdn, 3, d["C"])).astype(np.float32)
+    kc = rng.normal(0, 1, (n_attn, length, d["kvw"])).astype(np.float32)
+    vc = rng.normal(0, 1, (n_attn, length, d["kvw"])).astype(np.float32)
+    return gdn, conv, kc, vc
+
+
 def zipf_tokens(seed, n, vocab, s=1.1):
     out = np.empty(n, np.uint32)
-    _lib.lib().bcu_synth_zipf(seed, s, vocab, out.ctypes.data_as(_lib.PU32), n)
+    lib().bcu_synth_zipf(seed, s, vocab, out.ctypes.data_as(_lib.PU32), n)
     return out
 
 

@@ -188,17 +188,23 @@ bcu_status bcu_linear_set_local_build(bcu_linear* l, int32_t on) {
     return BCU_OK;
 }
 
+static int* static_error_word(int device);
+
 bcu_status bcu_linear_sync(bcu_linear* l, void* stream) {
     if (!l) return BCU_ERR_ARG;
     cudaSetDevice(l->device);
     if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return BCU_ERR_CUDA;
     int e = 0;
     if (cudaMemcpy(&e, l->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return BCU_ERR_CUDA;
-    if (e) {
-        cudaMemset(l->err, 0, 4);
-        return BCU_ERR_TIMEOUT;
+    if (e) cudaMemset(l->err, 0, 4);
+    // the error word of bcu_linear_rotate_forward_static (its static array), once that entry has run on this device
+    if (int* se = static_error_word(l->device)) {
+        int e2 = 0;
+        if (cudaMemcpy(&e2, se, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return BCU_ERR_CUDA;
+        if (e2) cudaMemset(se, 0, 4);
+        e |= e2;
     }
-    return BCU_OK;
+    return e ? BCU_ERR_TIMEOUT : BCU_OK;
 }
 
 // ------------------------------------------------------------------------------------------ no-allocation variant
@@ -206,9 +212,12 @@ bcu_status bcu_linear_sync(bcu_linear* l, void* stream) {
 // for callers that may not allocate device memory when they run the layer (a host whose device memory belongs to
 // its own pool, or a decode loop that must not stall on the synchronisation a cudaMalloc/cudaFree can cause).
 // Layout of the array: split-K partial sums (262144 floats, 1 MiB), then per-row-block counters (1024 words, so
-// O <= 131072 rows), then the error word. All calls share it: the counters and the error word are cleared on the
-// call's stream before its launch (the kernel's last CTA also leaves its counters at zero); the partial sums are
-// written before they are read. Calls that overlap on the GPU race on the array.
+// O <= 131072 rows), then the error word. All calls share it: the counters are cleared on the call's stream before
+// its launch (the kernel's last CTA also leaves them at zero); the partial sums are written before they are read.
+// The error word starts at zero with the module and is only ever OR-ed by a kernel that gave up a bounded wait, so
+// a failure stays recorded across later calls until bcu_linear_sync reads and clears it. Calls that overlap on the
+// GPU race on the array. The cached address belongs to the device's current primary context: after a
+// cudaDeviceReset the module is loaded again and the address must be looked up again (bcu_static_scratch_forget).
 constexpr size_t STATIC_PARTIAL_FLOATS = 262144;
 constexpr int STATIC_COUNTERS = 1024;
 constexpr size_t STATIC_SCRATCH_BYTES = STATIC_PARTIAL_FLOATS * 4 + STATIC_COUNTERS * 4 + 256;
@@ -230,6 +239,32 @@ static bcu_status static_scratch(int device, unsigned char** out) {
     return BCU_OK;
 }
 
+// The static entry's error word on `device`, or null when that entry has not run there yet.
+static int* static_error_word(int device) {
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    unsigned char* p = (unsigned char*)g_static_ptr[device];
+    return p ? (int*)(p + STATIC_PARTIAL_FLOATS * 4 + STATIC_COUNTERS * 4) : nullptr;
+}
+
+// Not in the ABI header. Drops the cached address of the static array on `device` (call after a cudaDeviceReset,
+// which reloads the module), and test hook: with plant != 0, first records a timeout in that device's error word,
+// as a kernel that gave up a wait would, so a test can check that bcu_linear_sync reports it.
+bcu_status bcu_static_scratch_debug(int32_t device, int32_t plant) {
+    if (plant) {
+        int* e = static_error_word(device);
+        if (!e) return BCU_ERR_STATE;
+        int v = ERR_MBAR_TIMEOUT;
+        if (cudaSetDevice(device) != cudaSuccess || cudaMemcpy(e, &v, 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return BCU_ERR_CUDA;
+        return BCU_OK;
+    }
+    if (device < 0 || device >= 64) return BCU_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    g_static_ptr[device] = nullptr;
+    return BCU_OK;
+}
+
 bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf16_dev, int32_t T, int32_t hadamard,
                                             const float* signs_dev, float* y_dev, void* stream) {
     if (!l || !x_bf16_dev || !y_dev || T < 1 || T > VMAX) return BCU_ERR_ARG;
@@ -247,7 +282,6 @@ bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf1
     unsigned* counters = (unsigned*)(scratch + STATIC_PARTIAL_FLOATS * 4);
     int* err = (int*)(scratch + STATIC_PARTIAL_FLOATS * 4 + STATIC_COUNTERS * 4);
     if (cudaMemsetAsync(counters, 0, (size_t)nrb * 4, st) != cudaSuccess) return BCU_ERR_CUDA;
-    if (cudaMemsetAsync(err, 0, 4, st) != cudaSuccess) return BCU_ERR_CUDA;
     ActSrc src;
     src.mode = ACT_EXT;
     src.xb = x_bf16_dev;

@@ -8,7 +8,7 @@
 #include <cstring>
 #include <vector>
 
-#include "../../include/bonsai_cuda.h"
+#include "../../include/bonsai_synth.h"
 
 namespace {
 

@@ -272,7 +272,8 @@ bcu_status bcu_linear_forward(bcu_linear* l, const float* x_dev, int32_t T, floa
  * memory accumulators, bulk-copy staging). Grows its activation scratch on the first call of a larger M (outside any
  * stream capture). Asynchronous: bcu_linear_sync waits and reports a device timeout. */
 bcu_status bcu_linear_gemm(bcu_linear* l, const float* x_dev, int32_t M, float* y_dev, void* stream);
-/* Waits for `stream` and returns BCU_ERR_TIMEOUT (clearing it) if a kernel of this handle gave up a bounded wait. */
+/* Waits for `stream` and returns BCU_ERR_TIMEOUT (clearing it) if a kernel of this handle, or a call of
+ * bcu_linear_rotate_forward_static on the handle's device (any handle), gave up a bounded wait. */
 bcu_status bcu_linear_sync(bcu_linear* l, void* stream);
 
 /* bcu_linear_rotate_forward for callers that may not allocate device memory when they run it: a host that hands
@@ -282,7 +283,8 @@ bcu_status bcu_linear_sync(bcu_linear* l, void* stream);
  * live in one static device array of 1 MiB + 4 KiB + 256 B in the library, so calls whose splits x T x O exceed
  * 262144 floats or whose O exceeds 131072 rows return BCU_ERR_TOO_LARGE. The first call on a device looks up that
  * array's address (make it before any stream capture). Every call shares the array and clears the counters it
- * needs on `stream` first; calls that overlap on the GPU (other streams, other threads) race on it. */
+ * needs on `stream` first; calls that overlap on the GPU (other streams, other threads) race on it. A wait that ran
+ * out is recorded in the array until bcu_linear_sync (on any handle of the device) reports and clears it. */
 bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf16_dev, int32_t T, int32_t hadamard,
                                             const float* signs_dev, float* y_dev, void* stream);
 
@@ -294,16 +296,6 @@ bcu_status bcu_linear_rotate_forward_static(bcu_linear* l, const uint16_t* x_bf1
 bcu_status bcu_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
                           const float* a_log, const float* dt_bias, float* state, float* y, int32_t T, int32_t NK,
                           int32_t NV, int32_t n, void* stream);
-
-/* ------------------------------------------------------------------ synthetic inputs */
-
-/* Deterministic seeded synthetic tensors (integer-only generators, identical on every host). kind: 0 = uniform
- * [a, b) fp32, 1 = approx-normal (mean a, std b) fp32, 2 = approx-normal bf16, 3 = ternary codes {0,1,2} packed
- * 16 per u32, 4 = uniform fp16 [a, b), 5 = +-1 fp32 signs, 6 = fp16 = -(value of another uniform fp16 stream)
- * (stream/seed as kind 4). n = elements (words for kind 3). */
-bcu_status bcu_synth_fill(int32_t kind, uint64_t seed, uint64_t stream, double a, double b, void* out, uint64_t n);
-/* Zipf(s) token ids in [0, vocab). */
-bcu_status bcu_synth_zipf(uint64_t seed, double s, int32_t vocab, uint32_t* out, int32_t n);
 
 /* ------------------------------------------------------------------ introspection */
 

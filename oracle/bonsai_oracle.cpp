@@ -772,6 +772,24 @@ void orc_model_restore(void* mp, const void* sp) {
 
 void orc_state_free(void* sp) { delete (Snap*)sp; }
 
+// Sets the committed state from the four parts of Text::state_parts (model.rs:1090-1099), the layout the device's
+// bcu_state_read/write use: GDN [gdn layer][NV][128][128], conv [gdn layer][3][C], K and V [attn layer][len][KV*256].
+// Lets a test start a pass at a long context without prefilling it. Returns -1 when len exceeds the context.
+int orc_model_set_state(void* mp, const float* gdn, const float* conv, const float* kc, const float* vc, int len) {
+    Model* m = (Model*)mp;
+    if (len < 0 || len > m->c.ctx) return -1;
+    std::copy(gdn, gdn + m->gdn.size(), m->gdn.begin());
+    std::copy(conv, conv + m->conv.size(), m->conv.begin());
+    size_t row = (size_t)m->kvw;
+    for (int a = 0; a < m->n_attn; a++) {
+        std::copy(kc + (size_t)a * len * row, kc + (size_t)(a + 1) * len * row, m->kc.begin() + (size_t)a * m->c.ctx * row);
+        std::copy(vc + (size_t)a * len * row, vc + (size_t)(a + 1) * len * row, m->vc.begin() + (size_t)a * m->c.ctx * row);
+    }
+    m->len = len;
+    m->pending = false;
+    return 0;
+}
+
 // One adapted linear (lora.rs:89-174): A [r][K] rounded to fp16, B [O][r] times fold rounded to fp16. Returns 0, or
 // -1 for an unknown layer/module or a shape mismatch. r = 0 removes it.
 int orc_model_set_lora(void* mp, int layer, const char* module, const float* a, const float* b, int r, float fold) {

@@ -52,6 +52,7 @@ def lib():
             "orc_model_snapshot": (P, [P]),
             "orc_model_restore": (None, [P, P]),
             "orc_state_free": (None, [P]),
+            "orc_model_set_state": (I, [P, P, P, P, P, I]),
             "orc_model_destroy": (None, [P]),
             "orc_greedy": (I, [P, ctypes.c_uint32, I, PU32, I, PU32]),
             "orc_model_set_lora": (I, [P, I, ctypes.c_char_p, P, P, I, ctypes.c_float]),
@@ -192,6 +193,12 @@ class OracleModel:
 
     def restore(self, s):
         lib().orc_model_restore(self.h, s)
+
+    def set_state(self, gdn, conv, kc, vc, length):
+        """The committed state from the four state parts (fp32 arrays in the bcu_state_read layout)."""
+        arrs = [np.ascontiguousarray(x, np.float32) for x in (gdn, conv, kc, vc)]
+        if lib().orc_model_set_state(self.h, *[ptr(x) for x in arrs], length) != 0:
+            raise ValueError("oracle: state longer than the context")
 
     def free_snapshot(self, s):
         lib().orc_state_free(s)

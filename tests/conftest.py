@@ -17,7 +17,7 @@ def pytest_configure(config):
     # the prebuilt files)
     if not os.path.exists(os.path.join(ROOT, "oracle", "_build", "libbonsai_oracle.so")):
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle")], check=True)
-    if not os.path.exists(os.path.join(PKG, "bonsai_b200", "libbonsai_cuda.so")):
+    if not all(os.path.exists(os.path.join(PKG, "bonsai_b200", f)) for f in ("libbonsai_cuda.so", "libbonsai_synth.so")):
         subprocess.run(["make", "-s", "-j8", "-C", PKG], check=True)
 
 

@@ -14,8 +14,8 @@ from oracle import oracle as orc
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def header_functions():
-    text = open(os.path.join(ROOT, "include", "bonsai_cuda.h")).read()
+def header_functions(name="bonsai_cuda.h"):
+    text = open(os.path.join(ROOT, "include", name)).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(bcu_[a-z0-9_]+)\s*\(", text)))
 
@@ -28,6 +28,15 @@ def test_exports_every_declared_symbol():
     assert not missing, missing
     for n in names:
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_synth_library_exports_its_header_and_backend_does_not():
+    names = header_functions("bonsai_synth.h")
+    assert names == ["bcu_synth_fill", "bcu_synth_zipf"]
+    S = synth.lib()
+    for n in names:
+        assert hasattr(S, n) and n in synth.SIGNATURES
+        assert not hasattr(_lib.lib(), n), f"{n} must not be in the CUDA backend"
 
 
 def test_config_check_mirrors_reference_rules():
@@ -47,9 +56,8 @@ def test_config_check_mirrors_reference_rules():
 
 
 def test_parse_reference_config_file():
-    path = "/root/reference/tests/data/config-2b.json"
-    if not os.path.exists(path):
-        pytest.skip("reference tree not present")
+    # the reference's own fixture (tests/data/config-2b.json), copied verbatim into tests/golden/
+    path = os.path.join(os.path.dirname(__file__), "golden", "ref_config-2b.json")
     c = config.parse_config(open(path).read())
     assert (c.hidden, c.intermediate, c.vocab, c.n_layers) == (2048, 6144, 248320, 24)
     assert (c.heads, c.kv_heads, c.lin_k_heads, c.lin_v_heads) == (8, 2, 16, 16)

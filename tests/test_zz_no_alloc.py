@@ -28,7 +28,8 @@ def _bf16_bits(torch, x):
     return torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("O,K,group,HB,signed", [(2048, 6144, 64, 512, True), (6144, 2048, 64, 2048, False)])
+@pytest.mark.parametrize("O,K,group,HB,signed", [(2048, 6144, 64, 512, True), (6144, 2048, 64, 2048, False),
+                                                  (2048, 2048, 128, 0, False)])
 def test_static_scratch_matches_allocating_entry(gpu, O, K, group, HB, signed):
     torch = pytest.importorskip("torch")
     L = _lib.lib()
@@ -51,10 +52,21 @@ def test_static_scratch_matches_allocating_entry(gpu, O, K, group, HB, signed):
             torch.cuda.synchronize()
             a, b = y_ref.cpu().numpy().astype(np.float64), y_new.cpu().numpy().astype(np.float64)
             assert np.isfinite(b).all()
-            _, xr = orc.rotate_ternary_linear(W, S, B, group, xb, HB, signs)
+            if HB:
+                want, xr = orc.rotate_ternary_linear(W, S, B, group, xb, HB, signs)
+            else:
+                xr = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).float().numpy()
+                want = orc.ternary_linear(W, S, B, group, xr)
             bound = 2e-5 * (np.abs(xr).astype(np.float64) @ np.abs(Wd).T) + 1e-5
             err = np.abs(a - b)
-            assert np.all(err <= bound), f"max err {err.max()}"
+            assert np.all(err <= bound), f"static vs allocating entry: max err {err.max()}"
+            err = np.abs(want.astype(np.float64) - b)
+            assert np.all(err <= bound), f"static entry vs oracle: max err {err.max()}"
+        # the error word of the static array: clean after these calls, and a recorded timeout is reported once
+        assert L.bcu_linear_sync(h, None) == _lib.OK
+        assert L.bcu_static_scratch_debug(0, 1) == _lib.OK
+        assert L.bcu_linear_sync(h, None) == _lib.ERR_TIMEOUT
+        assert L.bcu_linear_sync(h, None) == _lib.OK
     finally:
         L.bcu_linear_free(h)
 
@@ -76,5 +88,22 @@ def test_static_scratch_rejects_oversize(gpu):
         st = L.bcu_linear_rotate_forward_static(h, _vp(x), 9, 512, None, _vp(y), None)
         torch.cuda.synchronize()
         assert st == _lib.ERR_TOO_LARGE
+    finally:
+        L.bcu_linear_free(h)
+
+
+def test_static_scratch_rejects_too_many_row_blocks(gpu):
+    """131200 rows are 1025 row blocks: one more than the static array's 1024 counters."""
+    torch = pytest.importorskip("torch")
+    L = _lib.lib()
+    O, K, group = 131200, 512, 128
+    W = np.zeros((O, K // 16), np.uint32)
+    S = np.full((O, K // group), 0.01, dtype=np.float16).view(np.uint16)
+    h = ctypes.c_void_p()
+    assert L.bcu_linear_prepare(orc.ptr(W), orc.ptr(S), None, O, K, group, 0, ctypes.byref(h)) == _lib.OK
+    try:
+        x = torch.zeros((1, K), dtype=torch.int16, device="cuda")
+        y = torch.zeros((1, O), dtype=torch.float32, device="cuda")
+        assert L.bcu_linear_rotate_forward_static(h, _vp(x), 1, 0, None, _vp(y), None) == _lib.ERR_TOO_LARGE
     finally:
         L.bcu_linear_free(h)
