@@ -126,7 +126,10 @@ def model_tensors(cfg, seed=1234):
         packed(m + "up_proj", ff, d)
         packed(m + "down_proj", d, ff)
     norm(PFX + "norm.weight", d)
-    ts.add(PFX + "embed_tokens.weight", _lib.BF16, fill(2, seed, nxt(), 0.0, 0.02, (cfg.vocab, d), np.uint16))
+    if cfg.head_kind == 1:  # the reference's tied table: ternary-packed like the linears (model.rs:356, 962)
+        packed(PFX + "embed_tokens", cfg.vocab, d)
+    else:
+        ts.add(PFX + "embed_tokens.weight", _lib.BF16, fill(2, seed, nxt(), 0.0, 0.02, (cfg.vocab, d), np.uint16))
     return ts
 
 

@@ -6,11 +6,13 @@
 // function cites the reference lines it follows. OpenMP parallelises over output rows and heads only; each output is
 // computed by one thread in a fixed order, so results do not depend on the thread count.
 //
-// PARITY UNPINNED: the reference cannot be built or run here (no Rust toolchain, Metal is macOS-only, Vulkan needs
-// a graphics stack), and its only golden vectors (tests/golden/*/*.json) are MLX text outputs of the real PrismML
-// weights, which are not available. The restatement is pinned instead by independent known-answer checks in
-// tests/ (IEEE fp16/bf16 rounding against numpy, the Walsh-Hadamard transform against the Sylvester matrix, the
-// gated delta rule against its closed form on small cases) and by the fixtures in tests/golden/.
+// PINNED TO THE REFERENCE: the reference's own Metal text kernels (kernels.metal) are compiled for the host from
+// the reference tree (oracle/Makefile, oracle/ref_metal/: a Metal-language shim and a threadgroup scheduler) and
+// run in the reference's layer sequence (model.rs); tests/test_ref_pin.py checks this restatement against them
+// kernel by kernel (bit-exact where nothing reduces) and for whole passes of a model in the reference's format.
+// The host logic (drafting, policy, the prefix file) is Rust, which cannot be compiled here: it is pinned by
+// known-answer checks in tests/ only. The reference's golden vectors (tests/golden/*/*.json) are MLX text outputs
+// of the real PrismML weights, which are not available.
 //
 // Build: oracle/Makefile (g++ -O2 -fopenmp -ffp-contract=off), output under oracle/_build/.
 
@@ -118,6 +120,63 @@ float rms_scale(const float* x, int D) {
 }
 
 inline float sigmoidf_(float a) { return 1.0f / (1.0f + std::exp(-a)); }
+
+// norm_rotate (kernels.metal:118-144) on T rows of D: xn = rmsnorm(h) * w; xr = rotate(signs * xn).
+void norm_rotate_rows(const float* h, const float* w, const float* signs, int D, int HB, int T, float* xn, float* xr) {
+    for (int t = 0; t < T; t++) {
+        const float* x = h + (size_t)t * D;
+        float r = rms_scale(x, D);
+        float* o = xn + (size_t)t * D;
+        for (int i = 0; i < D; i++) o[i] = x[i] * r * w[i];
+        rotate(o, signs, D, HB, xr + (size_t)t * D);
+    }
+}
+
+// swiglu_rotate (kernels.metal:147-164): xr = rotate(signs * (g * u) * sigmoid(g)); xu = the unrotated product.
+void swiglu_rotate_rows(const float* g, const float* u, const float* signs, int D, int HB, int T, float* xu,
+                        float* xr) {
+    for (int t = 0; t < T; t++) {
+        float* xo = xu + (size_t)t * D;
+        for (int e = 0; e < D; e++) {
+            float a = g[(size_t)t * D + e];
+            xo[e] = (a * u[(size_t)t * D + e]) * (1.0f / (1.0f + std::exp(-a)));
+        }
+        rotate(xo, signs, D, HB, xr + (size_t)t * D);
+    }
+}
+
+// gate_rotate (kernels.metal:170-188): x[e] = attn[e] * sigmoid(gate), the gate from the q projection output
+// (per head 256 q then 256 gate values); xr = rotate(signs * x).
+void gate_rotate_rows(const float* attn, const float* qp, const float* signs, int W, int HB, int T, float* xu,
+                      float* xr) {
+    for (int t = 0; t < T; t++) {
+        float* xo = xu + (size_t)t * W;
+        for (int e = 0; e < W; e++) {
+            int hd = e >> 8, dd = e & 255;
+            float gt = qp[(size_t)t * 2 * W + hd * 512 + 256 + dd];
+            xo[e] = attn[(size_t)t * W + e] * sigmoidf_(gt);
+        }
+        rotate(xo, signs, W, HB, xr + (size_t)t * W);
+    }
+}
+
+// gated_norm_rotate (kernels.metal:199-226): per 128-wide head, a * y * rmsnorm scale * w * sigmoid(a) with a the
+// z projection (the reference's product order); xr = rotate(signs * x).
+void gated_norm_rotate_rows(const float* y, const float* z, const float* w, const float* signs, int W, int HB, int T,
+                            float* xu, float* xr) {
+    for (int t = 0; t < T; t++) {
+        float* xo = xu + (size_t)t * W;
+        for (int hd = 0; hd < W / 128; hd++) {
+            const float* yh = y + (size_t)t * W + hd * 128;
+            float r = rms_scale(yh, 128);
+            for (int dd = 0; dd < 128; dd++) {
+                float a = z[(size_t)t * W + hd * 128 + dd];
+                xo[hd * 128 + dd] = (((a * yh[dd]) * r) * w[dd]) * sigmoidf_(a);
+            }
+        }
+        rotate(xo, signs, W, HB, xr + (size_t)t * W);
+    }
+}
 
 // ----------------------------------------------------------------------------------------------- ternary linear
 // y[t][o] = sum over groups of (s * sum(c * x) + b * sum(x)), c the 2-bit code (MLX affine: w = s * c + b); with
@@ -297,6 +356,30 @@ size_t conv_state_size(const Model* m) { return (size_t)3 * m->C; }
 
 // embed (kernels.metal:230-246) for the ternary tied table: (code - 1) * scale rounded to fp16 (or c*s + b), fwht,
 // * INV_SQRT * signs, rounded to fp16. bf16 table: the row as is.
+// embed (kernels.metal:230-246) of one row of a ternary tied table: (code - 1) * scale (or c * s + b) rounded to
+// fp16, fwht, * INV_SQRT * signs, rounded to fp16.
+void embed_ternary_row(const uint32_t* W, const uint16_t* S, const uint16_t* Bi, const float* signs, int group, int HB,
+                       int d, uint32_t id, float* out) {
+    int kg = d / group;
+    std::vector<float> v(d);
+    for (int k = 0; k < d; k++) {
+        uint32_t wd = W[(size_t)id * (d / 16) + k / 16];
+        float c = (float)((wd >> (2 * (k & 15))) & 3u);
+        float s = f16_to_f32(S[(size_t)id * kg + k / group]);
+        float w = Bi ? c * s + f16_to_f32(Bi[(size_t)id * kg + k / group]) : (c - 1.0f) * s;
+        v[k] = f16_to_f32(f32_to_f16(w));
+    }
+    float inv = HB == 512 ? 0.044194173824159216f : (float)(1.0 / std::sqrt((double)HB));
+    for (int b0 = 0; b0 < d; b0 += HB) {
+        fwht(v.data() + b0, HB);
+        for (int i = 0; i < HB; i++) {
+            float sg = signs ? signs[b0 + i] : 1.0f;
+            out[b0 + i] = f16_to_f32(f32_to_f16(v[b0 + i] * inv * sg));
+        }
+    }
+}
+
+// embed (kernels.metal:230-246) for the ternary tied table; the bf16 table: the row as is.
 void embed_row(const Model* m, uint32_t id, float* out) {
     int d = m->c.hidden;
     if (m->c.head_kind == BCU_HEAD_BF16) {
@@ -304,35 +387,12 @@ void embed_row(const Model* m, uint32_t id, float* out) {
         return;
     }
     const Lin& e = m->head;
-    int kg = d / m->c.group_size, HB = m->c.hadamard;
-    std::vector<float> v(d);
-    for (int k = 0; k < d; k++) {
-        uint32_t wd = e.w[(size_t)id * (d / 16) + k / 16];
-        float c = (float)((wd >> (2 * (k & 15))) & 3u);
-        float s = f16_to_f32(e.s[(size_t)id * kg + k / m->c.group_size]);
-        float w = e.b ? c * s + f16_to_f32(e.b[(size_t)id * kg + k / m->c.group_size]) : (c - 1.0f) * s;
-        v[k] = f16_to_f32(f32_to_f16(w));
-    }
-    float inv = HB == 512 ? 0.044194173824159216f : (float)(1.0 / std::sqrt((double)HB));
-    for (int b0 = 0; b0 < d; b0 += HB) {
-        fwht(v.data() + b0, HB);
-        for (int i = 0; i < HB; i++) {
-            float sg = (m->c.has_signs && e.signs) ? e.signs[b0 + i] : 1.0f;
-            out[b0 + i] = f16_to_f32(f32_to_f16(v[b0 + i] * inv * sg));
-        }
-    }
+    embed_ternary_row(e.w, e.s, e.b, m->c.has_signs ? e.signs : nullptr, m->c.group_size, m->c.hadamard, d, id, out);
 }
 
 // norm_rotate (kernels.metal:118-144): xn = rmsnorm(h) * w; xr = rotate(signs * xn).
 void norm_rotate(const Model* m, const float* h, const float* w, const float* signs, int T, float* xn, float* xr) {
-    int D = m->c.hidden;
-    for (int t = 0; t < T; t++) {
-        const float* x = h + (size_t)t * D;
-        float r = rms_scale(x, D);
-        float* o = xn + (size_t)t * D;
-        for (int i = 0; i < D; i++) o[i] = x[i] * r * w[i];
-        rotate(o, m->c.has_signs ? signs : nullptr, D, m->c.hadamard, xr + (size_t)t * D);
-    }
+    norm_rotate_rows(h, w, m->c.has_signs ? signs : nullptr, m->c.hidden, m->c.hadamard, T, xn, xr);
 }
 
 // One forward of T rows from the committed state: Text::encode_layers(verify = true) + encode_head
@@ -416,18 +476,8 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
                 }
             }
             std::vector<float> xu((size_t)T * gw);
-            for (int t = 0; t < T; t++) {
-                float* xo = xu.data() + (size_t)t * gw;
-                for (int hd = 0; hd < NV; hd++) {
-                    const float* yh = y.data() + (size_t)t * gw + hd * 128;
-                    float r = rms_scale(yh, 128);
-                    for (int dd = 0; dd < 128; dd++) {
-                        float a = a2[(size_t)t * gw + hd * 128 + dd];
-                        xo[hd * 128 + dd] = (((a * yh[dd]) * r) * L.gnorm[dd]) * sigmoidf_(a);
-                    }
-                }
-                rotate(xo, c.has_signs ? L.out.signs : nullptr, gw, HB, xr.data() + (size_t)t * gw);
-            }
+            gated_norm_rotate_rows(y.data(), a2.data(), L.gnorm, c.has_signs ? L.out.signs : nullptr, gw, HB, T,
+                                   xu.data(), xr.data());
             ternary_linear(L.out.w, L.out.s, L.out.b, d, gw, c.group_size, xr.data(), T, tmp.data());
             for (size_t i = 0; i < (size_t)T * d; i++) h[i] += tmp[i];
             lora_add(L.out, xu.data(), T, h.data());
@@ -482,15 +532,7 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
                 for (int dd = 0; dd < 256; dd++) y[(size_t)t * aw + hh * 256 + dd] = acc[dd] / l;
             }
             std::vector<float> xu((size_t)T * aw);
-            for (int t = 0; t < T; t++) {
-                float* xo = xu.data() + (size_t)t * aw;
-                for (int e = 0; e < aw; e++) {
-                    int hd = e >> 8, dd = e & 255;
-                    float gt = qp[(size_t)t * 2 * aw + hd * 512 + 256 + dd];
-                    xo[e] = y[(size_t)t * aw + e] * sigmoidf_(gt);
-                }
-                rotate(xo, c.has_signs ? L.o.signs : nullptr, aw, HB, xr.data() + (size_t)t * aw);
-            }
+            gate_rotate_rows(y.data(), qp.data(), c.has_signs ? L.o.signs : nullptr, aw, HB, T, xu.data(), xr.data());
             ternary_linear(L.o.w, L.o.s, L.o.b, d, aw, c.group_size, xr.data(), T, tmp.data());
             for (size_t i = 0; i < (size_t)T * d; i++) h[i] += tmp[i];
             lora_add(L.o, xu.data(), T, h.data());
@@ -502,14 +544,7 @@ void forward(Model* m, const uint32_t* ids, int T, float* logits, uint32_t* pred
         lora_add(L.gate, xn.data(), T, a1.data());
         lora_add(L.up, xn.data(), T, a2.data());
         std::vector<float> xu((size_t)T * ff);
-        for (int t = 0; t < T; t++) {
-            float* xo = xu.data() + (size_t)t * ff;
-            for (int e = 0; e < ff; e++) {
-                float a = a1[(size_t)t * ff + e];
-                xo[e] = (a * a2[(size_t)t * ff + e]) * (1.0f / (1.0f + std::exp(-a)));
-            }
-            rotate(xo, c.has_signs ? L.down.signs : nullptr, ff, HB, xr.data() + (size_t)t * ff);
-        }
+        swiglu_rotate_rows(a1.data(), a2.data(), c.has_signs ? L.down.signs : nullptr, ff, HB, T, xu.data(), xr.data());
         ternary_linear(L.down.w, L.down.s, L.down.b, d, ff, c.group_size, xr.data(), T, tmp.data());
         for (size_t i = 0; i < (size_t)T * d; i++) h[i] += tmp[i];
         lora_add(L.down, xu.data(), T, h.data());
@@ -579,6 +614,28 @@ float orc_bf16_to_f32(uint16_t h) { return bf16_to_f32(h); }
 uint16_t orc_f32_to_bf16(float f) { return f32_to_bf16(f); }
 
 void orc_fwht(float* x, int n) { fwht(x, n); }
+
+// The rotation producers and the embedding on their own (the pieces forward() runs), for kernel-level checks.
+void orc_norm_rotate(const float* h, const float* w, const float* signs, int D, int HB, int T, float* xn, float* xr) {
+    norm_rotate_rows(h, w, signs, D, HB, T, xn, xr);
+}
+void orc_swiglu_rotate(const float* g, const float* u, const float* signs, int D, int HB, int T, float* xr) {
+    std::vector<float> xu((size_t)T * D);
+    swiglu_rotate_rows(g, u, signs, D, HB, T, xu.data(), xr);
+}
+void orc_gate_rotate(const float* attn, const float* qp, const float* signs, int W, int HB, int T, float* xr) {
+    std::vector<float> xu((size_t)T * W);
+    gate_rotate_rows(attn, qp, signs, W, HB, T, xu.data(), xr);
+}
+void orc_gated_norm_rotate(const float* y, const float* z, const float* w, const float* signs, int W, int HB, int T,
+                           float* xr) {
+    std::vector<float> xu((size_t)T * W);
+    gated_norm_rotate_rows(y, z, w, signs, W, HB, T, xu.data(), xr);
+}
+void orc_embed_ternary(const uint32_t* W, const uint16_t* S, const uint16_t* B, const float* signs, int group, int HB,
+                       int d, const uint32_t* ids, int T, float* out) {
+    for (int t = 0; t < T; t++) embed_ternary_row(W, S, B, signs, group, HB, d, ids[t], out + (size_t)t * d);
+}
 void orc_rotate(const float* x, const float* signs, int D, int HB, float* out) { rotate(x, signs, D, HB, out); }
 
 void orc_ternary_linear(const uint32_t* W, const uint16_t* S, const uint16_t* B, int O, int K, int group,

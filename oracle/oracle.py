@@ -1,7 +1,8 @@
 """ctypes wrapper of the CPU oracle (oracle/bonsai_oracle.cpp). TEST INFRASTRUCTURE ONLY: imported by tests/,
 __graft_entry__.smoke() and bench.py's cpu_baseline leg as the checker; never part of the product path.
 
-Parity unpinned against the reference itself (Rust + Metal/Vulkan, not runnable here); see bonsai_oracle.cpp.
+Pinned to the reference's own Metal kernels compiled for the host (oracle/ref.py, tests/test_ref_pin.py); the host
+logic restated from Rust (drafting, policy) is pinned by known-answer tests only.
 """
 import ctypes
 import os
@@ -36,6 +37,11 @@ def lib():
             "orc_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
             "orc_fwht": (None, [P, I]),
             "orc_rotate": (None, [P, P, I, I, P]),
+            "orc_norm_rotate": (None, [P, P, P, I, I, I, P, P]),
+            "orc_swiglu_rotate": (None, [P, P, P, I, I, I, P]),
+            "orc_gate_rotate": (None, [P, P, P, I, I, I, P]),
+            "orc_gated_norm_rotate": (None, [P, P, P, P, I, I, I, P]),
+            "orc_embed_ternary": (None, [P, P, P, P, I, I, I, PU32, I, P]),
             "orc_ternary_linear": (None, [P, P, P, I, I, I, P, I, P]),
             "orc_rotate_ternary_linear": (None, [P, P, P, I, I, I, P, I, I, P, P, P]),
             "orc_gdn_verify": (None, [P, P, P, P, P, P, P, P, P, I, I, I, I]),
@@ -103,6 +109,51 @@ def rotate(x, HB, signs=None):
     x = np.ascontiguousarray(x, np.float32)
     out = np.zeros_like(x)
     lib().orc_rotate(ptr(x), ptr(signs) if signs is not None else None, x.size, HB, ptr(out))
+    return out
+
+
+def _f(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def norm_rotate(h, w, signs, HB=512):
+    h = _f(h)
+    T, D = h.shape
+    xn, xr = np.zeros_like(h), np.zeros_like(h)
+    lib().orc_norm_rotate(ptr(h), ptr(_f(w)), ptr(_f(signs)) if signs is not None else None, D, HB, T, ptr(xn), ptr(xr))
+    return xn, xr
+
+
+def swiglu_rotate(g, u, signs, HB=512):
+    g, u = _f(g), _f(u)
+    T, D = g.shape
+    xr = np.zeros_like(g)
+    lib().orc_swiglu_rotate(ptr(g), ptr(u), ptr(_f(signs)) if signs is not None else None, D, HB, T, ptr(xr))
+    return xr
+
+
+def gate_rotate(attn, qp, signs, HB=512):
+    attn, qp = _f(attn), _f(qp)
+    T, W = attn.shape
+    xr = np.zeros_like(attn)
+    lib().orc_gate_rotate(ptr(attn), ptr(qp), ptr(_f(signs)) if signs is not None else None, W, HB, T, ptr(xr))
+    return xr
+
+
+def gated_norm_rotate(y, z, w, signs, HB=512):
+    y, z = _f(y), _f(z)
+    T, W = y.shape
+    xr = np.zeros_like(y)
+    lib().orc_gated_norm_rotate(ptr(y), ptr(z), ptr(_f(w)), ptr(_f(signs)) if signs is not None else None, W, HB, T,
+                                ptr(xr))
+    return xr
+
+
+def embed_ternary(W, S, B, signs, group, HB, d, ids):
+    ids = np.ascontiguousarray(ids, np.uint32)
+    out = np.zeros((len(ids), d), np.float32)
+    lib().orc_embed_ternary(ptr(W), ptr(S), ptr(B) if B is not None else None,
+                            ptr(_f(signs)) if signs is not None else None, group, HB, d, u32p(ids), len(ids), ptr(out))
     return out
 
 
