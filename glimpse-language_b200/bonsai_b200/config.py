@@ -46,10 +46,13 @@ def bonsai_4b_graded(ctx=4608):
 
 
 def tiny(*, group_size=64, has_bias=True, hadamard=512, has_signs=True, n_layers=4, vocab=4096, kv_heads=2, ctx=256,
-         hidden=512, intermediate=1024, heads=4, lin_k_heads=2, lin_v_heads=4):
-    """Small shapes for parity tests (every kernel path, seconds on the oracle)."""
-    return make_config(hidden, intermediate, vocab, n_layers, heads, kv_heads, lin_k_heads, lin_v_heads,
-                       group_size=group_size, has_bias=has_bias, hadamard=hadamard, has_signs=has_signs, ctx=ctx)
+         hidden=512, intermediate=1024, heads=4, lin_k_heads=2, lin_v_heads=4, head_kind=0):
+    """Small shapes for parity tests (every kernel path, seconds on the oracle). head_kind 1: the reference's ternary
+    tied embedding / head."""
+    c = make_config(hidden, intermediate, vocab, n_layers, heads, kv_heads, lin_k_heads, lin_v_heads,
+                    group_size=group_size, has_bias=has_bias, hadamard=hadamard, has_signs=has_signs, ctx=ctx)
+    c.head_kind = head_kind
+    return c
 
 
 def parse_config(text):

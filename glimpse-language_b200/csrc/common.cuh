@@ -158,6 +158,18 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return warp_max(r);
 }
 
+// The id of row t of this pass: the host's ids, the previous pass's bonus token (feed 1, row 0), or the planted
+// draft stream (feed 2).
+__device__ __forceinline__ uint32_t resolve_id(const Ctl* ctl, int t) {
+    int feed = ctl->in.feed;
+    if (feed == 1 && t == 0) return ctl->bonus;
+    if (feed == 2 && ctl->planted) {
+        int i = ctl->off - ctl->in.planted_base + t;
+        if (i >= 0 && i < ctl->planted_n) return ctl->planted[i];
+    }
+    return ctl->in.ids[t];
+}
+
 // Argmax merge with the reference's tie rule (kernels.metal:820,839): larger value wins, equal values go to the
 // lower index; NaN never wins.
 __device__ __forceinline__ void argmax_merge(float& bv, int& bi, float ov, int oi) {

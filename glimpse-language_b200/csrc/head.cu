@@ -77,6 +77,48 @@ __host__ __device__ inline size_t head_smem_bytes(int d, int nt, int stages) {
     return (size_t)(d / 16) * nt * 256 + (size_t)8 * stages * 4096 + (size_t)8 * stages * 8;
 }
 
+// End of the head (all CTAs): count this CTA's published (max, index) partials; the last CTA to arrive merges them in
+// CTA order, computes the predictions, the accept length m on the device (leading drafts equal to the predictions,
+// decode_spec's accept, runtime/mod.rs:866-868) and advances the control block (KV offset, replay count, parity).
+__device__ void head_finish(const HeadArgs& a, int T) {
+    __shared__ int s_last;
+    __shared__ uint32_t pred[16];
+    const int tid = threadIdx.x;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid < T) {
+        float v = -INFINITY;
+        int i = 0x7fffffff;
+        for (int c = 0; c < (int)gridDim.x; c++)
+            argmax_merge(v, i, __ldcg(a.pv + (size_t)c * T + tid), __ldcg(a.pi + (size_t)c * T + tid));
+        if (i == 0x7fffffff) i = 0;  // every logit NaN or -inf: index 0, like argmax2's initial value
+        pred[tid] = (uint32_t)i;
+        a.ctl->pred[tid] = (uint32_t)i;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        Ctl* c = a.ctl;
+        int m;
+        if (c->in.commit_all) {
+            m = T - 1;
+        } else {
+            m = 0;
+            while (m < T - 1 && c->used[m + 1] == pred[m]) m++;
+        }
+        c->accepted = m;
+        c->bonus = pred[m];
+        int nrows = c->in.commit_all ? T : m + 1;
+        c->replay_n = nrows;
+        c->off += nrows;
+        c->parity ^= 1;
+        *a.counter = 0;
+    }
+}
+
 // One CTA per SM, 8 warps; warp w streams a contiguous range of 16-row m-tiles (a contiguous byte range of the
 // repacked table) through its shared-memory ring with 4-KB bulk copies (cp.async.bulk, no multicast), so each warp
 // keeps a.stages x 4 KB of the table in flight while its tensor-core products run (head_stages(), fewer when the
@@ -88,7 +130,6 @@ __global__ void __launch_bounds__(256, 1) head_kernel(HeadArgs a) {
     uint2* s_b = (uint2*)smem;
     __shared__ float wbv[8][16];
     __shared__ int wbi[8][16];
-    __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nks = a.d / 16;
     const int T = a.T;
@@ -196,40 +237,7 @@ __global__ void __launch_bounds__(256, 1) head_kernel(HeadArgs a) {
         a.pv[(size_t)blockIdx.x * T + tid] = v;
         a.pi[(size_t)blockIdx.x * T + tid] = i;
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.counter, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    __shared__ uint32_t pred[16];
-    if (tid < T) {
-        float v = -INFINITY;
-        int i = 0x7fffffff;
-        for (int c = 0; c < (int)gridDim.x; c++)
-            argmax_merge(v, i, __ldcg(a.pv + (size_t)c * T + tid), __ldcg(a.pi + (size_t)c * T + tid));
-        if (i == 0x7fffffff) i = 0;  // every logit NaN or -inf: index 0, like argmax2's initial value
-        pred[tid] = (uint32_t)i;
-        a.ctl->pred[tid] = (uint32_t)i;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        Ctl* c = a.ctl;
-        int m;
-        if (c->in.commit_all) {
-            m = T - 1;
-        } else {
-            m = 0;
-            while (m < T - 1 && c->used[m + 1] == pred[m]) m++;
-        }
-        c->accepted = m;
-        c->bonus = pred[m];
-        int nrows = c->in.commit_all ? T : m + 1;
-        c->replay_n = nrows;
-        c->off += nrows;
-        c->parity ^= 1;
-        *a.counter = 0;
-    }
+    head_finish(a, T);
 }
 
 template <int NT>
@@ -253,6 +261,124 @@ void launch_head(const HeadArgs& a, int NT, int grid, cudaStream_t st) {
     else if (NT == 2) launch_head_t<2>(a, grid, st);
     else if (NT == 3) launch_head_t<3>(a, grid, st);
     else launch_head_t<4>(a, grid, st);
+}
+
+// ------------------------------------------------------------------------------------------------ ternary tied table
+// The reference's own embedding and head (model.rs:356, 941-985): a ternary-packed tied table [V][d] with Hadamard
+// signs. The head is the ternary GEMV (final norm + rotation by the table's signs, then the table) writing fp32
+// logits; head_argmax_kernel then takes the per-row argmax and ends the pass like head_kernel.
+
+// embed (kernels.metal:230-246) of each row of the pass: code -> (c - 1) s (or c s + b) rounded to fp16, the
+// 512-point transform in fwht512's lane layout (strides 1..16 across lanes, 32..256 in-lane: bit-identical to the
+// in-memory order), x INV_SQRT512 x sign rounded to fp16, written to the residual rows h. Also the row-block sums
+// of squares the first GEMV's RMSNorm reads ([d/128][VMAX]: lane l holds elements l + 32 e, so row block e / 4), and
+// the ids the pass embedded. One CTA per row, one warp per 512 inputs.
+__global__ void __launch_bounds__(256) embed_ternary_kernel(EmbedArgs a) {
+    pdl_trigger();
+    pdl_wait();  // the ids may be the previous pass's bonus token
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int d = a.d, b0 = warp * 512;
+    if (b0 >= d) return;
+    uint32_t id = resolve_id(a.ctl, t);
+    if (warp == 0 && lane == 0) {
+        a.ctl->used[t] = id;
+        if (id >= (uint32_t)a.V) atomicOr(&a.ctl->err, ERR_BAD_TOKEN);
+    }
+    if (id >= (uint32_t)a.V) id = 0;
+    const int kw = d / 16, kg = d / a.group;
+    const uint32_t* wr = a.w + (size_t)id * kw;
+    float v[16];
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+        const int k = b0 + lane + 32 * e;
+        const float c = (float)((wr[k >> 4] >> (2 * (k & 15))) & 3u);
+        const float sc = __half2float(__ushort_as_half(a.s[(size_t)id * kg + k / a.group]));
+        const float w = a.b ? __fadd_rn(__fmul_rn(c, sc), __half2float(__ushort_as_half(a.b[(size_t)id * kg + k / a.group])))
+                            : __fmul_rn(c - 1.0f, sc);
+        v[e] = __half2float(__float2half_rn(w));
+    }
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool up = (lane & m) != 0;
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[e], m);
+            v[e] = up ? __fsub_rn(o, v[e]) : __fadd_rn(v[e], o);
+        }
+    }
+#pragma unroll
+    for (int h = 1; h < 16; h <<= 1)
+#pragma unroll
+        for (int e = 0; e < 16; e++)
+            if ((e & h) == 0) {
+                const float x = v[e], y = v[e + h];
+                v[e] = __fadd_rn(x, y);
+                v[e + h] = __fsub_rn(x, y);
+            }
+    float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+        const int k = b0 + lane + 32 * e;
+        const float sg = a.signs ? a.signs[k] : 1.0f;
+        const float x = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(v[e], 0.044194173824159216f), sg)));
+        a.h[(size_t)t * d + k] = x;
+        ss[e >> 2] = __fadd_rn(ss[e >> 2], __fmul_rn(x, x));
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const float tot = warp_sum(ss[r]);
+        if (lane == 0) a.ss[(size_t)(b0 / 128 + r) * VMAX + t] = tot;
+    }
+}
+
+void launch_embed_ternary(const EmbedArgs& a, cudaStream_t st) {
+    EmbedArgs aa = a;
+    void* args[] = {&aa};
+    launch_pdl((const void*)embed_ternary_kernel, dim3(a.T), dim3(32 * (a.d / 512)), 0, st, args);
+}
+
+// Argmax over the logits [T][V] the ternary head GEMV wrote (argmax1/argmax2, kernels.metal:802-842): CTA c scans a
+// contiguous range of the vocabulary for every row (256 threads strided, then the warp and block merges, lowest index
+// on ties), publishes its partials and ends the pass through head_finish.
+__global__ void __launch_bounds__(256) head_argmax_kernel(HeadArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float wbv[8][VMAX];
+    __shared__ int wbi[8][VMAX];
+    const int T = a.T, V = a.V, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (V + gridDim.x - 1) / gridDim.x;
+    const int v0 = min(V, (int)blockIdx.x * per), v1 = min(V, v0 + per);
+    for (int t = 0; t < T; t++) {
+        const float* row = a.logits + (size_t)t * V;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int i = v0 + tid; i < v1; i += 256) argmax_merge(bv, bi, __ldcg(row + i), i);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            argmax_merge(bv, bi, ov, oi);
+        }
+        if (lane == 0) {
+            wbv[warp][t] = bv;
+            wbi[warp][t] = bi;
+        }
+    }
+    __syncthreads();
+    if (tid < T) {
+        float v = -INFINITY;
+        int i = 0x7fffffff;
+        for (int w = 0; w < 8; w++) argmax_merge(v, i, wbv[w][tid], wbi[w][tid]);
+        a.pv[(size_t)blockIdx.x * T + tid] = v;
+        a.pi[(size_t)blockIdx.x * T + tid] = i;
+    }
+    head_finish(a, T);
+}
+
+void launch_head_argmax(const HeadArgs& a, int grid, cudaStream_t st) {
+    HeadArgs aa = a;
+    void* args[] = {&aa};
+    launch_pdl((const void*)head_argmax_kernel, dim3(grid), dim3(256), 0, st, args);
 }
 
 }  // namespace bcu

@@ -163,6 +163,23 @@ struct HeadArgs {
     int stages = 0;          // 4-KB table units in flight per warp (set by launch_head)
 };
 void launch_head(const HeadArgs& a, int NT, int grid, cudaStream_t st);
+// Ternary tied table (the reference's format): the head is a ternary GEMV into logits, then this argmax + accept
+// kernel (uses ctl, logits, pv, pi, counter, V, T).
+void launch_head_argmax(const HeadArgs& a, int grid, cudaStream_t st);
+
+// Embedding rows of the ternary tied table (embed, kernels.metal:230-246) into the residual rows, with their
+// row-block sums of squares for the first GEMV's RMSNorm.
+struct EmbedArgs {
+    Ctl* ctl;
+    const uint32_t* w;       // MLX pack [V][d/16]
+    const uint16_t* s;       // fp16 scales [V][d/group]
+    const uint16_t* b;       // fp16 biases or null (the reference pack: weight = s (code - 1))
+    const float* signs;      // [d] or null
+    float* h;                // [T][d]
+    float* ss;               // [d/128][VMAX]
+    int V, d, group, T;
+};
+void launch_embed_ternary(const EmbedArgs& a, cudaStream_t st);
 // Largest hidden size whose head operand fits beside one ring stage (16-row tiles of 4 tokens, 16 rows at T = 16).
 constexpr int HEAD_MAX_HIDDEN = 3072;
 

@@ -65,6 +65,10 @@ struct bcu_model {
     std::vector<bcu::Layer> layers;
     uint32_t* head_w = nullptr;     // fragment-ordered bf16 table
     uint16_t* embed_rows = nullptr; // row-major bf16 table (gathers)
+    // ternary tied table (BCU_HEAD_TERNARY): the head GEMV's matrix (signs: the table's) and the MLX pack for gathers
+    bcu::Lin head_lin;
+    const uint32_t* emb_w = nullptr;
+    const uint16_t *emb_s = nullptr, *emb_b = nullptr;
     const float* final_norm = nullptr;
     float* inv_freq = nullptr;
 

@@ -98,7 +98,9 @@ bcu_status check_config(const bcu_config* c, std::string* why) {
         if (d % c->hadamard) return bad("activation widths must be multiples of the hadamard block");
     if (C % 128 || (2 * aw + 2 * kvw) % 128) return bad("projection widths must be multiples of 128");
     if (c->vocab < 16 || c->vocab % 16) return bad("vocab must be a multiple of 16");
-    if (c->head_kind != BCU_HEAD_BF16) return bad("only the bf16 tied head is implemented on the device");
+    if (c->head_kind != BCU_HEAD_BF16 && c->head_kind != BCU_HEAD_TERNARY) return bad("unknown head kind");
+    if (c->head_kind == BCU_HEAD_TERNARY && (c->hadamard != 512 || c->vocab % 128))
+        return bad("the ternary tied table needs 512-point rotation blocks and a vocab multiple of 128");
     int half = c->rotary_dims / 2;
     if (c->rotary_dims % 2 || c->rotary_dims > 256 || c->mrope[0] + c->mrope[1] + c->mrope[2] != half)
         return bad("rotary dims / mrope sections");
@@ -265,10 +267,27 @@ void enqueue_pass(bcu_model* m, int T) {
     resid.out = m->h;
     resid.add = 1;
     resid.ss_out = m->ssbuf;
+    const bool ternary_head = c.head_kind == BCU_HEAD_TERNARY;
+    if (ternary_head) {  // embed (kernels.metal:230-246) into h and its row-block sums of squares
+        EmbedArgs e;
+        e.ctl = m->ctl;
+        e.w = m->emb_w;
+        e.s = m->emb_s;
+        e.b = m->emb_b;
+        e.signs = m->head_lin.signs;
+        e.h = m->h;
+        e.ss = m->ssbuf;
+        e.V = c.vocab;
+        e.d = d;
+        e.group = c.group_size;
+        e.T = T;
+        launch_embed_ternary(e, st);
+        note("embedding", (size_t)-1);
+    }
     for (size_t li = 0; li < m->layers.size(); li++) {
         const Layer& L = m->layers[li];
         ActSrc in;
-        in.mode = li == 0 ? ACT_EMBED : ACT_NORM;
+        in.mode = li == 0 && !ternary_head ? ACT_EMBED : ACT_NORM;
         in.x = m->h;
         in.xb = m->embed_rows;
         in.w = L.in_norm;
@@ -352,6 +371,33 @@ void enqueue_pass(bcu_model* m, int T) {
         grid_built(sw, L.down, 0);
         launch_ternary_gemv(L.down.m, sw, T, resid, nullptr, st, lora_of(L.down));
         note("down GEMV", li);
+    }
+    if (ternary_head) {  // encode_head_to (model.rs:941-985): norm_rotate with the table's signs, the table, argmax
+        ActSrc hs;
+        hs.mode = ACT_NORM;
+        hs.x = m->h;
+        hs.w = m->final_norm;
+        hs.signs = m->head_lin.signs;
+        hs.ss = m->ssbuf;
+        hs.nss = d / 128;
+        hs.HB = c.hadamard;
+        grid_built(hs, m->head_lin, 0);
+        GemvOut ho = store;
+        ho.out = m->logits;
+        launch_ternary_gemv(m->head_lin.m, hs, T, ho, nullptr, st);
+        note("head GEMV", (size_t)-1);
+        HeadArgs ha{};
+        ha.ctl = m->ctl;
+        ha.logits = m->logits;
+        ha.pv = m->pv;
+        ha.pi = m->pi;
+        ha.counter = m->head_counter;
+        ha.V = c.vocab;
+        ha.d = d;
+        ha.T = T;
+        launch_head_argmax(ha, m->head_grid, st);
+        note("head argmax", (size_t)-1);
+        return;
     }
     HeadArgs ha{};
     ha.ctl = m->ctl;
@@ -543,7 +589,12 @@ bcu_status bcu_finalize(bcu_model* m) {
         }
         bytes += lin_bytes(2 * ff, d, g) + lin_bytes(d, ff, g) + 4 * align256((size_t)std::max(d, ff) * 4) + 8192;
     }
-    bytes += align256((size_t)c.vocab * d * 2) * 2 + align256((size_t)d * 4) + (4 << 20);
+    if (c.head_kind == BCU_HEAD_TERNARY)  // the table in the GEMV layout + its MLX pack for the row gathers + signs
+        bytes += lin_bytes(c.vocab, d, g) + align256((size_t)c.vocab * d / 4) +
+                 2 * align256((size_t)c.vocab * (d / g) * 2) + align256((size_t)d * 4);
+    else
+        bytes += align256((size_t)c.vocab * d * 2) * 2;
+    bytes += align256((size_t)d * 4) + (4 << 20);
     m->arena_bytes = bytes;
     CK(cudaMalloc(&m->arena, bytes));
     m->arena_used = 0;
@@ -579,14 +630,34 @@ bcu_status bcu_finalize(bcu_model* m) {
         TRY(build_lin(m, {{mlp + "down_proj", d}}, ff, &L.down));
     }
     TRY(arena_f32(m, p + "norm.weight", d, &m->final_norm));
-    const DevTensor* e = find(m, p + "embed_tokens.weight");
-    if (!e || e->dtype != BCU_BF16 || e->bytes != (size_t)c.vocab * d * 2)
-        return fail(m, BCU_ERR_NOT_FOUND, "missing bf16 embed_tokens.weight [vocab, hidden]");
-    m->embed_rows = (uint16_t*)arena_take(m, (size_t)c.vocab * d * 2);
-    CK(cudaMemcpyAsync(m->embed_rows, e->dev, (size_t)c.vocab * d * 2, cudaMemcpyDeviceToDevice, m->st));
-    m->head_w = (uint32_t*)arena_take(m, (size_t)c.vocab * d * 2);
-    repack_head_bf16((const uint16_t*)e->dev, c.vocab, d, m->head_w, m->st);
-    CK(cudaGetLastError());
+    if (c.head_kind == BCU_HEAD_TERNARY) {
+        // the reference's tied table (model.rs:356, 962): ternary-packed like the linears, with its own signs
+        TRY(build_lin(m, {{p + "embed_tokens", c.vocab}}, d, &m->head_lin));
+        const size_t wb = (size_t)c.vocab * d / 4, sb = (size_t)c.vocab * (d / g) * 2;
+        const DevTensor* w = find(m, p + "embed_tokens.weight");
+        const DevTensor* sc = find(m, p + "embed_tokens.scales");
+        const DevTensor* bi = c.has_bias ? find(m, p + "embed_tokens.biases") : nullptr;
+        uint32_t* ew = (uint32_t*)arena_take(m, wb);
+        uint16_t* es = (uint16_t*)arena_take(m, sb);
+        CK(cudaMemcpyAsync(ew, w->dev, wb, cudaMemcpyDeviceToDevice, m->st));
+        CK(cudaMemcpyAsync(es, sc->dev, sb, cudaMemcpyDeviceToDevice, m->st));
+        m->emb_w = ew;
+        m->emb_s = es;
+        if (bi) {
+            uint16_t* eb = (uint16_t*)arena_take(m, sb);
+            CK(cudaMemcpyAsync(eb, bi->dev, sb, cudaMemcpyDeviceToDevice, m->st));
+            m->emb_b = eb;
+        }
+    } else {
+        const DevTensor* e = find(m, p + "embed_tokens.weight");
+        if (!e || e->dtype != BCU_BF16 || e->bytes != (size_t)c.vocab * d * 2)
+            return fail(m, BCU_ERR_NOT_FOUND, "missing bf16 embed_tokens.weight [vocab, hidden]");
+        m->embed_rows = (uint16_t*)arena_take(m, (size_t)c.vocab * d * 2);
+        CK(cudaMemcpyAsync(m->embed_rows, e->dev, (size_t)c.vocab * d * 2, cudaMemcpyDeviceToDevice, m->st));
+        m->head_w = (uint32_t*)arena_take(m, (size_t)c.vocab * d * 2);
+        repack_head_bf16((const uint16_t*)e->dev, c.vocab, d, m->head_w, m->st);
+        CK(cudaGetLastError());
+    }
     {  // model.rs:316-321
         int half = c.rotary_dims / 2;
         std::vector<float> f(half);
@@ -626,6 +697,10 @@ bcu_status bcu_finalize(bcu_model* m) {
             pf = std::max(pf, (size_t)ln->m.nsplit * VMAX * ln->m.O);
             maxrb = std::max(maxrb, ln->m.O / 128);
         }
+    }
+    if (c.head_kind == BCU_HEAD_TERNARY) {
+        if (m->head_lin.m.nsplit > 1) pf = std::max(pf, (size_t)m->head_lin.m.nsplit * VMAX * m->head_lin.m.O);
+        maxrb = std::max(maxrb, m->head_lin.m.O / 128);
     }
     m->partial_floats = pf;
     TRY(dmalloc(m, &m->partial, pf * 4));
@@ -944,7 +1019,10 @@ bcu_status bcu_pass_bytes(const bcu_model* m, int32_t t, double* bytes) {
             double O = ln->m.O, K = ln->m.K, g = ln->m.group;
             b += O * K / 4 + O * (K / g) * 4;  // codes + fp16 scale and bias per group
         }
-    b += (double)c.vocab * c.hidden * 2;                                          // bf16 head
+    if (c.head_kind == BCU_HEAD_TERNARY)                                          // ternary tied head
+        b += (double)c.vocab * c.hidden / 4 + (double)c.vocab * (c.hidden / c.group_size) * 4;
+    else
+        b += (double)c.vocab * c.hidden * 2;                                      // bf16 head
     b += (double)m->n_gdn * 2 * c.lin_v_heads * c.hidden * 4;                     // dense a/b
     b += (double)m->n_gdn * c.lin_v_heads * 128 * 128 * 4 * 2;                    // GDN state r+w
     b += (double)m->n_gdn * 3 * m->C * 4 * 2;                                     // conv state r+w

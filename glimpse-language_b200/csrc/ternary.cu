@@ -146,16 +146,6 @@ struct GemvParams {
     int nrb;  // row blocks; CTA = ks * nrb + rb
 };
 
-__device__ __forceinline__ uint32_t resolve_id(const Ctl* ctl, int t) {
-    int feed = ctl->in.feed;
-    if (feed == 1 && t == 0) return ctl->bonus;
-    if (feed == 2 && ctl->planted) {
-        int i = ctl->off - ctl->in.planted_base + t;
-        if (i >= 0 && i < ctl->planted_n) return ctl->planted[i];
-    }
-    return ctl->in.ids[t];
-}
-
 // Per-row scalar of NORM / EMBED: r = rsqrt(mean(h^2) + eps). EMBED also records the id and, in CTA 0, writes the
 // row into the residual stream. Fixed-order reductions (lane strides, then the warp tree); loads are issued in
 // batches of 8 per lane so the row costs a few memory latencies, not one per element.

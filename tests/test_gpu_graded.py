@@ -88,3 +88,49 @@ def test_graded_planted_decode_matches_oracle_greedy(pair):
     assert list(got) == list(og)
     assert st.accepted == st.drafted
     snap.free()
+
+
+def reference_2b_4layers():
+    """The reference's own Bonsai-2B config (its tests/data/config-2b.json, copied into tests/golden/), cut to the
+    first four layers (3 GatedDeltaNet + 1 attention): hidden 2048, MLP 6144, 8 query / 2 KV heads, GDN 16 / 16
+    heads, vocab 248320, g128 pack without bias, 512-point blocks with signs, ternary tied embedding and head."""
+    import os
+
+    from bonsai_b200 import config
+
+    path = os.path.join(os.path.dirname(__file__), "golden", "ref_config-2b.json")
+    c = config.parse_config(open(path).read())
+    c.n_layers = 4
+    c.ctx = 2048
+    return c
+
+
+def test_reference_2b_config_ternary_head(gpu):
+    """A model in the reference's own format and shape loads (bcu_config_check accepts the parsed config) and its
+    9-row verify pass at 1290 cached keys matches the oracle: logits within 2e-3, argmax, accept length exact."""
+    cfg = reference_2b_4layers()
+    assert [cfg.layer_is_attn[i] for i in range(4)] == [0, 0, 0, 1] and cfg.head_kind == 1
+    ts = synth.model_tensors(cfg, 77)
+    m = Model(cfg).load(ts)
+    o = OracleModel(cfg, ts)
+    try:
+        length, first = 1290, 31337
+        snap, parts = start(m, o, cfg, length, seed=3)
+        greedy = o.greedy(first, 9)
+        o.set_state(*parts, length)
+        rows = np.array([first] + list(greedy[1:9]), np.uint32)
+        m.keep_logits(True)
+        pred, acc = m.verify(rows)
+        opred, ol = o.forward(rows, logits=True)
+        for t in range(9):
+            err = float(np.abs(m.logits(t) - ol[t]).max())
+            assert err <= LOGIT_TOL, f"row {t}: max logit error {err}"
+            if pred[t] != opred[t]:
+                top = np.sort(ol[t])[-2:]
+                assert top[1] - top[0] < LOGIT_TOL, f"row {t}: argmax differs, gap {top[1] - top[0]}"
+        m.keep_logits(False)
+        if list(pred) == list(opred):
+            assert acc == 8
+        snap.free()
+    finally:
+        m.close()

@@ -20,6 +20,8 @@ CONFIGS = {
     "g128_ref_pack": dict(group_size=128, has_bias=False, hadamard=512, has_signs=True, kv_heads=1),
     "g64_h1024_nosigns": dict(group_size=64, has_bias=True, hadamard=1024, has_signs=False, hidden=1024,
                               intermediate=2048, heads=4, lin_v_heads=8),
+    # the reference's own format: g128 pack, 512-point blocks with signs, ternary tied embedding and head
+    "reference_format": dict(group_size=128, has_bias=False, hadamard=512, has_signs=True, kv_heads=1, head_kind=1),
 }
 
 

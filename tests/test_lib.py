@@ -63,8 +63,12 @@ def test_parse_reference_config_file():
     assert (c.heads, c.kv_heads, c.lin_k_heads, c.lin_v_heads) == (8, 2, 16, 16)
     assert [c.layer_is_attn[i] for i in range(8)] == [0, 0, 0, 1, 0, 0, 0, 1]
     assert c.rotary_dims == 64 and list(c.mrope) == [11, 11, 10]
-    # the reference's tied ternary head is not implemented on the device yet: the check says so
-    assert config.check(c) == (False, "unsupported config: only the bf16 tied head is implemented on the device")
+    # the reference's own format (g128 pack, 512-point blocks with signs, ternary tied head) is accepted as is
+    assert c.head_kind == 1 and c.group_size == 128 and not c.has_bias
+    assert config.check(c) == (True, "")
+    c4 = config.parse_config(open(os.path.join(os.path.dirname(__file__), "golden", "ref_config-4b.json")).read())
+    assert (c4.hidden, c4.intermediate, c4.n_layers, c4.lin_v_heads) == (2560, 9216, 32, 32)
+    assert config.check(c4) == (True, "")
 
 
 def test_synth_is_deterministic_and_shaped():
