@@ -21,6 +21,12 @@ U32, F16, BF16, F32 = range(4)
 DRAFT_LOOKUP, DRAFT_PLANTED, DRAFT_RANDOM = range(3)
 
 
+# callbacks of bcu_set_encoder / bcu_set_emit
+ENCODE_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint8), ctypes.c_int32,
+                             ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32)
+EMIT_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_uint32)
+
+
 class BcuConfig(ctypes.Structure):
     _fields_ = [
         ("hidden", ctypes.c_int32),
@@ -133,6 +139,9 @@ SIGNATURES = {
          ctypes.POINTER(BcuStats)],
     ),
     "bcu_cancel": (I32, [P, I32]),
+    "bcu_set_fillers": (I32, [P, PU32, I32]),
+    "bcu_set_encoder": (I32, [P, P, P]),
+    "bcu_set_emit": (I32, [P, P, P]),
     "bcu_linear_prepare": (I32, [P, P, P, I32, I32, I32, I32, ctypes.POINTER(P)]),
     "bcu_linear_free": (None, [P]),
     "bcu_linear_rotate_forward": (I32, [P, P, I32, I32, P, P, P]),
@@ -155,6 +164,8 @@ SIGNATURES = {
     "bcu_debug_wait_timeout": (I32, [P]),
     "bcu_gemm_prep_debug": (I32, [P, P, I32, P, P]),
     "bcu_token_key": (U64, [P, U64]),
+    "bcu_draft_source_host": (I32, [PU32, I32, P, ctypes.POINTER(U64), I32, PU32, I32, PU32]),
+    "bcu_normalize_draft_host": (I32, [PU32, I32, ctypes.c_uint32, P, ctypes.POINTER(U64), I32, P, P]),
     "bcu_lookup": (I32, [PU32, I32, PU32, I32, ctypes.POINTER(U64), I32, I32, I32, I32, I32, I32, PU32, PI32]),
     "bcu_policy_choose": (I32, [ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_double), I32, I32,
                                 ctypes.c_double]),

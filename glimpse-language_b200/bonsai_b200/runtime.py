@@ -262,6 +262,42 @@ class Model:
         self._ck(self.L.bcu_set_vocab_bytes(self.h, buf.ctypes.data_as(ctypes.c_void_p),
                                             offs.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), len(tokens)))
 
+    def set_fillers(self, ids):
+        """draft_source's filler ids (the FILLERS that encode to one token); empty: derived from the vocab bytes."""
+        n = len(ids)
+        arr = _u32(ids) if n else np.zeros(1, np.uint32)
+        self._ck(self.L.bcu_set_fillers(self.h, arr.ctypes.data_as(_lib.PU32), n))
+
+    def set_encoder(self, encode):
+        """normalize_draft's tokenizer: encode(bytes) -> list of ids (None: drafts are not normalized)."""
+        if encode is None:
+            self._enc = None
+            self._ck(self.L.bcu_set_encoder(self.h, None, None))
+            return
+
+        def cb(user, text, n, out, cap):
+            try:
+                ids = encode(bytes(text[:n]))
+            except Exception:
+                return -1
+            if ids is None or len(ids) > cap:
+                return -1
+            for i, v in enumerate(ids):
+                out[i] = int(v)
+            return len(ids)
+
+        self._enc = _lib.ENCODE_FN(cb)  # kept alive as long as the model uses it
+        self._ck(self.L.bcu_set_encoder(self.h, ctypes.cast(self._enc, ctypes.c_void_p), None))
+
+    def set_emit(self, emit):
+        """Streaming emission: emit(id) for every token decode outputs, as it lands (None: off)."""
+        if emit is None:
+            self._emit = None
+            self._ck(self.L.bcu_set_emit(self.h, None, None))
+            return
+        self._emit = _lib.EMIT_FN(lambda user, tok: emit(int(tok)))
+        self._ck(self.L.bcu_set_emit(self.h, ctypes.cast(self._emit, ctypes.c_void_p), None))
+
     def cancel(self, flag=True):
         self._ck(self.L.bcu_cancel(self.h, 1 if flag else 0))
 

@@ -2,10 +2,12 @@
 // prompt-lookup drafting, the adaptive speculation policy, the verify/accept loop, and pipelined plain decoding.
 // The accept length is computed on the device; a verify round returns 8 bytes (m and the bonus token) to the host.
 //
-// Left out, because they need the tokenizer (out of scope for a backend): normalize_draft (mod.rs:699-729, re-encodes
-// changed words) and the filler / SOURCE_TAGS filtering of draft_source (mod.rs:733-768) — the draft source is the
-// user turn as given.
+// The tokenizer stays with the caller: draft_source's SOURCE_TAGS block and filler filtering (mod.rs:733-768) work on
+// the token bytes given to bcu_set_vocab_bytes (and the filler ids of bcu_set_fillers), and normalize_draft
+// (mod.rs:699-729) re-encodes changed words through the caller's bcu_encode_fn. Emitted tokens reach the caller as
+// they land through bcu_emit_fn (the `emit` of decode_spec / decode_plain, mod.rs:683, 892, 941).
 #include <algorithm>
+#include <cctype>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -50,6 +52,91 @@ struct Source {
     std::vector<std::pair<uint64_t, int>> words;
 };
 
+// The reference's word tables (runtime/mod.rs:130-146), kept as they are: drafting decisions must match its own.
+const char* const SOURCE_TAGS[2][2] = {{"<transcript>\n", "\n</transcript>"}, {"<text>\n", "\n</text>"}};
+const char* const CAPITALIZED[18] = {"monday", "tuesday", "wednesday", "thursday", "friday",  "saturday",
+                                     "sunday", "january", "february",  "march",    "april",   "june",
+                                     "july",   "august",  "september", "october",  "november", "december"};
+const char* const CONTRACTIONS[22][2] = {
+    {"dont", "don't"},     {"doesnt", "doesn't"},   {"didnt", "didn't"},     {"isnt", "isn't"},
+    {"wasnt", "wasn't"},   {"arent", "aren't"},     {"werent", "weren't"},   {"wont", "won't"},
+    {"cant", "can't"},     {"couldnt", "couldn't"}, {"wouldnt", "wouldn't"}, {"shouldnt", "shouldn't"},
+    {"havent", "haven't"}, {"hasnt", "hasn't"},     {"im", "I'm"},           {"ive", "I've"},
+    {"youre", "you're"},   {"theyre", "they're"},   {"thats", "that's"},     {"whats", "what's"},
+    {"theres", "there's"}, {"lets", "let's"}};
+const char* const FILLERS[12] = {" um", " uh", " Um", " Uh", " umm", " uhm", " erm", " hmm", "um", "uh", "Um", "Uh"};
+
+// The vocabulary as the drafting code sees it: token bytes (bcu_set_vocab_bytes), filler ids, the encoder.
+struct Vocab {
+    const std::vector<std::string>* bytes = nullptr;
+    const std::vector<uint32_t>* fillers = nullptr;
+    bcu_encode_fn encode = nullptr;
+    void* encode_user = nullptr;
+    const std::string& tb(uint32_t id) const {
+        static const std::string empty;
+        return bytes && id < bytes->size() ? (*bytes)[id] : empty;
+    }
+};
+
+bool ascii_ws(uint8_t c) { return c == ' ' || c == '\t' || c == '\n' || c == 0x0c || c == '\r'; }
+
+// trim_ascii_end().last() is one of . ? ! (mod.rs:702, 724)
+bool ends_sentence(const std::string& w) {
+    size_t e = w.size();
+    while (e > 0 && ascii_ws((uint8_t)w[e - 1])) e--;
+    return e > 0 && (w[e - 1] == '.' || w[e - 1] == '?' || w[e - 1] == '!');
+}
+
+// Model::normalize_draft (mod.rs:699-729): per word of the draft (a token, plus the tokens after it that start with
+// a letter or an apostrophe or are empty), a lowercase " word" becomes its contraction, or gets a capital when it is
+// " i", follows a sentence end or is a CAPITALIZED word; changed words are re-encoded (the caller's encoder; a failed
+// encoding keeps the word's tokens), and the draft keeps at most its length. No encoder: the draft is unchanged.
+void normalize_draft(const Vocab& vb, std::vector<uint32_t>& draft, uint32_t last) {
+    if (!vb.encode || !vb.bytes || vb.bytes->empty()) return;
+    const size_t k = draft.size();
+    std::vector<uint32_t> out;
+    bool prev_end = ends_sentence(vb.tb(last));
+    size_t i = 0;
+    while (i < draft.size() && out.size() < k) {
+        size_t j = i + 1;
+        while (j < draft.size()) {
+            const std::string& b = vb.tb(draft[j]);
+            if (!b.empty() && !(std::isalpha((uint8_t)b[0]) && (uint8_t)b[0] < 128) && b[0] != '\'') break;
+            j++;
+        }
+        std::string w;
+        for (size_t q = i; q < j; q++) w += vb.tb(draft[q]);
+        std::string v = w;
+        bool lower = v.size() > 1 && v[0] == ' ';
+        for (size_t q = 1; q < v.size() && lower; q++) lower = v[q] >= 'a' && v[q] <= 'z';
+        if (lower) {
+            const std::string bare = w.substr(1);
+            const char* to = nullptr;
+            for (auto& c : CONTRACTIONS)
+                if (bare == c[0]) { to = c[1]; break; }
+            bool cap = bare == "i" || prev_end;
+            for (const char* c : CAPITALIZED) cap = cap || bare == c;
+            if (to) v = std::string(" ") + to;
+            else if (cap) v[1] = (char)(v[1] - 'a' + 'A');
+        }
+        bool done = false;
+        if (v != w) {
+            std::vector<uint32_t> ids(v.size() + 16);
+            int32_t n = vb.encode(vb.encode_user, (const uint8_t*)v.data(), (int32_t)v.size(), ids.data(),
+                                  (int32_t)ids.size());
+            if (n >= 0 && n <= (int32_t)ids.size()) {
+                out.insert(out.end(), ids.begin(), ids.begin() + n);
+                done = true;
+            }
+        }
+        if (!done) out.insert(out.end(), draft.begin() + i, draft.begin() + j);
+        prev_end = ends_sentence(w);
+        i = j;
+    }
+    if (out.size() > k) out.resize(k);
+    draft = out;
+}
+
 struct Keys {
     const std::vector<uint64_t>* table;
     uint64_t operator()(uint32_t id) const {
@@ -60,14 +147,67 @@ struct Keys {
     }
 };
 
-Source draft_source(const uint32_t* user, int n, const Keys& keys) {
+// Model::draft_source (mod.rs:733-768): the user tokens inside the first SOURCE_TAGS block of the turn's bytes (all
+// of them when there is none, or when no token bytes are known), fillers removed, with the keys of its word tokens.
+Source draft_source(const uint32_t* user, int n, const Keys& keys, const Vocab& vb) {
     Source s;
-    s.ids.assign(user, user + n);
+    size_t lo = 0, hi = 0;
+    std::vector<size_t> ends(n);
+    const bool have = vb.bytes && !vb.bytes->empty();
+    if (have) {
+        std::string text;
+        for (int i = 0; i < n; i++) {
+            text += vb.tb(user[i]);
+            ends[i] = text.size();
+        }
+        hi = text.size();
+        for (auto& tag : SOURCE_TAGS) {
+            size_t a = text.find(tag[0]);
+            if (a == std::string::npos) continue;
+            a += std::strlen(tag[0]);
+            size_t b = text.find(tag[1], a);
+            if (b == std::string::npos) continue;
+            lo = a;
+            hi = b;
+            break;
+        }
+    }
     for (int i = 0; i < n; i++) {
-        uint64_t k = keys(user[i]);
+        const uint32_t id = user[i];
+        if (have) {
+            const size_t len = vb.tb(id).size();
+            if (!(ends[i] > lo && ends[i] - len >= lo && ends[i] <= hi)) continue;
+        }
+        if (vb.fillers && std::find(vb.fillers->begin(), vb.fillers->end(), id) != vb.fillers->end()) continue;
+        s.ids.push_back(id);
+    }
+    for (int i = 0; i < (int)s.ids.size(); i++) {
+        uint64_t k = keys(s.ids[i]);
         if (k & 1) s.words.push_back({k, i});
     }
     return s;
+}
+
+// The filler ids: the caller's (bcu_set_fillers), else every FILLERS string that is exactly one token's bytes (the
+// reference keeps the fillers whose encoding is a single id, mod.rs:750-756).
+std::vector<uint32_t> default_fillers(const std::vector<std::string>& bytes) {
+    std::vector<uint32_t> f;
+    for (const char* w : FILLERS)
+        for (size_t id = 0; id < bytes.size(); id++)
+            if (bytes[id] == w) {
+                f.push_back((uint32_t)id);
+                break;
+            }
+    return f;
+}
+
+Vocab vocab_of(bcu_model* m) {
+    Vocab v;
+    v.bytes = &m->vocab_bytes;
+    v.fillers = &m->fillers;
+    v.encode = m->encode_fn;
+    v.encode_user = m->encode_user;
+    return v;
 }
 
 // lookup (mod.rs:87-124).
@@ -167,9 +307,10 @@ struct Run {
     int max_tokens;
     uint32_t* out;
     int n = 0;
-    bool push(uint32_t id) {  // false: stop (EOS or cap)
+    bool push(uint32_t id) {  // false: stop (EOS or cap); an accepted token is emitted as it lands
         if (is_eos(id, eos, n_eos) || n >= max_tokens) return false;
         out[n++] = id;
+        if (m->emit_fn) m->emit_fn(m->emit_user, id);
         return true;
     }
 };
@@ -243,9 +384,38 @@ extern "C" {
 bcu_status bcu_set_vocab_bytes(bcu_model* m, const uint8_t* bytes, const uint64_t* offsets, int32_t vocab) {
     if (!m) return BCU_ERR_ARG;
     m->keys.clear();
+    m->vocab_bytes.clear();
+    if (!m->fillers_given) m->fillers.clear();
     if (!bytes || !offsets || vocab <= 0) return BCU_OK;
     m->keys.resize(vocab);
-    for (int i = 0; i < vocab; i++) m->keys[i] = token_key(bytes + offsets[i], offsets[i + 1] - offsets[i]);
+    m->vocab_bytes.resize(vocab);
+    for (int i = 0; i < vocab; i++) {
+        m->keys[i] = token_key(bytes + offsets[i], offsets[i + 1] - offsets[i]);
+        m->vocab_bytes[i].assign((const char*)bytes + offsets[i], offsets[i + 1] - offsets[i]);
+    }
+    if (!m->fillers_given) m->fillers = default_fillers(m->vocab_bytes);
+    return BCU_OK;
+}
+
+bcu_status bcu_set_fillers(bcu_model* m, const uint32_t* ids, int32_t n) {
+    if (!m || n < 0 || (n && !ids)) return BCU_ERR_ARG;
+    m->fillers.assign(ids, ids + n);
+    m->fillers_given = n > 0;
+    if (!n) m->fillers = default_fillers(m->vocab_bytes);
+    return BCU_OK;
+}
+
+bcu_status bcu_set_encoder(bcu_model* m, bcu_encode_fn fn, void* user) {
+    if (!m) return BCU_ERR_ARG;
+    m->encode_fn = fn;
+    m->encode_user = user;
+    return BCU_OK;
+}
+
+bcu_status bcu_set_emit(bcu_model* m, bcu_emit_fn fn, void* user) {
+    if (!m) return BCU_ERR_ARG;
+    m->emit_fn = fn;
+    m->emit_user = user;
     return BCU_OK;
 }
 
@@ -263,12 +433,48 @@ int32_t bcu_lookup(const uint32_t* src, int32_t n_src, const uint32_t* seq, int3
                    int32_t cursor, uint32_t* out, int32_t* dpos) {
     std::vector<uint64_t> table(keys, keys + n_keys);
     Keys k{&table};
-    Source s = draft_source(src, n_src, k);
+    Source s = draft_source(src, n_src, k, Vocab());
     std::vector<uint32_t> sq(seq, seq + n_seq);
     int dp;
     std::vector<uint32_t> d = lookup(s, sq, k, ngram_max, ngram_min, draft_max, limit, cursor, &dp);
     for (size_t i = 0; i < d.size(); i++) out[i] = d[i];
     *dpos = dp;
+    return (int32_t)d.size();
+}
+
+// draft_source and normalize_draft on a vocabulary given as one byte string (offsets: vocab + 1 entries), for tests
+// of the host logic without a device. fillers: n_fillers ids, or n_fillers < 0 for the default derived from the bytes.
+static std::vector<std::string> vocab_strings(const uint8_t* bytes, const uint64_t* offsets, int32_t vocab) {
+    std::vector<std::string> v(vocab > 0 ? vocab : 0);
+    for (int i = 0; i < vocab; i++) v[i].assign((const char*)bytes + offsets[i], offsets[i + 1] - offsets[i]);
+    return v;
+}
+
+int32_t bcu_draft_source_host(const uint32_t* user, int32_t n, const uint8_t* bytes, const uint64_t* offsets,
+                              int32_t vocab, const uint32_t* fillers, int32_t n_fillers, uint32_t* out) {
+    std::vector<std::string> vb = vocab_strings(bytes, offsets, vocab);
+    std::vector<uint64_t> keys(vb.size());
+    for (size_t i = 0; i < vb.size(); i++) keys[i] = token_key((const uint8_t*)vb[i].data(), vb[i].size());
+    std::vector<uint32_t> fl = n_fillers < 0 ? default_fillers(vb) : std::vector<uint32_t>(fillers, fillers + n_fillers);
+    Vocab v;
+    v.bytes = &vb;
+    v.fillers = &fl;
+    Keys k{&keys};
+    Source s = draft_source(user, n, k, v);
+    for (size_t i = 0; i < s.ids.size(); i++) out[i] = s.ids[i];
+    return (int32_t)s.ids.size();
+}
+
+int32_t bcu_normalize_draft_host(uint32_t* draft, int32_t n, uint32_t last, const uint8_t* bytes,
+                                 const uint64_t* offsets, int32_t vocab, bcu_encode_fn fn, void* user) {
+    std::vector<std::string> vb = vocab_strings(bytes, offsets, vocab);
+    Vocab v;
+    v.bytes = &vb;
+    v.encode = fn;
+    v.encode_user = user;
+    std::vector<uint32_t> d(draft, draft + n);
+    normalize_draft(v, d, last);
+    for (size_t i = 0; i < d.size(); i++) draft[i] = d[i];
     return (int32_t)d.size();
 }
 
@@ -312,7 +518,8 @@ bcu_status bcu_decode(bcu_model* m, uint32_t first, const uint32_t* user, int32_
     static const double unit[9] = {1, 1, 1, 1, 1, 1, 1, 1, 1};
     Policy pol{forced ? unit : m->cost, std::min(draft_max, 7)};
     Keys keys{&m->keys};
-    Source src = draft_source(user, n_user, keys);
+    const Vocab vb = vocab_of(m);
+    Source src = draft_source(user, n_user, keys, vb);
     std::vector<uint32_t> seq(user, user + n_user);
     seq.push_back(first);
     int cursor = 0;
@@ -397,6 +604,7 @@ bcu_status bcu_decode(bcu_model* m, uint32_t first, const uint32_t* user, int32_
             st.switches++;
             continue;
         }
+        if (!forced) normalize_draft(vb, draft, last);
         std::vector<uint32_t> ids;
         ids.push_back(last);
         ids.insert(ids.end(), draft.begin(), draft.end());

@@ -126,6 +126,12 @@ struct bcu_model {
     // drafting
     std::vector<uint64_t> keys;   // token_key per vocab id
     std::vector<std::string> vocab_bytes;
+    std::vector<uint32_t> fillers;  // draft_source's filler ids (bcu_set_fillers, or derived from the token bytes)
+    bool fillers_given = false;
+    bcu_encode_fn encode_fn = nullptr;  // normalize_draft's tokenizer (bcu_set_encoder)
+    void* encode_user = nullptr;
+    bcu_emit_fn emit_fn = nullptr;      // streaming emission (bcu_set_emit)
+    void* emit_user = nullptr;
     double cost[9] = {0};         // verify cost per draft count (policy), measured on first use
     bool cost_ready = false;
 };

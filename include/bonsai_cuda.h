@@ -240,8 +240,26 @@ typedef struct {
  * token counts as a word keyed by its id. */
 bcu_status bcu_set_vocab_bytes(bcu_model* m, const uint8_t* bytes, const uint64_t* offsets, int32_t vocab);
 
+/* The filler ids Model::draft_source drops from the draft source (FILLERS, runtime/mod.rs:146, 750-756: the
+ * hesitation words " um", " uh", ... whose encoding is one token). n = 0 returns to the default: the ids whose bytes
+ * (bcu_set_vocab_bytes) equal a filler string exactly. */
+bcu_status bcu_set_fillers(bcu_model* m, const uint32_t* ids, int32_t n);
+
+/* The tokenizer Model::normalize_draft re-encodes changed draft words with (self.tok.encode, runtime/mod.rs:720):
+ * encode n bytes of UTF-8 text into at most cap ids and return their count, or -1 (the word keeps its tokens).
+ * NULL (the default) leaves drafts as lookup found them. Called on the thread that runs bcu_decode. */
+typedef int32_t (*bcu_encode_fn)(void* user, const uint8_t* text, int32_t n, uint32_t* out, int32_t cap);
+bcu_status bcu_set_encoder(bcu_model* m, bcu_encode_fn fn, void* user);
+
+/* Streaming emission: fn(user, id) for every token bcu_decode outputs, in order, as it lands (the `emit` of
+ * decode_spec / decode_plain, runtime/mod.rs:683, 892, 941; generate_streaming builds text from these ids). EOS is
+ * not emitted. NULL (the default) disables. Called on the thread that runs bcu_decode. */
+typedef void (*bcu_emit_fn)(void* user, uint32_t id);
+bcu_status bcu_set_emit(bcu_model* m, bcu_emit_fn fn, void* user);
+
 /* Model::decode_spec / decode_plain after the prompt has been prefilled: `first` is the token prefill returned,
- * `user` the user-turn ids (draft source, runtime/mod.rs:733-768). spec == NULL decodes plainly (pipelined). Writes
+ * `user` the user-turn ids (draft source: its first SOURCE_TAGS block, fillers removed, runtime/mod.rs:733-768;
+ * lookup drafts are normalized when an encoder is set). spec == NULL decodes plainly (pipelined). Writes
  * up to max_tokens ids into out (first included) and returns the count in *n_out. planted/planted_n: the draft
  * stream for BCU_DRAFT_PLANTED (output token i+1 is planted[i]); seed for BCU_DRAFT_RANDOM. eos/n_eos: stop ids
  * (the reference's EOS, runtime/mod.rs:24); n_eos = 0 ignores EOS (ignore_eos). */

@@ -989,6 +989,113 @@ int orc_lookup(const uint32_t* src, int n_src, const uint32_t* seq, int n_seq, c
     return 0;
 }
 
+// draft_source (mod.rs:733-768). The vocabulary is one byte string: token i = bytes[offsets[i]..offsets[i+1]).
+// Concatenate the user turn's bytes, find the first of SOURCE_TAGS (mod.rs:130) whose opening and then closing tag
+// both occur, keep the tokens lying wholly inside (end > lo, start >= lo, end <= hi), drop the filler ids.
+int orc_draft_source(const uint32_t* user, int n, const uint8_t* bytes, const uint64_t* offsets, int vocab,
+                     const uint32_t* fillers, int n_fillers, uint32_t* out) {
+    static const char* tags[2][2] = {{"<transcript>\n", "\n</transcript>"}, {"<text>\n", "\n</text>"}};
+    auto tok = [&](uint32_t id) {
+        return (int)id < vocab ? std::string((const char*)bytes + offsets[id], offsets[id + 1] - offsets[id]) : std::string();
+    };
+    std::string text;
+    std::vector<size_t> ends;
+    for (int i = 0; i < n; i++) {
+        text += tok(user[i]);
+        ends.push_back(text.size());
+    }
+    // Rust's find: first window equal to pat at or after `from`
+    auto find = [&](const std::string& pat, size_t from, size_t* at) {
+        for (size_t i = from; i + pat.size() <= text.size(); i++)
+            if (text.compare(i, pat.size(), pat) == 0) { *at = i; return true; }
+        return false;
+    };
+    size_t lo = 0, hi = text.size();
+    for (int t = 0; t < 2; t++) {
+        size_t a, b;
+        if (!find(tags[t][0], 0, &a)) continue;
+        a += std::strlen(tags[t][0]);
+        if (!find(tags[t][1], a, &b)) continue;
+        lo = a;
+        hi = b;
+        break;
+    }
+    int m = 0;
+    for (int i = 0; i < n; i++) {
+        size_t len = tok(user[i]).size();
+        if (!(ends[i] > lo && ends[i] - len >= lo && ends[i] <= hi)) continue;
+        bool filler = false;
+        for (int f = 0; f < n_fillers; f++) filler |= fillers[f] == user[i];
+        if (!filler) out[m++] = user[i];
+    }
+    return m;
+}
+
+// normalize_draft (mod.rs:699-729) with the tokenizer as a callback: encode(user, text, n, out, cap) -> count.
+typedef int32_t (*orc_encode_fn)(void* user, const uint8_t* text, int32_t n, uint32_t* out, int32_t cap);
+int orc_normalize_draft(uint32_t* draft, int n, uint32_t last, const uint8_t* bytes, const uint64_t* offsets, int vocab,
+                        orc_encode_fn encode, void* user) {
+    static const char* capitalized[18] = {"monday", "tuesday", "wednesday", "thursday", "friday", "saturday",
+                                          "sunday", "january", "february", "march", "april", "june", "july",
+                                          "august", "september", "october", "november", "december"};
+    static const char* contractions[22][2] = {
+        {"dont", "don't"}, {"doesnt", "doesn't"}, {"didnt", "didn't"}, {"isnt", "isn't"}, {"wasnt", "wasn't"},
+        {"arent", "aren't"}, {"werent", "weren't"}, {"wont", "won't"}, {"cant", "can't"}, {"couldnt", "couldn't"},
+        {"wouldnt", "wouldn't"}, {"shouldnt", "shouldn't"}, {"havent", "haven't"}, {"hasnt", "hasn't"},
+        {"im", "I'm"}, {"ive", "I've"}, {"youre", "you're"}, {"theyre", "they're"}, {"thats", "that's"},
+        {"whats", "what's"}, {"theres", "there's"}, {"lets", "let's"}};
+    auto tok = [&](uint32_t id) {
+        return (int)id < vocab ? std::string((const char*)bytes + offsets[id], offsets[id + 1] - offsets[id]) : std::string();
+    };
+    // trim_ascii_end().last() in ".?!"
+    auto sentence_end = [](std::string w) {
+        while (!w.empty() && (w.back() == ' ' || w.back() == '\t' || w.back() == '\n' || w.back() == '\f' || w.back() == '\r'))
+            w.pop_back();
+        return !w.empty() && (w.back() == '.' || w.back() == '?' || w.back() == '!');
+    };
+    const int k = n;
+    std::vector<uint32_t> d(draft, draft + n), out;
+    bool prev_end = sentence_end(tok(last));
+    int i = 0;
+    while (i < (int)d.size() && (int)out.size() < k) {
+        int j = i + 1;
+        for (; j < (int)d.size(); j++) {
+            std::string b = tok(d[j]);
+            if (b.empty()) continue;
+            unsigned char c = (unsigned char)b[0];
+            bool alpha = (c >= 'a' && c <= 'z') || (c >= 'A' && c <= 'Z');
+            if (!alpha && c != '\'') break;
+        }
+        std::string w;
+        for (int q = i; q < j; q++) w += tok(d[q]);
+        std::string v = w;
+        bool lower = v.size() > 1 && v[0] == ' ';
+        for (size_t q = 1; lower && q < v.size(); q++) lower = v[q] >= 'a' && v[q] <= 'z';
+        if (lower) {
+            std::string bare = w.substr(1);
+            int ci = -1;
+            for (int c = 0; c < 22; c++)
+                if (bare == contractions[c][0]) { ci = c; break; }
+            bool cap = bare == "i" || prev_end;
+            for (int c = 0; c < 18; c++) cap = cap || bare == capitalized[c];
+            if (ci >= 0) v = std::string(" ") + contractions[ci][1];
+            else if (cap) v[1] = (char)(v[1] - 32);
+        }
+        if (v != w) {
+            std::vector<uint32_t> ids(v.size() + 16);
+            int c = encode(user, (const uint8_t*)v.data(), (int32_t)v.size(), ids.data(), (int32_t)ids.size());
+            out.insert(out.end(), ids.begin(), ids.begin() + c);
+        } else {
+            out.insert(out.end(), d.begin() + i, d.begin() + j);
+        }
+        prev_end = sentence_end(w);
+        i = j;
+    }
+    if ((int)out.size() > k) out.resize(k);
+    for (size_t q = 0; q < out.size(); q++) draft[q] = out[q];
+    return (int)out.size();
+}
+
 // Policy::choose (mod.rs:187-202): best k in 1..=min(kmax, limit) by E(k)/cost[k], E(k) = (1 - p^(k+1)) / (1 - p).
 int orc_policy_choose(double acc, double rej, const double* cost, int kmax, int limit, double min_gain, double* gain) {
     double p = (acc + 3.4) / (acc + rej + 3.4 + 0.6);

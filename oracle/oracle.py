@@ -66,6 +66,8 @@ def lib():
             "orc_lora_add": (None, [P, P, I, I, I, P, I, P]),
             "orc_token_key": (ctypes.c_uint64, [P, I]),
             "orc_lookup": (I, [PU32, I, PU32, I, ctypes.POINTER(ctypes.c_uint64), I, I, I, I, I, I, PU32, ctypes.POINTER(I)]),
+            "orc_draft_source": (I, [PU32, I, P, ctypes.POINTER(ctypes.c_uint64), I, PU32, I, PU32]),
+            "orc_normalize_draft": (I, [PU32, I, ctypes.c_uint32, P, ctypes.POINTER(ctypes.c_uint64), I, P, P]),
             "orc_policy_choose": (I, [ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_double), I, I,
                                       ctypes.c_double, ctypes.POINTER(ctypes.c_double)]),
         }

@@ -240,3 +240,39 @@ def test_errors_are_reported(gpu):
     m.reset()
     assert m.prefill(np.arange(10, dtype=np.uint32)) < cfg.vocab  # the model still works after the errors
     m.close()
+
+
+def synthetic_vocab(V):
+    """Token bytes for a V-id vocabulary: a few words normalize_draft rewrites, sentence ends, and lowercase words."""
+    special = [b" i", b" I", b" dont", b" don", b"'t", b" monday", b" Monday", b".", b" um", b" hello", b" Hello"]
+    return special + [b" w%d" % i for i in range(V - len(special))]
+
+
+def test_lookup_decode_with_vocab_fillers_normalize_and_emit(pair):
+    """Lookup drafting with the token bytes, the default filler ids, a tokenizer for normalize_draft and streaming
+    emission: the output still equals greedy decoding token for token, and the emitted ids are the output, in order."""
+    name, cfg, m, o = pair
+    tb = synthetic_vocab(cfg.vocab)
+    index = {b: i for i, b in enumerate(tb)}
+    m.set_vocab_bytes(tb)
+    m.set_encoder(lambda text: [index[text]] if text in index else ([index[b" don"], index[b"'t"]]
+                                                                      if text == b" don't" else None))
+    got = []
+    m.set_emit(got.append)
+    try:
+        ids = np.concatenate([prompt(cfg, 24, seed=6), np.array([7, 0, 2, 5, 9, 8], np.uint32)])
+        m.reset()
+        first = m.prefill(ids)
+        snap = m.snapshot()
+        m.set_emit(None)
+        greedy, _ = m.decode(first, speculate=False, max_tokens=32)
+        m.set_emit(got.append)
+        m.restore(snap)
+        look, st = m.decode(first, user=ids, mode=_lib.DRAFT_LOOKUP, max_tokens=32)
+        assert list(look) == list(greedy)
+        assert got == [int(t) for t in look]
+        snap.free()
+    finally:
+        m.set_emit(None)
+        m.set_encoder(None)
+        m.set_vocab_bytes([])
