@@ -2,26 +2,27 @@
 // write (attn_prep, kernels.metal:627-662), split-K causal GQA over the cache (attn_split :713-780) and the log-sum-exp
 // merge (attn_combine :783-799), done by the last split CTA of each (row, kv head).
 //
-// Grid (KV, NSPLIT_ATTN, T), 256 threads (one per head dim), two CTAs per SM. The grid is fixed for graph capture;
-// each CTA derives its key range [j0, j1) of [0, off + t] from the device-side KV offset, so one captured graph serves
-// every length and a row's key partition depends only on its own position (batch invariance). Keys of this pass
-// (positions >= off) are normalised and rotated by the CTA whose range holds them, which also writes them to the
-// cache; older keys and values stream from the cache through shared memory in double-buffered blocks of KST keys
-// (cp.async, every copy of a block in flight at once), and the softmax is accumulated online block by block.
+// Grid (KV, NSPLIT_ATTN, T), 256 threads, two CTAs per SM. The grid is fixed for graph capture; each CTA derives its
+// key range [j0, j1) of [0, off + t] from the device-side KV offset, so one captured graph serves every length and a
+// row's key partition depends only on its own position (batch invariance). Keys of this pass (positions >= off) are
+// normalised and rotated by every CTA whose range holds them (identical bits; that CTA also writes them to the cache).
+// Inside a CTA the range is scored in rounds of up to SUB keys: each warp takes every 8th key (a lane holds 8 of the
+// 256 dims of the key and of each query head, so one coalesced 1-KB row read per key), the heads' partial dot
+// products are summed across the warp by a halving butterfly, the round's softmax statistics are taken per head,
+// and the thread of each head dim accumulates P.V over the round's keys in key order. Three barriers per round;
+// one round covers 16 x 512 = 8192 keys of context.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace bcu {
 
 constexpr float EPS_A = 1e-6f;
-constexpr int KST = 16;  // cached keys per staged block
+constexpr int SUB = 512;  // keys scored per round
 
-// Shared memory (floats): queries [QP][256], cached K and V blocks [2][KST][256] each, this pass's keys and values
-// [VMAX][256] each (also the staging of the normed rows), block scores [QP][KST], block probabilities [KST][QP],
-// row sums [8][32] + row scales [32], running max / sum / rescale [3][QP] (+pad), cos/sin table [(1 + VMAX)][rot].
+// Shared memory (floats): queries [QP][256], this pass's keys and values in range [VMAX][256] each, scores then
+// probabilities of a round [SUB][QP], running max / sum / rescale [4][QP], cos/sin table [(1 + VMAX)][rot].
 __host__ __device__ inline size_t attn_smem_floats(int qp, int rot) {
-    return (size_t)qp * 256 + 4 * KST * 256 + 2 * VMAX * 256 + 2 * (size_t)qp * KST + 288 + 4 * (size_t)qp +
-           (size_t)(1 + VMAX) * rot;
+    return (size_t)qp * 256 + 2 * VMAX * 256 + (size_t)SUB * qp + 4 * (size_t)qp + (size_t)(1 + VMAX) * rot;
 }
 
 // QP = query heads per kv head rounded up to a power of two (heads qper..QP-1 are zero padding).
@@ -29,21 +30,18 @@ template <int QP>
 __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     __shared__ int s_last;
+    constexpr int HG = QP < 8 ? QP : 8;  // heads scored per pass over the keys (their queries live in registers)
+    constexpr int LHG = HG >= 8 ? 3 : (HG >= 4 ? 2 : (HG >= 2 ? 1 : 0));
     const int kh = blockIdx.x, s = blockIdx.y, t = blockIdx.z;
     const int H = a.H, KV = a.KV, qper = H / KV, aw = H * 256, kvw = KV * 256;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, d = threadIdx.x;
     const int half = a.rot / 2;
-    float* qs = sm;                    // [QP][256]
-    float* ks = qs + QP * 256;         // [2][KST][256]
-    float* vs = ks + 2 * KST * 256;    // [2][KST][256]
-    float* nk = vs + 2 * KST * 256;    // [VMAX][256]
-    float* nv = nk + VMAX * 256;       // [VMAX][256]
-    float* sc = nv + VMAX * 256;       // [QP][KST] scores of the current block
-    float* pj = sc + QP * KST;         // [KST][QP] probabilities of the current block
-    float* rr = pj + QP * KST;         // [8][32] row sums of squares, then [32] row scales at rr + 256
-    float* stt = rr + 288;             // [QP] running max, [QP] running sum, [QP] rescale of the current block
-    float* tab = stt + 4 * QP;         // [1 + VMAX][half] (cos, sin): row 0 the query position, 1 + i new key u0 + i
-    const float wq = a.qn[d], wk = a.kn[d];
+    float* qs = sm;                  // [QP][256]
+    float* nk = qs + QP * 256;       // [VMAX][256] keys of this pass in range, index u - u0
+    float* nv = nk + VMAX * 256;     // [VMAX][256] their values
+    float* pr = nv + VMAX * 256;     // [SUB][QP] scores, then probabilities
+    float* stt = pr + SUB * QP;      // [QP] running max, [QP] running sum, [QP] rescale of the round
+    float* tab = stt + 4 * QP;       // [1 + VMAX][half] (cos, sin): row 0 the query position, 1 + i key u0 + i
     pdl_trigger();
     pdl_wait();
     const int off = a.ctl->off;
@@ -56,37 +54,7 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
         return;
     }
     if (j0 < j1) {
-        // cached keys [j0, jc1): blocks of KST, two in flight
-        const int jc1 = min(j1, off);
-        const int nst = (max(jc1 - j0, 0) + KST - 1) / KST;
-        auto issue = [&](int st) {
-            const int jb = j0 + st * KST, nr = min(KST, jc1 - jb);
-            float* kd = ks + (st & 1) * KST * 256;
-            float* vd = vs + (st & 1) * KST * 256;
-            for (int i = threadIdx.x; i < nr * 64; i += 256) {
-                const int r = i >> 6, c = (i & 63) * 4;
-                const size_t src = ((size_t)(jb + r) * KV + kh) * 256 + c;
-                cp_async16(kd + r * 256 + c, a.kc + src);
-                cp_async16(vd + r * 256 + c, a.vc + src);
-            }
-            cp_async_commit();
-        };
-        // rows to prepare: the qper query heads of row t, then this pass's keys in range (positions >= off),
-        // all loaded at once, ahead of the cached blocks
         const int u0 = max(j0, off) - off, u1 = j1 - off, nkeys = max(u1 - u0, 0);
-        const int nrows = qper + nkeys;  // <= 16 + 16
-        float x[32], vvals[16];
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-            x[i] = 0.0f;
-            if (i < qper) x[i] = a.qkv[(size_t)t * a.ld + (kh * qper + i) * 512 + d];
-            else if (i < nrows) x[i] = a.qkv[(size_t)(u0 + i - qper) * a.ld + 2 * aw + kh * 256 + d];
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++)
-            if (i < nkeys) vvals[i] = a.qkv[(size_t)(u0 + i) * a.ld + 2 * aw + kvw + kh * 256 + d];
-        if (nst > 0) issue(0);
-        if (nst > 1) issue(1);
         for (int e = threadIdx.x; e < (1 + nkeys) * half; e += 256) {
             const int pi = e / half, f = e - pi * half;
             const int pos = pi == 0 ? off + t : off + u0 + pi - 1;
@@ -95,151 +63,129 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             tab[2 * e] = cs;
             tab[2 * e + 1] = sn;
         }
-        // sums of squares of the 32 rows: halving butterfly, lane l ends with its warp's part of row l
-        {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = x[i] * x[i];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const bool up = (lane & o) != 0;
-#pragma unroll
-                for (int j = 0; j < o; j++) {
-                    const float send = up ? v[j] : v[j + o];
-                    const float keep = up ? v[j + o] : v[j];
-                    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                }
-            }
-            rr[w * 32 + lane] = v[0];
-        }
-        __syncthreads();
-        if (d < 32) {
-            float ss = 0.0f;
-#pragma unroll
-            for (int q = 0; q < 8; q++) ss += rr[q * 32 + d];
-            rr[256 + d] = rsqrtf(ss / 256.0f + EPS_A);
-        }
-        __syncthreads();
-        float* xs = nk;  // staging of the normed rows [nrows][256] (nk/nv regions are free until below)
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-            if (i < nrows) xs[i * 256 + d] = (x[i] * rr[256 + i]) * (i < qper ? wq : wk);
-        __syncthreads();
-        // interleaved mRoPE on the first `rot` dims; text positions: the three position rows are equal
-        float y[32];
-        const int f = d < half ? d : d - half;
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-            if (i < nrows) {
-                float xv = xs[i * 256 + d];
-                if (d < a.rot) {
-                    const int pi = i < qper ? 0 : 1 + (i - qper);
-                    const float cs = tab[2 * (pi * half + f)], sn = tab[2 * (pi * half + f) + 1];
-                    xv = d < half ? xv * cs - xs[i * 256 + d + half] * sn : xv * cs + xs[i * 256 + d - half] * sn;
-                }
-                y[i] = xv;
-            }
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-            if (i < qper) qs[i * 256 + d] = y[i] * 0.0625f;  // queries scaled by 1/sqrt(256)
-            else if (i < nrows) {
-                int u = u0 + i - qper;
-                nk[u * 256 + d] = y[i];
-                a.kc[((size_t)(off + u) * KV + kh) * 256 + d] = y[i];
-            }
-        }
-        for (int h = qper; h < QP; h++) qs[h * 256 + d] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; i++)
-            if (i < nkeys) {
-                int u = u0 + i;
-                nv[u * 256 + d] = vvals[i];
-                a.vc[((size_t)(off + u) * KV + kh) * 256 + d] = vvals[i];
-            }
+        for (int e = threadIdx.x; e < (QP - qper) * 256; e += 256) qs[qper * 256 + e] = 0.0f;
         if (d < QP) {
             stt[d] = -INFINITY;
             stt[QP + d] = 0.0f;
         }
+        // values of this pass's keys in range: to shared memory and the cache
+        for (int e = threadIdx.x; e < nkeys * 64; e += 256) {
+            const int i = e >> 6, c = (e & 63) * 4;
+            const float4 v4 = *(const float4*)(a.qkv + (size_t)(u0 + i) * a.ld + 2 * aw + kvw + kh * 256 + c);
+            *(float4*)(nv + i * 256 + c) = v4;
+            *(float4*)(a.vc + ((size_t)(off + u0 + i) * KV + kh) * 256 + c) = v4;
+        }
+        __syncthreads();  // the cos/sin table
+        // rows to prepare, one warp each: the qper query heads of row t, then this pass's keys in range. A lane holds
+        // dims [8 lane, 8 lane + 8): RMSNorm (warp sum of squares), weight, then the rotation of the first `rot`
+        // dims against their partner d +- rot/2 read back from the row in shared memory.
+        for (int r = w; r < qper + nkeys; r += 8) {
+            const bool isq = r < qper;
+            const float* src = isq ? a.qkv + (size_t)t * a.ld + (kh * qper + r) * 512
+                                   : a.qkv + (size_t)(u0 + r - qper) * a.ld + 2 * aw + kh * 256;
+            float* dst = isq ? qs + r * 256 : nk + (r - qper) * 256;
+            const float* wn = isq ? a.qn : a.kn;
+            float x[8];
+            *(float4*)&x[0] = *(const float4*)(src + lane * 8);
+            *(float4*)&x[4] = *(const float4*)(src + lane * 8 + 4);
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) ss += x[i] * x[i];
+            const float rs = rsqrtf(warp_sum(ss) / 256.0f + EPS_A);
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = (x[i] * rs) * wn[lane * 8 + i];
+            *(float4*)(dst + lane * 8) = *(const float4*)&x[0];
+            *(float4*)(dst + lane * 8 + 4) = *(const float4*)&x[4];
+            __syncwarp();
+            float y[8];
+            const int pi = isq ? 0 : 1 + (r - qper);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int dd = lane * 8 + i;
+                y[i] = x[i];
+                if (dd < a.rot) {
+                    const int f = dd < half ? dd : dd - half;
+                    const float cs = tab[2 * (pi * half + f)], sn = tab[2 * (pi * half + f) + 1];
+                    y[i] = dd < half ? x[i] * cs - dst[dd + half] * sn : x[i] * cs + dst[dd - half] * sn;
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; i++) y[i] = isq ? y[i] * 0.0625f : y[i];  // queries scaled by 1/sqrt(256)
+            *(float4*)(dst + lane * 8) = *(const float4*)&y[0];
+            *(float4*)(dst + lane * 8 + 4) = *(const float4*)&y[4];
+            if (!isq) {
+                float* kd = a.kc + ((size_t)(off + u0 + r - qper) * KV + kh) * 256 + lane * 8;
+                *(float4*)kd = *(const float4*)&y[0];
+                *(float4*)(kd + 4) = *(const float4*)&y[4];
+            }
+        }
+        __syncthreads();
 
-        // blocks of keys in order: the cached blocks, then this pass's keys; online softmax per query head
         float acc[QP];
 #pragma unroll
         for (int h = 0; h < QP; h++) acc[h] = 0.0f;
-        const int kj = d >> 4, kc = d & 15;  // score mapping: key kj of the block, dims 4 kc + 64 i (i < 4)
-        const int nblk = nst + (nkeys > 0 ? 1 : 0);
-        for (int st = 0; st < nblk; st++) {
-            const bool cached = st < nst;
-            const float *kb, *vb;
-            int nr;
-            if (cached) {
-                if (st + 1 < nst) cp_async_wait_group<1>();
-                else cp_async_wait_group<0>();
-                kb = ks + (st & 1) * KST * 256;
-                vb = vs + (st & 1) * KST * 256;
-                nr = min(KST, jc1 - (j0 + st * KST));
-            } else {
-                kb = nk + u0 * 256;
-                vb = nv + u0 * 256;
-                nr = nkeys;
-            }
-            __syncthreads();
-            // scores: 16 threads per key, each 16 dims for all heads, then a halving butterfly over the 16
-            {
-                float part[QP];
+        const int hsel = HG > 1 ? (lane >> (5 - LHG)) & (HG - 1) : 0;
+        const bool writer = (lane & ((32 >> LHG) - 1)) == 0;
+        for (int jb = j0; jb < j1; jb += SUB) {
+            const int nr = min(SUB, j1 - jb);
+            // scores of the round: warp w takes keys jb + w, jb + w + 8, ...
 #pragma unroll
-                for (int h = 0; h < QP; h++) part[h] = 0.0f;
-                if (kj < nr) {
-                    float4 k4[4];
+            for (int hg = 0; hg < QP; hg += HG) {
+                float qr[HG][8];
 #pragma unroll
-                    for (int i = 0; i < 4; i++) k4[i] = *(const float4*)(kb + kj * 256 + 4 * kc + 64 * i);
+                for (int h = 0; h < HG; h++) {
+                    *(float4*)&qr[h][0] = *(const float4*)(qs + (hg + h) * 256 + lane * 8);
+                    *(float4*)&qr[h][4] = *(const float4*)(qs + (hg + h) * 256 + lane * 8 + 4);
+                }
+                for (int j = w; j < nr; j += 8) {
+                    const int jj = jb + j;
+                    const float* kp = jj < off ? a.kc + ((size_t)jj * KV + kh) * 256 : nk + (jj - off - u0) * 256;
+                    float k[8];
+                    *(float4*)&k[0] = *(const float4*)(kp + lane * 8);
+                    *(float4*)&k[4] = *(const float4*)(kp + lane * 8 + 4);
+                    float part[HG];
 #pragma unroll
-                    for (int h = 0; h < QP; h++) {
+                    for (int h = 0; h < HG; h++) {
                         float a2 = 0.0f;
 #pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const float4 q4 = *(const float4*)(qs + h * 256 + 4 * kc + 64 * i);
-                            a2 += q4.x * k4[i].x + q4.y * k4[i].y + q4.z * k4[i].z + q4.w * k4[i].w;
-                        }
+                        for (int i = 0; i < 8; i++) a2 += qr[h][i] * k[i];
                         part[h] = a2;
                     }
-                }
-                // reduce over the 16 lanes of the key (offsets 8, 4, 2, 1): lane kc ends with head kc * QP / 16
-                // (QP >= 16) or, for QP < 16, head (kc >> log2(16 / QP)) summed over the remaining lanes
+                    // halving butterfly: lane ends with the warp total of head hsel
 #pragma unroll
-                for (int o = 8, nn = QP; o > 0; o >>= 1) {
-                    if (nn > 1) {
-                        const bool up = (lane & o) != 0;
-                        const int hn = nn / 2;
+                    for (int o = 16, nn = HG; o > 0; o >>= 1) {
+                        if (nn > 1) {
+                            const bool up = (lane & o) != 0;
+                            const int hn = nn / 2;
 #pragma unroll
-                        for (int j = 0; j < hn; j++) {
-                            const float send = up ? part[j] : part[j + hn];
-                            const float keep = up ? part[j + hn] : part[j];
-                            part[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                            for (int q = 0; q < hn; q++) {
+                                const float send = up ? part[q] : part[q + hn];
+                                const float keep = up ? part[q + hn] : part[q];
+                                part[q] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                            }
+                            nn = hn;
+                        } else {
+                            part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
                         }
-                        nn = hn;
-                    } else {
-                        part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
                     }
+                    if (writer) pr[j * QP + hg + hsel] = part[0];
                 }
-                // lane bits (from offset 8 down) select the half kept at each halving stage
-                int hsel = 0, nn2 = QP;
-#pragma unroll
-                for (int o = 8; o > 0 && nn2 > 1; o >>= 1) {
-                    hsel = hsel * 2 + ((lane & o) ? 1 : 0);
-                    nn2 >>= 1;
-                }
-                const int lanes_per_head = 16 / (QP < 16 ? QP : 16);
-                if (kj < nr && (kc % lanes_per_head) == 0 && hsel < QP) sc[hsel * KST + kj] = part[0];
             }
             __syncthreads();
+            // softmax statistics of the round per head (warp h), probabilities in place
             for (int h = w; h < qper; h += 8) {
-                const float sv = lane < nr ? sc[h * KST + lane] : -INFINITY;
+                float mx = -INFINITY;
+                for (int j = lane; j < nr; j += 32) mx = fmaxf(mx, pr[j * QP + h]);
                 const float mo = stt[h];
-                const float mn = fmaxf(mo, warp_max(sv));
-                const float p = lane < nr ? expf(sv - mn) : 0.0f;
-                const float ps = warp_sum(p);
-                if (lane < KST) pj[lane * QP + h] = p;
+                const float mn = fmaxf(mo, warp_max(mx));
+                float ps = 0.0f;
+                for (int j = lane; j < nr; j += 32) {
+                    const float p = expf(pr[j * QP + h] - mn);
+                    pr[j * QP + h] = p;
+                    ps += p;
+                }
+                ps = warp_sum(ps);
                 if (lane == 0) {
                     const float al = expf(mo - mn);
                     stt[2 * QP + h] = al;
@@ -248,33 +194,27 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
                 }
             }
             __syncthreads();
-            // P.V: thread = head dim, keys in order
-            {
-                float al[QP];
+            // P.V: thread = head dim, keys in order, 8 value loads in flight
 #pragma unroll
-                for (int h = 0; h < QP; h++) al[h] = h < qper ? stt[2 * QP + h] : 0.0f;
+            for (int h = 0; h < QP; h++) acc[h] *= h < qper ? stt[2 * QP + h] : 0.0f;
+            for (int j8 = 0; j8 < nr; j8 += 8) {
+                float vv[8];
 #pragma unroll
-                for (int h = 0; h < QP; h++) acc[h] *= al[h];
-                float vv[KST];
+                for (int q = 0; q < 8; q++) {
+                    const int jj = jb + j8 + q;
+                    vv[q] = 0.0f;
+                    if (j8 + q < nr)
+                        vv[q] = jj < off ? a.vc[((size_t)jj * KV + kh) * 256 + d] : nv[(jj - off - u0) * 256 + d];
+                }
 #pragma unroll
-                for (int j = 0; j < KST; j++) vv[j] = j < nr ? vb[j * 256 + d] : 0.0f;
+                for (int q = 0; q < 8; q++)
+                    if (j8 + q < nr) {
+                        const float* pj = pr + (j8 + q) * QP;
 #pragma unroll
-                for (int j = 0; j < KST; j++)
-                    if (j < nr) {
-#pragma unroll
-                        for (int h4 = 0; h4 < (QP + 3) / 4; h4++) {
-                            float4 p4;
-                            if (QP >= 4) p4 = *(const float4*)(pj + j * QP + 4 * h4);
-                            else p4 = make_float4(pj[j * QP], QP > 1 ? pj[j * QP + 1] : 0.0f, 0.0f, 0.0f);
-                            if (4 * h4 + 0 < QP) acc[4 * h4 + 0] += p4.x * vv[j];
-                            if (4 * h4 + 1 < QP) acc[4 * h4 + 1] += p4.y * vv[j];
-                            if (4 * h4 + 2 < QP) acc[4 * h4 + 2] += p4.z * vv[j];
-                            if (4 * h4 + 3 < QP) acc[4 * h4 + 3] += p4.w * vv[j];
-                        }
+                        for (int h = 0; h < QP; h++) acc[h] += pj[h] * vv[q];
                     }
             }
-            __syncthreads();  // the block's buffers are free
-            if (cached && st + 2 < nst) issue(st + 2);
+            __syncthreads();  // the round's scores are consumed
         }
 #pragma unroll
         for (int h = 0; h < QP; h++)
