@@ -22,7 +22,8 @@ constexpr int SUB = 512;  // keys scored per round
 // Shared memory (floats): queries [QP][256], this pass's keys and values in range [VMAX][256] each, scores then
 // probabilities of a round [SUB][QP], running max / sum / rescale [4][QP], cos/sin table [(1 + VMAX)][rot].
 __host__ __device__ inline size_t attn_smem_floats(int qp, int rot) {
-    return (size_t)qp * 256 + 2 * VMAX * 256 + (size_t)SUB * qp + 4 * (size_t)qp + (size_t)(1 + VMAX) * rot;
+    return (size_t)qp * 256 + 2 * VMAX * 256 + (size_t)(SUB > 1024 ? SUB : 1024) * qp + 4 * (size_t)qp +
+           (size_t)(1 + VMAX) * rot;
 }
 
 // QP = query heads per kv head rounded up to a power of two (heads qper..QP-1 are zero padding).
@@ -39,8 +40,8 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
     float* qs = sm;                  // [QP][256]
     float* nk = qs + QP * 256;       // [VMAX][256] keys of this pass in range, index u - u0
     float* nv = nk + VMAX * 256;     // [VMAX][256] their values
-    float* pr = nv + VMAX * 256;     // [SUB][QP] scores, then probabilities
-    float* stt = pr + SUB * QP;      // [QP] running max, [QP] running sum, [QP] rescale of the round
+    float* pr = nv + VMAX * 256;     // [SUB][QP] scores, then probabilities; at the end the P.V phases [4][QP][256]
+    float* stt = pr + (SUB > 1024 ? SUB : 1024) * QP;  // [QP] running max, [QP] running sum, [QP] rescale
     float* tab = stt + 4 * QP;       // [1 + VMAX][half] (cos, sin): row 0 the query position, 1 + i key u0 + i
     pdl_trigger();
     pdl_wait();
@@ -122,9 +123,10 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
         }
         __syncthreads();
 
-        float acc[QP];
+        float acc[QP][4];
 #pragma unroll
-        for (int h = 0; h < QP; h++) acc[h] = 0.0f;
+        for (int h = 0; h < QP; h++) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.0f;
+        const int ph = threadIdx.x >> 6, dc = (threadIdx.x & 63) * 4;
         const int hsel = HG > 1 ? (lane >> (5 - LHG)) & (HG - 1) : 0;
         const bool writer = (lane & ((32 >> LHG) - 1)) == 0;
         for (int jb = j0; jb < j1; jb += SUB) {
@@ -132,44 +134,59 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             // scores of the round: warp w takes keys jb + w, jb + w + 8, ...
 #pragma unroll
             for (int hg = 0; hg < QP; hg += HG) {
-                float qr[HG][8];
+                // KU keys per warp iteration, their loads issued together; each query head's 8 dims are read from
+                // shared memory once per iteration and applied to the KU keys
+                constexpr int KU = 4;
+                for (int j = w; j < nr; j += 8 * KU) {
+                    float k[KU][8];
 #pragma unroll
-                for (int h = 0; h < HG; h++) {
-                    *(float4*)&qr[h][0] = *(const float4*)(qs + (hg + h) * 256 + lane * 8);
-                    *(float4*)&qr[h][4] = *(const float4*)(qs + (hg + h) * 256 + lane * 8 + 4);
-                }
-                for (int j = w; j < nr; j += 8) {
-                    const int jj = jb + j;
-                    const float* kp = jj < off ? a.kc + ((size_t)jj * KV + kh) * 256 : nk + (jj - off - u0) * 256;
-                    float k[8];
-                    *(float4*)&k[0] = *(const float4*)(kp + lane * 8);
-                    *(float4*)&k[4] = *(const float4*)(kp + lane * 8 + 4);
-                    float part[HG];
-#pragma unroll
-                    for (int h = 0; h < HG; h++) {
-                        float a2 = 0.0f;
-#pragma unroll
-                        for (int i = 0; i < 8; i++) a2 += qr[h][i] * k[i];
-                        part[h] = a2;
-                    }
-                    // halving butterfly: lane ends with the warp total of head hsel
-#pragma unroll
-                    for (int o = 16, nn = HG; o > 0; o >>= 1) {
-                        if (nn > 1) {
-                            const bool up = (lane & o) != 0;
-                            const int hn = nn / 2;
-#pragma unroll
-                            for (int q = 0; q < hn; q++) {
-                                const float send = up ? part[q] : part[q + hn];
-                                const float keep = up ? part[q + hn] : part[q];
-                                part[q] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                            }
-                            nn = hn;
+                    for (int u = 0; u < KU; u++) {
+                        const int jl = j + 8 * u, jj = jb + jl;
+                        if (jl < nr) {
+                            const float* kp = jj < off ? a.kc + ((size_t)jj * KV + kh) * 256 : nk + (jj - off - u0) * 256;
+                            *(float4*)&k[u][0] = *(const float4*)(kp + lane * 8);
+                            *(float4*)&k[u][4] = *(const float4*)(kp + lane * 8 + 4);
                         } else {
-                            part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+#pragma unroll
+                            for (int i = 0; i < 8; i++) k[u][i] = 0.0f;
                         }
                     }
-                    if (writer) pr[j * QP + hg + hsel] = part[0];
+                    float part[KU][HG];
+#pragma unroll
+                    for (int h = 0; h < HG; h++) {
+                        float qv[8];
+                        *(float4*)&qv[0] = *(const float4*)(qs + (hg + h) * 256 + lane * 8);
+                        *(float4*)&qv[4] = *(const float4*)(qs + (hg + h) * 256 + lane * 8 + 4);
+#pragma unroll
+                        for (int u = 0; u < KU; u++) {
+                            float a2 = 0.0f;
+#pragma unroll
+                            for (int i = 0; i < 8; i++) a2 += qv[i] * k[u][i];
+                            part[u][h] = a2;
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < KU; u++) {
+                        const int jl = j + 8 * u;
+                        // halving butterfly: lane ends with the warp total of head hsel
+#pragma unroll
+                        for (int o = 16, nn = HG; o > 0; o >>= 1) {
+                            if (nn > 1) {
+                                const bool up = (lane & o) != 0;
+                                const int hn = nn / 2;
+#pragma unroll
+                                for (int q = 0; q < hn; q++) {
+                                    const float send = up ? part[u][q] : part[u][q + hn];
+                                    const float keep = up ? part[u][q + hn] : part[u][q];
+                                    part[u][q] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                                }
+                                nn = hn;
+                            } else {
+                                part[u][0] += __shfl_xor_sync(0xffffffffu, part[u][0], o);
+                            }
+                        }
+                        if (writer && jl < nr) pr[jl * QP + hg + hsel] = part[u][0];
+                    }
                 }
             }
             __syncthreads();
@@ -194,38 +211,57 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
                 }
             }
             __syncthreads();
-            // P.V: thread = head dim, keys in order, 8 value loads in flight
+            // P.V: thread = (key phase ph = tid / 64, dims 4 (tid % 64) .. + 3); phase ph takes the round's keys
+            // ph, ph + 4, ... in order, 4 value rows in flight; the phases are summed in order after the keys
 #pragma unroll
-            for (int h = 0; h < QP; h++) acc[h] *= h < qper ? stt[2 * QP + h] : 0.0f;
-            for (int j8 = 0; j8 < nr; j8 += 8) {
-                float vv[8];
+            for (int h = 0; h < QP; h++) {
+                const float al = h < qper ? stt[2 * QP + h] : 0.0f;
 #pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const int jj = jb + j8 + q;
-                    vv[q] = 0.0f;
-                    if (j8 + q < nr)
-                        vv[q] = jj < off ? a.vc[((size_t)jj * KV + kh) * 256 + d] : nv[(jj - off - u0) * 256 + d];
+                for (int c = 0; c < 4; c++) acc[h][c] *= al;
+            }
+            for (int j4 = ph; j4 < nr; j4 += 16) {
+                float4 vv[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int jl = j4 + 4 * q, jj = jb + jl;
+                    vv[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (jl < nr)
+                        vv[q] = jj < off ? *(const float4*)(a.vc + ((size_t)jj * KV + kh) * 256 + dc)
+                                         : *(const float4*)(nv + (jj - off - u0) * 256 + dc);
                 }
 #pragma unroll
-                for (int q = 0; q < 8; q++)
-                    if (j8 + q < nr) {
-                        const float* pj = pr + (j8 + q) * QP;
+                for (int q = 0; q < 4; q++)
+                    if (j4 + 4 * q < nr) {
+                        const float* pj = pr + (j4 + 4 * q) * QP;
 #pragma unroll
-                        for (int h = 0; h < QP; h++) acc[h] += pj[h] * vv[q];
+                        for (int h = 0; h < QP; h++) {
+                            const float pv = pj[h];
+                            acc[h][0] += pv * vv[q].x;
+                            acc[h][1] += pv * vv[q].y;
+                            acc[h][2] += pv * vv[q].z;
+                            acc[h][3] += pv * vv[q].w;
+                        }
                     }
             }
             __syncthreads();  // the round's scores are consumed
         }
+        // the four key phases, summed in phase order (the round buffer is free): [ph][h][256]
+        float* ps = pr;
 #pragma unroll
         for (int h = 0; h < QP; h++)
-            if (h < qper) {
-                float* ph = pp + (size_t)h * NSPLIT_ATTN * 258;
-                if (d == 0) {
-                    ph[0] = stt[h];
-                    ph[1] = stt[QP + h];
-                }
-                ph[2 + d] = acc[h];
+            if (h < qper) *(float4*)(ps + ((size_t)ph * QP + h) * 256 + dc) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        __syncthreads();
+        for (int h = 0; h < qper; h++) {
+            float o = ps[(size_t)h * 256 + d];
+#pragma unroll
+            for (int q = 1; q < 4; q++) o += ps[((size_t)q * QP + h) * 256 + d];
+            float* pq = pp + (size_t)h * NSPLIT_ATTN * 258;
+            if (d == 0) {
+                pq[0] = stt[h];
+                pq[1] = stt[QP + h];
             }
+            pq[2 + d] = o;
+        }
     } else if (d < qper) {
         pp[(size_t)d * NSPLIT_ATTN * 258] = -INFINITY;
         pp[(size_t)d * NSPLIT_ATTN * 258 + 1] = 0.0f;
