@@ -159,6 +159,7 @@ SIGNATURES = {
     "bcu_stream": (I32, [P, ctypes.POINTER(P)]),
     # host-logic exports (not in the ABI header: test hooks of the decode driver and the operand build)
     "bcu_set_local_build": (I32, [P, I32]),
+    "bcu_set_batched_prefill": (I32, [P, I32]),
     "bcu_linear_set_local_build": (I32, [P, I32]),
     "bcu_static_scratch_debug": (I32, [I32, I32]),
     "bcu_debug_wait_timeout": (I32, [P]),

@@ -163,6 +163,10 @@ class Model:
         self.adapter = ident
         self.prefixes = [p for p in self.prefixes if p[1] == ident]
 
+    def set_batched_prefill(self, on=True):
+        """Test hook: bcu_prefill runs long prompts as tcgen05 GEMM chunks (on, the default) or as verify passes."""
+        self._ck(self.L.bcu_set_batched_prefill(self.h, 1 if on else 0))
+
     def set_local_build(self, local=True):
         """Test hook: every GEMV builds its operand per CTA instead of once across its grid."""
         self._ck(self.L.bcu_set_local_build(self.h, 1 if local else 0))

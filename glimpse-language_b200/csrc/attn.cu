@@ -45,18 +45,22 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
     float* tab = stt + 4 * QP;       // [1 + VMAX][half] (cos, sin): row 0 the query position, 1 + i key u0 + i
     pdl_trigger();
     pdl_wait();
-    const int off = a.ctl->off;
+    // prefill mode (a.qprep): the queries come prepared and every key of the chunk is already in the cache
+    const bool pre = a.qprep != nullptr;
+    const int off = pre ? a.off0 : a.ctl->off;
     const int n = off + t + 1;
-    const int chunk = (n + NSPLIT_ATTN - 1) / NSPLIT_ATTN;
+    const int NS = a.nsplit;
+    const int chunk = (n + NS - 1) / NS;
     const int j0 = s * chunk, j1 = min(n, j0 + chunk);
-    float* pp = a.part + ((size_t)t * H + kh * qper) * NSPLIT_ATTN * 258 + (size_t)s * 258;
+    const int koff = pre ? n : off;  // keys below koff are read from the cache, the others were prepared here
+    float* pp = a.part + ((size_t)t * H + kh * qper) * NS * 258 + (size_t)s * 258;
     if (n > a.ctx) {
         if (d == 0 && s == 0 && kh == 0) atomicOr(&((Ctl*)a.ctl)->err, ERR_CTX_FULL);
         return;
     }
     if (j0 < j1) {
-        const int u0 = max(j0, off) - off, u1 = j1 - off, nkeys = max(u1 - u0, 0);
-        for (int e = threadIdx.x; e < (1 + nkeys) * half; e += 256) {
+        const int u0 = max(j0, koff) - koff, u1 = j1 - koff, nkeys = max(u1 - u0, 0);
+        for (int e = threadIdx.x; e < (pre ? 0 : (1 + nkeys) * half); e += 256) {
             const int pi = e / half, f = e - pi * half;
             const int pos = pi == 0 ? off + t : off + u0 + pi - 1;
             float sn, cs;
@@ -82,6 +86,12 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
         // dims against their partner d +- rot/2 read back from the row in shared memory.
         for (int r = w; r < qper + nkeys; r += 8) {
             const bool isq = r < qper;
+            if (pre) {  // prepared query rows [T][H][256] (normed, rotated, scaled)
+                const float* qsrc = a.qprep + ((size_t)t * H + kh * qper + r) * 256 + lane * 8;
+                *(float4*)(qs + r * 256 + lane * 8) = *(const float4*)qsrc;
+                *(float4*)(qs + r * 256 + lane * 8 + 4) = *(const float4*)(qsrc + 4);
+                continue;
+            }
             const float* src = isq ? a.qkv + (size_t)t * a.ld + (kh * qper + r) * 512
                                    : a.qkv + (size_t)(u0 + r - qper) * a.ld + 2 * aw + kh * 256;
             float* dst = isq ? qs + r * 256 : nk + (r - qper) * 256;
@@ -143,7 +153,7 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
                     for (int u = 0; u < KU; u++) {
                         const int jl = j + 8 * u, jj = jb + jl;
                         if (jl < nr) {
-                            const float* kp = jj < off ? a.kc + ((size_t)jj * KV + kh) * 256 : nk + (jj - off - u0) * 256;
+                            const float* kp = jj < koff ? a.kc + ((size_t)jj * KV + kh) * 256 : nk + (jj - koff - u0) * 256;
                             *(float4*)&k[u][0] = *(const float4*)(kp + lane * 8);
                             *(float4*)&k[u][4] = *(const float4*)(kp + lane * 8 + 4);
                         } else {
@@ -226,8 +236,8 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
                     const int jl = j4 + 4 * q, jj = jb + jl;
                     vv[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                     if (jl < nr)
-                        vv[q] = jj < off ? *(const float4*)(a.vc + ((size_t)jj * KV + kh) * 256 + dc)
-                                         : *(const float4*)(nv + (jj - off - u0) * 256 + dc);
+                        vv[q] = jj < koff ? *(const float4*)(a.vc + ((size_t)jj * KV + kh) * 256 + dc)
+                                          : *(const float4*)(nv + (jj - koff - u0) * 256 + dc);
                 }
 #pragma unroll
                 for (int q = 0; q < 4; q++)
@@ -255,7 +265,7 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             float o = ps[(size_t)h * 256 + d];
 #pragma unroll
             for (int q = 1; q < 4; q++) o += ps[((size_t)q * QP + h) * 256 + d];
-            float* pq = pp + (size_t)h * NSPLIT_ATTN * 258;
+            float* pq = pp + (size_t)h * NS * 258;
             if (d == 0) {
                 pq[0] = stt[h];
                 pq[1] = stt[QP + h];
@@ -263,8 +273,8 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             pq[2 + d] = o;
         }
     } else if (d < qper) {
-        pp[(size_t)d * NSPLIT_ATTN * 258] = -INFINITY;
-        pp[(size_t)d * NSPLIT_ATTN * 258 + 1] = 0.0f;
+        pp[(size_t)d * NS * 258] = -INFINITY;
+        pp[(size_t)d * NS * 258 + 1] = 0.0f;
     }
     // the last split CTA of (t, kh) merges (fixed split order)
     __syncthreads();
@@ -274,11 +284,11 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
                      : "=r"(old)
                      : "l"(a.counters + t * KV + kh)
                      : "memory");
-        s_last = old == NSPLIT_ATTN - 1;
+        s_last = old == (unsigned)(NS - 1);
     }
     __syncthreads();
     if (!s_last) return;
-    const float* p0 = a.part + ((size_t)t * H + kh * qper) * NSPLIT_ATTN * 258;
+    const float* p0 = a.part + ((size_t)t * H + kh * qper) * NS * 258;
     float* mls = qs;  // [qper][NSPLIT][2]
     float av[2][NSPLIT_ATTN], an[2][NSPLIT_ATTN];
     auto load_av = [&](int h0, float (*dst)[NSPLIT_ATTN]) {
@@ -286,12 +296,12 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
         for (int hh = 0; hh < 2; hh++)
 #pragma unroll
             for (int q = 0; q < NSPLIT_ATTN; q++)
-                dst[hh][q] = h0 + hh < qper ? __ldcg(p0 + (size_t)(h0 + hh) * NSPLIT_ATTN * 258 + q * 258 + 2 + d) : 0.0f;
+                dst[hh][q] = h0 + hh < qper && q < NS ? __ldcg(p0 + (size_t)(h0 + hh) * NS * 258 + q * 258 + 2 + d) : 0.0f;
     };
     load_av(0, av);
-    for (int e = threadIdx.x; e < qper * NSPLIT_ATTN * 2; e += 256) {
-        const int h = e / (2 * NSPLIT_ATTN), r = e - h * 2 * NSPLIT_ATTN;
-        mls[e] = __ldcg(p0 + (size_t)h * NSPLIT_ATTN * 258 + (r >> 1) * 258 + (r & 1));
+    for (int e = threadIdx.x; e < qper * NS * 2; e += 256) {
+        const int h = e / (2 * NS), r = e - h * 2 * NS;
+        mls[h * NSPLIT_ATTN * 2 + r] = __ldcg(p0 + (size_t)h * NS * 258 + (r >> 1) * 258 + (r & 1));
     }
     __syncthreads();
     for (int h0 = 0; h0 < qper; h0 += 2) {
@@ -303,11 +313,12 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
             const float* m2 = mls + h * NSPLIT_ATTN * 2;
             float M = -INFINITY;
 #pragma unroll
-            for (int q = 0; q < NSPLIT_ATTN; q++) M = fmaxf(M, m2[2 * q]);
+            for (int q = 0; q < NSPLIT_ATTN; q++)
+                if (q < NS) M = fmaxf(M, m2[2 * q]);
             float L = 0.0f, o = 0.0f;
 #pragma unroll
             for (int q = 0; q < NSPLIT_ATTN; q++) {
-                if (m2[2 * q] == -INFINITY) continue;
+                if (q >= NS || m2[2 * q] == -INFINITY) continue;
                 const float wgt = expf(m2[2 * q] - M);
                 L += m2[2 * q + 1] * wgt;
                 o += av[hh][q] * wgt;
@@ -332,7 +343,7 @@ static void launch_attn_t(const AttnArgs& a, cudaStream_t st) {
     }
     AttnArgs aa = a;
     void* args[] = {&aa};
-    launch_pdl((const void*)attn_kernel<QP>, dim3(a.KV, NSPLIT_ATTN, a.T), dim3(256), smem, st, args);
+    launch_pdl((const void*)attn_kernel<QP>, dim3(a.KV, a.nsplit, a.T), dim3(256), smem, st, args);
 }
 
 void launch_attn(const AttnArgs& a, cudaStream_t st) {

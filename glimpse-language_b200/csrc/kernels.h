@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "ctl.h"
+
 namespace bcu {
 
 struct Ctl;
@@ -141,6 +143,11 @@ struct AttnArgs {
     unsigned* counters;    // [VMAX][KV] zero between launches
     float* out;            // [T][H*256]
     int H, KV, rot, T, ld, ctx;
+    int nsplit = NSPLIT_ATTN;       // key splits per (row, kv head), 1..NSPLIT_ATTN
+    // prefill mode: queries prepared by pf_attn_prep ([T][H][256]), every key of rows [0, off0 + T) in the cache,
+    // row t at position off0 + t (counters [T][KV], part [T][H][nsplit][258])
+    const float* qprep = nullptr;
+    int off0 = 0;
 };
 void launch_attn(const AttnArgs& a, cudaStream_t st);
 
@@ -193,6 +200,32 @@ void gemm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int O, i
 void gemm_prep_only(const float* x, int M, int K, int G, uint8_t* bop, int* ex, cudaStream_t st);
 cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int G, const float* x, int M, uint8_t* bop,
                      int* ex, float* y, int* err, int num_sms, cudaStream_t st);
+
+// ------------------------------------------------------------------------------------------------ batched prefill
+// Producer kernels of the prefill chunk (prefill.cu): one row per CTA, x of the mode, signs, Walsh-Hadamard in blocks
+// of hb, fp32 rows for the GEMM.
+enum PfMode : int { PF_NORM = 0, PF_GATED = 1, PF_GATE = 2, PF_SWIGLU = 3 };
+struct PfRowArgs {
+    int mode = PF_NORM, D = 0, ld2 = 0;
+    float* h = nullptr;            // NORM: [M][D] residual rows (updated when add != null)
+    const float* add = nullptr;    // NORM: [M][D] added to h first, or null
+    const float* src = nullptr;    // GATED: y [M][D]; GATE: attn [M][D]; SWIGLU: [M][2D]
+    const float* src2 = nullptr;   // GATED: z rows; GATE: q projection rows (row stride ld2)
+    const float* w = nullptr;      // NORM: [D]; GATED: [128]
+    const float* signs = nullptr;  // [D] or null
+    float* xn = nullptr;           // NORM: unrotated normed rows, or null
+    float* xr = nullptr;           // [M][D] rotated rows
+};
+void launch_pf_rows(const PfRowArgs& a, int M, int hb, cudaStream_t st);
+void launch_pf_embed(const uint32_t* ids, int M, int V, int d, const uint16_t* bf16, const uint32_t* tw,
+                     const uint16_t* ts, const uint16_t* tb, const float* signs, int group, float* h, int* err,
+                     cudaStream_t st);
+void launch_pf_gdn_ab(const float* wa, const float* wb, const float* xn, float* ga, float* gb, int NV, int d, int M,
+                      cudaStream_t st);
+void launch_pf_gdn_conv(const float* qkv, int ld, float* cstate, const float* cw, float* q, float* k, float* v, int NK,
+                        int NV, int C, int M, cudaStream_t st);
+void launch_pf_attn_prep(const float* mix, int ld, const float* qn, const float* kn, const float* inv_freq, int rot,
+                         int H, int KV, int off, int M, float* qout, float* kc, float* vc, cudaStream_t st);
 
 // Generic launch helper (PDL attribute on).
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args);

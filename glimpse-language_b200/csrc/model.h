@@ -24,6 +24,20 @@ struct Lin {
     TernaryMat m;
     const float* signs = nullptr;
     LoraArgs lora;  // a == null: no adapter on this linear
+    // the same matrix in the prefill GEMM's layout (gemm.cu), null when a part is not whole 256-row tiles
+    uint8_t* gwt = nullptr;
+    uint8_t* gbias = nullptr;
+};
+
+// Scratch of the batched prefill, sized for PF_CHUNK rows on first use.
+struct Prefill {
+    int cap = 0;
+    float *h = nullptr, *xr = nullptr, *xn = nullptr, *mix = nullptr, *y = nullptr, *gu = nullptr, *tmp = nullptr;
+    float *q = nullptr, *k = nullptr, *v = nullptr, *ga = nullptr, *gb = nullptr, *qbuf = nullptr, *part = nullptr;
+    unsigned* counters = nullptr;
+    uint8_t* bop = nullptr;
+    int* ex = nullptr;
+    uint32_t* ids = nullptr;
 };
 
 struct Layer {
@@ -122,6 +136,11 @@ struct bcu_model {
     float* lora_upart = nullptr;
     int lora_rank = 0, lora_linears = 0;
     size_t lora_bytes = 0;  // fp16 A and B of every adapted group, read once per pass
+
+    // batched prefill (prefill.cu) and every other allocation freed with the model
+    bcu::Prefill pf;
+    bool pf_off = false;  // test hook: prefill with verify passes only
+    std::vector<void*> extra_allocs;
 
     // drafting
     std::vector<uint64_t> keys;   // token_key per vocab id

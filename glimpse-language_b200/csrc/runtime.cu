@@ -183,6 +183,30 @@ bcu_status build_lin(bcu_model* m, const std::vector<Part>& parts, int K, Lin* o
     }
     plan_ternary(tm, m->num_sms, m->c.hadamard);
     out->m = tm;
+    // the same matrix in the prefill GEMM's layout (gemm.cu), when every part is whole 256-row tiles
+    bool tiles = true;
+    for (auto& p : parts) tiles = tiles && p.O % 256 == 0;
+    out->gwt = out->gbias = nullptr;
+    if (tiles) {
+        uint8_t *gw = nullptr, *gb = nullptr;
+        if (cudaMalloc(&gw, gemm_w_bytes(O, K)) != cudaSuccess) return fail(m, BCU_ERR_OOM, "prefill GEMM weights");
+        m->extra_allocs.push_back(gw);
+        if (cudaMalloc(&gb, gemm_bias_bytes(O, K, group)) != cudaSuccess)
+            return fail(m, BCU_ERR_OOM, "prefill GEMM weights");
+        m->extra_allocs.push_back(gb);
+        int r = 0;
+        for (auto& p : parts) {
+            const DevTensor* w = find(m, p.name + ".weight");
+            const DevTensor* s = find(m, p.name + ".scales");
+            const DevTensor* b = m->c.has_bias ? find(m, p.name + ".biases") : nullptr;
+            gemm_pack((const uint32_t*)w->dev, (const uint16_t*)s->dev, b ? (const uint16_t*)b->dev : nullptr, p.O, K,
+                      group, gw + gemm_w_bytes(r, K), gb + gemm_bias_bytes(r, K, group), m->st);
+            CK(cudaGetLastError());
+            r += p.O;
+        }
+        out->gwt = gw;
+        out->gbias = gb;
+    }
     out->signs = nullptr;
     if (m->c.has_signs) {
         const DevTensor* sg = find(m, parts[0].name + ".signs");
@@ -761,6 +785,7 @@ void bcu_destroy(bcu_model* m) {
                     m->opbuf, m->op_counters, m->lora_buf, m->lora_upart};
     for (void* b : bufs)
         if (b) cudaFree(b);
+    for (void* b : m->extra_allocs) cudaFree(b);
     if (m->h_in) cudaFreeHost(m->h_in);
     if (m->in_ring) cudaFreeHost(m->in_ring);
     for (auto e : m->in_ev)
@@ -784,10 +809,198 @@ bcu_status bcu_device_name(const bcu_model* m, char* out, size_t out_len) {
     return BCU_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+constexpr int PF_CHUNK = 512;  // rows per batched prefill chunk (the reference's TMAX, model.rs:9)
+constexpr int PF_MIN = 64;     // shorter prompts run as verify passes
+constexpr int PF_NSPLIT = 4;   // key splits per (row, kv head) of the chunk's attention
+
+// Whether the batched prefill can run: every linear has its GEMM layout, and no adapter is set (the prefill GEMM has
+// no LoRA epilogue; adapted models prefill with verify passes).
+bool pf_supported(const bcu_model* m) {
+    if (m->lora_linears > 0) return false;
+    for (auto& L : m->layers)
+        for (const Lin* ln : {&L.mix_in, &L.mix_out, &L.gu, &L.down})
+            if (!ln->gwt) return false;
+    return true;
+}
+
+bcu_status pf_alloc(bcu_model* m) {
+    Prefill& p = m->pf;
+    if (p.cap) return BCU_OK;
+    const bcu_config& c = m->c;
+    const size_t P = PF_CHUNK, d = c.hidden, ff = c.intermediate;
+    const size_t wide = std::max(std::max(d, ff), (size_t)std::max(m->gw, m->aw));
+    const size_t mixw = std::max(m->C + m->gw, 2 * m->aw + 2 * m->kvw);
+    const int kmax = (int)std::max(std::max(d, ff), (size_t)std::max(m->gw, m->aw));
+    auto get = [&](auto** ptr, size_t bytes) -> bcu_status {
+        TRY(dmalloc(m, ptr, bytes));
+        m->extra_allocs.push_back((void*)*ptr);
+        return BCU_OK;
+    };
+    TRY(get(&p.h, P * d * 4));
+    TRY(get(&p.xr, P * wide * 4));
+    TRY(get(&p.xn, P * d * 4));
+    TRY(get(&p.mix, P * mixw * 4));
+    TRY(get(&p.y, P * std::max(m->gw, m->aw) * 4));
+    TRY(get(&p.gu, P * 2 * ff * 4));
+    TRY(get(&p.tmp, P * d * 4));
+    TRY(get(&p.q, P * c.lin_k_heads * 128 * 4));
+    TRY(get(&p.k, P * c.lin_k_heads * 128 * 4));
+    TRY(get(&p.v, P * c.lin_v_heads * 128 * 4));
+    TRY(get(&p.ga, P * c.lin_v_heads * 4));
+    TRY(get(&p.gb, P * c.lin_v_heads * 4));
+    TRY(get(&p.qbuf, P * m->aw * 4));
+    TRY(get(&p.part, P * c.heads * PF_NSPLIT * 258 * 4));
+    TRY(get(&p.counters, P * c.kv_heads * 4));
+    TRY(get(&p.bop, gemm_act_bytes((int)P, kmax, c.group_size)));
+    TRY(get(&p.ex, P * 4));
+    TRY(get(&p.ids, P * 4));
+    p.cap = (int)P;
+    return BCU_OK;
+}
+
+// One linear of the chunk on the tcgen05 GEMM: y[M][O] = W . x.
+bcu_status pf_gemm(bcu_model* m, const Lin& ln, const float* x, int M, float* y) {
+    CK(gemm_run(ln.gwt, ln.gbias, ln.m.O, ln.m.K, ln.m.group, x, M, m->pf.bop, m->pf.ex, y, &m->ctl->err, m->num_sms,
+                m->st));
+    return BCU_OK;
+}
+
+// Model::prefill's forward of M rows (ids on the host) at positions off .. off + M - 1 (encode_layers_at,
+// model.rs:670-934, without the head): the committed state advances by M rows. par: the control block's parity
+// (the committed conv rows live in half par ^ 1 of each layer's double buffer).
+bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) {
+    const bcu_config& c = m->c;
+    Prefill& p = m->pf;
+    cudaStream_t st = m->st;
+    const int d = c.hidden, ff = c.intermediate, HB = c.hadamard, NK = c.lin_k_heads, NV = c.lin_v_heads;
+    const int C = m->C, gw = m->gw, aw = m->aw, kvw = m->kvw;
+    CK(cudaMemcpyAsync(p.ids, ids, (size_t)M * 4, cudaMemcpyHostToDevice, st));
+    const bool tern = c.head_kind == BCU_HEAD_TERNARY;
+    launch_pf_embed(p.ids, M, c.vocab, d, tern ? nullptr : m->embed_rows, m->emb_w, m->emb_s, m->emb_b,
+                    m->head_lin.signs, c.group_size, p.h, &m->ctl->err, st);
+    const float* pending = nullptr;  // the previous residual linear's output, added to h by the next RMSNorm
+    for (size_t li = 0; li < m->layers.size(); li++) {
+        const Layer& L = m->layers[li];
+        const bool last = li + 1 == m->layers.size();
+        PfRowArgs in;
+        in.mode = PF_NORM;
+        in.D = d;
+        in.h = p.h;
+        in.add = pending;
+        in.w = L.in_norm;
+        in.signs = L.mix_in.signs;
+        in.xn = L.attn ? nullptr : p.xn;
+        in.xr = p.xr;
+        launch_pf_rows(in, M, HB, st);
+        TRY(pf_gemm(m, L.mix_in, p.xr, M, p.mix));
+        PfRowArgs out;
+        out.D = L.attn ? aw : gw;
+        out.src = p.y;
+        out.signs = L.mix_out.signs;
+        out.xr = p.xr;
+        if (!L.attn) {
+            launch_pf_gdn_ab(L.wa, L.wb, p.xn, p.ga, p.gb, NV, d, M, st);
+            float* cs = m->conv + ((size_t)L.gi * 2 + (par ^ 1)) * 3 * C;  // the committed half
+            launch_pf_gdn_conv(p.mix, C + gw, cs, L.convw, p.q, p.k, p.v, NK, NV, C, M, st);
+            launch_gdn_verify(p.q, p.k, p.v, p.ga, p.gb, L.a_log, L.dt_bias,
+                              m->gdn + (size_t)L.gi * NV * 128 * 128, p.y, M, NK, NV, M, st);
+            out.mode = PF_GATED;
+            out.src2 = p.mix + C;
+            out.ld2 = C + gw;
+            out.w = L.gnorm;
+        } else {
+            const int ld = 2 * aw + 2 * kvw;
+            float* kc = m->kc + (size_t)L.ai * c.ctx * kvw;
+            float* vc = m->vc + (size_t)L.ai * c.ctx * kvw;
+            launch_pf_attn_prep(p.mix, ld, L.qn, L.kn, m->inv_freq, c.rotary_dims, c.heads, c.kv_heads, off, M, p.qbuf,
+                                kc, vc, st);
+            AttnArgs a{};
+            a.ctl = m->ctl;
+            a.qkv = p.mix;
+            a.qn = L.qn;
+            a.kn = L.kn;
+            a.inv_freq = m->inv_freq;
+            a.kc = kc;
+            a.vc = vc;
+            a.part = p.part;
+            a.counters = p.counters;
+            a.out = p.y;
+            a.H = c.heads;
+            a.KV = c.kv_heads;
+            a.rot = c.rotary_dims;
+            a.T = M;
+            a.ld = ld;
+            a.ctx = c.ctx;
+            a.nsplit = PF_NSPLIT;
+            a.qprep = p.qbuf;
+            a.off0 = off;
+            launch_attn(a, st);
+            out.mode = PF_GATE;
+            out.src2 = p.mix;
+            out.ld2 = ld;
+        }
+        CK(cudaGetLastError());
+        // the last layer's outputs only feed the residual rows of this chunk, which nothing reads: its state
+        // updates above are all the chunk needs from it
+        if (last) break;
+        launch_pf_rows(out, M, HB, st);
+        TRY(pf_gemm(m, L.mix_out, p.xr, M, p.tmp));
+        PfRowArgs post;
+        post.mode = PF_NORM;
+        post.D = d;
+        post.h = p.h;
+        post.add = p.tmp;
+        post.w = L.post_norm;
+        post.signs = L.gu.signs;
+        post.xr = p.xr;
+        launch_pf_rows(post, M, HB, st);
+        TRY(pf_gemm(m, L.gu, p.xr, M, p.gu));
+        PfRowArgs sw;
+        sw.mode = PF_SWIGLU;
+        sw.D = ff;
+        sw.src = p.gu;
+        sw.signs = L.down.signs;
+        sw.xr = p.xr;
+        launch_pf_rows(sw, M, HB, st);
+        TRY(pf_gemm(m, L.down, p.xr, M, p.tmp));
+        pending = p.tmp;
+        CK(cudaGetLastError());
+    }
+    return BCU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 bcu_status bcu_prefill(bcu_model* m, const uint32_t* ids, int32_t n, uint32_t* next) {
     if (!m || !ids || n < 1) return fail(m, BCU_ERR_ARG, "prefill needs at least one id");
     CK(cudaSetDevice(m->device));
     if (m->len + n > m->c.ctx) return fail(m, BCU_ERR_STATE, "context full");
+    // batched: every row but the last through the tcgen05 GEMM in chunks; the last row then runs as a one-row pass,
+    // which returns the next token
+    if (n - 1 >= PF_MIN && !m->pf_off && pf_supported(m)) {
+        TRY(bcu_flush(m));
+        TRY(read_ctl(m));
+        const int par = m->h_out->parity, off = m->h_out->off;
+        TRY(pf_alloc(m));
+        for (int i = 0; i < n - 1; i += PF_CHUNK) {
+            const int M = std::min(PF_CHUNK, n - 1 - i);
+            TRY(pf_chunk(m, ids + i, M, off + i, par));
+        }
+        TRY(read_ctl(m));  // device errors of the chunks
+        ctl_set_kernel<<<1, 1, 0, m->st>>>(m->ctl, off + n - 1, 0);
+        CK(cudaGetLastError());
+        m->len = off + n - 1;
+        m->pending_n = 0;
+        TRY(run_pass(m, ids + n - 1, 1, 1, 0, true));
+        if (next) *next = m->h_out->bonus;
+        return BCU_OK;
+    }
     int chunk = m->c.vmax;
     for (int i = 0; i < n; i += chunk) {
         int t = std::min(chunk, n - i);
@@ -1121,6 +1334,14 @@ bcu_status bcu_debug_wait_timeout(bcu_model* m) {
     wait_timeout_kernel<<<1, 1, 0, m->st>>>(m->ctl, m->op_counters + 256, 1u << 14);
     CK(cudaGetLastError());
     return read_ctl(m);
+}
+
+// Test hook (not in the ABI header): batched != 0 lets bcu_prefill use the tcgen05 GEMM chunks (the default), 0 keeps
+// it to verify passes, so tests can compare the two.
+bcu_status bcu_set_batched_prefill(bcu_model* m, int32_t batched) {
+    if (!m) return BCU_ERR_ARG;
+    m->pf_off = batched == 0;
+    return BCU_OK;
 }
 
 // Test hook (not in the ABI header): local != 0 makes every GEMV build its operand per CTA (build_operand) instead of
