@@ -250,11 +250,12 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
     launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(256), gdn_smem_bytes(), st, args);
 }
 
-// Graded config 2: T rows from explicit q/k/v/gate inputs, outputs for every row, and the state written back as it
-// was after the first n rows (the checkpoint taken in registers while the rows run). CTA = (value head, 16 dv rows),
-// 256 threads: warp w owns dv rows 2w, 2w + 1 (short per-warp step chains: the steps are latency-bound). Rows are
-// staged in shared memory GV_CHUNK at a time, every load of a chunk in flight at once, so the sequential steps wait
-// on no global load.
+// Graded config 2 (and the prefill chunk's recurrence): T rows from explicit q/k/v/gate inputs, outputs for every
+// row, and the state written back as it was after the first n rows (the checkpoint taken in registers while the rows
+// run). CTA = (value head, 16 dv rows), 256 threads: warp w owns dv rows 2w, 2w + 1 (short per-warp step chains: the
+// steps are latency-bound). Rows are staged in shared memory GV_CHUNK at a time in two buffers: the loads of chunk
+// c + 1 are issued before the steps of chunk c and stored after them, so the sequential steps never wait on a global
+// load after the first chunk.
 constexpr int GV_CHUNK = 16;
 struct __align__(16) GvSmem {
     float q[GV_CHUNK][128];
@@ -267,23 +268,18 @@ __global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const f
                                                          const float* a_in, const float* b_in, const float* a_log,
                                                          const float* dt_bias, float* state, float* y, int T, int NK,
                                                          int NV, int n) {
-    __shared__ GvSmem sm;
+    __shared__ GvSmem sm[2];
     const int hd = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int hk = hd / (NV / NK);
     const int dvb = blockIdx.y * 16, dv0 = dvb + w * 2;
     const int ch = tid & 127;           // q channel (threads < 128) or k channel (the others) staged by this thread
     const float* qk = tid < 128 ? q : k;
-    float (*sqk)[128] = tid < 128 ? sm.q : sm.k;
     float4 st[2], keep[2];
     float* S = state + ((size_t)hd * 128 + dv0) * 128 + lane * 4;
     const float ea = expf(a_log[hd]), dtb = dt_bias[hd];
-    pdl_trigger();
-    pdl_wait();
-#pragma unroll
-    for (int r = 0; r < 2; r++) keep[r] = st[r] = *(const float4*)(S + (size_t)r * 128);
-    for (int t0 = 0; t0 < T; t0 += GV_CHUNK) {
+    float lqk[GV_CHUNK], lv[GV_CHUNK], ga = 0.0f, gb = 0.0f;
+    auto load = [&](int t0) {  // chunk at row t0 into registers
         const int nr = min(GV_CHUNK, T - t0);
-        float lqk[GV_CHUNK], lv[GV_CHUNK];
 #pragma unroll
         for (int r = 0; r < GV_CHUNK; r++)
             if (r < nr) {
@@ -291,33 +287,49 @@ __global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const f
                 lqk[r] = qk[(t * NK + hk) * 128 + ch];
                 lv[r] = tid < 16 ? v[(t * NV + hd) * 128 + dvb + tid] : 0.0f;
             }
-        float ga = 0.0f, gb = 0.0f;
         if (tid < nr) {
             ga = a_in[(size_t)(t0 + tid) * NV + hd];
             gb = b_in[(size_t)(t0 + tid) * NV + hd];
         }
+    };
+    auto store = [&](int t0, GvSmem& b) {  // registers into a staging buffer
+        const int nr = min(GV_CHUNK, T - t0);
+        float (*sqk)[128] = tid < 128 ? b.q : b.k;
 #pragma unroll
         for (int r = 0; r < GV_CHUNK; r++)
             if (r < nr) {
                 sqk[r][ch] = lqk[r];
-                if (tid < 16) sm.v[r][tid] = lv[r];
+                if (tid < 16) b.v[r][tid] = lv[r];
             }
-        if (tid < nr) gates(ga, gb, ea, dtb, sm.g[tid], sm.beta[tid]);
-        __syncthreads();
+        if (tid < nr) gates(ga, gb, ea, dtb, b.g[tid], b.beta[tid]);
+    };
+    pdl_trigger();
+    pdl_wait();
+#pragma unroll
+    for (int r = 0; r < 2; r++) keep[r] = st[r] = *(const float4*)(S + (size_t)r * 128);
+    load(0);
+    store(0, sm[0]);
+    __syncthreads();
+    for (int t0 = 0, c = 0; t0 < T; t0 += GV_CHUNK, c++) {
+        const int nr = min(GV_CHUNK, T - t0);
+        const bool more = t0 + GV_CHUNK < T;
+        if (more) load(t0 + GV_CHUNK);
+        const GvSmem& b = sm[c & 1];
         for (int r = 0; r < nr; r++) {
-            const float4 qq = *(const float4*)&sm.q[r][lane * 4];
-            const float4 kk = *(const float4*)&sm.k[r][lane * 4];
-            const float2 v2 = *(const float2*)&sm.v[r][w * 2];
+            const float4 qq = *(const float4*)&b.q[r][lane * 4];
+            const float4 kk = *(const float4*)&b.k[r][lane * 4];
+            const float2 v2 = *(const float2*)&b.v[r][w * 2];
             const float vv[2] = {v2.x, v2.y};
             float o[2];
-            gdn_step_fused<2>(st, qq, kk, vv, sm.g[r], sm.beta[r], o);
+            gdn_step_fused<2>(st, qq, kk, vv, b.g[r], b.beta[r], o);
             if (lane < 2) y[((size_t)(t0 + r) * NV + hd) * 128 + dv0 + lane] = lane == 0 ? o[0] : o[1];
             if (t0 + r + 1 == n) {
                 keep[0] = st[0];
                 keep[1] = st[1];
             }
         }
-        __syncthreads();  // the next chunk overwrites the rows
+        if (more) store(t0 + GV_CHUNK, sm[(c + 1) & 1]);
+        __syncthreads();  // the next chunk is staged; this one's buffer may be refilled after the next barrier
     }
 #pragma unroll
     for (int r = 0; r < 2; r++) *(float4*)(S + (size_t)r * 128) = keep[r];

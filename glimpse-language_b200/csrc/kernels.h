@@ -224,6 +224,9 @@ void launch_pf_gdn_ab(const float* wa, const float* wb, const float* xn, float* 
                       cudaStream_t st);
 void launch_pf_gdn_conv(const float* qkv, int ld, float* cstate, const float* cw, float* q, float* k, float* v, int NK,
                         int NV, int C, int M, cudaStream_t st);
+// y[M][O] += B (A xu) of one adapted linear (LoRA, the device layout of LoraArgs), u [M][R] scratch.
+void launch_pf_lora(const uint16_t* A, const uint16_t* B, int R, int r, int m1, int m2, int K, int O, int hb,
+                    const float* xu, float* u, float* y, int M, cudaStream_t st);
 void launch_pf_attn_prep(const float* mix, int ld, const float* qn, const float* kn, const float* inv_freq, int rot,
                          int H, int KV, int off, int M, float* qout, float* kc, float* vc, cudaStream_t st);
 

@@ -34,6 +34,7 @@ struct Prefill {
     int cap = 0;
     float *h = nullptr, *xr = nullptr, *xn = nullptr, *mix = nullptr, *y = nullptr, *gu = nullptr, *tmp = nullptr;
     float *q = nullptr, *k = nullptr, *v = nullptr, *ga = nullptr, *gb = nullptr, *qbuf = nullptr, *part = nullptr;
+    float* lu = nullptr;  // LoRA A products [rows][3 x 256]
     unsigned* counters = nullptr;
     uint8_t* bop = nullptr;
     int* ex = nullptr;

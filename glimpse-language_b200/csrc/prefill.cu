@@ -49,7 +49,8 @@ __device__ __forceinline__ void fwht_block(float* v) {
 
 // One row per CTA (256 threads): the producer value x_k of the mode, then xr = rotate(signs * x) in blocks of
 // HB = 32 VPL (warp w takes blocks w, w + 8, ...). NORM: x = rmsnorm(h) * w, after h += add (the residual of the
-// previous linear, written back); xn (optional) keeps x unrotated for the GDN a/b rows. GATED: per 128-wide head
+// previous linear, written back). xn (optional, every mode) keeps x unrotated: the GDN a/b rows' input and the
+// LoRA input of the linear that follows (lora.rs:1-3: the adapter sees the unrotated input). GATED: per 128-wide head
 // (((z * y) * rsqrt(mean(y^2) + eps)) * w) * sigmoid(z), z at src2 (row stride ld2). GATE: attn * sigmoid(gate),
 // the gate half of the q projection at src2 (per head 256 q then 256 gate values). SWIGLU: (g * u) * sigmoid(g), g
 // and u the two halves of a [2D] row.
@@ -118,6 +119,10 @@ __global__ void __launch_bounds__(256) pf_rows_kernel(PfRowArgs a) {
                 const float g = a.src[(size_t)row * 2 * D + k], u = a.src[(size_t)row * 2 * D + D + k];
                 v[e] = __fmul_rn(__fmul_rn(g, u), sigm_p(g));
             }
+        }
+        if (a.xn && a.mode != PF_NORM) {
+#pragma unroll
+            for (int e = 0; e < VPL; e++) a.xn[(size_t)row * D + b0 + lane + 32 * e] = v[e];
         }
         if (a.signs) {
 #pragma unroll
@@ -260,6 +265,58 @@ __global__ void __launch_bounds__(256) pf_attn_prep_kernel(const float* mix, int
     }
     if (isq) qout[((size_t)t * H + hh) * 256 + d] = y * 0.0625f;
     else kc[((size_t)pos * KV + (hh - H)) * 256 + d] = y;
+}
+
+// LoRA A of a linear over the chunk (norm_rotate's fused A rows, kernels.metal:70-116): u[t][q] = A[q] . xu[t] for
+// the R stacked rows of the adapter's group, A fp16 in the device layout [K / HB][R][32 lanes][HB / 32] (element e of
+// lane l of block b is input b HB + l + 32 e). One warp per (row, A row): lane l sums its inputs (blocks in order,
+// elements in order), then the warp tree.
+template <int VPL>
+__global__ void __launch_bounds__(256) pf_lora_a_kernel(const uint16_t* A, int R, int K, const float* xu, float* u) {
+    const int t = blockIdx.x, q = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (q >= R) return;
+    constexpr int HB = VPL * 32;
+    const float* x = xu + (size_t)t * K;
+    float acc = 0.0f;
+    for (int b = 0; b < K / HB; b++) {
+        const uint4* ap = (const uint4*)(A + (((size_t)b * R + q) * 32 + lane) * VPL);
+#pragma unroll
+        for (int w8 = 0; w8 < VPL / 8; w8++) {
+            const uint4 w = __ldg(ap + w8);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const float2 f = __half22float2(*(const __half2*)&ws[h]);
+                const int e = 8 * w8 + 2 * h;
+                acc = fmaf(f.x, x[b * HB + lane + 32 * e], acc);
+                acc = fmaf(f.y, x[b * HB + lane + 32 * (e + 1)], acc);
+            }
+        }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) u[(size_t)t * R + q] = acc;
+}
+
+// LoRA B (store_post's up projection, kernels.metal:251-262): y[t][o] += B[o] . u[t][member of o], B fp16 [O][r],
+// members at rows [0, m1), [m1, m2), [m2, O) with u columns [i r, (i + 1) r). One thread per output.
+__global__ void __launch_bounds__(256) pf_lora_b_kernel(const uint16_t* B, int r, int R, int m1, int m2, int O,
+                                                        const float* u, float* y) {
+    const int t = blockIdx.x, o = blockIdx.y * 256 + threadIdx.x;
+    if (o >= O) return;
+    const int mem = (o >= m1) + (o >= m2);
+    const float* ut = u + (size_t)t * R + mem * r;
+    const __half* br = (const __half*)B + (size_t)o * r;
+    float a = 0.0f;
+    for (int j = 0; j < r; j++) a = fmaf(ut[j], __half2float(br[j]), a);
+    y[(size_t)t * O + o] += a;
+}
+
+void launch_pf_lora(const uint16_t* A, const uint16_t* B, int R, int r, int m1, int m2, int K, int O, int hb,
+                    const float* xu, float* u, float* y, int M, cudaStream_t st) {
+    const dim3 ga(M, (R + 7) / 8);
+    if (hb == 512) pf_lora_a_kernel<16><<<ga, 256, 0, st>>>(A, R, K, xu, u);
+    else pf_lora_a_kernel<32><<<ga, 256, 0, st>>>(A, R, K, xu, u);
+    pf_lora_b_kernel<<<dim3(M, (O + 255) / 256), 256, 0, st>>>(B, r, R, m1, m2, O, u, y);
 }
 
 void launch_pf_embed(const uint32_t* ids, int M, int V, int d, const uint16_t* bf16, const uint32_t* tw,

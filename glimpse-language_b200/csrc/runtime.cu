@@ -813,14 +813,15 @@ bcu_status bcu_device_name(const bcu_model* m, char* out, size_t out_len) {
 
 namespace {
 
-constexpr int PF_CHUNK = 512;  // rows per batched prefill chunk (the reference's TMAX, model.rs:9)
+// rows per batched prefill chunk: larger than the reference's TMAX (512, model.rs:9) for fuller GEMM tiles; every
+// row's result is independent of the chunking (row-local producers and GEMM, a row's attention splits set by its own
+// position, the recurrence sequential)
+constexpr int PF_CHUNK = 2048;
 constexpr int PF_MIN = 64;     // shorter prompts run as verify passes
 constexpr int PF_NSPLIT = 4;   // key splits per (row, kv head) of the chunk's attention
 
-// Whether the batched prefill can run: every linear has its GEMM layout, and no adapter is set (the prefill GEMM has
-// no LoRA epilogue; adapted models prefill with verify passes).
+// Whether the batched prefill can run: every linear has its GEMM layout.
 bool pf_supported(const bcu_model* m) {
-    if (m->lora_linears > 0) return false;
     for (auto& L : m->layers)
         for (const Lin* ln : {&L.mix_in, &L.mix_out, &L.gu, &L.down})
             if (!ln->gwt) return false;
@@ -842,7 +843,8 @@ bcu_status pf_alloc(bcu_model* m) {
     };
     TRY(get(&p.h, P * d * 4));
     TRY(get(&p.xr, P * wide * 4));
-    TRY(get(&p.xn, P * d * 4));
+    TRY(get(&p.xn, P * wide * 4));
+    TRY(get(&p.lu, P * 3 * 256 * 4));
     TRY(get(&p.mix, P * mixw * 4));
     TRY(get(&p.y, P * std::max(m->gw, m->aw) * 4));
     TRY(get(&p.gu, P * 2 * ff * 4));
@@ -862,10 +864,16 @@ bcu_status pf_alloc(bcu_model* m) {
     return BCU_OK;
 }
 
-// One linear of the chunk on the tcgen05 GEMM: y[M][O] = W . x.
-bcu_status pf_gemm(bcu_model* m, const Lin& ln, const float* x, int M, float* y) {
+// One linear of the chunk on the tcgen05 GEMM: y[M][O] = W . x (rotated rows), plus its adapter's B (A xu) on the
+// unrotated rows xu when one is set.
+bcu_status pf_gemm(bcu_model* m, const Lin& ln, const float* x, const float* xu, int M, float* y) {
     CK(gemm_run(ln.gwt, ln.gbias, ln.m.O, ln.m.K, ln.m.group, x, M, m->pf.bop, m->pf.ex, y, &m->ctl->err, m->num_sms,
                 m->st));
+    if (ln.lora.a) {
+        const LoraArgs& L = ln.lora;
+        launch_pf_lora(L.a, L.b, L.R, L.r, L.m1, L.m2, ln.m.K, ln.m.O, m->c.hadamard, xu, m->pf.lu, y, M, m->st);
+        CK(cudaGetLastError());
+    }
     return BCU_OK;
 }
 
@@ -893,14 +901,15 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         in.add = pending;
         in.w = L.in_norm;
         in.signs = L.mix_in.signs;
-        in.xn = L.attn ? nullptr : p.xn;
+        in.xn = p.xn;
         in.xr = p.xr;
         launch_pf_rows(in, M, HB, st);
-        TRY(pf_gemm(m, L.mix_in, p.xr, M, p.mix));
+        TRY(pf_gemm(m, L.mix_in, p.xr, p.xn, M, p.mix));
         PfRowArgs out;
         out.D = L.attn ? aw : gw;
         out.src = p.y;
         out.signs = L.mix_out.signs;
+        out.xn = p.xn;
         out.xr = p.xr;
         if (!L.attn) {
             launch_pf_gdn_ab(L.wa, L.wb, p.xn, p.ga, p.gb, NV, d, M, st);
@@ -948,7 +957,7 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         // updates above are all the chunk needs from it
         if (last) break;
         launch_pf_rows(out, M, HB, st);
-        TRY(pf_gemm(m, L.mix_out, p.xr, M, p.tmp));
+        TRY(pf_gemm(m, L.mix_out, p.xr, p.xn, M, p.tmp));
         PfRowArgs post;
         post.mode = PF_NORM;
         post.D = d;
@@ -956,17 +965,19 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         post.add = p.tmp;
         post.w = L.post_norm;
         post.signs = L.gu.signs;
+        post.xn = p.xn;
         post.xr = p.xr;
         launch_pf_rows(post, M, HB, st);
-        TRY(pf_gemm(m, L.gu, p.xr, M, p.gu));
+        TRY(pf_gemm(m, L.gu, p.xr, p.xn, M, p.gu));
         PfRowArgs sw;
         sw.mode = PF_SWIGLU;
         sw.D = ff;
         sw.src = p.gu;
         sw.signs = L.down.signs;
+        sw.xn = p.xn;
         sw.xr = p.xr;
         launch_pf_rows(sw, M, HB, st);
-        TRY(pf_gemm(m, L.down, p.xr, M, p.tmp));
+        TRY(pf_gemm(m, L.down, p.xr, p.xn, M, p.tmp));
         pending = p.tmp;
         CK(cudaGetLastError());
     }

@@ -179,3 +179,30 @@ def test_lora_errors_keep_installed_adapter(setup):
             assert m.lora_info() == (len(lins), 8)  # unchanged
     finally:
         m.set_lora_linears([], 1.0)
+
+
+def test_lora_batched_prefill_matches_oracle(setup):
+    """A 150-token prompt with the adapter runs through the batched prefill (tcgen05 GEMM chunks plus the adapter's
+    A and B kernels): the next token and the verify-pass logits after it match the oracle with the same adapter."""
+    name, cfg, ts, m, o = setup
+    if cfg.ctx < 170:
+        pytest.skip("context too short for a batched prefill")
+    ids = synth.zipf_tokens(13, 150, cfg.vocab)
+    rows = synth.zipf_tokens(14, 9, cfg.vocab)
+    lins = synth.lora_linears(cfg, 16, seed=9, std_b=0.05)
+    m.set_lora_linears(lins, 2.0)
+    o.set_lora(lins, 2.0)
+    try:
+        m.reset()
+        o.reset()
+        assert m.prefill(ids) == o.prefill(ids)
+        m.keep_logits(True)
+        m.verify(rows)
+        got = np.stack([m.logits(t) for t in range(len(rows))])
+        m.keep_logits(False)
+        want = o.forward(rows, logits=True)[1]
+        err = np.abs(got - want).max()
+        assert err <= LOGIT_TOL, f"{name}: max logit error {err}"
+    finally:
+        m.set_lora_linears([], 1.0)
+        o.clear_lora()
