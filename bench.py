@@ -188,7 +188,139 @@ WORKLOAD_5 = ("config5 (linears only): the 96 ternary GEMMs of the Bonsai-2B sha
               "2048 tokens = 65536 prefill rows per GPU, fp32 activations in HBM")
 
 
+SESSIONS_5, TOKENS_5 = 32, 2048
+WORKLOAD_5M = ("config5: whole-model batched prefill of the Bonsai-2B shape (random-init, g64 + bias, bf16 tied head), "
+               "32 sessions x 2048 Zipf(1.1) tokens per GPU, each session's prompt through bcu_prefill (tcgen05 GEMM "
+               "chunks for the first 2047 rows, then one verify-pass row that returns the next token)")
+
+
+def prefill_flops(cfg, rows):
+    """Algorithmic flops of a batched prefill of `rows` rows from an empty context: 2 M O K per executed linear (the
+    last layer runs only up to its state update: its mixer output and MLP linears feed nothing) plus causal attention
+    (q.k and p.v, 4 flops per query-key-dim) of every attention layer but the last."""
+    from bonsai_b200.config import dims
+
+    d, ff = cfg.hidden, cfg.intermediate
+    dm = dims(cfg)
+    n = cfg.n_layers
+    f = 0.0
+    for i in range(n):
+        attn = bool(cfg.layer_is_attn[i])
+        mix_in = (2 * dm["aw"] + 2 * dm["kvw"]) if attn else (dm["C"] + dm["gw"])
+        f += 2.0 * rows * mix_in * d
+        if i == n - 1:
+            break
+        f += 2.0 * rows * d * (dm["aw"] if attn else dm["gw"]) + 2.0 * rows * 2 * ff * d + 2.0 * rows * d * ff
+        if attn:
+            f += 4.0 * cfg.heads * 256 * rows * (rows + 1) / 2
+    return f
+
+
 def run_config5(args, ws, rank, local):
+    """Config 5: whole-model batched prefill, 32 sessions x 2048 tokens per GPU (sessions one after another on one
+    model; each bcu_prefill runs its prompt as tcgen05 GEMM chunks)."""
+    import torch
+
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    from bonsai_b200 import config, synth
+    from bonsai_b200.runtime import Model
+
+    cfg = config.bonsai_2b_graded(ctx=TOKENS_5 + 64)
+    ts = synth.model_tensors(cfg, args.seed)
+    m = Model(cfg, device=0).load(ts)
+    prompts = [synth.zipf_tokens(args.seed + 100 + s, TOKENS_5, cfg.vocab) for s in range(SESSIONS_5)]
+    stream = torch.cuda.ExternalStream(m.stream())
+
+    def step():
+        nxt = []
+        for ids in prompts:
+            m.reset()
+            nxt.append(m.prefill(ids))
+        return nxt
+
+    for _ in range(max(1, args.warmup)):
+        m.reset()
+        m.prefill(prompts[0])
+    clocks = Clocks(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    firsts = None
+    for _ in range(args.steps):
+        firsts = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    ck = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
+    e2e_s = max_over_ranks(wall, dist, "cuda")
+    rows = SESSIONS_5 * TOKENS_5
+    flops_step = SESSIONS_5 * prefill_flops(cfg, TOKENS_5 - 1)
+    achieved = flops_step / (ms / args.steps / 1000) / 1e12
+    pk = peaks() or {}
+    peak = pk.get("bf16_tflops_sustained", 1400.0)
+    n_attn = sum(cfg.layer_is_attn[i] for i in range(cfg.n_layers))
+    n_gdn = cfg.n_layers - n_attn
+    # launches of one session: embed, per GDN layer 4 producers + 4 x (prep + GEMM) + a/b, conv, conv rows,
+    # recurrence; per attention layer 4 producers + 4 x 2 + prep + attention; the last layer stops after its state
+    # update (the last layer is attention here: producer + 2 + prep); then the one-row pass and its control update
+    per_session = 1 + n_gdn * 16 + (n_attn - 1) * 14 + 4 + m.pass_launches(1) + 1
+    line = {
+        "metric": "prefill tok/s/GPU (whole model, Bonsai-2B shape, batched prefill on tcgen05)",
+        "value": whole_job_rate(ws, rows * args.steps, ms / 1000), "unit": "tok/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": max(1, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 activations (fp16 hi + lo on the tensor cores) x fp16 weights, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights, Zipf(1.1) prompts)",
+        "config": {"workload": WORKLOAD_5M, "sessions": SESSIONS_5, "tokens_per_session": TOKENS_5,
+                   "rows_per_step": rows, "parallelism": f"replicas x{ws}",
+                   "l2": "inputs larger than L2 (1.6 GB of weights and 0.5 GB of activations per chunk)"},
+        "e2e": {"value": whole_job_rate(ws, rows * args.steps, e2e_s), "unit": "tok/s",
+                "h2d_bytes_per_step": rows * 4, "d2h_bytes_per_step": SESSIONS_5 * 4 + SESSIONS_5 * 1024,
+                "path": "bcu_prefill (C ABI) per session: prompt ids from host memory, next token back"},
+        "gpu_launches": ws * args.steps * SESSIONS_5 * per_session,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "whole prefill (linears on ternary_gemm_kernel, attention, GDN recurrence, producers)",
+                     "flops_per_step": flops_step,
+                     "note": "algorithmic flops: 2 M O K of the executed linears + causal attention; the fp16 hi + lo "
+                             "split issues 2x the linear flops on the tensor cores",
+                     "peak_source": "MEASURED_PEAKS.json bf16 sustained" if pk else "fallback"},
+        "first_tokens": [int(t) for t in firsts[:4]],
+        "clocks": ck,
+    }
+    if rank == 0 and not args.no_cpu and ws == 1:
+        from oracle.oracle import OracleModel
+
+        o = OracleModel(cfg, ts)
+        sample = 16
+        t0 = time.perf_counter()
+        o.prefill(prompts[0][:sample], chunk=sample)
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": sample / secs, "unit": "tok/s",
+                                "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": "port",
+                                "sample": f"the oracle's prefill of the first {sample} tokens of a session (one chunk; "
+                                          "its head runs on every row)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_config5_linears(args, ws, rank, local):
     import ctypes
 
     import torch
@@ -511,10 +643,13 @@ def main():
                     help="profiling run for ncu: prefill --profile-prefix tokens, then this many 9-row verify passes")
     ap.add_argument("--profile-prefix", type=int, default=256)
     ap.add_argument("--rows", type=int, default=PREFILL_M,
-                    help="config5 only: prefill rows per step (65536 = 32 sessions x 2048; smaller for profiling)")
-    ap.add_argument("--workload", default="config3", choices=["config1", "config2", "config3", "config4", "config5"],
+                    help="config5-linears only: prefill rows per step (65536 = 32 sessions x 2048; smaller for "
+                         "profiling)")
+    ap.add_argument("--workload", default="config3",
+                    choices=["config1", "config2", "config3", "config4", "config5", "config5-linears"],
                     help="config3 (default, the headline); config1 / config2 (single ops), config4 (4B shape + LoRA), "
-                         "config5 (prefill linears)")
+                         "config5 (whole-model batched prefill, 32 x 2048 tokens), config5-linears (its 96 GEMMs "
+                         "alone at 65536 rows)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
 
@@ -526,6 +661,9 @@ def main():
         return
     if args.workload == "config5":
         run_config5(args, ws, rank, local)
+        return
+    if args.workload == "config5-linears":
+        run_config5_linears(args, ws, rank, local)
         return
     if args.workload in ("config1", "config2"):
         if rank == 0:
@@ -566,7 +704,8 @@ def main():
         torch.cuda.synchronize()
         t_pf = max_over_ranks(time.perf_counter() - t0, dist, "cuda")
         prefill_info = {"tokens": PROMPT_4B, "s": t_pf, "tok_s": whole_job_rate(ws, PROMPT_4B, t_pf),
-                        "path": "bcu_prefill (16-row verify passes), wall clock with synchronisation"}
+                        "path": "bcu_prefill (tcgen05 GEMM chunks, the adapter's A and B kernels; the last row as "
+                                "a verify pass), wall clock with synchronisation"}
         base_len = PROMPT_4B
     else:
         prefix = synth.zipf_tokens(args.seed + 1, PREFIX, cfg.vocab)

@@ -947,7 +947,7 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
             a.nsplit = PF_NSPLIT;
             a.qprep = p.qbuf;
             a.off0 = off;
-            launch_attn(a, st);
+            if (!last) launch_attn(a, st);  // the last layer needs only its K/V rows (written by the prep)
             out.mode = PF_GATE;
             out.src2 = p.mix;
             out.ld2 = ld;
