@@ -236,7 +236,8 @@ def run_config5(args, ws, rank, local):
     cfg = config.bonsai_2b_graded(ctx=TOKENS_5 + 64)
     ts = synth.model_tensors(cfg, args.seed)
     m = Model(cfg, device=0).load(ts)
-    prompts = [synth.zipf_tokens(args.seed + 100 + s, TOKENS_5, cfg.vocab) for s in range(SESSIONS_5)]
+    sessions = args.sessions or SESSIONS_5
+    prompts = [synth.zipf_tokens(args.seed + 100 + s, TOKENS_5, cfg.vocab) for s in range(sessions)]
     stream = torch.cuda.ExternalStream(m.stream())
 
     def step():
@@ -266,8 +267,8 @@ def run_config5(args, ws, rank, local):
     ck = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
     e2e_s = max_over_ranks(wall, dist, "cuda")
-    rows = SESSIONS_5 * TOKENS_5
-    flops_step = SESSIONS_5 * prefill_flops(cfg, TOKENS_5 - 1)
+    rows = sessions * TOKENS_5
+    flops_step = sessions * prefill_flops(cfg, TOKENS_5 - 1)
     achieved = flops_step / (ms / args.steps / 1000) / 1e12
     pk = peaks() or {}
     peak = pk.get("bf16_tflops_sustained", 1400.0)
@@ -284,13 +285,13 @@ def run_config5(args, ws, rank, local):
         "scaling": "weak", "vs_baseline": None,
         "dtype": "fp32 activations (fp16 hi + lo on the tensor cores) x fp16 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init weights, Zipf(1.1) prompts)",
-        "config": {"workload": WORKLOAD_5M, "sessions": SESSIONS_5, "tokens_per_session": TOKENS_5,
+        "config": {"workload": WORKLOAD_5M, "sessions": sessions, "tokens_per_session": TOKENS_5,
                    "rows_per_step": rows, "parallelism": f"replicas x{ws}",
                    "l2": "inputs larger than L2 (1.6 GB of weights and 0.5 GB of activations per chunk)"},
         "e2e": {"value": whole_job_rate(ws, rows * args.steps, e2e_s), "unit": "tok/s",
-                "h2d_bytes_per_step": rows * 4, "d2h_bytes_per_step": SESSIONS_5 * 4 + SESSIONS_5 * 1024,
+                "h2d_bytes_per_step": rows * 4, "d2h_bytes_per_step": sessions * (4 + 1024),
                 "path": "bcu_prefill (C ABI) per session: prompt ids from host memory, next token back"},
-        "gpu_launches": ws * args.steps * SESSIONS_5 * per_session,
+        "gpu_launches": ws * args.steps * sessions * per_session,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None,
                      "kernel": "whole prefill (linears on ternary_gemm_kernel, attention, GDN recurrence, producers)",
@@ -642,6 +643,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="profiling run for ncu: prefill --profile-prefix tokens, then this many 9-row verify passes")
     ap.add_argument("--profile-prefix", type=int, default=256)
+    ap.add_argument("--sessions", type=int, default=0,
+                    help="config5 only: sessions per step (default 32; fewer for profiling)")
     ap.add_argument("--rows", type=int, default=PREFILL_M,
                     help="config5-linears only: prefill rows per step (65536 = 32 sessions x 2048; smaller for "
                          "profiling)")
