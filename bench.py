@@ -289,7 +289,9 @@ def run_config5(args, ws, rank, local):
                    "rows_per_step": rows, "parallelism": f"replicas x{ws}",
                    "l2": "inputs larger than L2 (1.6 GB of weights and 0.5 GB of activations per chunk)"},
         "e2e": {"value": whole_job_rate(ws, rows * args.steps, e2e_s), "unit": "tok/s",
-                "h2d_bytes_per_step": rows * 4, "d2h_bytes_per_step": sessions * (4 + 1024),
+                # per session: the ids up; three control-block reads (248 B each: after the flush, after the chunks,
+                # after the last row's pass, which carries the next token) down
+                "h2d_bytes_per_step": rows * 4, "d2h_bytes_per_step": sessions * 3 * 248,
                 "path": "bcu_prefill (C ABI) per session: prompt ids from host memory, next token back"},
         "gpu_launches": ws * args.steps * sessions * per_session,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
