@@ -252,15 +252,18 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
 
 // Graded config 2 (and the prefill chunk's recurrence): T rows from explicit q/k/v/gate inputs, outputs for every
 // row, and the state written back as it was after the first n rows (the checkpoint taken in registers while the rows
-// run). CTA = (value head, 16 dv rows), 256 threads: warp w owns dv rows 2w, 2w + 1 (short per-warp step chains: the
-// steps are latency-bound). Rows are staged in shared memory GV_CHUNK at a time in two buffers: the loads of chunk
-// c + 1 are issued before the steps of chunk c and stored after them, so the sequential steps never wait on a global
-// load after the first chunk.
+// run). CTA = (value head, 32 dv rows), 256 threads: warp w owns dv rows 4w .. 4w + 3, eight lanes per row, lane
+// (r = lane / 8, s = lane % 8) holds dk entries [16 s, 16 s + 16) of row 4w + r. A step is the one-round form of
+// gdn_step_fused: u = S.k and z = S.q of the state before the step, S' = g S + delta k with delta = (v - g u) beta,
+// output g z + delta (k.q) (kernels.metal:607-620), the dot products summed over the row's 8 lanes in 3 levels.
+// Rows are staged in shared memory GV_CHUNK at a time in two buffers: the loads of chunk c + 1 are issued before the
+// steps of chunk c and stored after them, so the sequential steps never wait on a global load after the first chunk.
 constexpr int GV_CHUNK = 16;
+constexpr int GV_ROWS = 32;  // dv rows per CTA
 struct __align__(16) GvSmem {
     float q[GV_CHUNK][128];
     float k[GV_CHUNK][128];
-    float v[GV_CHUNK][16];
+    float v[GV_CHUNK][GV_ROWS];
     float g[GV_CHUNK], beta[GV_CHUNK];
 };
 
@@ -271,21 +274,22 @@ __global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const f
     __shared__ GvSmem sm[2];
     const int hd = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int hk = hd / (NV / NK);
-    const int dvb = blockIdx.y * 16, dv0 = dvb + w * 2;
+    const int dvb = blockIdx.y * GV_ROWS;
+    const int r = lane >> 3, sg = lane & 7, row = w * 4 + r;  // this lane's dv row (CTA-relative) and dk segment
     const int ch = tid & 127;           // q channel (threads < 128) or k channel (the others) staged by this thread
     const float* qk = tid < 128 ? q : k;
-    float4 st[2], keep[2];
-    float* S = state + ((size_t)hd * 128 + dv0) * 128 + lane * 4;
+    float st[16], keep[16];
+    float* S = state + ((size_t)hd * 128 + dvb + row) * 128 + sg * 16;
     const float ea = expf(a_log[hd]), dtb = dt_bias[hd];
     float lqk[GV_CHUNK], lv[GV_CHUNK], ga = 0.0f, gb = 0.0f;
     auto load = [&](int t0) {  // chunk at row t0 into registers
         const int nr = min(GV_CHUNK, T - t0);
 #pragma unroll
-        for (int r = 0; r < GV_CHUNK; r++)
-            if (r < nr) {
-                const size_t t = (size_t)(t0 + r);
-                lqk[r] = qk[(t * NK + hk) * 128 + ch];
-                lv[r] = tid < 16 ? v[(t * NV + hd) * 128 + dvb + tid] : 0.0f;
+        for (int i = 0; i < GV_CHUNK; i++)
+            if (i < nr) {
+                const size_t t = (size_t)(t0 + i);
+                lqk[i] = qk[(t * NK + hk) * 128 + ch];
+                lv[i] = tid < GV_ROWS ? v[(t * NV + hd) * 128 + dvb + tid] : 0.0f;
             }
         if (tid < nr) {
             ga = a_in[(size_t)(t0 + tid) * NV + hd];
@@ -296,17 +300,23 @@ __global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const f
         const int nr = min(GV_CHUNK, T - t0);
         float (*sqk)[128] = tid < 128 ? b.q : b.k;
 #pragma unroll
-        for (int r = 0; r < GV_CHUNK; r++)
-            if (r < nr) {
-                sqk[r][ch] = lqk[r];
-                if (tid < 16) b.v[r][tid] = lv[r];
+        for (int i = 0; i < GV_CHUNK; i++)
+            if (i < nr) {
+                sqk[i][ch] = lqk[i];
+                if (tid < GV_ROWS) b.v[i][tid] = lv[i];
             }
         if (tid < nr) gates(ga, gb, ea, dtb, b.g[tid], b.beta[tid]);
     };
     pdl_trigger();
     pdl_wait();
 #pragma unroll
-    for (int r = 0; r < 2; r++) keep[r] = st[r] = *(const float4*)(S + (size_t)r * 128);
+    for (int i = 0; i < 16; i += 4) {
+        const float4 x = *(const float4*)(S + i);
+        st[i] = keep[i] = x.x;
+        st[i + 1] = keep[i + 1] = x.y;
+        st[i + 2] = keep[i + 2] = x.z;
+        st[i + 3] = keep[i + 3] = x.w;
+    }
     load(0);
     store(0, sm[0]);
     __syncthreads();
@@ -315,31 +325,52 @@ __global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const f
         const bool more = t0 + GV_CHUNK < T;
         if (more) load(t0 + GV_CHUNK);
         const GvSmem& b = sm[c & 1];
-        for (int r = 0; r < nr; r++) {
-            const float4 qq = *(const float4*)&b.q[r][lane * 4];
-            const float4 kk = *(const float4*)&b.k[r][lane * 4];
-            const float2 v2 = *(const float2*)&b.v[r][w * 2];
-            const float vv[2] = {v2.x, v2.y};
-            float o[2];
-            gdn_step_fused<2>(st, qq, kk, vv, b.g[r], b.beta[r], o);
-            if (lane < 2) y[((size_t)(t0 + r) * NV + hd) * 128 + dv0 + lane] = lane == 0 ? o[0] : o[1];
-            if (t0 + r + 1 == n) {
-                keep[0] = st[0];
-                keep[1] = st[1];
+        for (int i = 0; i < nr; i++) {
+            float qq[16], kk[16];
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                *(float4*)&qq[j] = *(const float4*)&b.q[i][sg * 16 + j];
+                *(float4*)&kk[j] = *(const float4*)&b.k[i][sg * 16 + j];
+            }
+            float u0 = 0.0f, u1 = 0.0f, z0 = 0.0f, z1 = 0.0f, kq0 = 0.0f, kq1 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+                u0 = fmaf(st[j], kk[j], u0);
+                u1 = fmaf(st[j + 1], kk[j + 1], u1);
+                z0 = fmaf(st[j], qq[j], z0);
+                z1 = fmaf(st[j + 1], qq[j + 1], z1);
+                kq0 = fmaf(kk[j], qq[j], kq0);
+                kq1 = fmaf(kk[j + 1], qq[j + 1], kq1);
+            }
+            float u = u0 + u1, z = z0 + z1, kq = kq0 + kq1;
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                u += __shfl_xor_sync(0xffffffffu, u, o);
+                z += __shfl_xor_sync(0xffffffffu, z, o);
+                kq += __shfl_xor_sync(0xffffffffu, kq, o);
+            }
+            const float g = b.g[i], beta = b.beta[i];
+            const float delta = (b.v[i][row] - g * u) * beta;
+#pragma unroll
+            for (int j = 0; j < 16; j++) st[j] = g * st[j] + kk[j] * delta;
+            if (sg == 0) y[((size_t)(t0 + i) * NV + hd) * 128 + dvb + row] = g * z + delta * kq;
+            if (t0 + i + 1 == n) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) keep[j] = st[j];
             }
         }
         if (more) store(t0 + GV_CHUNK, sm[(c + 1) & 1]);
         __syncthreads();  // the next chunk is staged; this one's buffer may be refilled after the next barrier
     }
 #pragma unroll
-    for (int r = 0; r < 2; r++) *(float4*)(S + (size_t)r * 128) = keep[r];
+    for (int i = 0; i < 16; i += 4) *(float4*)(S + i) = make_float4(keep[i], keep[i + 1], keep[i + 2], keep[i + 3]);
 }
 
 void launch_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
                        const float* a_log, const float* dt_bias, float* state, float* y, int T, int NK, int NV,
                        int n, cudaStream_t st) {
     void* args[] = {&q, &k, &v, &a_in, &b_in, &a_log, &dt_bias, &state, &y, &T, &NK, &NV, &n};
-    launch_pdl((const void*)gdn_verify_kernel, dim3(NV, 8), dim3(256), 0, st, args);
+    launch_pdl((const void*)gdn_verify_kernel, dim3(NV, 128 / GV_ROWS), dim3(256), 0, st, args);
 }
 
 }  // namespace bcu
