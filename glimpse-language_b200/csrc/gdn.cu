@@ -258,7 +258,7 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
 // per lane and the row's 8 lanes in 3 levels. Rows are staged in shared memory GV_CHUNK at a time in two buffers (the
 // loads of chunk c + 1 are issued before the steps of chunk c and stored after them), q and k in the order
 // [float4 j][segment s][4] so the eight segments' float4 reads of one j hit 32 different banks. Measured against two
-// rows per warp with 32 lanes per row: 741 against 936 us for 2047 rows of 32 heads, equal at 9 rows.
+// rows per warp with 32 lanes per row: 706 against 936 us for 2047 rows of 32 heads, equal at 9 rows.
 constexpr int GV_CHUNK = 16;
 constexpr int GV_ROWS = 32;  // dv rows per CTA
 constexpr int GV_LPR = 8;    // lanes per dv row
@@ -292,13 +292,13 @@ __global__ void __launch_bounds__(256) gdn_verify_kernel(const float* q, const f
     float lqk[GV_CHUNK], lv[GV_CHUNK], ga = 0.0f, gb = 0.0f;
     auto load = [&](int t0) {  // chunk at row t0 into registers
         const int nr = min(GV_CHUNK, T - t0);
+        // Two separate loops: fused into one, the build ran twice as slow at 2047 rows (1491 against 706 us).
 #pragma unroll
         for (int i = 0; i < GV_CHUNK; i++)
-            if (i < nr) {
-                const size_t t = (size_t)(t0 + i);
-                lqk[i] = qk[(t * NK + hk) * 128 + ch];
-                lv[i] = tid < GV_ROWS ? v[(t * NV + hd) * 128 + dvb + tid] : 0.0f;
-            }
+            if (i < nr) lqk[i] = qk[((size_t)(t0 + i) * NK + hk) * 128 + ch];
+#pragma unroll
+        for (int i = 0; i < GV_CHUNK; i++)
+            if (i < nr) lv[i] = tid < GV_ROWS ? v[((size_t)(t0 + i) * NV + hd) * 128 + dvb + tid] : 0.0f;
         if (tid < nr) {
             ga = a_in[(size_t)(t0 + tid) * NV + hd];
             gb = b_in[(size_t)(t0 + tid) * NV + hd];
@@ -380,7 +380,11 @@ void launch_gdn_verify(const float* q, const float* k, const float* v, const flo
                        const float* a_log, const float* dt_bias, float* state, float* y, int T, int NK, int NV,
                        int n, cudaStream_t st) {
     void* args[] = {&q, &k, &v, &a_in, &b_in, &a_log, &dt_bias, &state, &y, &T, &NK, &NV, &n};
-    launch_pdl((const void*)gdn_verify_kernel, dim3(NV, 128 / GV_ROWS), dim3(256), 0, st, args);
+    // a verify-sized call overlaps its prologue with the previous kernel; a prefill chunk's long sequential run is
+    // launched plainly: with the programmatic-launch attribute its dependent's early CTAs slowed it (737 -> 994 us at
+    // 2047 rows, measured)
+    if (T <= VMAX) launch_pdl((const void*)gdn_verify_kernel, dim3(NV, 128 / GV_ROWS), dim3(256), 0, st, args);
+    else gdn_verify_kernel<<<dim3(NV, 128 / GV_ROWS), 256, 0, st>>>(q, k, v, a_in, b_in, a_log, dt_bias, state, y, T, NK, NV, n);
 }
 
 }  // namespace bcu
