@@ -188,10 +188,11 @@ WORKLOAD_5 = ("config5 (linears only): the 96 ternary GEMMs of the Bonsai-2B sha
               "2048 tokens = 65536 prefill rows per GPU, fp32 activations in HBM")
 
 
-SESSIONS_5, TOKENS_5 = 32, 2048
+SESSIONS_5, TOKENS_5, CONCURRENT_5 = 32, 2048, 4
 WORKLOAD_5M = ("config5: whole-model batched prefill of the Bonsai-2B shape (random-init, g64 + bias, bf16 tied head), "
                "32 sessions x 2048 Zipf(1.1) tokens per GPU, each session's prompt through bcu_prefill (tcgen05 GEMM "
-               "chunks for the first 2047 rows, then one verify-pass row that returns the next token)")
+               "chunks for the first 2047 rows, then one verify-pass row that returns the next token); sessions in "
+               "flight at once on their own model instances and streams, each driven by its own host thread")
 
 
 def prefill_flops(cfg, rows):
@@ -217,8 +218,12 @@ def prefill_flops(cfg, rows):
 
 
 def run_config5(args, ws, rank, local):
-    """Config 5: whole-model batched prefill, 32 sessions x 2048 tokens per GPU (sessions one after another on one
-    model; each bcu_prefill runs its prompt as tcgen05 GEMM chunks)."""
+    """Config 5: whole-model batched prefill, 32 sessions x 2048 tokens per GPU. --concurrent sessions are in flight
+    at once: each on its own model instance (weights, state, stream) driven by its own host thread (the C calls
+    release the GIL), so one session's sequential kernels (the chunk's gated delta rule, the one-row pass) overlap
+    another's GEMMs; each bcu_prefill runs its prompt as tcgen05 GEMM chunks."""
+    import concurrent.futures
+
     import torch
 
     dist = None
@@ -235,35 +240,54 @@ def run_config5(args, ws, rank, local):
 
     cfg = config.bonsai_2b_graded(ctx=TOKENS_5 + 64)
     ts = synth.model_tensors(cfg, args.seed)
-    m = Model(cfg, device=0).load(ts)
     sessions = args.sessions or SESSIONS_5
+    conc = max(1, min(args.concurrent or CONCURRENT_5, sessions))
+    models = [Model(cfg, device=local).load(ts) for _ in range(conc)]
+    m = models[0]
     prompts = [synth.zipf_tokens(args.seed + 100 + s, TOKENS_5, cfg.vocab) for s in range(sessions)]
-    stream = torch.cuda.ExternalStream(m.stream())
+    streams = [torch.cuda.ExternalStream(mm.stream()) for mm in models]
+    pool = concurrent.futures.ThreadPoolExecutor(conc)
+
+    def worker(i):  # sessions i, i + conc, ... on model i
+        out = []
+        for s in range(i, sessions, conc):
+            models[i].reset()
+            out.append((s, models[i].prefill(prompts[s])))
+        return out
 
     def step():
-        nxt = []
-        for ids in prompts:
-            m.reset()
-            nxt.append(m.prefill(ids))
+        nxt = [0] * sessions
+        for part in pool.map(worker, range(conc)):
+            for s, t in part:
+                nxt[s] = t
         return nxt
 
     for _ in range(max(1, args.warmup)):
-        m.reset()
-        m.prefill(prompts[0])
+        for mm in models:
+            mm.reset()
+            mm.prefill(prompts[0])
     clocks = Clocks(local)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
+    stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
     e0.record(stream)
+    for st in streams:  # the sessions' streams start after e0
+        st.wait_event(e0)
     firsts = None
     for _ in range(args.steps):
         firsts = step()
+    for st in streams:  # e1 after every session stream's work
+        ev = torch.cuda.Event()
+        ev.record(st)
+        stream.wait_event(ev)
     e1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
+    pool.shutdown()
     ck = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
     e2e_s = max_over_ranks(wall, dist, "cuda")
@@ -286,7 +310,7 @@ def run_config5(args, ws, rank, local):
         "dtype": "fp32 activations (fp16 hi + lo on the tensor cores) x fp16 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init weights, Zipf(1.1) prompts)",
         "config": {"workload": WORKLOAD_5M, "sessions": sessions, "tokens_per_session": TOKENS_5,
-                   "rows_per_step": rows, "parallelism": f"replicas x{ws}",
+                   "concurrent_sessions": conc, "rows_per_step": rows, "parallelism": f"replicas x{ws}",
                    "l2": "inputs larger than L2 (1.6 GB of weights and 0.5 GB of activations per chunk)"},
         "e2e": {"value": whole_job_rate(ws, rows * args.steps, e2e_s), "unit": "tok/s",
                 # per session: the ids up; three control-block reads (248 B each: after the flush, after the chunks,
@@ -318,7 +342,8 @@ def run_config5(args, ws, rank, local):
                                           "its head runs on every row)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    m.close()
+    for mm in models:
+        mm.close()
     if dist:
         dist.destroy_process_group()
 
@@ -647,6 +672,8 @@ def main():
     ap.add_argument("--profile-prefix", type=int, default=256)
     ap.add_argument("--sessions", type=int, default=0,
                     help="config5 only: sessions per step (default 32; fewer for profiling)")
+    ap.add_argument("--concurrent", type=int, default=0,
+                    help="config5 only: sessions in flight at once, each on its own model instance (default 4)")
     ap.add_argument("--rows", type=int, default=PREFILL_M,
                     help="config5-linears only: prefill rows per step (65536 = 32 sessions x 2048; smaller for "
                          "profiling)")

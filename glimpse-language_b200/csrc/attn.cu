@@ -336,11 +336,7 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
 template <int QP>
 static void launch_attn_t(const AttnArgs& a, cudaStream_t st) {
     size_t smem = attn_smem_floats(QP, a.rot) * 4;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(attn_kernel<QP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-    }
+    raise_smem_limit((const void*)attn_kernel<QP>, 200 * 1024);
     AttnArgs aa = a;
     void* args[] = {&aa};
     launch_pdl((const void*)attn_kernel<QP>, dim3(a.KV, a.nsplit, a.T), dim3(256), smem, st, args);

@@ -240,11 +240,7 @@ __global__ void __launch_bounds__(256, 2) gdn_layer_kernel(GdnArgs a) {
 }
 
 void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(gdn_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-        attr = true;
-    }
+    raise_smem_limit((const void*)gdn_layer_kernel, 100 * 1024);
     GdnArgs aa = a;
     void* args[] = {&aa};
     launch_pdl((const void*)gdn_layer_kernel, dim3(a.NV, 8), dim3(256), gdn_smem_bytes(), st, args);

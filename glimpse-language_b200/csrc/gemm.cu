@@ -21,7 +21,6 @@
 // E per token from its row maximum), so every product is exact and sums are fp32: y = (D_hi + D_lo) 2^-E.
 // Every wait is bounded; on a timeout the kernel records ERR_MBAR_TIMEOUT, every role stops, the MMA issuer waits
 // (bounded) for its last MMAs, and the tensor memory is freed.
-#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -454,10 +453,7 @@ cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int 
     p.nbias = nbias;
     p.n_rt = gemm_row_tiles(O);
     p.n_tiles = p.n_rt * ((M + GM_TOK - 1) / GM_TOK);
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(ternary_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
-    });
+    raise_smem_limit((const void*)ternary_gemm_kernel, GM_SMEM);
     const int grid = p.n_tiles < num_sms ? p.n_tiles : num_sms;
     ternary_gemm_kernel<<<grid, GM_THREADS, GM_SMEM, st>>>(p);
     return cudaGetLastError();

@@ -245,11 +245,7 @@ static void launch_head_t(const HeadArgs& a, int grid, cudaStream_t st) {
     int stages = head_stages<NT>();
     while (stages > 1 && head_smem_bytes(a.d, NT, stages) > HEAD_SMEM_MAX) stages--;
     size_t smem = head_smem_bytes(a.d, NT, stages);
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(head_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)HEAD_SMEM_MAX);
-        attr = true;
-    }
+    raise_smem_limit((const void*)head_kernel<NT>, (int)HEAD_SMEM_MAX);
     HeadArgs aa = a;
     aa.stages = stages;
     void* args[] = {&aa};

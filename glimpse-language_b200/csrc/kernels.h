@@ -107,6 +107,9 @@ bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sm
 // One launch per GDN layer: conv (with the deferred conv-state commit) + gated delta rule (with the deferred replay)
 // for CTA = (value head, 16 dv rows). Inputs are staged in shared memory, so the sequential rows run without global
 // loads on the critical path.
+// Raises a kernel's dynamic shared-memory limit on the current device, once per (kernel, device); thread-safe.
+void raise_smem_limit(const void* fn, int bytes);
+
 struct GdnArgs {
     const Ctl* ctl;
     const float* qkvz;     // [T][C + gw] GEMV output (qkv first)

@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <mutex>
 #include <set>
+#include <utility>
 #include "common.cuh"
 #include "kernels.h"
 #include "operand.cuh"
@@ -1150,17 +1151,23 @@ template <int NT>
 static const void* gemv_fn_gpc(int group, int hb, bool lora) {
     return group == 64 ? gemv_fn_vpl<NT, 2>(hb, lora) : gemv_fn_vpl<NT, 1>(hb, lora);
 }
-// The kernel for nt column tiles, its shared-memory limit raised once.
+// The kernel for nt column tiles, its shared-memory limit raised on this device.
 static const void* gemv_fn(int nt, int group, int hb, bool lora) {
     const void* fn = nt == 1 ? gemv_fn_gpc<1>(group, hb, lora)
                    : nt == 2 ? gemv_fn_gpc<2>(group, hb, lora)
                    : nt == 3 ? gemv_fn_gpc<3>(group, hb, lora)
                              : gemv_fn_gpc<4>(group, hb, lora);
-    static std::mutex mu;
-    static std::set<const void*> raised;
-    std::lock_guard<std::mutex> g(mu);
-    if (raised.insert(fn).second) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+    raise_smem_limit(fn, 220 * 1024);
     return fn;
+}
+
+void raise_smem_limit(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> raised;  // (kernel, device): the attribute is per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (raised.insert({fn, dev}).second) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 int gemv_grid(const TernaryMat& m, int ab_rows) { return (m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS; }
