@@ -23,17 +23,17 @@
 // (bounded) for its last MMAs, and the tensor memory is freed.
 
 #include "common.cuh"
+#include "gemm_act.cuh"
 #include "kernels.h"
 #include "operand.cuh"  // pow2f
 
 namespace bcu {
 
 // A tile is 256 weight rows (two halves of 128, one MMA each) x 128 tokens; a chunk is 64 inputs.
-constexpr int GM_ROWS = 128, GM_TOK = 128, GM_KC = 64;  // rows per half, tile tokens, inputs per chunk
+constexpr int GM_ROWS = 128;  // rows per half (GM_TOK tokens per tile and GM_KC inputs per chunk: gemm_act.cuh)
 constexpr int GM_SB = 4;  // activation + code stages (the loader runs up to 3 chunks ahead of the MMAs)
 constexpr int GM_SA = 2;  // decoded-weight buffers (the decoders run 1 chunk ahead)
 constexpr int GM_A_BYTES = GM_ROWS * GM_KC * 2;           // 16 KB decoded weights per half
-constexpr int GM_B_BYTES = 2 * GM_TOK * GM_KC * 2;        // 32 KB activations (hi and lo)
 constexpr int GM_W_BYTES = GM_ROWS * 16 + GM_ROWS * 2;    // per half: codes [128][4 u32] + scales [128] fp16
 // shared memory: B[GM_SB] (32 KB each) | A[GM_SA] (two 16-KB halves each) | W[GM_SB] (two halves of codes + scales)
 // | barriers; tiles on 1024-byte boundaries
@@ -79,13 +79,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
                  : "r"(taddr));
 }
 
-// Operand tiles in shared memory: K-major with the 128-byte swizzle. A row of a tile is one chunk of 64 fp16 inputs
-// (128 bytes); rows are contiguous; 16-byte piece j of row r sits at r * 128 + ((j ^ (r % 8)) * 16), so 8 rows form a
-// 1024-byte swizzle atom (tiles start on 1024-byte boundaries).
-__host__ __device__ inline int sw128(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
-// Its matrix descriptor for the k16 step at byte offset koff (0, 32, 64, 96) of the rows: start address, leading
-// byte offset 16 (unused by swizzled K-major layouts), stride byte offset 1024 (8-row groups), version 1 (bit 46),
-// layout SWIZZLE_128B (2 in bits 61-63).
+// Matrix descriptor of a swizzled operand tile (sw128, gemm_act.cuh) for the k16 step at byte offset koff (0, 32, 64,
+// 96) of the rows: start address, leading byte offset 16 (unused by swizzled K-major layouts), stride byte offset
+// 1024 (8-row groups), version 1 (bit 46), layout SWIZZLE_128B (2 in bits 61-63).
 __device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile, uint32_t koff) {
     const uint64_t a = smem_u32(tile) + koff;
     return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
@@ -137,16 +133,7 @@ __global__ void gemm_pack_bias_kernel(const uint16_t* __restrict__ s, const uint
 }
 
 // ----------------------------------------------------------------------------------------------- activations
-// Order of the inputs inside a chunk: the weight decode takes two codes of one packed word per LOP3, codes i and i + 8
-// (i < 8) of word w (inputs 16 w + i, 16 w + i + 8), so half p of 16-byte piece kk of a chunk row holds input
-// 16 (kk / 2) + 4 (kk % 2) + p / 2 + 8 (p % 2). The activations use the same order (any order of the inputs gives
-// the same dot products, as long as A and B agree).
-__host__ __device__ inline int gemm_k_of(int kk, int p) { return 16 * (kk >> 1) + 4 * (kk & 1) + (p >> 1) + 8 * (p & 1); }
-
-// One warp per token: exponent E = clamp(14 - frexp exponent of max |x|), then x 2^E split into fp16 hi + lo written
-// to the token tile's chunks in the B operand's layout (256 rows of 64 fp16 with the 128-byte swizzle, rows 0..127
-// hi, 128..255 lo, inputs in the decode order above), and the group sums x 2^(E - log2 G) (hi + lo) to the bias
-// chunks. Lane l takes packed word w = l + 32 i: inputs 16 w .. 16 w + 15, two 16-byte pieces of each row.
+// One warp per token: the exponent of its row maximum, then its tiles (gemm_act.cuh).
 __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int G, int nmain, int nbias,
                                  uint8_t* __restrict__ bop, int* __restrict__ ex) {
     const int lane = threadIdx.x & 31, t = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -158,63 +145,9 @@ __global__ void gemm_prep_kernel(const float* __restrict__ x, int M, int K, int 
         am = fmaxf(am, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
     am = warp_max(am);
-    int E = 0;
-    if (am > 0.0f && am < INFINITY) {
-        int e2;
-        frexpf(am, &e2);
-        E = min(max(14 - e2, -60), 100);
-    }
+    const int E = gemm_act_exponent(am);
     if (lane == 0) ex[t] = E;
-    const float f = E > 60 ? pow2f(60) * pow2f(E - 60) : (E < -60 ? pow2f(-60) * pow2f(E + 60) : pow2f(E));
-    const int nch = nmain + nbias, tt = t / GM_TOK, tl = t % GM_TOK;
-    uint8_t* tile0 = bop + (size_t)tt * nch * GM_B_BYTES;
-    const int n_hi = tl, n_lo = GM_TOK + tl;  // rows of the B tile
-    const int lg = G == 64 ? 6 : 7, lanes_per_group = G / 16;
-    const float fb = pow2f(E - lg > 100 ? 100 : E - lg);
-    for (int w0 = 0; w0 < K / 16; w0 += 32) {
-        const int w = w0 + lane;  // inputs 16 w .. 16 w + 15
-        float gs = 0.0f;
-        if (w < K / 16) {
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float4 a = *(const float4*)(row + 16 * w + 4 * i);
-                v[4 * i] = a.x;
-                v[4 * i + 1] = a.y;
-                v[4 * i + 2] = a.z;
-                v[4 * i + 3] = a.w;
-            }
-#pragma unroll
-            for (int e = 0; e < 16; e++) gs += v[e];
-            uint8_t* chunk = tile0 + (size_t)(w / 4) * GM_B_BYTES;
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int kk = 2 * (w % 4) + h;
-                uint16_t hv[8], lv[8];
-#pragma unroll
-                for (int p = 0; p < 8; p++) {
-                    const float s = v[4 * h + (p >> 1) + 8 * (p & 1)] * f;
-                    const __half hh = __float2half_rn(s);
-                    hv[p] = __half_as_ushort(hh);
-                    lv[p] = __half_as_ushort(__float2half_rn(s - __half2float(hh)));
-                }
-                *(uint4*)(chunk + sw128(n_hi, kk)) = *(const uint4*)hv;
-                *(uint4*)(chunk + sw128(n_lo, kk)) = *(const uint4*)lv;
-            }
-        }
-        // group sums: the G / 16 consecutive lanes of one group, summed in a fixed tree
-        for (int o = 1; o < lanes_per_group; o <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, o);
-        if (w < K / 16 && (lane % lanes_per_group) == 0) {
-            const int g = w / lanes_per_group;
-            const float s = gs * fb;
-            const __half hh = __float2half_rn(s);
-            const __half ll = __float2half_rn(s - __half2float(hh));
-            uint8_t* chunk = tile0 + (size_t)(nmain + g / GM_KC) * GM_B_BYTES;
-            const int kk = (g % GM_KC) / 8;
-            ((__half*)(chunk + sw128(n_hi, kk)))[g % 8] = hh;
-            ((__half*)(chunk + sw128(n_lo, kk)))[g % 8] = ll;
-        }
-    }
+    gemm_act_words(row, t, K, G, nmain, nbias, E, 0, 32, bop);
 }
 
 // ----------------------------------------------------------------------------------------------- GEMM
@@ -439,7 +372,7 @@ void gemm_prep_only(const float* x, int M, int K, int G, uint8_t* bop, int* ex, 
 cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int G, const float* x, int M, uint8_t* bop,
                      int* ex, float* y, int* err, int num_sms, cudaStream_t st) {
     const int nmain = K / GM_KC, nbias = gemm_bias_chunks(K, G);
-    gemm_prep_kernel<<<(unsigned)((M + 7) / 8), 256, 0, st>>>(x, M, K, G, nmain, nbias, bop, ex);
+    if (x) gemm_prep_kernel<<<(unsigned)((M + 7) / 8), 256, 0, st>>>(x, M, K, G, nmain, nbias, bop, ex);
     GemmParams p;
     p.wt = wt;
     p.abias = abias;

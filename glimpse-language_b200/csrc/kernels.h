@@ -200,13 +200,15 @@ size_t gemm_bias_bytes(int O, int K, int G);
 size_t gemm_act_bytes(int M, int K, int G);
 void gemm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int O, int K, int G, uint8_t* wt,
                uint8_t* abias, cudaStream_t st);
+int gemm_bias_chunks(int K, int G);
 void gemm_prep_only(const float* x, int M, int K, int G, uint8_t* bop, int* ex, cudaStream_t st);
+// x null: bop and ex already hold the activation tiles (written by the prefill producers).
 cudaError_t gemm_run(const uint8_t* wt, const uint8_t* abias, int O, int K, int G, const float* x, int M, uint8_t* bop,
                      int* ex, float* y, int* err, int num_sms, cudaStream_t st);
 
 // ------------------------------------------------------------------------------------------------ batched prefill
 // Producer kernels of the prefill chunk (prefill.cu): one row per CTA, x of the mode, signs, Walsh-Hadamard in blocks
-// of hb, fp32 rows for the GEMM.
+// of hb, written as the GEMM's activation tiles.
 enum PfMode : int { PF_NORM = 0, PF_GATED = 1, PF_GATE = 2, PF_SWIGLU = 3 };
 struct PfRowArgs {
     int mode = PF_NORM, D = 0, ld2 = 0;
@@ -217,7 +219,9 @@ struct PfRowArgs {
     const float* w = nullptr;      // NORM: [D]; GATED: [128]
     const float* signs = nullptr;  // [D] or null
     float* xn = nullptr;           // NORM: unrotated normed rows, or null
-    float* xr = nullptr;           // [M][D] rotated rows
+    uint8_t* bop = nullptr;        // the GEMM's activation tiles (gemm_act_bytes(M, D, G)) and exponents ex [M]
+    int* ex = nullptr;
+    int G = 0, nbias = 0;          // group size of the GEMM's weights, its bias chunks (gemm_bias_chunks(D, G))
 };
 void launch_pf_rows(const PfRowArgs& a, int M, int hb, cudaStream_t st);
 void launch_pf_embed(const uint32_t* ids, int M, int V, int d, const uint16_t* bf16, const uint32_t* tw,

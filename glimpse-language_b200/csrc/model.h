@@ -32,7 +32,7 @@ struct Lin {
 // Scratch of the batched prefill, sized for PF_CHUNK rows on first use.
 struct Prefill {
     int cap = 0;
-    float *h = nullptr, *xr = nullptr, *xn = nullptr, *mix = nullptr, *y = nullptr, *gu = nullptr, *tmp = nullptr;
+    float *h = nullptr, *xn = nullptr, *mix = nullptr, *y = nullptr, *gu = nullptr, *tmp = nullptr;
     float *q = nullptr, *k = nullptr, *v = nullptr, *ga = nullptr, *gb = nullptr, *qbuf = nullptr, *part = nullptr;
     float* lu = nullptr;  // LoRA A products [rows][3 x 256]
     unsigned* counters = nullptr;

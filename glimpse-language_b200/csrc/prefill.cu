@@ -11,6 +11,7 @@
 // cache (attn_kernel in its prepared-query mode). The chunk leaves the committed state exactly as M committed rows
 // of verify passes would (the conv rows in the double buffer's committed half, no rows to replay).
 #include "common.cuh"
+#include "gemm_act.cuh"
 #include "kernels.h"
 
 namespace bcu {
@@ -47,8 +48,10 @@ __device__ __forceinline__ void fwht_block(float* v) {
     for (int e = 0; e < VPL; e++) v[e] = __fmul_rn(v[e], inv);
 }
 
-// One row per CTA (256 threads): the producer value x_k of the mode, then xr = rotate(signs * x) in blocks of
-// HB = 32 VPL (warp w takes blocks w, w + 8, ...). NORM: x = rmsnorm(h) * w, after h += add (the residual of the
+// One row per CTA (256 threads): the producer value x_k of the mode, then rotate(signs * x) in blocks of HB = 32 VPL
+// (warp w takes blocks w, w + 8, ...), written straight into the GEMM's activation tiles: the rotated row is kept in
+// shared memory, its maximum gives the exponent, and the CTA's 8 warps write the tiles with gemm_act_words (the bits
+// gemm_prep_kernel would write from the same row in global memory). NORM: x = rmsnorm(h) * w, after h += add (the residual of the
 // previous linear, written back). xn (optional, every mode) keeps x unrotated: the GDN a/b rows' input and the
 // LoRA input of the linear that follows (lora.rs:1-3: the adapter sees the unrotated input). GATED: per 128-wide head
 // (((z * y) * rsqrt(mean(y^2) + eps)) * w) * sigmoid(z), z at src2 (row stride ld2). GATE: attn * sigmoid(gate),
@@ -56,10 +59,12 @@ __device__ __forceinline__ void fwht_block(float* v) {
 // and u the two halves of a [2D] row.
 template <int VPL>
 __global__ void __launch_bounds__(256) pf_rows_kernel(PfRowArgs a) {
+    extern __shared__ __align__(16) float s_row[];  // [D] the rotated row
     __shared__ float red[32];
     __shared__ float s_r;
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, D = a.D;
     constexpr int HB = VPL * 32;
+    float am = 0.0f;  // largest magnitude of this warp's rotated values
     if (a.mode == PF_NORM) {
         float* hr = a.h + (size_t)row * D;
         float ss = 0.0f;
@@ -130,14 +135,24 @@ __global__ void __launch_bounds__(256) pf_rows_kernel(PfRowArgs a) {
         }
         fwht_block<VPL>(v);
 #pragma unroll
-        for (int e = 0; e < VPL; e++) a.xr[(size_t)row * D + b0 + lane + 32 * e] = v[e];
+        for (int e = 0; e < VPL; e++) {
+            s_row[b0 + lane + 32 * e] = v[e];
+            am = fmaxf(am, fabsf(v[e]));
+        }
     }
+    const int E = gemm_act_exponent(block_max(am, red));  // its barriers also publish s_row
+    if (tid == 0) a.ex[row] = E;
+    gemm_act_words(s_row, row, D, a.G, D / GM_KC, a.nbias, E, 32 * warp, 256, a.bop);
 }
 
 void launch_pf_rows(const PfRowArgs& a, int M, int hb, cudaStream_t st) {
-    if (hb == 512) pf_rows_kernel<16><<<M, 256, 0, st>>>(a);
-    else if (hb == 1024) pf_rows_kernel<32><<<M, 256, 0, st>>>(a);
-    else pf_rows_kernel<64><<<M, 256, 0, st>>>(a);
+    const void* fn = hb == 512 ? (const void*)pf_rows_kernel<16>
+                   : hb == 1024 ? (const void*)pf_rows_kernel<32> : (const void*)pf_rows_kernel<64>;
+    const size_t smem = (size_t)a.D * 4;
+    if (smem > 48 * 1024) raise_smem_limit(fn, 200 * 1024);
+    PfRowArgs aa = a;
+    void* args[] = {&aa};
+    cudaLaunchKernel(fn, dim3(M), dim3(256), args, smem, st);
 }
 
 // Embedding rows of the chunk: the bf16 table's row as is, or the ternary tied table's embed (kernels.metal:230-246,

@@ -842,7 +842,6 @@ bcu_status pf_alloc(bcu_model* m) {
         return BCU_OK;
     };
     TRY(get(&p.h, P * d * 4));
-    TRY(get(&p.xr, P * wide * 4));
     TRY(get(&p.xn, P * wide * 4));
     TRY(get(&p.lu, P * 3 * 256 * 4));
     TRY(get(&p.mix, P * mixw * 4));
@@ -877,6 +876,17 @@ bcu_status pf_gemm(bcu_model* m, const Lin& ln, const float* x, const float* xu,
     return BCU_OK;
 }
 
+// A producer over the chunk's rows straight into the GEMM's activation tiles, then that linear.
+bcu_status pf_rows_gemm(bcu_model* m, PfRowArgs r, const Lin& ln, int M, float* y) {
+    Prefill& p = m->pf;
+    r.bop = p.bop;
+    r.ex = p.ex;
+    r.G = ln.m.group;
+    r.nbias = gemm_bias_chunks(r.D, r.G);
+    launch_pf_rows(r, M, m->c.hadamard, m->st);
+    return pf_gemm(m, ln, nullptr, p.xn, M, y);
+}
+
 // Model::prefill's forward of M rows (ids on the host) at positions off .. off + M - 1 (encode_layers_at,
 // model.rs:670-934, without the head): the committed state advances by M rows. par: the control block's parity
 // (the committed conv rows live in half par ^ 1 of each layer's double buffer).
@@ -884,7 +894,7 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
     const bcu_config& c = m->c;
     Prefill& p = m->pf;
     cudaStream_t st = m->st;
-    const int d = c.hidden, ff = c.intermediate, HB = c.hadamard, NK = c.lin_k_heads, NV = c.lin_v_heads;
+    const int d = c.hidden, ff = c.intermediate, NK = c.lin_k_heads, NV = c.lin_v_heads;
     const int C = m->C, gw = m->gw, aw = m->aw, kvw = m->kvw;
     CK(cudaMemcpyAsync(p.ids, ids, (size_t)M * 4, cudaMemcpyHostToDevice, st));
     const bool tern = c.head_kind == BCU_HEAD_TERNARY;
@@ -902,15 +912,12 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         in.w = L.in_norm;
         in.signs = L.mix_in.signs;
         in.xn = p.xn;
-        in.xr = p.xr;
-        launch_pf_rows(in, M, HB, st);
-        TRY(pf_gemm(m, L.mix_in, p.xr, p.xn, M, p.mix));
+        TRY(pf_rows_gemm(m, in, L.mix_in, M, p.mix));
         PfRowArgs out;
         out.D = L.attn ? aw : gw;
         out.src = p.y;
         out.signs = L.mix_out.signs;
         out.xn = p.xn;
-        out.xr = p.xr;
         if (!L.attn) {
             launch_pf_gdn_ab(L.wa, L.wb, p.xn, p.ga, p.gb, NV, d, M, st);
             float* cs = m->conv + ((size_t)L.gi * 2 + (par ^ 1)) * 3 * C;  // the committed half
@@ -956,8 +963,7 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         // the last layer's outputs only feed the residual rows of this chunk, which nothing reads: its state
         // updates above are all the chunk needs from it
         if (last) break;
-        launch_pf_rows(out, M, HB, st);
-        TRY(pf_gemm(m, L.mix_out, p.xr, p.xn, M, p.tmp));
+        TRY(pf_rows_gemm(m, out, L.mix_out, M, p.tmp));
         PfRowArgs post;
         post.mode = PF_NORM;
         post.D = d;
@@ -966,18 +972,14 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         post.w = L.post_norm;
         post.signs = L.gu.signs;
         post.xn = p.xn;
-        post.xr = p.xr;
-        launch_pf_rows(post, M, HB, st);
-        TRY(pf_gemm(m, L.gu, p.xr, p.xn, M, p.gu));
+        TRY(pf_rows_gemm(m, post, L.gu, M, p.gu));
         PfRowArgs sw;
         sw.mode = PF_SWIGLU;
         sw.D = ff;
         sw.src = p.gu;
         sw.signs = L.down.signs;
         sw.xn = p.xn;
-        sw.xr = p.xr;
-        launch_pf_rows(sw, M, HB, st);
-        TRY(pf_gemm(m, L.down, p.xr, p.xn, M, p.tmp));
+        TRY(pf_rows_gemm(m, sw, L.down, M, p.tmp));
         pending = p.tmp;
         CK(cudaGetLastError());
     }
