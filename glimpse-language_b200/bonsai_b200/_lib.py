@@ -150,6 +150,8 @@ SIGNATURES = {
     "bcu_linear_sync": (I32, [P, P]),
     "bcu_linear_rotate_forward_static": (I32, [P, P, I32, I32, P, P, P]),
     "bcu_gdn_verify": (I32, [P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
+    "bcu_gdn_prefill_workspace": (I32, [I32, I32, ctypes.POINTER(U64)]),
+    "bcu_gdn_prefill": (I32, [P, P, P, P, P, P, P, P, P, I32, I32, I32, P, P]),
     "bcu_pass_launches": (I32, [P, I32, PI32]),
     "bcu_pass_bytes": (I32, [P, I32, ctypes.POINTER(ctypes.c_double)]),
     "bcu_time_pass": (I32, [P, I32, I32, ctypes.POINTER(ctypes.c_float)]),

@@ -126,6 +126,13 @@ struct GdnArgs {
 };
 void launch_gdn_layer(const GdnArgs& a, cudaStream_t st);
 
+// The prefill chunk's gated delta rule in chunks of 64 rows (gdn_chunk.cu): state advanced by all T rows, outputs of
+// every row. ws: gdn_chunk_workspace_bytes(T, NV) of device memory.
+size_t gdn_chunk_workspace_bytes(int T, int NV);
+void launch_gdn_chunked(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
+                        const float* a_log, const float* dt_bias, float* state, float* y, int T, int NK, int NV,
+                        float* ws, cudaStream_t st);
+
 // Standalone verify step with rollback (graded config 2).
 void launch_gdn_verify(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
                        const float* a_log, const float* dt_bias, float* state, float* y, int T, int NK, int NV,

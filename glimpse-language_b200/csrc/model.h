@@ -35,6 +35,7 @@ struct Prefill {
     float *h = nullptr, *xn = nullptr, *mix = nullptr, *y = nullptr, *gu = nullptr, *tmp = nullptr;
     float *q = nullptr, *k = nullptr, *v = nullptr, *ga = nullptr, *gb = nullptr, *qbuf = nullptr, *part = nullptr;
     float* lu = nullptr;  // LoRA A products [rows][3 x 256]
+    float* gws = nullptr; // chunked gated delta rule workspace (gdn_chunk_workspace_bytes)
     unsigned* counters = nullptr;
     uint8_t* bop = nullptr;
     int* ex = nullptr;

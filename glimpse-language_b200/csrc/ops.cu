@@ -305,4 +305,20 @@ bcu_status bcu_gdn_verify(const float* q, const float* k, const float* v, const 
     return cudaGetLastError() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
 }
 
+bcu_status bcu_gdn_prefill_workspace(int32_t T, int32_t NV, uint64_t* bytes) {
+    if (T < 1 || NV < 1 || !bytes) return BCU_ERR_ARG;
+    *bytes = gdn_chunk_workspace_bytes(T, NV);
+    return BCU_OK;
+}
+
+bcu_status bcu_gdn_prefill(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
+                           const float* a_log, const float* dt_bias, float* state, float* y, int32_t T, int32_t NK,
+                           int32_t NV, void* workspace, void* stream) {
+    if (!q || !k || !v || !a_in || !b_in || !a_log || !dt_bias || !state || !y || !workspace) return BCU_ERR_ARG;
+    if (T < 1 || NK < 1 || NV < 1 || NV % NK) return BCU_ERR_ARG;
+    launch_gdn_chunked(q, k, v, a_in, b_in, a_log, dt_bias, state, y, T, NK, NV, (float*)workspace,
+                       (cudaStream_t)stream);
+    return cudaGetLastError() == cudaSuccess ? BCU_OK : BCU_ERR_CUDA;
+}
+
 }  // extern "C"

@@ -844,6 +844,7 @@ bcu_status pf_alloc(bcu_model* m) {
     TRY(get(&p.h, P * d * 4));
     TRY(get(&p.xn, P * wide * 4));
     TRY(get(&p.lu, P * 3 * 256 * 4));
+    TRY(get(&p.gws, gdn_chunk_workspace_bytes((int)P, c.lin_v_heads)));
     TRY(get(&p.mix, P * mixw * 4));
     TRY(get(&p.y, P * std::max(m->gw, m->aw) * 4));
     TRY(get(&p.gu, P * 2 * ff * 4));
@@ -922,8 +923,8 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
             launch_pf_gdn_ab(L.wa, L.wb, p.xn, p.ga, p.gb, NV, d, M, st);
             float* cs = m->conv + ((size_t)L.gi * 2 + (par ^ 1)) * 3 * C;  // the committed half
             launch_pf_gdn_conv(p.mix, C + gw, cs, L.convw, p.q, p.k, p.v, NK, NV, C, M, st);
-            launch_gdn_verify(p.q, p.k, p.v, p.ga, p.gb, L.a_log, L.dt_bias,
-                              m->gdn + (size_t)L.gi * NV * 128 * 128, p.y, M, NK, NV, M, st);
+            launch_gdn_chunked(p.q, p.k, p.v, p.ga, p.gb, L.a_log, L.dt_bias,
+                               m->gdn + (size_t)L.gi * NV * 128 * 128, p.y, M, NK, NV, p.gws, st);
             out.mode = PF_GATED;
             out.src2 = p.mix + C;
             out.ld2 = C + gw;

@@ -315,6 +315,16 @@ bcu_status bcu_gdn_verify(const float* q, const float* k, const float* v, const 
                           const float* a_log, const float* dt_bias, float* state, float* y, int32_t T, int32_t NK,
                           int32_t NV, int32_t n, void* stream);
 
+/* The gated delta rule of a prefill chunk (Model::prefill, runtime/mod.rs:341-386, runs gdn_recurrent,
+ * kernels.metal:566-622, over the chunk's rows): the same inputs as bcu_gdn_verify, the state advanced by all T rows
+ * (no rollback), y the outputs of every row. Computed in chunks of 64 rows (the per-row recurrence re-associated
+ * into products within a chunk; results equal it within fp32 rounding). workspace: device memory of the size
+ * bcu_gdn_prefill_workspace returns for (T, NV). Device pointers. */
+bcu_status bcu_gdn_prefill_workspace(int32_t T, int32_t NV, uint64_t* bytes);
+bcu_status bcu_gdn_prefill(const float* q, const float* k, const float* v, const float* a_in, const float* b_in,
+                           const float* a_log, const float* dt_bias, float* state, float* y, int32_t T, int32_t NK,
+                           int32_t NV, void* workspace, void* stream);
+
 /* ------------------------------------------------------------------ introspection */
 
 /* Kernel launches in the last pass (graph nodes), for the benchmark's gpu_launches. */

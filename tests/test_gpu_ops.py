@@ -144,3 +144,40 @@ def test_gdn_verify_rows_past_one_chunk(gpu, T, n):
     torch.cuda.synchronize()
     np.testing.assert_allclose(y.cpu().numpy(), want_y, rtol=2e-4, atol=2e-6)
     np.testing.assert_allclose(st.cpu().numpy(), want_s, rtol=2e-4, atol=2e-6)
+
+
+def run_gdn_prefill(torch, case, T, NK, NV):
+    q, k, v, a, b, alog, dtb, S = case
+    t = [dev(torch, x) for x in (q, k, v, a, b, alog, dtb)]
+    st = dev(torch, S)
+    y = torch.empty((T, NV, 128), dtype=torch.float32, device="cuda")
+    nb = ctypes.c_uint64()
+    assert _lib.lib().bcu_gdn_prefill_workspace(T, NV, ctypes.byref(nb)) == _lib.OK
+    ws = torch.empty(nb.value // 4, dtype=torch.float32, device="cuda")
+    assert _lib.lib().bcu_gdn_prefill(*[vp(x) for x in t], vp(st), vp(y), T, NK, NV, vp(ws), None) == _lib.OK
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), st.cpu().numpy()
+
+
+@pytest.mark.parametrize("T", [1, 5, 63, 64, 65, 130, 300])
+def test_gdn_prefill_chunks_match_oracle(gpu, T):
+    """The prefill chunk's gated delta rule in 64-row chunks against the oracle's row-by-row recurrence (n = T):
+    one partial chunk, exactly one chunk, chunk boundaries, several chunks."""
+    torch = pytest.importorskip("torch")
+    NK, NV = 2, 4
+    case = gdn_case(T, NK, NV, 300 + T)
+    want_y, want_s = orc.gdn_verify(*case, T)
+    y, st = run_gdn_prefill(torch, case, T, NK, NV)
+    np.testing.assert_allclose(y, want_y, rtol=2e-4, atol=2e-6)
+    np.testing.assert_allclose(st, want_s, rtol=2e-4, atol=2e-6)
+
+
+def test_gdn_prefill_graded_heads_long_chunk(gpu):
+    """The benchmark's GDN widths (16 key / 32 value heads) over a 2047-row prefill chunk, with a starting state."""
+    torch = pytest.importorskip("torch")
+    T, NK, NV = 2047, 16, 32
+    case = gdn_case(T, NK, NV, 4242)
+    want_y, want_s = orc.gdn_verify(*case, T)
+    y, st = run_gdn_prefill(torch, case, T, NK, NV)
+    np.testing.assert_allclose(y, want_y, rtol=2e-4, atol=2e-6)
+    np.testing.assert_allclose(st, want_s, rtol=2e-4, atol=2e-6)
