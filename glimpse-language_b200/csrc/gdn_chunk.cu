@@ -14,26 +14,30 @@
 // anything but the chunk it lies in.
 //
 // gdn_chunk_prep_kernel (grid value heads x chunks, all chunks at once): L, X and P of every chunk, from q, k and the
-// gate inputs only. gdn_chunk_scan_kernel (grid value heads x 4 blocks of 32 dv rows): the chunks in order, the state
-// block in shared memory, each chunk five small products (S k and S q of the 64 rows, X R, P Delta, Delta^T K).
+// gate inputs only; (I + A)^-1 from the inverses of its four 16 x 16 diagonal blocks (one warp each, no barrier) and
+// six block steps for the blocks below them. gdn_chunk_scan_kernel (grid value heads x 4 blocks of 32 dv rows): the
+// chunks in order, the state block in shared memory, each chunk five small products (S k and S q of the 64 rows,
+// X R, P Delta, Delta^T K). Every product runs on the tensor cores as mma.sync tf32 with the three-product split
+// (mma_tf32.cuh), fp32-accurate.
 #include "common.cuh"
 #include "kernels.h"
+#include "mma_tf32.cuh"
 
 namespace bcu {
 
 constexpr int GC = 64;      // rows per chunk
 constexpr int GCP = 132;    // padded row stride (floats) of staged q/k rows and of the state block
 constexpr int GXP = 68;     // padded row stride of 64 x 64 matrices (16-byte rows, 4-bank shift per row)
-constexpr int GVP = 36;     // padded row stride of 64 x 32 blocks
+constexpr int GVP = 40;     // padded row stride of 64 x 32 blocks (conflict-free k-major fragment reads)
 constexpr int GS_ROWS = 32; // dv rows per scan CTA
 
 struct GcPrepSmem {
     float k[GC][GCP];
     float q[GC][GCP];
     float a[GC][GXP];   // A (strictly lower)
-    float x[GC][GXP];   // X = (I + A)^-1 diag(beta)
+    float m[GC][GXP];   // (I + A)^-1, built from its 16 x 16 blocks
+    float tmp[GC][GXP]; // block products on the way
     float lg[GC], L[GC], beta[GC];
-    float red[4][GC];
 };
 
 struct GcScanSmem {
@@ -104,61 +108,99 @@ __global__ void __launch_bounds__(256) gdn_chunk_prep_kernel(const float* q, con
         ls[2 * lane] = l0;
         ls[2 * lane + 1] = l0 + a1;
     }
-    // K K^T and Q K^T: thread (ti, tj) takes rows t = ti + 16 a and columns i = tj + 16 b (a, b < 4)
-    const int ti = tid >> 4, tj = tid & 15;
-    float g[4][4], p[4][4];
+    // K K^T and Q K^T on the tensor cores: warp w takes rows 16 (w / 2) .. + 15 and columns 32 (w % 2) .. + 31
+    const int w = tid >> 5, g = lane >> 2, qd = lane & 3;
+    const int mi = w >> 1, nb = 4 * (w & 1);
+    float accg[4][4], accp[4][4];
 #pragma unroll
-    for (int a = 0; a < 4; a++)
+    for (int n = 0; n < 4; n++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) g[a][b] = p[a][b] = 0.0f;
-    for (int d = 0; d < 128; d += 4) {
-        float4 kr[4], qr[4], kc[4];
+        for (int e = 0; e < 4; e++) accg[n][e] = accp[n][e] = 0.0f;
+    __syncthreads();  // the staged rows; L
+#pragma unroll 2
+    for (int ks = 0; ks < 16; ks++) {
+        Tf32x2 ak[4], aq[4];
+        frag_a_rows(&sm.k[0][0], GCP, 16 * mi, 8 * ks, ak);
+        frag_a_rows(&sm.q[0][0], GCP, 16 * mi, 8 * ks, aq);
 #pragma unroll
-        for (int a = 0; a < 4; a++) {
-            kr[a] = *(const float4*)&sm.k[ti + 16 * a][d];
-            qr[a] = *(const float4*)&sm.q[ti + 16 * a][d];
-            kc[a] = *(const float4*)&sm.k[tj + 16 * a][d];
+        for (int n = 0; n < 4; n++) {
+            Tf32x2 bk[2];
+            frag_b_nrows(&sm.k[0][0], GCP, 8 * ks, 8 * (nb + n), bk);  // (dk, i) = k_i[dk]
+            mma_tf32x3(accg[n], ak, bk);
+            mma_tf32x3(accp[n], aq, bk);
         }
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                g[a][b] = fmaf(kr[a].x, kc[b].x, g[a][b]);
-                g[a][b] = fmaf(kr[a].y, kc[b].y, g[a][b]);
-                g[a][b] = fmaf(kr[a].z, kc[b].z, g[a][b]);
-                g[a][b] = fmaf(kr[a].w, kc[b].w, g[a][b]);
-                p[a][b] = fmaf(qr[a].x, kc[b].x, p[a][b]);
-                p[a][b] = fmaf(qr[a].y, kc[b].y, p[a][b]);
-                p[a][b] = fmaf(qr[a].z, kc[b].z, p[a][b]);
-                p[a][b] = fmaf(qr[a].w, kc[b].w, p[a][b]);
-            }
     }
-    __syncthreads();  // L
+    // A_ti = beta_t exp(L_t - L_i) (k_i . k_t) for i < t; P_ti = exp(L_t - L_i) (q_t . k_i) for i <= t
 #pragma unroll
-    for (int a = 0; a < 4; a++)
+    for (int n = 0; n < 4; n++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            const int t = ti + 16 * a, i = tj + 16 * b;
-            const float e = i <= t ? expf(sm.L[t] - sm.L[i]) : 0.0f;
-            sm.a[t][i] = i < t ? sm.beta[t] * (g[a][b] * e) : 0.0f;
-            ps[t * GC + i] = p[a][b] * e;
+        for (int hf = 0; hf < 2; hf++) {
+            const int t = 16 * mi + g + 8 * hf, i = 8 * (nb + n) + 2 * qd;
+            float av[2], pv[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const float dcy = i + e <= t ? expf(sm.L[t] - sm.L[i + e]) : 0.0f;
+                av[e] = i + e < t ? sm.beta[t] * (accg[n][2 * hf + e] * dcy) : 0.0f;
+                pv[e] = accp[n][2 * hf + e] * dcy;
+            }
+            sm.a[t][i] = av[0];
+            sm.a[t][i + 1] = av[1];
+            *(float2*)&ps[t * GC + i] = make_float2(pv[0], pv[1]);
         }
     __syncthreads();
-    // X = (I + A)^-1 diag(beta) by forward substitution: X_t = beta_t e_t - sum_{i<t} A_ti X_i; thread (part, j)
-    // sums i = part, part + 4, ... for column j, the four parts added in order
-    {
-        const int j = tid & 63, part = tid >> 6;
-        for (int t = 0; t < GC; t++) {
-            float s = 0.0f;
-            for (int i = part; i < t; i += 4) s = fmaf(sm.a[t][i], sm.x[i][j], s);
-            sm.red[part][j] = s;
-            __syncthreads();
-            if (part == 0)
-                sm.x[t][j] = (t == j ? sm.beta[t] : 0.0f) - ((sm.red[0][j] + sm.red[1][j]) + (sm.red[2][j] + sm.red[3][j]));
-            __syncthreads();
+    // (I + A)^-1 from its 16 x 16 blocks. Diagonal blocks N_b = (I + A_bb)^-1 by forward substitution, one per warp
+    // 0..3, lane j < 16 holding column j in registers (no barrier inside): n_t = [t == j] - sum_{i<t} A_ti n_i.
+    if (w < 4 && lane < 16) {
+        const int b0 = 16 * w, j = lane;
+        float nv[16];
+#pragma unroll
+        for (int t = 0; t < 16; t++) {
+            float sacc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < t; i++) sacc = fmaf(sm.a[b0 + t][b0 + i], nv[i], sacc);
+            nv[t] = (t == j ? 1.0f : 0.0f) - sacc;
         }
+#pragma unroll
+        for (int t = 0; t < 16; t++) sm.m[b0 + t][b0 + j] = nv[t];
     }
-    for (int i = tid; i < GC * GC; i += 256) xs[i] = sm.x[i >> 6][i & 63];
+    // blocks above the diagonal are zero
+    for (int i = tid; i < GC * GC; i += 256) {
+        const int r = i >> 6, cc = i & 63;
+        if ((cc >> 4) > (r >> 4)) sm.m[r][cc] = 0.0f;
+    }
+    __syncthreads();
+    // the blocks below the diagonal, M_bc = -N_b sum_{c<=k<b} A_bk M_kc, by distance b - c; thread (r, cc) of 16 x 16
+    {
+        const int r = tid >> 4, cc = tid & 15;
+        // out(B) += sign * L(Lb) . R(Rb) for 16 x 16 blocks at block coordinates
+        auto prod = [&](float (*L)[GXP], int lb, int lc, float (*R)[GXP], int rb, int rc) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 16; kk++) acc = fmaf(L[16 * lb + r][16 * lc + kk], R[16 * rb + kk][16 * rc + cc], acc);
+            return acc;
+        };
+        // distance 1: T = A_{c+1,c} N_c, then M_{c+1,c} = -N_{c+1} T
+        for (int c2 = 0; c2 < 3; c2++) sm.tmp[16 * (c2 + 1) + r][16 * c2 + cc] = prod(sm.a, c2 + 1, c2, sm.m, c2, c2);
+        __syncthreads();
+        for (int c2 = 0; c2 < 3; c2++)
+            sm.m[16 * (c2 + 1) + r][16 * c2 + cc] = -prod(sm.m, c2 + 1, c2 + 1, sm.tmp, c2 + 1, c2);
+        __syncthreads();
+        // distance 2: U = A_{c+2,c} N_c + A_{c+2,c+1} M_{c+1,c}, then M_{c+2,c} = -N_{c+2} U
+        for (int c2 = 0; c2 < 2; c2++)
+            sm.tmp[16 * (c2 + 2) + r][16 * c2 + cc] =
+                prod(sm.a, c2 + 2, c2, sm.m, c2, c2) + prod(sm.a, c2 + 2, c2 + 1, sm.m, c2 + 1, c2);
+        __syncthreads();
+        for (int c2 = 0; c2 < 2; c2++)
+            sm.m[16 * (c2 + 2) + r][16 * c2 + cc] = -prod(sm.m, c2 + 2, c2 + 2, sm.tmp, c2 + 2, c2);
+        __syncthreads();
+        // distance 3: U = A_30 N_0 + A_31 M_10 + A_32 M_20, then M_30 = -N_3 U
+        sm.tmp[48 + r][cc] = (prod(sm.a, 3, 0, sm.m, 0, 0) + prod(sm.a, 3, 1, sm.m, 1, 0)) + prod(sm.a, 3, 2, sm.m, 2, 0);
+        __syncthreads();
+        sm.m[48 + r][cc] = -prod(sm.m, 3, 3, sm.tmp, 3, 0);
+        __syncthreads();
+    }
+    // X = (I + A)^-1 diag(beta)
+    for (int i = tid; i < GC * GC; i += 256) xs[i] = sm.m[i >> 6][i & 63] * sm.beta[i & 63];
 }
 
 // ---------------------------------------------------------------------------------------------------------- scan
@@ -216,10 +258,11 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(const float* q, 
     cp_async_wait_all();
     __syncthreads();
 
-    // thread tiles: rows t = tg + 16 a (a < 4) x dv = dg + 16 b (b < 2) for steps 1-3; dv row sr, dk = 4 sg + 32 j
-    // (j < 4) for the state update
-    const int tg = tid >> 4, dg = tid & 15;
-    const int sr = tid >> 3, sg = tid & 7;
+    // warp tiles (tensor cores, 3 x tf32): steps 1-3 rows 16 mi .. + 15 x dv 16 nh .. + 15 (two 8-wide n tiles);
+    // step 4 dv rows 16 m4 .. + 15 x dk 32 n4 .. + 31 (four n tiles)
+    const int lane = tid & 31, w = tid >> 5, g = lane >> 2, qd = lane & 3;
+    const int mi = w >> 1, nh = 16 * (w & 1);
+    const int m4 = w & 1, n4 = 32 * (w >> 1);
     for (int c = 0; c < nch; c++) {
         const int t0 = c * GC, nr = min(GC, T - t0);
         if (tid < GC) {
@@ -229,48 +272,38 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(const float* q, 
         }
         const float gC = expf(sm.L[GC - 1]);
         __syncthreads();  // gam, wl; L may be refilled
-        // ---- step 1: u = S k_t and z = S q_t for the 64 rows; R = v - gamma u, Z = gamma z
-        float z[4][2];
+        // ---- step 1: U = K S^T and Zq = Q S^T for the 64 rows; R = v - gamma U, Z = gamma Zq
+        float z[2][4];
         {
-            float u[4][2];
+            float u[2][4];
 #pragma unroll
-            for (int a = 0; a < 4; a++)
+            for (int n = 0; n < 2; n++)
 #pragma unroll
-                for (int b = 0; b < 2; b++) u[a][b] = z[a][b] = 0.0f;
-            for (int d = 0; d < 128; d += 4) {
-                float4 kr[4], qr[4], sv[2];
+                for (int e = 0; e < 4; e++) u[n][e] = z[n][e] = 0.0f;
+#pragma unroll 2
+            for (int ks = 0; ks < 16; ks++) {
+                Tf32x2 ak[4], aq[4];
+                frag_a_rows(&sm.k[0][0], GCP, 16 * mi, 8 * ks, ak);
+                frag_a_rows(&sm.q[0][0], GCP, 16 * mi, 8 * ks, aq);
 #pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    kr[a] = *(const float4*)&sm.k[tg + 16 * a][d];
-                    qr[a] = *(const float4*)&sm.q[tg + 16 * a][d];
-                }
-#pragma unroll
-                for (int b = 0; b < 2; b++) sv[b] = *(const float4*)&sm.s[dg + 16 * b][d];
-#pragma unroll
-                for (int a = 0; a < 4; a++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) {
-                        u[a][b] = fmaf(kr[a].x, sv[b].x, u[a][b]);
-                        u[a][b] = fmaf(kr[a].y, sv[b].y, u[a][b]);
-                        u[a][b] = fmaf(kr[a].z, sv[b].z, u[a][b]);
-                        u[a][b] = fmaf(kr[a].w, sv[b].w, u[a][b]);
-                        z[a][b] = fmaf(qr[a].x, sv[b].x, z[a][b]);
-                        z[a][b] = fmaf(qr[a].y, sv[b].y, z[a][b]);
-                        z[a][b] = fmaf(qr[a].z, sv[b].z, z[a][b]);
-                        z[a][b] = fmaf(qr[a].w, sv[b].w, z[a][b]);
-                    }
-            }
-#pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const int t = tg + 16 * a;
-                const float gm = sm.gam[t];
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    const int dv = dg + 16 * b;
-                    sm.r[t][dv] = sm.v[t][dv] - gm * u[a][b];
-                    z[a][b] *= gm;
+                for (int n = 0; n < 2; n++) {
+                    Tf32x2 bs[2];
+                    frag_b_nrows(&sm.s[0][0], GCP, 8 * ks, nh + 8 * n, bs);  // (dk, dv) = S[dv][dk]
+                    mma_tf32x3(u[n], ak, bs);
+                    mma_tf32x3(z[n], aq, bs);
                 }
             }
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const int t = 16 * mi + g + 8 * hf, dv = nh + 8 * n + 2 * qd;
+                    const float gm = sm.gam[t];
+                    const float2 vv = *(const float2*)&sm.v[t][dv];
+                    *(float2*)&sm.r[t][dv] = make_float2(vv.x - gm * u[n][2 * hf], vv.y - gm * u[n][2 * hf + 1]);
+                    z[n][2 * hf] *= gm;
+                    z[n][2 * hf + 1] *= gm;
+                }
         }
         __syncthreads();  // R; q, v and L are free
         if (c + 1 < nch) {
@@ -280,93 +313,91 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_scan_kernel(const float* q, 
         }
         // ---- step 2: Delta = X R (X lower triangular: columns past the row are zero)
         {
-            float dl[4][2];
+            float dl[2][4];
 #pragma unroll
-            for (int a = 0; a < 4; a++) dl[a][0] = dl[a][1] = 0.0f;
-            for (int i = 0; i < GC; i += 4) {
-                float4 xr[4];
+            for (int n = 0; n < 2; n++)
 #pragma unroll
-                for (int a = 0; a < 4; a++) xr[a] = *(const float4*)&sm.x[tg + 16 * a][i];
-                float rv[4][2];
+                for (int e = 0; e < 4; e++) dl[n][e] = 0.0f;
+#pragma unroll 2
+            for (int ks = 0; ks < 8; ks++) {
+                Tf32x2 ax[4];
+                frag_a_rows(&sm.x[0][0], GXP, 16 * mi, 8 * ks, ax);
 #pragma unroll
-                for (int e = 0; e < 4; e++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) rv[e][b] = sm.r[i + e][dg + 16 * b];
-#pragma unroll
-                for (int a = 0; a < 4; a++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) {
-                        dl[a][b] = fmaf(xr[a].x, rv[0][b], dl[a][b]);
-                        dl[a][b] = fmaf(xr[a].y, rv[1][b], dl[a][b]);
-                        dl[a][b] = fmaf(xr[a].z, rv[2][b], dl[a][b]);
-                        dl[a][b] = fmaf(xr[a].w, rv[3][b], dl[a][b]);
-                    }
+                for (int n = 0; n < 2; n++) {
+                    Tf32x2 br[2];
+                    frag_b_krows(&sm.r[0][0], GVP, 8 * ks, nh + 8 * n, br);
+                    mma_tf32x3(dl[n], ax, br);
+                }
             }
 #pragma unroll
-            for (int a = 0; a < 4; a++)
+            for (int n = 0; n < 2; n++)
 #pragma unroll
-                for (int b = 0; b < 2; b++) sm.d[tg + 16 * a][dg + 16 * b] = dl[a][b];
+                for (int hf = 0; hf < 2; hf++) {
+                    const int t = 16 * mi + g + 8 * hf, dv = nh + 8 * n + 2 * qd;
+                    *(float2*)&sm.d[t][dv] = make_float2(dl[n][2 * hf], dl[n][2 * hf + 1]);
+                }
         }
         __syncthreads();  // Delta; X is free
         if (c + 1 < nch) load_mat(c + 1, 0);
         // ---- step 3: outputs o = Z + P Delta
         {
-            float o[4][2];
+            float o[2][4];
 #pragma unroll
-            for (int a = 0; a < 4; a++) o[a][0] = o[a][1] = 0.0f;
-            for (int i = 0; i < GC; i += 4) {
-                float4 pr[4];
+            for (int n = 0; n < 2; n++)
 #pragma unroll
-                for (int a = 0; a < 4; a++) pr[a] = *(const float4*)&sm.p[tg + 16 * a][i];
-                float dv4[4][2];
+                for (int e = 0; e < 4; e++) o[n][e] = 0.0f;
+#pragma unroll 2
+            for (int ks = 0; ks < 8; ks++) {
+                Tf32x2 ap[4];
+                frag_a_rows(&sm.p[0][0], GXP, 16 * mi, 8 * ks, ap);
 #pragma unroll
-                for (int e = 0; e < 4; e++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) dv4[e][b] = sm.d[i + e][dg + 16 * b];
-#pragma unroll
-                for (int a = 0; a < 4; a++)
-#pragma unroll
-                    for (int b = 0; b < 2; b++) {
-                        o[a][b] = fmaf(pr[a].x, dv4[0][b], o[a][b]);
-                        o[a][b] = fmaf(pr[a].y, dv4[1][b], o[a][b]);
-                        o[a][b] = fmaf(pr[a].z, dv4[2][b], o[a][b]);
-                        o[a][b] = fmaf(pr[a].w, dv4[3][b], o[a][b]);
-                    }
-            }
-#pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const int t = tg + 16 * a;
-                if (t < nr)
-#pragma unroll
-                    for (int b = 0; b < 2; b++)
-                        y[((size_t)(t0 + t) * NV + h) * 128 + dvb + dg + 16 * b] = z[a][b] + o[a][b];
-            }
-        }
-        __syncthreads();  // P is free
-        if (c + 1 < nch) load_mat(c + 1, 1);
-        // ---- step 4: S' = gamma_63 S + sum_i exp(L_63 - L_i) Delta_i k_i^T (this thread: row sr, dk 4 sg + 32 j)
-        {
-            float acc[4][4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-            for (int i = 0; i < GC; i++) {
-                const float dw = sm.wl[i] * sm.d[i][sr];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float4 kk = *(const float4*)&sm.k[i][4 * sg + 32 * j];
-                    acc[j][0] = fmaf(dw, kk.x, acc[j][0]);
-                    acc[j][1] = fmaf(dw, kk.y, acc[j][1]);
-                    acc[j][2] = fmaf(dw, kk.z, acc[j][2]);
-                    acc[j][3] = fmaf(dw, kk.w, acc[j][3]);
+                for (int n = 0; n < 2; n++) {
+                    Tf32x2 bd[2];
+                    frag_b_krows(&sm.d[0][0], GVP, 8 * ks, nh + 8 * n, bd);
+                    mma_tf32x3(o[n], ap, bd);
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float4* sp = (float4*)&sm.s[sr][4 * sg + 32 * j];
-                const float4 o = *sp;
-                *sp = make_float4(fmaf(gC, o.x, acc[j][0]), fmaf(gC, o.y, acc[j][1]), fmaf(gC, o.z, acc[j][2]),
-                                  fmaf(gC, o.w, acc[j][3]));
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const int t = 16 * mi + g + 8 * hf, dv = nh + 8 * n + 2 * qd;
+                    if (t < nr)
+                        *(float2*)&y[((size_t)(t0 + t) * NV + h) * 128 + dvb + dv] =
+                            make_float2(z[n][2 * hf] + o[n][2 * hf], z[n][2 * hf + 1] + o[n][2 * hf + 1]);
+                }
+        }
+        __syncthreads();  // P is free
+        if (c + 1 < nch) load_mat(c + 1, 1);
+        // ---- step 4: S' = gamma_63 S + (wl . Delta)^T K, accumulated onto gamma_63 S
+        {
+            float acc[4][4];
+#pragma unroll
+            for (int n = 0; n < 4; n++)
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const float2 sv = *(const float2*)&sm.s[16 * m4 + g + 8 * hf][n4 + 8 * n + 2 * qd];
+                    acc[n][2 * hf] = gC * sv.x;
+                    acc[n][2 * hf + 1] = gC * sv.y;
+                }
+#pragma unroll 2
+            for (int ks = 0; ks < 8; ks++) {
+                Tf32x2 ad[4];
+                frag_a_cols(&sm.d[0][0], GVP, 16 * m4, 8 * ks, sm.wl, ad);  // (dv, i) = wl_i Delta[i][dv]
+#pragma unroll
+                for (int n = 0; n < 4; n++) {
+                    Tf32x2 bk[2];
+                    frag_b_krows(&sm.k[0][0], GCP, 8 * ks, n4 + 8 * n, bk);  // (i, dk) = k_i[dk]
+                    mma_tf32x3(acc[n], ad, bk);
+                }
             }
+            // each warp reads and writes only its own tile of S here (step 1's reads ended at its barrier)
+#pragma unroll
+            for (int n = 0; n < 4; n++)
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++)
+                    *(float2*)&sm.s[16 * m4 + g + 8 * hf][n4 + 8 * n + 2 * qd] =
+                        make_float2(acc[n][2 * hf], acc[n][2 * hf + 1]);
         }
         __syncthreads();  // k is free
         if (c + 1 < nch) load_qk(c + 1, true);
