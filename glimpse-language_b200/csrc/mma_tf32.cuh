@@ -44,6 +44,22 @@ __device__ __forceinline__ void mma_tf32x3(float* c, const Tf32x2* a, const Tf32
     mma_tf32(c, a[0].hi, a[1].hi, a[2].hi, a[3].hi, b[0].hi, b[1].hi);
 }
 
+// The same three products into three accumulators (hi.hi, lo.hi, hi.lo), each its own dependency chain; the result
+// is (c[1] + c[2]) + c[0] (mma3_sum). For warps that are short of independent work.
+struct Acc3 {
+    float c[3][4];
+};
+__device__ __forceinline__ void acc3_zero(Acc3& r) {
+#pragma unroll
+    for (int j = 0; j < 3; j++) r.c[j][0] = r.c[j][1] = r.c[j][2] = r.c[j][3] = 0.0f;
+}
+__device__ __forceinline__ void mma_tf32x3_acc(Acc3& r, const Tf32x2* a, const Tf32x2* b) {
+    mma_tf32(r.c[1], a[0].lo, a[1].lo, a[2].lo, a[3].lo, b[0].hi, b[1].hi);
+    mma_tf32(r.c[2], a[0].hi, a[1].hi, a[2].hi, a[3].hi, b[0].lo, b[1].lo);
+    mma_tf32(r.c[0], a[0].hi, a[1].hi, a[2].hi, a[3].hi, b[0].hi, b[1].hi);
+}
+__device__ __forceinline__ float mma3_sum(const Acc3& r, int e) { return (r.c[1][e] + r.c[2][e]) + r.c[0][e]; }
+
 // A fragment of rows m0.. and columns k0.. of a row-major fp32 matrix in shared memory (row stride ld floats).
 __device__ __forceinline__ void frag_a_rows(const float* m, int ld, int m0, int k0, Tf32x2* a) {
     const int g = (threadIdx.x & 31) >> 2, q = threadIdx.x & 3;
