@@ -160,6 +160,11 @@ struct AttnArgs {
     int off0 = 0;
 };
 void launch_attn(const AttnArgs& a, cudaStream_t st);
+// Prefill chunk attention on the tensor cores (attn_prefill.cu): queries prepared [T][H][256], every key of positions
+// [0, off0 + T) in the cache, out [T][H * 256]; for query heads per kv head dividing 32.
+bool attn_prefill_supported(int H, int KV);
+void launch_attn_prefill(const float* qprep, const float* kc, const float* vc, float* out, int T, int H, int KV,
+                         int off0, cudaStream_t st);
 
 // ------------------------------------------------------------------------------------------------ head + accept
 // bf16 tied head in mma fragment order: [V/16][d/16][32 lanes][4] u32.

@@ -955,7 +955,12 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
             a.nsplit = PF_NSPLIT;
             a.qprep = p.qbuf;
             a.off0 = off;
-            if (!last) launch_attn(a, st);  // the last layer needs only its K/V rows (written by the prep)
+            if (!last) {  // the last layer needs only its K/V rows (written by the prep)
+                if (attn_prefill_supported(c.heads, c.kv_heads))
+                    launch_attn_prefill(p.qbuf, kc, vc, p.y, M, c.heads, c.kv_heads, off, st);
+                else
+                    launch_attn(a, st);
+            }
             out.mode = PF_GATE;
             out.src2 = p.mix;
             out.ld2 = ld;
