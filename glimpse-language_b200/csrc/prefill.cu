@@ -10,6 +10,8 @@
 // the q/k norm + mRoPE + KV write of the chunk (pf_attn_prep_kernel) and the causal attention of its rows over the
 // cache (attn_kernel in its prepared-query mode). The chunk leaves the committed state exactly as M committed rows
 // of verify passes would (the conv rows in the double buffer's committed half, no rows to replay).
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm_act.cuh"
 #include "kernels.h"
@@ -48,8 +50,8 @@ __device__ __forceinline__ void fwht_block(float* v) {
     for (int e = 0; e < VPL; e++) v[e] = __fmul_rn(v[e], inv);
 }
 
-// One row per CTA (256 threads): the producer value x_k of the mode, then rotate(signs * x) in blocks of HB = 32 VPL
-// (warp w takes blocks w, w + 8, ...), written straight into the GEMM's activation tiles: the rotated row is kept in
+// One row per CTA (one warp per Hadamard block of the row, at most 8): the producer value x_k of the mode, then
+// rotate(signs * x) in blocks of HB = 32 VPL (warp w takes blocks w, w + nw, ...), written straight into the GEMM's activation tiles: the rotated row is kept in
 // shared memory, its maximum gives the exponent, and the CTA's 8 warps write the tiles with gemm_act_words (the bits
 // gemm_prep_kernel would write from the same row in global memory). NORM: x = rmsnorm(h) * w, after h += add (the residual of the
 // previous linear, written back). xn (optional, every mode) keeps x unrotated: the GDN a/b rows' input and the
@@ -63,12 +65,13 @@ __global__ void __launch_bounds__(256) pf_rows_kernel(PfRowArgs a) {
     __shared__ float red[32];
     __shared__ float s_r;
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, D = a.D;
+    const int nth = blockDim.x, nw = nth >> 5;
     constexpr int HB = VPL * 32;
     float am = 0.0f;  // largest magnitude of this warp's rotated values
     if (a.mode == PF_NORM) {
         float* hr = a.h + (size_t)row * D;
         float ss = 0.0f;
-        for (int k = tid; k < D; k += 256) {
+        for (int k = tid; k < D; k += nth) {
             float x = hr[k];
             if (a.add) {
                 x = __fadd_rn(x, a.add[(size_t)row * D + k]);
@@ -80,7 +83,7 @@ __global__ void __launch_bounds__(256) pf_rows_kernel(PfRowArgs a) {
         if (tid == 0) s_r = rsqrtf(tot / (float)D + EPS_P);
         __syncthreads();
     }
-    for (int b0 = warp * HB; b0 < D; b0 += 8 * HB) {
+    for (int b0 = warp * HB; b0 < D; b0 += nw * HB) {
         float v[VPL];
         if (a.mode == PF_NORM) {
             const float r = s_r;
@@ -142,7 +145,7 @@ __global__ void __launch_bounds__(256) pf_rows_kernel(PfRowArgs a) {
     }
     const int E = gemm_act_exponent(block_max(am, red));  // its barriers also publish s_row
     if (tid == 0) a.ex[row] = E;
-    gemm_act_words(s_row, row, D, a.G, D / GM_KC, a.nbias, E, 32 * warp, 256, a.bop);
+    gemm_act_words(s_row, row, D, a.G, D / GM_KC, a.nbias, E, 32 * warp, nth, a.bop);
 }
 
 void launch_pf_rows(const PfRowArgs& a, int M, int hb, cudaStream_t st) {
@@ -152,7 +155,8 @@ void launch_pf_rows(const PfRowArgs& a, int M, int hb, cudaStream_t st) {
     if (smem > 48 * 1024) raise_smem_limit(fn, 200 * 1024);
     PfRowArgs aa = a;
     void* args[] = {&aa};
-    cudaLaunchKernel(fn, dim3(M), dim3(256), args, smem, st);
+    const int nth = 32 * std::min(8, a.D / hb);  // a warp per Hadamard block
+    cudaLaunchKernel(fn, dim3(M), dim3(nth), args, smem, st);
 }
 
 // Embedding rows of the chunk: the bf16 table's row as is, or the ternary tied table's embed (kernels.metal:230-246,
