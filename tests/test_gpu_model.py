@@ -276,3 +276,37 @@ def test_lookup_decode_with_vocab_fillers_normalize_and_emit(pair):
         m.set_emit(None)
         m.set_encoder(None)
         m.set_vocab_bytes([])
+
+
+def test_models_on_concurrent_host_threads(gpu):
+    """Serving several sessions at once (the config-5 bench's form): model instances on their own streams, each driven
+    by its own host thread, give the tokens they give when run one after another (batched prefill of 100 tokens,
+    then speculative decode with planted drafts)."""
+    import concurrent.futures
+
+    cfg = tiny(**CONFIGS["g64_bias_h512_signs"])
+    ts = synth.model_tensors(cfg, 12)
+    models = [Model(cfg).load(ts) for _ in range(3)]
+    prompts = [prompt(cfg, 100, seed=20 + i) for i in range(3)]
+
+    def session(i):
+        m = models[i]
+        m.reset()
+        first = m.prefill(prompts[i])
+        g, _ = m.decode(first, speculate=False, max_tokens=20)
+        m.reset()
+        m.prefill(prompts[i])
+        s, _ = m.decode(first, mode=_lib.DRAFT_PLANTED, planted=g[1:], max_tokens=20, draft_max=8)
+        return first, list(g), list(s)
+
+    try:
+        alone = [session(i) for i in range(3)]
+        with concurrent.futures.ThreadPoolExecutor(3) as ex:
+            for _ in range(2):
+                together = list(ex.map(session, range(3)))
+                assert together == alone
+        for first, g, s in alone:
+            assert g == s
+    finally:
+        for m in models:
+            m.close()
