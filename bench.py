@@ -298,10 +298,11 @@ def run_config5(args, ws, rank, local):
     peak = pk.get("bf16_tflops_sustained", 1400.0)
     n_attn = sum(cfg.layer_is_attn[i] for i in range(cfg.n_layers))
     n_gdn = cfg.n_layers - n_attn
-    # launches of one session: embed, per GDN layer 4 producers + 4 x (prep + GEMM) + a/b, conv, conv rows,
-    # recurrence; per attention layer 4 producers + 4 x 2 + prep + attention; the last layer stops after its state
-    # update (the last layer is attention here: producer + 2 + prep); then the one-row pass and its control update
-    per_session = 1 + n_gdn * 16 + (n_attn - 1) * 14 + 4 + m.pass_launches(1) + 1
+    # launches of one session: embed; per GDN layer 4 producers (writing the GEMM tiles) + 4 GEMMs + a/b, conv,
+    # conv rows, recurrence prep + scan; per attention layer 4 producers + 4 GEMMs + prep + attention; the last layer
+    # stops after its state update (the last layer is attention here: producer + GEMM + prep); then the one-row pass
+    # and its control update (410 for the 2B shape, as the ncu launch list of one prefill counts)
+    per_session = 1 + n_gdn * 13 + (n_attn - 1) * 10 + 3 + m.pass_launches(1) + 1
     line = {
         "metric": "prefill tok/s/GPU (whole model, Bonsai-2B shape, batched prefill on tcgen05)",
         "value": whole_job_rate(ws, rows * args.steps, ms / 1000), "unit": "tok/s", "n_gpus": ws,

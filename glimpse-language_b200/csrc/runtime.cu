@@ -912,13 +912,13 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         in.add = pending;
         in.w = L.in_norm;
         in.signs = L.mix_in.signs;
-        in.xn = p.xn;
+        in.xn = (!L.attn || L.mix_in.lora.a) ? p.xn : nullptr;  // the GDN a/b rows or the adapter read it
         TRY(pf_rows_gemm(m, in, L.mix_in, M, p.mix));
         PfRowArgs out;
         out.D = L.attn ? aw : gw;
         out.src = p.y;
         out.signs = L.mix_out.signs;
-        out.xn = p.xn;
+        out.xn = L.mix_out.lora.a ? p.xn : nullptr;  // unrotated rows: only an adapter reads them
         if (!L.attn) {
             launch_pf_gdn_ab(L.wa, L.wb, p.xn, p.ga, p.gb, NV, d, M, st);
             float* cs = m->conv + ((size_t)L.gi * 2 + (par ^ 1)) * 3 * C;  // the committed half
@@ -977,14 +977,14 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
         post.add = p.tmp;
         post.w = L.post_norm;
         post.signs = L.gu.signs;
-        post.xn = p.xn;
+        post.xn = L.gu.lora.a ? p.xn : nullptr;
         TRY(pf_rows_gemm(m, post, L.gu, M, p.gu));
         PfRowArgs sw;
         sw.mode = PF_SWIGLU;
         sw.D = ff;
         sw.src = p.gu;
         sw.signs = L.down.signs;
-        sw.xn = p.xn;
+        sw.xn = L.down.lora.a ? p.xn : nullptr;
         TRY(pf_rows_gemm(m, sw, L.down, M, p.tmp));
         pending = p.tmp;
         CK(cudaGetLastError());
