@@ -112,3 +112,43 @@ def test_graded_shape_batched_prefill_equals_verify_pass_prefill(gpu):
     finally:
         m.set_batched_prefill(True)
         m.close()
+
+
+@pytest.mark.parametrize("shape", [dict(heads=4, kv_heads=4, lin_k_heads=4, lin_v_heads=4),
+                                   dict(heads=16, kv_heads=1, lin_k_heads=1, lin_v_heads=4)])
+def test_chunk_kernels_other_head_ratios(gpu, shape):
+    """The chunk attention at one query head per kv head (32-row blocks) and at 16 (2-row blocks), the chunked
+    recurrence at one value head per key head and at four: batched prefill of 300 tokens leaves the state that
+    verify-pass prefill leaves, and the verify pass that follows matches the oracle."""
+    cfg = tiny(ctx=512, **shape)
+    ts = synth.model_tensors(cfg, 17)
+    m = Model(cfg).load(ts)
+    o = OracleModel(cfg, ts)
+    try:
+        ids = synth.zipf_tokens(8, 300, cfg.vocab)
+        parts = {}
+        for batched in (True, False):
+            m.set_batched_prefill(batched)
+            m.reset()
+            nxt = m.prefill(ids)
+            s = m.snapshot()
+            parts[batched] = (nxt, [np.frombuffer(s.read(i).tobytes(), np.float32) for i in range(4)])
+            s.free()
+        assert parts[True][0] == parts[False][0]
+        for i in range(4):
+            a, b = parts[True][1][i], parts[False][1][i]
+            assert np.abs(a - b).max() <= 2e-4 * max(float(np.abs(b).max()), 1e-6), f"state part {i}"
+        m.set_batched_prefill(True)
+        m.reset()
+        o.reset()
+        assert m.prefill(ids) == o.prefill(ids, chunk=16)
+        rows = synth.zipf_tokens(9, 9, cfg.vocab).astype(np.uint32)
+        m.keep_logits(True)
+        m.verify(rows)
+        _, ol = o.forward(rows, logits=True)
+        for t in range(9):
+            assert float(np.abs(m.logits(t) - ol[t]).max()) <= LOGIT_TOL
+        m.keep_logits(False)
+    finally:
+        m.set_batched_prefill(True)
+        m.close()
