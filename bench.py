@@ -171,7 +171,9 @@ def run_reference(args, ws, rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded random-init)",
             "config": {"workload": WORKLOAD, "cpu_sample": cb["sample"]},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "the reference (Rust + Metal/Vulkan) cannot run here; its CPU-runnable restatement (oracle/) is "
+            "note": "the reference's Rust host and Metal/Vulkan backends cannot run here; its Metal kernels compiled "
+                    "for the host (oracle/_ref, the oracle's pin) take only the reference's own pack (g128, ternary "
+                    "tied head), not this workload's g64 + bias + bf16 head, so the CPU restatement (oracle/) is "
                     "timed on the host cores"}
     print(json.dumps(line), flush=True)
 
