@@ -1,6 +1,7 @@
-// attn.cu — gated full-attention core of the verify pass in one kernel: q/k RMSNorm with interleaved mRoPE and the KV
-// write (attn_prep, kernels.metal:627-662), split-K causal GQA over the cache (attn_split :713-780) and the log-sum-exp
-// merge (attn_combine :783-799), done by the last split CTA of each (row, kv head).
+// attn.cu — gated full-attention core of the verify pass in two kernels: q/k RMSNorm with interleaved mRoPE and the KV
+// write (attn_prep, kernels.metal:627-662) with split-K causal GQA over the cache (attn_split :713-780), then the
+// log-sum-exp merge of the splits (attn_combine :783-799) by attn_merge_kernel, one CTA per (row, query head). The
+// merge was first done by the last split CTA of each (row, kv head): 13 us of the layer's 32 in the pass graph.
 //
 // Grid (KV, NSPLIT_ATTN, T), 256 threads, two CTAs per SM. The grid is fixed for graph capture; each CTA derives its
 // key range [j0, j1) of [0, off + t] from the device-side KV offset, so one captured graph serves every length and a
@@ -30,7 +31,6 @@ __host__ __device__ inline size_t attn_smem_floats(int qp, int rot) {
 template <int QP>
 __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
-    __shared__ int s_last;
     constexpr int HG = QP < 8 ? QP : 8;  // heads scored per pass over the keys (their queries live in registers)
     constexpr int LHG = HG >= 8 ? 3 : (HG >= 4 ? 2 : (HG >= 2 ? 1 : 0));
     const int kh = blockIdx.x, s = blockIdx.y, t = blockIdx.z;
@@ -276,61 +276,38 @@ __global__ void __launch_bounds__(256, 2) attn_kernel(AttnArgs a) {
         pp[(size_t)d * NS * 258] = -INFINITY;
         pp[(size_t)d * NS * 258 + 1] = 0.0f;
     }
-    // the last split CTA of (t, kh) merges (fixed split order)
-    __syncthreads();
-    if (d == 0) {
-        unsigned old;
-        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
-                     : "=r"(old)
-                     : "l"(a.counters + t * KV + kh)
-                     : "memory");
-        s_last = old == (unsigned)(NS - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    const float* p0 = a.part + ((size_t)t * H + kh * qper) * NS * 258;
-    float* mls = qs;  // [qper][NSPLIT][2]
-    float av[2][NSPLIT_ATTN], an[2][NSPLIT_ATTN];
-    auto load_av = [&](int h0, float (*dst)[NSPLIT_ATTN]) {
+}
+
+// The merge of the key splits (attn_combine, kernels.metal:783-799), after the split kernel: one CTA per (row, query
+// head), thread = head dim; the splits' running maxima, sums and partial outputs read together, combined in split
+// order. Each row's splits and their order depend only on its own position (batch invariance).
+__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a) {
+    const int t = blockIdx.x, hq = blockIdx.y, d = threadIdx.x;
+    const int H = a.H, NS = a.nsplit;
+    pdl_trigger();
+    pdl_wait();
+    const float* p0 = a.part + ((size_t)t * H + hq) * NS * 258;
+    float mv[NSPLIT_ATTN], lv[NSPLIT_ATTN], ov[NSPLIT_ATTN];
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++)
-#pragma unroll
-            for (int q = 0; q < NSPLIT_ATTN; q++)
-                dst[hh][q] = h0 + hh < qper && q < NS ? __ldcg(p0 + (size_t)(h0 + hh) * NS * 258 + q * 258 + 2 + d) : 0.0f;
-    };
-    load_av(0, av);
-    for (int e = threadIdx.x; e < qper * NS * 2; e += 256) {
-        const int h = e / (2 * NS), r = e - h * 2 * NS;
-        mls[h * NSPLIT_ATTN * 2 + r] = __ldcg(p0 + (size_t)h * NS * 258 + (r >> 1) * 258 + (r & 1));
-    }
-    __syncthreads();
-    for (int h0 = 0; h0 < qper; h0 += 2) {
-        if (h0 + 2 < qper) load_av(h0 + 2, an);  // the next heads' loads in flight while these are merged
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const int h = h0 + hh;
-            if (h >= qper) break;
-            const float* m2 = mls + h * NSPLIT_ATTN * 2;
-            float M = -INFINITY;
-#pragma unroll
-            for (int q = 0; q < NSPLIT_ATTN; q++)
-                if (q < NS) M = fmaxf(M, m2[2 * q]);
-            float L = 0.0f, o = 0.0f;
-#pragma unroll
-            for (int q = 0; q < NSPLIT_ATTN; q++) {
-                if (q >= NS || m2[2 * q] == -INFINITY) continue;
-                const float wgt = expf(m2[2 * q] - M);
-                L += m2[2 * q + 1] * wgt;
-                o += av[hh][q] * wgt;
-            }
-            a.out[(size_t)t * aw + (kh * qper + h) * 256 + d] = o / L;
+    for (int q = 0; q < NSPLIT_ATTN; q++)
+        if (q < NS) {
+            mv[q] = __ldcg(p0 + q * 258);
+            lv[q] = __ldcg(p0 + q * 258 + 1);
+            ov[q] = __ldcg(p0 + q * 258 + 2 + d);
         }
+    float M = -INFINITY;
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++)
+    for (int q = 0; q < NSPLIT_ATTN; q++)
+        if (q < NS) M = fmaxf(M, mv[q]);
+    float L = 0.0f, o = 0.0f;
 #pragma unroll
-            for (int q = 0; q < NSPLIT_ATTN; q++) av[hh][q] = an[hh][q];
+    for (int q = 0; q < NSPLIT_ATTN; q++) {
+        if (q >= NS || mv[q] == -INFINITY) continue;
+        const float wgt = expf(mv[q] - M);
+        L += lv[q] * wgt;
+        o += ov[q] * wgt;
     }
-    if (d == 0) a.counters[t * KV + kh] = 0;
+    a.out[(size_t)t * H * 256 + hq * 256 + d] = o / L;
 }
 
 template <int QP>
@@ -340,6 +317,7 @@ static void launch_attn_t(const AttnArgs& a, cudaStream_t st) {
     AttnArgs aa = a;
     void* args[] = {&aa};
     launch_pdl((const void*)attn_kernel<QP>, dim3(a.KV, a.nsplit, a.T), dim3(256), smem, st, args);
+    launch_pdl((const void*)attn_merge_kernel, dim3(a.T, a.H), dim3(256), 0, st, args);
 }
 
 void launch_attn(const AttnArgs& a, cudaStream_t st) {

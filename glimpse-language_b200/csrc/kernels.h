@@ -149,16 +149,16 @@ struct AttnArgs {
     const float* inv_freq; // [rot/2]
     float* kc;             // [ctx][KV][256]
     float* vc;
-    float* part;           // [T][H][NSPLIT][258]
-    unsigned* counters;    // [VMAX][KV] zero between launches
+    float* part;           // [T][H][NSPLIT][258]: per split the running maximum, sum and partial output
     float* out;            // [T][H*256]
     int H, KV, rot, T, ld, ctx;
     int nsplit = NSPLIT_ATTN;       // key splits per (row, kv head), 1..NSPLIT_ATTN
     // prefill mode: queries prepared by pf_attn_prep ([T][H][256]), every key of rows [0, off0 + T) in the cache,
-    // row t at position off0 + t (counters [T][KV], part [T][H][nsplit][258])
+    // row t at position off0 + t (part [T][H][nsplit][258])
     const float* qprep = nullptr;
     int off0 = 0;
 };
+// The split kernel, then attn_merge_kernel (two launches).
 void launch_attn(const AttnArgs& a, cudaStream_t st);
 // Prefill chunk attention on the tensor cores (attn_prefill.cu): queries prepared [T][H][256], every key of positions
 // [0, off0 + T) in the cache, out [T][H * 256]; for query heads per kv head dividing 32.

@@ -36,7 +36,6 @@ struct Prefill {
     float *q = nullptr, *k = nullptr, *v = nullptr, *ga = nullptr, *gb = nullptr, *qbuf = nullptr, *part = nullptr;
     float* lu = nullptr;  // LoRA A products [rows][3 x 256]
     float* gws = nullptr; // chunked gated delta rule workspace (gdn_chunk_workspace_bytes)
-    unsigned* counters = nullptr;
     uint8_t* bop = nullptr;
     int* ex = nullptr;
     uint32_t* ids = nullptr;
@@ -96,7 +95,6 @@ struct bcu_model {
     // scratch
     float *h = nullptr, *mix = nullptr, *gubuf = nullptr, *y = nullptr, *apart = nullptr;
     float* ssbuf = nullptr;           // [hidden/128][VMAX] sums of squares of h by row block
-    unsigned* attn_counters = nullptr;
     float* logits = nullptr;
     float* partial = nullptr;
     unsigned* counters = nullptr;

@@ -358,7 +358,6 @@ void enqueue_pass(bcu_model* m, int T) {
             a.kc = m->kc + (size_t)L.ai * c.ctx * m->kvw;
             a.vc = m->vc + (size_t)L.ai * c.ctx * m->kvw;
             a.part = m->apart;
-            a.counters = m->attn_counters;
             a.out = m->y;
             a.H = c.heads;
             a.KV = c.kv_heads;
@@ -711,7 +710,6 @@ bcu_status bcu_finalize(bcu_model* m) {
     TRY(dmalloc(m, &m->y, (size_t)VMAX * std::max(m->gw, m->aw) * 4));
     TRY(dmalloc(m, &m->apart, (size_t)VMAX * c.heads * NSPLIT_ATTN * 258 * 4));
     TRY(dmalloc(m, &m->ssbuf, (size_t)(d / 128) * VMAX * 4));
-    TRY(dmalloc(m, &m->attn_counters, (size_t)VMAX * c.kv_heads * 4));
     TRY(dmalloc(m, &m->logits, (size_t)VMAX * c.vocab * 4));
     (void)wide;
     size_t pf = 0;
@@ -758,7 +756,6 @@ bcu_status bcu_reset(bcu_model* m) {
     const int NV = m->c.lin_v_heads;
     CK(cudaMemsetAsync(m->gdn, 0, (size_t)m->n_gdn * NV * 128 * 128 * 4, m->st));
     CK(cudaMemsetAsync(m->conv, 0, (size_t)m->n_gdn * 2 * 3 * m->C * 4, m->st));
-    CK(cudaMemsetAsync(m->attn_counters, 0, (size_t)VMAX * m->c.kv_heads * 4, m->st));
     CK(cudaMemsetAsync(m->op_counters, 0, 512 * 4, m->st));
     Ctl z;
     memset(&z, 0, sizeof(z));
@@ -780,7 +777,7 @@ void bcu_destroy(bcu_model* m) {
         if (g) cudaGraphExecDestroy(g);
     for (auto& kv : m->staged) cudaFree(kv.second.dev);
     void* bufs[] = {m->arena, m->gdn, m->conv, m->kc, m->vc, m->pend_qkv, m->pend_qkvc, m->pend_ab, m->h,
-                    m->mix, m->gubuf, m->y, m->apart, m->ssbuf, m->attn_counters, m->logits,
+                    m->mix, m->gubuf, m->y, m->apart, m->ssbuf, m->logits,
                     m->partial, m->counters, m->head_counter, m->pv, m->pi, m->ctl, m->planted_dev,
                     m->opbuf, m->op_counters, m->lora_buf, m->lora_upart};
     for (void* b : bufs)
@@ -856,7 +853,6 @@ bcu_status pf_alloc(bcu_model* m) {
     TRY(get(&p.gb, P * c.lin_v_heads * 4));
     TRY(get(&p.qbuf, P * m->aw * 4));
     TRY(get(&p.part, P * c.heads * PF_NSPLIT * 258 * 4));
-    TRY(get(&p.counters, P * c.kv_heads * 4));
     TRY(get(&p.bop, gemm_act_bytes((int)P, kmax, c.group_size)));
     TRY(get(&p.ex, P * 4));
     TRY(get(&p.ids, P * 4));
@@ -944,7 +940,6 @@ bcu_status pf_chunk(bcu_model* m, const uint32_t* ids, int M, int off, int par) 
             a.kc = kc;
             a.vc = vc;
             a.part = p.part;
-            a.counters = p.counters;
             a.out = p.y;
             a.H = c.heads;
             a.KV = c.kv_heads;
