@@ -28,36 +28,48 @@ __device__ __forceinline__ void gates(float a_in, float b_in, float ea, float dt
     beta = 1.0f / (1.0f + expf(-b_in));
 }
 
-// One gated-delta step for the R dv rows of a warp (lane = 4 dk entries), with one reduction round: with u = S.k and
+// One gated-delta step for the 2 dv rows of a warp (lane = 4 dk entries), with one reduction round: with u = S.k and
 // z = S.q of the state before the step, S' = g S + delta k with delta = (v - g u) beta, and the output
-// S'.q = g z + delta (k.q) (kernels.metal:607-620 computes the same quantities in sequence, with two rounds).
-template <int R>
-__device__ __forceinline__ void gdn_step_fused(float4* st, float4 q, float4 k, const float* vv, float g, float beta,
-                                               float* o4) {
-    float u[R], z[R];
+// S'.q = g z + delta (k.q) (kernels.metal:607-620 computes the same quantities in sequence, with two rounds). The five
+// warp sums (u and z of both rows, k.q) take 14 shuffles instead of 25: a halving butterfly over offsets 16, 8, 4
+// leaves lane l with the sum over its 8-lane group of value 4 b4 + 2 b3 + b2 (b_i the bits of l), offsets 2 and 1
+// complete that value's sum, and each lane then reads the five totals from lanes 0, 4, 8, 12 and 16. A fixed tree:
+// a row's result does not depend on the other rows of the pass.
+__device__ __forceinline__ void gdn_step_fused2(float4* st, float4 q, float4 k, const float* vv, float g, float beta,
+                                                float* o2) {
+    const int lane = threadIdx.x & 31;
+    float p[8];
 #pragma unroll
-    for (int i = 0; i < R; i++) {
-        u[i] = st[i].x * k.x + st[i].y * k.y + st[i].z * k.z + st[i].w * k.w;
-        z[i] = st[i].x * q.x + st[i].y * q.y + st[i].z * q.z + st[i].w * q.w;
+    for (int i = 0; i < 2; i++) {
+        p[i] = st[i].x * k.x + st[i].y * k.y + st[i].z * k.z + st[i].w * k.w;
+        p[2 + i] = st[i].x * q.x + st[i].y * q.y + st[i].z * q.z + st[i].w * q.w;
     }
-    float kq = k.x * q.x + k.y * q.y + k.z * q.z + k.w * q.w;
+    p[4] = k.x * q.x + k.y * q.y + k.z * q.z + k.w * q.w;
+    p[5] = p[6] = p[7] = 0.0f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
+    for (int o = 16, n = 4; o >= 4; o >>= 1, n >>= 1) {
+        const bool up = (lane & o) != 0;
 #pragma unroll
-        for (int i = 0; i < R; i++) {
-            u[i] += __shfl_xor_sync(0xffffffffu, u[i], o);
-            z[i] += __shfl_xor_sync(0xffffffffu, z[i], o);
+        for (int j = 0; j < n; j++) {
+            const float send = up ? p[j] : p[j + n];
+            const float keep = up ? p[j + n] : p[j];
+            p[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
-        kq += __shfl_xor_sync(0xffffffffu, kq, o);
     }
+    float t = p[0];
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    const float u[2] = {__shfl_sync(0xffffffffu, t, 0), __shfl_sync(0xffffffffu, t, 4)};
+    const float z[2] = {__shfl_sync(0xffffffffu, t, 8), __shfl_sync(0xffffffffu, t, 12)};
+    const float kq = __shfl_sync(0xffffffffu, t, 16);
 #pragma unroll
-    for (int i = 0; i < R; i++) {
+    for (int i = 0; i < 2; i++) {
         const float delta = (vv[i] - g * u[i]) * beta;
         st[i].x = g * st[i].x + k.x * delta;
         st[i].y = g * st[i].y + k.y * delta;
         st[i].z = g * st[i].z + k.z * delta;
         st[i].w = g * st[i].w + k.w * delta;
-        o4[i] = g * z[i] + delta * kq;
+        o2[i] = g * z[i] + delta * kq;
     }
 }
 
@@ -221,7 +233,7 @@ __global__ void __launch_bounds__(256, 2) gdn_layer_kernel(GdnArgs a) {
         }
     __syncthreads();
 
-    // ---- gated delta rule: replay (commit), then this pass's rows, one reduction round per step (gdn_step_fused);
+    // ---- gated delta rule: replay (commit), then this pass's rows, one reduction round per step (gdn_step_fused2);
     // warp w owns dv rows 2w, 2w + 1
     for (int r = 0; r < rn + T; r++) {
         const float4 q = *(const float4*)&sm.q[r][lane * 4];
@@ -229,7 +241,7 @@ __global__ void __launch_bounds__(256, 2) gdn_layer_kernel(GdnArgs a) {
         const float2 v2 = *(const float2*)&sm.v[r][w * 2];
         const float vv[2] = {v2.x, v2.y};
         float o2[2];
-        gdn_step_fused<2>(st, q, k, vv, sm.g[r], sm.beta[r], o2);
+        gdn_step_fused2(st, q, k, vv, sm.g[r], sm.beta[r], o2);
         if (r == rn - 1) {
 #pragma unroll
             for (int i = 0; i < 2; i++) *(float4*)(S + (size_t)i * 128) = st[i];
@@ -249,7 +261,7 @@ void launch_gdn_layer(const GdnArgs& a, cudaStream_t st) {
 // Graded config 2 (and the prefill chunk's recurrence): T rows from explicit q/k/v/gate inputs, outputs for every
 // row, and the state written back as it was after the first n rows. CTA = (value head, 32 dv rows), 256 threads:
 // eight lanes per dv row, lane (row = tid / 8, s = tid % 8) holds dk entries [16 s, 16 s + 16) of that row. A step is
-// the one-round form of gdn_step_fused: u = S.k and z = S.q of the state before the step, S' = g S + delta k with
+// the one-round step of gdn_step_fused2: u = S.k and z = S.q of the state before the step, S' = g S + delta k with
 // delta = (v - g u) beta, output g z + delta (k.q) (kernels.metal:607-620), each dot product over four partial sums
 // per lane and the row's 8 lanes in 3 levels. Rows are staged in shared memory GV_CHUNK at a time in two buffers (the
 // loads of chunk c + 1 are issued before the steps of chunk c and stored after them), q and k in the order
