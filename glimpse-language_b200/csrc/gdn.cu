@@ -84,6 +84,49 @@ struct __align__(16) GdnSmem {
 
 __host__ __device__ inline size_t gdn_smem_bytes() { return sizeof(GdnSmem); }
 
+// What a GDN layer pass reads of the previous pass's results (gdn_layer_kernel): control words, this warp's state rows,
+// the replayed rows' conv outputs, rows rn .. rn + 2 of [committed conv rows; previous raw rows], the replayed rows'
+// gate inputs.
+struct GdnPrev {
+    int par, rn;
+    float4 st[2];
+    float lx[VMAX], lv[VMAX];
+    float rx[3 + VMAX], rv[3 + VMAX];
+    float ga, gb;
+};
+
+__device__ __forceinline__ void gdn_load_previous(const GdnArgs& a, const float* S, int cx, int cv, bool has_v, int tid,
+                                                  int hd, GdnPrev& p) {
+    const int C = a.C, NV = a.NV;
+    p.par = a.ctl->parity;
+    p.rn = a.ctl->replay_n;
+    const int prev = p.par ^ 1, rn = p.rn;
+#pragma unroll
+    for (int r = 0; r < 2; r++) p.st[r] = *(const float4*)(S + (size_t)r * 128);
+    const float* pqc = a.pend_qkvc + (size_t)prev * VMAX * C;
+#pragma unroll
+    for (int r = 0; r < VMAX; r++)
+        if (r < rn) {
+            p.lx[r] = pqc[(size_t)r * C + cx];
+            p.lv[r] = has_v ? pqc[(size_t)r * C + cv] : 0.0f;
+        }
+    const float* cs_in = a.conv_state + (size_t)prev * 3 * C;  // committed state lives at the previous parity
+    const float* pq = a.pend_qkv + (size_t)prev * VMAX * C;
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const int kk = rn + j;
+        const float* src = kk < 3 ? cs_in + (size_t)kk * C : pq + (size_t)(kk - 3) * C;
+        p.rx[j] = src[cx];
+        p.rv[j] = has_v ? src[cv] : 0.0f;
+    }
+    p.ga = p.gb = 0.0f;
+    if (tid < rn) {
+        const float* ab = a.pend_ab + ((size_t)prev * VMAX + tid) * 2 * NV;
+        p.ga = ab[hd];
+        p.gb = ab[NV + hd];
+    }
+}
+
 __global__ void __launch_bounds__(256, 2) gdn_layer_kernel(GdnArgs a) {
     extern __shared__ __align__(16) uint8_t gsm[];
     GdnSmem& sm = *(GdnSmem*)gsm;
@@ -107,48 +150,35 @@ __global__ void __launch_bounds__(256, 2) gdn_layer_kernel(GdnArgs a) {
     }
     const float ea = expf(a.a_log[hd]), dtb = a.dt_bias[hd];
     pdl_trigger();
-    pdl_wait();
-    const int par = a.ctl->parity, prev = par ^ 1, rn = a.ctl->replay_n;
-
     // ---- every load of the layer in flight at once: the state rows of this warp, the replayed rows (conv outputs
-    // of the previous pass), the committed conv state, the previous pass's raw rows, this pass's rows, gate inputs
+    // of the previous pass), the committed conv state, the previous pass's raw rows, this pass's rows, gate inputs.
+    // What the previous pass left (its control words, this layer's state, its pending rows and gate inputs) is read
+    // before the dependency wait inside the pass graph (a.prefetch: the previous pass has completed, and no earlier
+    // kernel of this pass writes any of it), after it otherwise; this pass's rows and gate inputs after it.
     float* S = a.gdn_state + ((size_t)hd * 128 + dv0 + w * 2) * 128 + lane * 4;
-    float4 st[2];
-#pragma unroll
-    for (int r = 0; r < 2; r++) st[r] = *(const float4*)(S + (size_t)r * 128);
-    const float* pqc = a.pend_qkvc + (size_t)prev * VMAX * C;
-    float lx[VMAX], lv[VMAX];
-#pragma unroll
-    for (int r = 0; r < VMAX; r++)
-        if (r < rn) {
-            lx[r] = pqc[(size_t)r * C + cx];
-            lv[r] = has_v ? pqc[(size_t)r * C + cv] : 0.0f;
-        }
-    const float* cs_in = a.conv_state + (size_t)prev * 3 * C;  // committed state lives at the previous parity
-    const float* pq = a.pend_qkv + (size_t)prev * VMAX * C;
+    GdnPrev pv;
+    if (a.prefetch) gdn_load_previous(a, S, cx, cv, has_v, tid, hd, pv);
+    pdl_wait();
+    if (!a.prefetch) gdn_load_previous(a, S, cx, cv, has_v, tid, hd, pv);
+    const int par = pv.par, rn = pv.rn;
+    float4 st[2] = {pv.st[0], pv.st[1]};
     const int ld = C + NV * 128;
-    // rows rn..rn+2 of [state(3); previous raw rows], then this pass's rows
-    float rx[3 + VMAX], rv[3 + VMAX];
-#pragma unroll
-    for (int j = 0; j < 3; j++) {
-        const int kk = rn + j;
-        const float* src = kk < 3 ? cs_in + (size_t)kk * C : pq + (size_t)(kk - 3) * C;
-        rx[j] = src[cx];
-        rv[j] = has_v ? src[cv] : 0.0f;
-    }
+    float* rx = pv.rx;
+    float* rv = pv.rv;
 #pragma unroll
     for (int t = 0; t < VMAX; t++)
         if (t < T) {
             rx[3 + t] = a.qkvz[(size_t)t * ld + cx];
             rv[3 + t] = has_v ? a.qkvz[(size_t)t * ld + cv] : 0.0f;
         }
-    float ga = 0.0f, gb = 0.0f;
-    if (tid < rn + T) {
-        const float* ab = tid < rn ? a.pend_ab + ((size_t)prev * VMAX + tid) * 2 * NV
-                                   : a.pend_ab + ((size_t)par * VMAX + tid - rn) * 2 * NV;
+    float ga = pv.ga, gb = pv.gb;
+    if (tid >= rn && tid < rn + T) {
+        const float* ab = a.pend_ab + ((size_t)par * VMAX + tid - rn) * 2 * NV;
         ga = ab[hd];
         gb = ab[NV + hd];
     }
+    const float* lx = pv.lx;
+    const float* lv = pv.lv;
 
     // ---- stage the replayed rows and the gates of every row
 #pragma unroll

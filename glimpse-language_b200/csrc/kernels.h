@@ -123,6 +123,7 @@ struct GdnArgs {
     float* pend_ab;        // [2][VMAX][2NV] gate inputs (replay; written by the qkvz GEMV)
     float* y;              // [T][NV*128]
     int C, NK, NV, T;
+    int prefetch;          // read what the previous pass left before the dependency wait (pass graphs only)
 };
 void launch_gdn_layer(const GdnArgs& a, cudaStream_t st);
 

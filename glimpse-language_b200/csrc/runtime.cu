@@ -255,6 +255,7 @@ GdnArgs gdn_args(bcu_model* m, const Layer& L, int T) {
     g.NK = c.lin_k_heads;
     g.NV = c.lin_v_heads;
     g.T = T;
+    g.prefetch = T > 0;  // the passes run as graphs, each after the previous one completed; the flush (T = 0) does not
     return g;
 }
 
