@@ -317,116 +317,121 @@ __device__ __forceinline__ void transform(const ActSrc& s, int K, const RawTok<V
     }
 }
 
-// One token's 2048-point block built by four warps (warp q of the group holds elements e = 16 q + e', e' < 16, of the
-// one-warp lane layout, i.e. inputs blk0 + 512 q + lane + 32 e'): the radix-2 stages of strides 1..256 run inside the
-// warp, the last two (512, 1024) through shared memory (xch: [q][e'][lane]), with the same operations in the same
-// order as the one-warp transform (emit_token with 64 values per lane), so the region gets the same bits; the
-// exponent is the maximum over the four quarters (s_am: [q]). Writes token t's columns of the 2048-input region reg.
+// One token's HB-point block (HB = 512, 1024 or 2048) built by four warps: warp q of the group holds elements
+// e = VQ q + e', e' < VQ = HB / 128, of the one-warp lane layout, i.e. inputs blk0 + (HB / 4) q + lane + 32 e'. The
+// radix-2 stages of strides 1..16 run across the lanes and 32..HB/8 inside the lane, the last two (HB/4, HB/2) through
+// shared memory (xch: [q][e'][lane]), with the same operations in the same order as the one-warp transform
+// (emit_token with HB / 32 values per lane), so the region gets the same bits; the exponent is the maximum over the
+// four quarters (s_am: [q]). Writes token t's columns of the HB-input region reg. A quarter of a 512-point block is
+// one 128-wide head, so the gated norm's head sums stay inside a warp. Four warps per block shorten the build's chain
+// (the producer, the transform and the hi/lo split of a token block) about fourfold against one warp per block.
 // Called by every thread of the CTA (it holds block-wide barriers); warps with has = false only pass them. writer:
 // this token's builders write the embedding row to the residual stream (EMBED sources).
-constexpr int QX_FLOATS = 4 * 16 * 32;  // exchanged values of one group of four warps
-template <int GPC>
+constexpr int QX_FLOATS = 4 * 16 * 32;  // exchanged values of one group of four warps (2048-point blocks: HB floats)
+template <int HB, int GPC>
 __device__ void quarter_token(const ActSrc& s, int K, int t, int blk0, bool has, bool writer, uint8_t* reg, float* xch,
                               float* s_am) {
-    constexpr int G = 128 / GPC, EPG = G / 32, NGQ = 512 / G;  // groups per quarter
+    constexpr int VQ = HB / 128, QW = HB / 4;  // values per lane, inputs per quarter
+    constexpr int G = 128 / GPC, EPG = G / 32, NGQ = QW / G;  // groups per quarter
+    constexpr float INV = HB == 512 ? 0.044194173824159216f : (HB == 2048 ? 0.02209708691207961f : 0.03125f);
     const int lane = threadIdx.x & 31, q = (threadIdx.x >> 5) & 3;
     const bool rot = s.HB > 0;
-    const int base = blk0 + 512 * q;
-    float v[16];
+    const int base = blk0 + QW * q;
+    float v[VQ];
     if (has) {
-        float sg[16];
+        float sg[VQ];
         if (s.signs) {
 #pragma unroll
-            for (int e = 0; e < 16; e++) sg[e] = s.signs[base + lane + 32 * e];
+            for (int e = 0; e < VQ; e++) sg[e] = s.signs[base + lane + 32 * e];
         }
         if (s.mode == ACT_EMBED) {
             uint32_t id = 0;
             const float r = row_scale(s, t, K, &id, writer && q == 0);  // one writer of the residual row
-            act_values<16>(s, t, base, K, r, id, v);
+            act_values<VQ>(s, t, base, K, r, id, v);
         } else {
-            float wn[16];
+            float wn[VQ > 4 ? VQ : 4];
             if (s.mode == ACT_NORM) {
 #pragma unroll
-                for (int e = 0; e < 16; e++) wn[e] = s.w[base + lane + 32 * e];
+                for (int e = 0; e < VQ; e++) wn[e] = s.w[base + lane + 32 * e];
             } else if (s.mode == ACT_GATED) {
 #pragma unroll
                 for (int k = 0; k < 4; k++) wn[k] = s.w[(lane + 32 * k) & 127];
             }
-            RawTok<16> R;
-            load_raw<16>(s, t, base, K, R);
-            transform<16>(s, K, R, wn, v);
+            RawTok<VQ> R;
+            load_raw<VQ>(s, t, base, K, R);
+            transform<VQ>(s, K, R, wn, v);
         }
         if (s.signs) {
 #pragma unroll
-            for (int e = 0; e < 16; e++) v[e] *= sg[e];
+            for (int e = 0; e < VQ; e++) v[e] *= sg[e];
         }
         if (rot) {
 #pragma unroll
             for (int m = 1; m < 32; m <<= 1) {
                 const float sgn = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
-                for (int e = 0; e < 16; e++) {
+                for (int e = 0; e < VQ; e++) {
                     const float o = __shfl_xor_sync(0xffffffffu, v[e], m);
                     v[e] = fmaf(v[e], sgn, o);  // lower lane: v + o, upper lane: o - v
                 }
             }
 #pragma unroll
-            for (int h = 1; h < 16; h <<= 1)
+            for (int h = 1; h < VQ; h <<= 1)
 #pragma unroll
-                for (int e = 0; e < 16; e++)
+                for (int e = 0; e < VQ; e++)
                     if ((e & h) == 0) {
                         const float a = v[e], c = v[e + h];
                         v[e] = a + c;
                         v[e + h] = a - c;
                     }
 #pragma unroll
-            for (int e = 0; e < 16; e++) xch[(q * 16 + e) * 32 + lane] = v[e];
+            for (int e = 0; e < VQ; e++) xch[(q * VQ + e) * 32 + lane] = v[e];
         }
     }
     __syncthreads();
     if (has) {
-        if (rot) {  // strides 512 (quarters 0|1, 2|3), then 1024 (0|2, 1|3), then the normalisation
+        if (rot) {  // strides HB/4 (quarters 0|1, 2|3), then HB/2 (0|2, 1|3), then the normalisation
 #pragma unroll
-            for (int e = 0; e < 16; e++) {
-                const float y0 = xch[e * 32 + lane], y1 = xch[(16 + e) * 32 + lane];
-                const float y2 = xch[(32 + e) * 32 + lane], y3 = xch[(48 + e) * 32 + lane];
+            for (int e = 0; e < VQ; e++) {
+                const float y0 = xch[e * 32 + lane], y1 = xch[(VQ + e) * 32 + lane];
+                const float y2 = xch[(2 * VQ + e) * 32 + lane], y3 = xch[(3 * VQ + e) * 32 + lane];
                 const float u0 = y0 + y1, u1 = y0 - y1, u2 = y2 + y3, u3 = y2 - y3;
                 const float z = q == 0 ? u0 + u2 : (q == 1 ? u1 + u3 : (q == 2 ? u0 - u2 : u1 - u3));
-                v[e] = z * 0.02209708691207961f;
+                v[e] = z * INV;
             }
         }
-        float am[16];
+        float am[VQ];
 #pragma unroll
-        for (int e = 0; e < 16; e++) am[e] = fabsf(v[e]);
+        for (int e = 0; e < VQ; e++) am[e] = fabsf(v[e]);
 #pragma unroll
-        for (int h = 8; h > 0; h >>= 1)
+        for (int h = VQ / 2; h > 0; h >>= 1)
 #pragma unroll
             for (int e = 0; e < h; e++) am[e] = fmaxf(am[e], am[e + h]);
         const float qmax = warp_max(am[0]);
         if (lane == 0) s_am[q] = qmax;
     }
     __syncthreads();
+    int E = 0;
     if (has) {
         const float amax = fmaxf(fmaxf(s_am[0], s_am[1]), fmaxf(s_am[2], s_am[3]));
-        int E = 0;
         if (amax > 0.0f && amax < INFINITY) {
             int ex;
             frexpf(amax, &ex);  // amax < 2^ex
             E = min(max(14 - ex, -60), 100);
         }
-        const int nsteps = 2048 / 16, nbs = op_bias_steps(2048, G);
+        const int nsteps = HB / 16, nbs = op_bias_steps(HB, G);
         const int col = (t & 3) * 2;
         if (lane == 0 && q == 0) ((int*)(reg + (nsteps + nbs) * 256))[t & 3] = E;
-        {   // hi + lo of x * 2^E * 4^-j (emit_token's layout): element e' of quarter q is k = 512 q + lane + 32 e'
+        {   // hi + lo of x * 2^E * 4^-j (emit_token's layout): element e' of quarter q is k = QW q + lane + 32 e'
             const int j = lane >> 3;
             const int t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
             const int E1 = E - 2 * j;
             const float f = E1 > 60 ? pow2f(60) * pow2f(E1 - 60) : (E1 < -60 ? pow2f(-60) * pow2f(E1 + 60) : pow2f(E1));
             uint16_t* r16 = (uint16_t*)reg;
             const int h_hi = ((col * 4 + t4) * 2 + which) * 2 + (lane & 1), h_lo = h_hi + 16;
-            const int step0 = (lane >> 4) + 32 * q;
+            const int step0 = (lane >> 4) + (QW / 16) * q;
 #pragma unroll
-            for (int e = 0; e < 16; e++) {
+            for (int e = 0; e < VQ; e++) {
                 const float a = v[e] * f;
                 const __half h = __float2half_rn(a);
                 const __half l = __float2half_rn(a - __half2float(h));
@@ -446,28 +451,32 @@ __device__ void quarter_token(const ActSrc& s, int K, int t, int blk0, bool has,
         for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
             for (int g = 0; g < NGQ; g++) gs[g] += __shfl_xor_sync(0xffffffffu, gs[g], o);
-        if (lane < 16) {  // the bias-step words whose two groups are this quarter's
-            const int hl = lane >> 3, t4 = (lane >> 1) & 3, wh = lane & 1;
-            const int kk0 = wh * 8 + t4 * 2;
-            const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
-            uint32_t* rw = (uint32_t*)reg;
-            for (int bs = 0; bs < nbs; bs++) {
-                const int g0 = bs * 16 + kk0 - q * NGQ;
-                if (g0 < 0 || g0 >= NGQ) continue;
-                float s0 = 0.0f, s1 = 0.0f;
+        // the block's group sums to shared memory (the exchange buffer is free past the barrier above): a bias
+        // word pairs groups 2 i, 2 i + 1, which for 128-input groups of a 512-point block lie in two quarters
+        if (lane == 0) {
 #pragma unroll
-                for (int g = 0; g < NGQ; g++) {
-                    if (g == g0) s0 = gs[g];
-                    if (g == g0 + 1) s1 = gs[g];
-                }
-                const float a0 = s0 * fb, a1 = s1 * fb;
-                __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
-                if (hl) {
-                    h0 = __float2half_rn(a0 - __half2float(h0));
-                    h1 = __float2half_rn(a1 - __half2float(h1));
-                }
-                rw[(nsteps + bs) * 64 + ((col + hl) * 4 + t4) * 2 + wh] = pack_half2(h0, h1);
+            for (int g = 0; g < NGQ; g++) xch[q * NGQ + g] = gs[g];
+        }
+    }
+    __syncthreads();
+    if (has && q == 0 && lane < 16) {  // every bias word of the token's columns, as emit_token writes them
+        constexpr int NG = HB / G;     // groups in the block; the step's slots past them are zero
+        const int nsteps = HB / 16, nbs = op_bias_steps(HB, G);
+        const int col = (t & 3) * 2;
+        const int hl = lane >> 3, t4 = (lane >> 1) & 3, wh = lane & 1;
+        const int kk0 = wh * 8 + t4 * 2;
+        const float fb = pow2f(E - 6 > 100 ? 100 : E - 6);
+        uint32_t* rw = (uint32_t*)reg;
+        for (int bs = 0; bs < nbs; bs++) {
+            const int g0 = bs * 16 + kk0;
+            const float s0 = g0 < NG ? xch[g0] : 0.0f, s1 = g0 + 1 < NG ? xch[g0 + 1] : 0.0f;
+            const float a0 = s0 * fb, a1 = s1 * fb;
+            __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
+            if (hl) {
+                h0 = __float2half_rn(a0 - __half2float(h0));
+                h1 = __float2half_rn(a1 - __half2float(h1));
             }
+            rw[(nsteps + bs) * 64 + ((col + hl) * 4 + t4) * 2 + wh] = pack_half2(h0, h1);
         }
     }
     __syncthreads();
@@ -551,7 +560,7 @@ __device__ void build_operand_quarters(const GemvParams& p, int ks, int NT, uint
             if (warp == 0) zero_token(t, 2048, G, reg);
             continue;
         }
-        quarter_token<GPC>(p.src, p.K, t, ks * p.kslice, warp < 4, blockIdx.x == 0, reg, xch, s_am);
+        quarter_token<2048, GPC>(p.src, p.K, t, ks * p.kslice, warp < 4, blockIdx.x == 0, reg, xch, s_am);
     }
 }
 
@@ -565,74 +574,41 @@ __device__ void build_operand(const GemvParams& p, int ks, int sbsz, int nb, int
         build_operand_warps<VPL, GPC>(p, ks, sbsz, nb, NT, s_op, rsz);
 }
 
-// Grid-build tasks (token t, 2048-point block b) for groups of four warps: task i = CTA + n_main * grp for warp group
+// Grid-build tasks (token t, HB-point block b) for groups of four warps: task i = CTA + n_main * grp for warp group
 // grp (at most two per CTA), built by quarter_token into the group's scratch region, then stored to the buffer.
-// Shared memory: two task regions, then the exchanged values and the quarter maxima of each group.
-template <int GPC>
+// Shared memory: two task regions, then the exchanged values (HB floats) and the quarter maxima of each group.
+template <int HB, int GPC>
 __device__ void build_quarters(const GemvParams& p, uint8_t* scratch) {
     constexpr int G = 128 / GPC;
     const ActSrc& s = p.src;
     const int warp = threadIdx.x >> 5, grp = warp >> 2, q = warp & 3;
-    const int nblk = p.K / 2048, ntask = p.T * nblk;
+    const int nblk = p.K / HB, ntask = p.T * nblk;
     const int i = blockIdx.x + p.n_main * grp;
     const bool has = i < ntask;
-    const int rsz = op_region_bytes(2048, G);
+    const int rsz = op_region_bytes(HB, G);
     const int t = has ? i / nblk : 0, b = has ? i % nblk : 0;
     uint8_t* reg = scratch + (size_t)grp * rsz;
-    float* xch = (float*)(scratch + 2 * rsz) + grp * QX_FLOATS;
-    float* s_am = (float*)(scratch + 2 * rsz) + 2 * QX_FLOATS + grp * 4;
-    quarter_token<GPC>(s, p.K, t, b * 2048, has, b == 0, reg, xch, s_am);
-    if (has && q == 0) store_token_columns(t, 2048, G, reg, s.opbuf + ((size_t)b * 4 + (t >> 2)) * rsz);
+    float* xch = (float*)(scratch + 2 * rsz) + grp * HB;
+    float* s_am = (float*)(scratch + 2 * rsz) + 2 * HB + grp * 4;
+    quarter_token<HB, GPC>(s, p.K, t, b * HB, has, b == 0, reg, xch, s_am);
+    if (has && q == 0) store_token_columns(t, HB, G, reg, s.opbuf + ((size_t)b * 4 + (t >> 2)) * rsz);
 }
 
 // The whole operand of the GEMV, built once by its CTAs together into the global buffer src.opbuf: task i = (token
-// i / nblk, Hadamard block i % nblk of the K inputs) is built by warp i / n_main of CTA i % n_main (load, producer,
-// signs, Walsh-Hadamard, fp16 hi/lo, exponent, group sums) into a scratch region in shared memory, whose columns for
-// the token are then stored to the buffer. Then every CTA waits (bounded) until all builder CTAs have counted
+// i / nblk, Hadamard block i % nblk of the K inputs) is built by the four warps of group i / n_main of CTA i % n_main
+// (quarter_token: load, producer, signs, Walsh-Hadamard, fp16 hi/lo, exponent, group sums) into a scratch region in
+// shared memory, whose columns for the token are then stored to the buffer. Then every CTA waits (bounded) until all builder CTAs have counted
 // themselves; the grid is resident at once (the host checks), so the wait ends. counters[0] counts builders,
 // counters[1] the CTAs past the wait (the last resets both for the next GEMV).
 template <int VPL, int GPC>
 __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
-    constexpr int HBe = VPL * 32, G = 128 / GPC;
+    constexpr int HBe = VPL * 32;
     const ActSrc& s = p.src;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, c = blockIdx.x;
     const int T = p.T, K = p.K, nblk = K / HBe, ntask = T * nblk;
-    const int c = blockIdx.x, ncta = p.n_main;
+    const int ncta = p.n_main;
     const int nbuild = ntask < ncta ? ntask : ncta;  // CTAs with at least one task
-    const int rsz = op_region_bytes(HBe, G);
-    const OpGeo geo{HBe, 0, VPL, 0, s.HB > 0};
-    const int i = c + ncta * warp;
-    if constexpr (VPL == 64) {
-        build_quarters<GPC>(p, scratch);
-    } else if (i < ntask) {
-        const int t = i / nblk, b = i % nblk, blk0 = b * HBe;
-        uint8_t* reg = scratch + (size_t)warp * rsz;
-        float v[VPL], sg[VPL];
-        if (s.signs) {
-#pragma unroll
-            for (int e = 0; e < VPL; e++) sg[e] = s.signs[blk0 + lane + 32 * e];
-        }
-        if (s.mode == ACT_EMBED) {
-            uint32_t id = 0;
-            const float r = row_scale(s, t, K, &id, b == 0);  // the builder of block 0 writes the residual row
-            act_values<VPL>(s, t, blk0, K, r, id, v);
-        } else {
-            float wn[VPL];
-            if (s.mode == ACT_NORM) {
-#pragma unroll
-                for (int e = 0; e < VPL; e++) wn[e] = s.w[blk0 + lane + 32 * e];
-            } else if (s.mode == ACT_GATED) {
-#pragma unroll
-                for (int q = 0; q < 4; q++) wn[q] = s.w[(lane + 32 * q) & 127];
-            }
-            RawTok<VPL> R;
-            load_raw<VPL>(s, t, blk0, K, R);
-            transform<VPL>(s, K, R, wn, v);
-        }
-        emit_token<VPL, GPC>(geo, t, reg, v, s.signs ? sg : nullptr);
-        __syncwarp();
-        store_token_columns(t, HBe, G, reg, s.opbuf + ((size_t)b * 4 + (t >> 2)) * rsz);
-    }
+    build_quarters<HBe, GPC>(p, scratch);
     __syncthreads();  // this CTA's tasks are stored
     if (tid == 0) {
         if (c < nbuild) arrive_release(s.op_counters);
@@ -1123,9 +1099,8 @@ static size_t gemv_smem(int kslice, int nt, int group, int T, int K, int ab, int
     int sbsz = hb < kslice ? hb : kslice;
     size_t ops = (size_t)nt * (kslice / sbsz) * op_region_bytes(sbsz, group);
     if (hb == 2048 && !tpc) ops += (QX_FLOATS + 4) * 4;  // build_operand_quarters' exchange after the regions
-    size_t scratch = (size_t)tpc * op_region_bytes(hb, group);
-    if (hb == 2048 && tpc)  // build_quarters: two task regions, the exchanged values, the quarter maxima
-        scratch = 2 * (size_t)op_region_bytes(2048, group) + (2 * QX_FLOATS + 8) * 4;
+    // build_quarters: two task regions, the exchanged values (hb floats per group), the quarter maxima
+    const size_t scratch = tpc ? 2 * (size_t)op_region_bytes(hb, group) + (2 * (size_t)hb + 8) * 4 : 0;
     size_t main = GEMV_HDR + (size_t)kslice * 32 + (size_t)(kslice / 128) * 8 * 2 * gpc * 32 + (ops > scratch ? ops : scratch);
     size_t red = GEMV_HDR + (size_t)4 * 2 * 4 * nt * 2 * 32 * 4 + (size_t)T * (128 + lora_r) * 4;
     size_t abs_ = ab ? ((size_t)(AB_ROWS + T) * K + 8 * 64 + 32) * 4 : 0;
@@ -1173,12 +1148,12 @@ void raise_smem_limit(const void* fn, int bytes) {
 int gemv_grid(const TernaryMat& m, int ab_rows) { return (m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS; }
 
 // Whether this GEMV's CTAs can build its operand together (grid_build): every CTA of the grid resident at once
-// (they wait for one another) and at most 8 tasks (one per warp) per CTA.
+// (they wait for one another) and at most 2 tasks (one per group of four warps) per CTA.
 bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms, int lora_r) {
     const int nt = (2 * T + 7) / 8;
     const int tpc = grid_build_tpc(m, T, hb);
-    // at most one task per warp (per group of four warps for 2048-point blocks); the buffer's regions hold whole blocks
-    if (tpc > (hb == 2048 ? 2 : 8) || hb <= 0 || hb > m.kslice) return false;
+    // at most one task per group of four warps; the buffer's regions hold whole blocks
+    if (tpc > 2 || hb <= 0 || hb > m.kslice) return false;
     const void* fn = gemv_fn(nt, m.group, hb, lora_r > 0);
     const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, tpc, lora_r);
     if (smem > 220 * 1024) return false;
