@@ -599,7 +599,8 @@ __device__ void build_quarters(const GemvParams& p, uint8_t* scratch) {
 // (quarter_token: load, producer, signs, Walsh-Hadamard, fp16 hi/lo, exponent, group sums) into a scratch region in
 // shared memory, whose columns for the token are then stored to the buffer. Then every CTA waits (bounded) until all builder CTAs have counted
 // themselves; the grid is resident at once (the host checks), so the wait ends. counters[0] counts builders,
-// counters[1] the CTAs past the wait (the last resets both for the next GEMV).
+// counters[1] the CTAs past the wait (grid_build_release: the last resets both for the next GEMV). Only thread 0
+// waits; the others meet it at the caller's next barrier.
 template <int VPL, int GPC>
 __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
     constexpr int HBe = VPL * 32;
@@ -614,14 +615,18 @@ __device__ void grid_build(const GemvParams& p, uint8_t* scratch, int* s_ok) {
         if (c < nbuild) arrive_release(s.op_counters);
         *s_ok = spin_until_geq(s.op_counters, (unsigned)nbuild);
         if (!*s_ok) atomicOr(p.o.err, ERR_SPIN_TIMEOUT);
-        unsigned old;
-        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(s.op_counters + 1) : "memory");
-        if (old == (unsigned)(ncta - 1)) {  // every CTA is past the wait
-            s.op_counters[0] = 0;
-            s.op_counters[1] = 0;
-        }
     }
-    __syncthreads();
+}
+
+// After the slice's copies are issued (off the build's critical path): count this CTA past the grid-wide wait; the
+// last one resets both counters for the next GEMV. Thread 0.
+__device__ __forceinline__ void grid_build_release(const GemvParams& p) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.src.op_counters + 1) : "memory");
+    if (old == (unsigned)(p.n_main - 1)) {  // every CTA is past the wait
+        p.src.op_counters[0] = 0;
+        p.src.op_counters[1] = 0;
+    }
 }
 
 // LoRA A of a GEMV's input (norm_rotate's fused A rows, kernels.metal:70-116), in a short kernel launched just before
@@ -861,6 +866,7 @@ __global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
             for (int b = 0; b < nb; b++)
                 bulk_g2s(s_op + (size_t)b * NT * rsz, p.src.opbuf + ((size_t)(ks * nb + b) * 4) * rsz,
                          (uint32_t)(NT * rsz), bar_op);
+            grid_build_release(p);
         }
     }
     if (!prebuilt) build_operand<VPL, GPC>(p, ks, sbsz, nb, NT, s_op, rsz);
