@@ -810,8 +810,11 @@ __device__ void ab_rows(const GemvParams& p, int r0, int nr, uint8_t* smem) {
     }
 }
 
-template <int NT, int GPC, int VPL, bool LORA>
-__global__ void __launch_bounds__(256) ternary_gemv_kernel(GemvParams p) {
+// MINB: 1 for grids that fit the SMs in one wave (up to 255 registers a thread, one CTA per SM: the main loop's
+// fragments and accumulators stay in registers; 2.137 -> 1.959 ms per 2B pass), 2 for larger grids (128 registers,
+// two CTAs per SM, which the 4B shape's 400-720-CTA GEMVs need: 1294 against 1486 tok/s with one).
+template <int NT, int GPC, int VPL, bool LORA, int MINB>
+__global__ void __launch_bounds__(256, MINB) ternary_gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows (whole clusters of their own: n_main % cluster == 0)
@@ -1119,27 +1122,40 @@ static int grid_build_tpc(const TernaryMat& m, int T, int hb) {
     return (ntask + ncta - 1) / ncta;
 }
 
-template <int NT, int GPC>
+template <int NT, int GPC, int MINB>
 static const void* gemv_fn_vpl(int hb, bool lora) {
     if (lora)  // LoRA variants: 512- and 1024-point blocks (bcu_set_lora checks)
-        return hb == 512 ? (const void*)ternary_gemv_kernel<NT, GPC, 16, true>
-                         : (const void*)ternary_gemv_kernel<NT, GPC, 32, true>;
-    if (hb == 512) return (const void*)ternary_gemv_kernel<NT, GPC, 16, false>;
-    if (hb == 1024) return (const void*)ternary_gemv_kernel<NT, GPC, 32, false>;
-    return (const void*)ternary_gemv_kernel<NT, GPC, 64, false>;
+        return hb == 512 ? (const void*)ternary_gemv_kernel<NT, GPC, 16, true, MINB>
+                         : (const void*)ternary_gemv_kernel<NT, GPC, 32, true, MINB>;
+    if (hb == 512) return (const void*)ternary_gemv_kernel<NT, GPC, 16, false, MINB>;
+    if (hb == 1024) return (const void*)ternary_gemv_kernel<NT, GPC, 32, false, MINB>;
+    return (const void*)ternary_gemv_kernel<NT, GPC, 64, false, MINB>;
 }
 template <int NT>
-static const void* gemv_fn_gpc(int group, int hb, bool lora) {
-    return group == 64 ? gemv_fn_vpl<NT, 2>(hb, lora) : gemv_fn_vpl<NT, 1>(hb, lora);
+static const void* gemv_fn_gpc(int group, int hb, bool lora, bool wide) {
+    if (wide) return group == 64 ? gemv_fn_vpl<NT, 2, 1>(hb, lora) : gemv_fn_vpl<NT, 1, 1>(hb, lora);
+    return group == 64 ? gemv_fn_vpl<NT, 2, 2>(hb, lora) : gemv_fn_vpl<NT, 1, 2>(hb, lora);
 }
-// The kernel for nt column tiles, its shared-memory limit raised on this device.
-static const void* gemv_fn(int nt, int group, int hb, bool lora) {
-    const void* fn = nt == 1 ? gemv_fn_gpc<1>(group, hb, lora)
-                   : nt == 2 ? gemv_fn_gpc<2>(group, hb, lora)
-                   : nt == 3 ? gemv_fn_gpc<3>(group, hb, lora)
-                             : gemv_fn_gpc<4>(group, hb, lora);
+// The kernel for nt column tiles (wide: the one-CTA-per-SM register budget), its shared-memory limit raised on this
+// device.
+static const void* gemv_fn(int nt, int group, int hb, bool lora, bool wide) {
+    const void* fn = nt == 1 ? gemv_fn_gpc<1>(group, hb, lora, wide)
+                   : nt == 2 ? gemv_fn_gpc<2>(group, hb, lora, wide)
+                   : nt == 3 ? gemv_fn_gpc<3>(group, hb, lora, wide)
+                             : gemv_fn_gpc<4>(group, hb, lora, wide);
     raise_smem_limit(fn, 220 * 1024);
     return fn;
+}
+
+// SMs of the current device (cached per device).
+static int device_sms() {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (dev >= 0 && dev < 64 && !cache[dev]) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+    return dev >= 0 && dev < 64 ? cache[dev] : 148;
 }
 
 void raise_smem_limit(const void* fn, int bytes) {
@@ -1160,7 +1176,7 @@ bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sm
     const int tpc = grid_build_tpc(m, T, hb);
     // at most one task per group of four warps; the buffer's regions hold whole blocks
     if (tpc > 2 || hb <= 0 || hb > m.kslice) return false;
-    const void* fn = gemv_fn(nt, m.group, hb, lora_r > 0);
+    const void* fn = gemv_fn(nt, m.group, hb, lora_r > 0, gemv_grid(m, ab_rows) <= num_sms);
     const size_t smem = gemv_smem(m.kslice, nt, m.group, T, m.K, ab_rows > 0, hb, tpc, lora_r);
     if (smem > 220 * 1024) return false;
     int per_sm = 0;
@@ -1196,7 +1212,7 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
         launch_pdl(hb == 512 ? (const void*)lora_a_kernel<16> : (const void*)lora_a_kernel<32>,
                    dim3((unsigned)((tasks + 7) / 8)), dim3(256), 0, st, largs);
     }
-    const void* fn = gemv_fn(nt, m.group, hb, p.lora.a != nullptr);
+    const void* fn = gemv_fn(nt, m.group, hb, p.lora.a != nullptr, gemv_grid(m, p.ab_rows) <= device_sms());
     void* args[] = {&p};
     const int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
     launch_pdl(fn, dim3((unsigned)(p.n_main + n_ab)), dim3(256), smem, st, args);
