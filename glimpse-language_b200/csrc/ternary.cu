@@ -1024,20 +1024,32 @@ __global__ void __launch_bounds__(256, MINB) ternary_gemv_kernel(GemvParams p) {
         }
         __syncthreads();
         if (!s_last) return;
-        for (int e = tid; e < 128 * T; e += 256) {
-            int token = e >> 7, rloc = e & 127;
-            const float* src = p.o.partial + (size_t)token * O + rb * 128 + rloc;
-            float v = 0.0f;
-            for (int s0 = 0; s0 < p.nsplit; s0 += 16) {  // loads of a chunk in flight together, sums in split order
-                float pv[16];
+        // The other CTAs' partials: a thread's elements e = tid + 256 i (up to 8 of the T x 128 block) and 8 splits
+        // at a time have all their loads in flight together (one L2 round trip per 8 splits, not one per element);
+        // each element is summed in split order.
+        constexpr int EPT = VMAX * 128 / 256;
+        float v[EPT];
 #pragma unroll
-                for (int s = 0; s < 16; s++) pv[s] = s0 + s < p.nsplit ? __ldcg(src + (size_t)(s0 + s) * T * O) : 0.0f;
+        for (int i = 0; i < EPT; i++) v[i] = 0.0f;
+        for (int s0 = 0; s0 < p.nsplit; s0 += 8) {
+            float pv[EPT][8];
 #pragma unroll
-                for (int s = 0; s < 16; s++)
-                    if (s0 + s < p.nsplit) v += pv[s];
+            for (int i = 0; i < EPT; i++) {
+                const int e = tid + 256 * i;
+                const float* src = p.o.partial + (size_t)(e >> 7) * O + rb * 128 + (e & 127);
+#pragma unroll
+                for (int s = 0; s < 8; s++)
+                    pv[i][s] = e < 128 * T && s0 + s < p.nsplit ? __ldcg(src + (size_t)(s0 + s) * T * O) : 0.0f;
             }
-            fin[token * 128 + rloc] = v;
+#pragma unroll
+            for (int i = 0; i < EPT; i++)
+#pragma unroll
+                for (int s = 0; s < 8; s++)
+                    if (s0 + s < p.nsplit) v[i] += pv[i][s];
         }
+#pragma unroll
+        for (int i = 0; i < EPT; i++)
+            if (tid + 256 * i < 128 * T) fin[tid + 256 * i] = v[i];
         if (tid == 0) p.o.counters[rb] = 0;
     }
     __syncthreads();
