@@ -163,6 +163,7 @@ SIGNATURES = {
     "bcu_set_local_build": (I32, [P, I32]),
     "bcu_set_batched_prefill": (I32, [P, I32]),
     "bcu_linear_set_local_build": (I32, [P, I32]),
+    "bcu_gemv_set_clusters": (I32, [I32]),
     "bcu_static_scratch_debug": (I32, [I32, I32]),
     "bcu_debug_wait_timeout": (I32, [P]),
     "bcu_gemm_prep_debug": (I32, [P, P, I32, P, P]),

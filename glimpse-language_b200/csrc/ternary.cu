@@ -16,10 +16,15 @@
 // together (grid_build: one (token, Hadamard block) per warp into a global buffer, a bounded grid-wide wait, then one
 // bulk copy per block into each CTA), or, when the grid cannot be resident at once (and for standalone inputs), by
 // each CTA for its own K-slice (build_operand). Split-K partials are summed in a fixed order by the last CTA of each
-// row block, which applies the residual add, the LoRA up projection and the sums of squares the next norm needs.
+// row block, which applies the residual add, the LoRA up projection and the sums of squares the next norm needs; when
+// a row block's splits (at most 8) fit as one thread-block cluster, they sum through the cluster's shared memory
+// instead of the global partial buffer.
+#include <atomic>
 #include <cstdio>
+#include <map>
 #include <mutex>
 #include <set>
+#include <tuple>
 #include <utility>
 #include "common.cuh"
 #include "kernels.h"
@@ -42,6 +47,26 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// launch_pdl with thread-block clusters of `csize` CTAs along x (the grid a multiple of csize).
+static cudaError_t launch_pdl_cluster(const void* fn, dim3 grid, int csize, size_t smem, cudaStream_t st,
+                                      void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)csize;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
@@ -144,8 +169,25 @@ struct GemvParams {
     AbArgs ab;
     LoraArgs lora;
     int O, K, group, kslice, nsplit, T, n_main, ab_rows;
-    int nrb;  // row blocks; CTA = ks * nrb + rb
+    int nrb;     // row blocks; CTA = ks * nrb + rb, or rb * nsplit + ks with csplit
+    int csplit;  // the K-splits of a row block form one thread-block cluster and sum through its shared memory
 };
+
+// Cluster barrier (all threads of every CTA of the cluster): release this CTA's shared-memory writes, acquire the
+// others'.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// The float at this CTA's shared address `p` in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ float ld_cluster_f32(const float* p, int rank) {
+    uint32_t a;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
 
 // Per-row scalar of NORM / EMBED: r = rsqrt(mean(h^2) + eps). EMBED also records the id and, in CTA 0, writes the
 // row into the residual stream. Fixed-order reductions (lane strides, then the warp tree); loads are issued in
@@ -817,7 +859,7 @@ template <int NT, int GPC, int VPL, bool LORA, int MINB>
 __global__ void __launch_bounds__(256, MINB) ternary_gemv_kernel(GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows (whole clusters of their own: n_main % cluster == 0)
+    if ((int)blockIdx.x >= p.n_main) {  // GDN a/b gate rows: the CTAs past the GEMV's own
         pdl_trigger();
         int r0 = ((int)blockIdx.x - p.n_main) * AB_ROWS;
         if (r0 < p.ab_rows) ab_rows(p, r0, min(AB_ROWS, p.ab_rows - r0), smem);
@@ -837,7 +879,8 @@ __global__ void __launch_bounds__(256, MINB) ternary_gemv_kernel(GemvParams p) {
     uint8_t* s_op = smem + GEMV_HDR + codes_bytes + sb_bytes;  // regions [nb][NT]
     const bool prebuilt = p.src.opbuf != nullptr;  // operand built by the whole grid (grid_build)
 
-    const int rb = blockIdx.x % p.nrb, ks = blockIdx.x / p.nrb;
+    const int rb = p.csplit ? blockIdx.x / p.nsplit : blockIdx.x % p.nrb;
+    const int ks = p.csplit ? blockIdx.x % p.nsplit : blockIdx.x / p.nrb;  // with csplit: the CTA's cluster rank
     const int nkc_all = p.K / 128;
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -879,6 +922,11 @@ __global__ void __launch_bounds__(256, MINB) ternary_gemv_kernel(GemvParams p) {
         if (tid == 0) atomicOr(p.o.err, ERR_MBAR_TIMEOUT);
         mbar_wait_bounded(bar, 0, 1u << 20);
         if (prebuilt) mbar_wait_bounded(bar_op, 0, 1u << 20);
+        if (p.csplit) {  // both cluster barrier phases of the split sum, so that no other rank waits for this one
+            cluster_sync_all();
+            cluster_arrive();
+            cluster_wait();
+        }
         return;
     }
     if (tid < p.T * nb) {  // exponents to the header (the regions are overwritten by the reduction)
@@ -1010,11 +1058,40 @@ __global__ void __launch_bounds__(256, MINB) ternary_gemv_kernel(GemvParams p) {
         v += red[quarter + e] * pow2f(-et[blk_of_q[1]]);
         v += red[2 * quarter + e] * pow2f(-et[blk_of_q[2]]);
         v += red[3 * quarter + e] * pow2f(-et[blk_of_q[3]]);
-        if (p.nsplit == 1) fin[token * 128 + rloc] = v;
+        if (p.nsplit == 1 || p.csplit) fin[token * 128 + rloc] = v;
         else p.o.partial[((size_t)ks * T + token) * O + rb * 128 + rloc] = v;
     }
     __shared__ int s_last;
-    if (p.nsplit > 1) {
+    if (p.csplit) {
+        // The K-splits of this row block are the ranks of one cluster, each with its sums in its own shared memory
+        // (fin). Rank 0 reads every rank's value of its elements over the cluster's shared memory and sums them in
+        // split order (the same sums, in the same order, as the partial-buffer path below, without its global
+        // atomic and the L2 round trips of the last CTA's loads); then it releases the other ranks, whose shared
+        // memory must stay valid until it has read it.
+        cluster_sync_all();
+        if (ks != 0) {
+            cluster_arrive();
+            cluster_wait();
+            return;
+        }
+        constexpr int EPT = VMAX * 128 / 256;
+        float v[EPT];
+#pragma unroll
+        for (int i = 0; i < EPT; i++) {
+            const int e = tid + 256 * i;
+            float pv[8];
+#pragma unroll
+            for (int s = 0; s < 8; s++) pv[s] = e < 128 * T && s < p.nsplit ? ld_cluster_f32(fin + e, s) : 0.0f;
+            v[i] = 0.0f;
+#pragma unroll
+            for (int s = 0; s < 8; s++)
+                if (s < p.nsplit) v[i] += pv[s];
+        }
+        cluster_arrive();  // the other ranks' shared memory is read
+#pragma unroll
+        for (int i = 0; i < EPT; i++)
+            if (tid + 256 * i < 128 * T) fin[tid + 256 * i] = v[i];
+    } else if (p.nsplit > 1) {
         __syncthreads();  // every partial of this CTA is stored
         if (tid == 0) {
             // release: this CTA's partials before its count; acquire: the other CTAs' partials after theirs
@@ -1181,6 +1258,42 @@ void raise_smem_limit(const void* fn, int bytes) {
 
 int gemv_grid(const TernaryMat& m, int ab_rows) { return (m.O / 128) * m.nsplit + (ab_rows + AB_ROWS - 1) / AB_ROWS; }
 
+// Split sums through cluster shared memory (1, default) or the global partial buffer (0); a test hook compares them.
+static std::atomic<int> g_gemv_clusters{1};
+
+// Whether `nclusters` clusters of `csize` CTAs of kernel fn (256 threads, smem bytes of dynamic shared memory) are
+// resident on the current device at once, as the grid-built operand's wait needs (a cluster's CTAs share one GPC).
+// Cached per (kernel, shared memory, cluster size, clusters, device).
+static bool gemv_clusters_fit(const void* fn, size_t smem, int csize, int nclusters) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, size_t, int, int, int>, bool> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_tuple(fn, smem, csize, nclusters, dev);
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(csize * nclusters));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const bool ok = cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n >= nclusters;
+    if (!ok) cudaGetLastError();  // a refused query leaves no sticky error behind
+    std::lock_guard<std::mutex> g(mu);
+    cache[key] = ok;
+    return ok;
+}
+
 // Whether this GEMV's CTAs can build its operand together (grid_build): every CTA of the grid resident at once
 // (they wait for one another) and at most 2 tasks (one per group of four warps) per CTA.
 bool gemv_coresident(const TernaryMat& m, int T, int ab_rows, int hb, int num_sms, int lora_r) {
@@ -1227,7 +1340,28 @@ void launch_ternary_gemv(const TernaryMat& m, const ActSrc& src, int T, const Ge
     const void* fn = gemv_fn(nt, m.group, hb, p.lora.a != nullptr, gemv_grid(m, p.ab_rows) <= device_sms());
     void* args[] = {&p};
     const int n_ab = (p.ab_rows + AB_ROWS - 1) / AB_ROWS;
+    // a row block's K-splits as one cluster (at most 8, the portable size) when every cluster is resident at once
+    p.csplit = 0;
+    if (m.nsplit > 1 && m.nsplit <= 8 && g_gemv_clusters.load(std::memory_order_relaxed)) {
+        const int ncl = p.nrb + (n_ab + m.nsplit - 1) / m.nsplit;  // the a/b gate CTAs padded to whole clusters
+        if (gemv_clusters_fit(fn, smem, m.nsplit, ncl)) {
+            p.csplit = 1;
+            launch_pdl_cluster(fn, dim3((unsigned)(ncl * m.nsplit)), m.nsplit, smem, st, args);
+            return;
+        }
+    }
     launch_pdl(fn, dim3((unsigned)(p.n_main + n_ab)), dim3(256), smem, st, args);
 }
+
+}  // namespace bcu
+
+// Test hook (not in the ABI header): 0 = split GEMVs sum through the global partial buffer, 1 = through cluster
+// shared memory where the clusters fit (the default). Both give the same bits.
+extern "C" int bcu_gemv_set_clusters(int on) {
+    bcu::g_gemv_clusters.store(on ? 1 : 0);
+    return 0;
+}
+
+namespace bcu {
 
 }  // namespace bcu

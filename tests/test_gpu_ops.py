@@ -114,6 +114,31 @@ def test_rotate_linear_grid_and_local_build_agree(gpu, O, K, group, HB, T):
     assert np.all(np.abs(grid.astype(np.float64) - want) <= bound)
 
 
+@pytest.mark.parametrize("O,K,group,HB,T", [(2048, 4096, 64, 512, 9), (2048, 6144, 64, 512, 9),
+                                            (2048, 4096, 64, 512, 16), (1024, 2560, 64, 512, 1),
+                                            (1024, 8192, 128, 512, 4)])
+def test_split_sums_cluster_and_partial_buffer_agree(gpu, O, K, group, HB, T):
+    """A row block's K-split sums through the shared memory of a thread-block cluster (the default when the clusters
+    fit; 8 and 6 splits here, 5 for the 4B shape's 2560 inputs) and through the global partial buffer (the path for
+    more than 8 splits, the last case): the same sums in the same order, so the outputs are the same bits."""
+    torch = pytest.importorskip("torch")
+    W, S, B, X = ternary_case(O, K, group, T, "neg", 500 + K + T)
+    xb = bf16_bits(torch, X)
+    signs = np.where(np.random.default_rng(K).random(K) < 0.5, -1, 1).astype(np.float32)
+    lin = Linear(W, S, B, group)
+    try:
+        cl = lin.rotate_forward(torch, xb, HB, signs)
+        assert lin.L.bcu_gemv_set_clusters(0) == 0
+        buf = lin.rotate_forward(torch, xb, HB, signs)
+    finally:
+        lin.L.bcu_gemv_set_clusters(1)
+    assert np.array_equal(cl.view(np.uint32), buf.view(np.uint32))
+    want, xr = orc.rotate_ternary_linear(W, S, B, group, xb, HB, signs)
+    Wd = refimpl.dense_weights(W, S, B, group)
+    bound = 2e-5 * (np.abs(xr).astype(np.float64) @ np.abs(Wd).T) + 1e-5
+    assert np.all(np.abs(cl.astype(np.float64) - want) <= bound)
+
+
 @pytest.mark.parametrize("n", list(range(10)))
 def test_config2_gdn_verify_rollback(gpu, n):
     torch = pytest.importorskip("torch")
