@@ -30,18 +30,20 @@ bcu_status fail(bcu_model* m, bcu_status s, const std::string& msg) {
                         std::string(#call) + ": " + cudaGetErrorString(e_));                                  \
     } while (0)
 
-// Polls the model stream with a deadline instead of blocking (every host wait is bounded).
+// Polls the model stream with a deadline instead of blocking (every host wait is bounded). The first SPIN_S seconds
+// poll without sleeping: a verify pass ends a few ms after it is launched, and a sleep (which the OS may stretch to
+// tens of µs) would add its wake-up latency to every decode round; longer waits poll every 20 µs.
 bcu_status wait_stream(bcu_model* m, double seconds) {
+    constexpr double SPIN_S = 0.01;
     CK(cudaEventRecord(m->ev_done, m->st));
     auto t0 = std::chrono::steady_clock::now();
-    int spins = 0;
     for (;;) {
         cudaError_t e = cudaEventQuery(m->ev_done);
         if (e == cudaSuccess) break;
         if (e != cudaErrorNotReady) return fail(m, BCU_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(e));
-        if (++spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
         double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (el > seconds) return fail(m, BCU_ERR_TIMEOUT, "device work did not finish within the deadline");
+        if (el > SPIN_S) std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
     return BCU_OK;
 }
