@@ -43,7 +43,8 @@ __device__ void head_operand(const HeadArgs& a, int t, uint32_t* s_b) {
     for (int i = lane; i < a.nss; i += 32) ss += a.ss[i * VMAX + t];
     float r = rsqrtf(warp_sum(ss) / (float)d + 1e-6f);
     const int nt = t >> 2, gb = (t & 3) * 2, t4 = (lane & 7) >> 1, which = (lane & 15) >> 3;
-    for (int kb = 0; kb < d; kb += 256) {  // 8 loads per lane in flight together
+#pragma unroll 4
+    for (int kb = 0; kb < d; kb += 256) {  // 8 loads per lane and step, four steps' loads in flight together
         float hv[8], wv[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) hv[i] = a.h[(size_t)t * d + kb + i * 32 + lane];
@@ -90,14 +91,37 @@ __device__ void head_finish(const HeadArgs& a, int T) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (tid < T) {
+    // one warp per row: lane l takes the partials of CTAs l, l + 32, ... with all its loads in flight together, then
+    // a butterfly over the lanes. argmax_merge is a total order on (value, index) pairs (NaN never enters), so any
+    // merge order gives the same winner.
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int t = warp; t < T; t += 8) {
         float v = -INFINITY;
         int i = 0x7fffffff;
-        for (int c = 0; c < (int)gridDim.x; c++)
-            argmax_merge(v, i, __ldcg(a.pv + (size_t)c * T + tid), __ldcg(a.pi + (size_t)c * T + tid));
-        if (i == 0x7fffffff) i = 0;  // every logit NaN or -inf: index 0, like argmax2's initial value
-        pred[tid] = (uint32_t)i;
-        a.ctl->pred[tid] = (uint32_t)i;
+        for (int c0 = 0; c0 < (int)gridDim.x; c0 += 256) {
+            float pv[8];
+            int pi[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int c = c0 + lane + 32 * j;
+                const bool in = c < (int)gridDim.x;
+                pv[j] = in ? __ldcg(a.pv + (size_t)c * T + t) : -INFINITY;
+                pi[j] = in ? __ldcg(a.pi + (size_t)c * T + t) : 0x7fffffff;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) argmax_merge(v, i, pv[j], pi[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+            argmax_merge(v, i, ov, oi);
+        }
+        if (lane == 0) {
+            if (i == 0x7fffffff) i = 0;  // every logit NaN or -inf: index 0, like argmax2's initial value
+            pred[t] = (uint32_t)i;
+            a.ctl->pred[t] = (uint32_t)i;
+        }
     }
     __syncthreads();
     if (tid == 0) {
