@@ -11,7 +11,9 @@
  *  - Plain C types only; every call returns a bcu_status; bcu_last_error() gives the message of the last failure.
  *  - One bcu_model per host thread at a time (the reference serialises the model behind a mutex, handle.rs:96-103).
  *  - Host buffers passed to a call are borrowed for the duration of that call only.
- *  - Every host wait has a deadline (BCU_ERR_TIMEOUT) instead of blocking forever.
+ *  - Every host wait has a deadline (BCU_ERR_TIMEOUT) instead of blocking forever. A wait polls the device without
+ *    sleeping for its first 10 ms (a verify pass takes a few ms, and a sleep's wake-up latency would be added to every
+ *    decode round), then every 20 us: the calling thread keeps one host core busy while it waits.
  *  - Token ids are uint32 (the reference's u32 ids, runtime/mod.rs:24).
  */
 #ifndef BONSAI_CUDA_H
